@@ -1,0 +1,375 @@
+#!/usr/bin/env python
+"""MoE-layer tokens/s on B200 (llm.c's moe_forward hot path).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c5]
+  python bench.py --impl reference ...   # the reference's CPU moe_forward
+
+A step is one forward of the MoE layer over the config's T tokens.  With N
+GPUs (torchrun) the layer runs expert-parallel: tokens are split across
+ranks, experts' work is balanced across ranks, and NCCL all-to-alls carry
+the dispatch and the combine; `value` is the whole job's tokens/s and the
+timing is the max over ranks.  Inputs are seeded synthetic tensors with
+the config's shapes and distributions (no dataset is involved).
+
+Printed: one JSON line on rank 0 (see the keys in `main`).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "llm.c_b200"))
+
+CONFIGS = {
+    # name: T, d, E, k, F, seed, bias
+    "c1": dict(T=2048, d=256, E=8, k=2, F=1024, seed=0, bias=None),
+    "c3": dict(T=16384, d=1024, E=16, k=2, F=4096, seed=1, bias="normal"),
+    "c4": dict(T=256, d=2048, E=32, k=4, F=5632, seed=0, bias=None),
+    "c5": dict(T=65536, d=4096, E=64, k=2, F=14336, seed=0, bias="zipf"),
+}
+W_STD = 0.02
+ZIPF_S = 1.1
+
+
+def flops_per_step(c):
+    T, d, E, k, F = c["T"], c["d"], c["E"], c["k"], c["F"]
+    return 2.0 * T * d * E + 6.0 * T * k * d * F
+
+
+def min_bytes_per_step(c, experts_touched):
+    T, d, E, k, F = c["T"], c["d"], c["E"], c["k"], c["F"]
+    return 4.0 * (d * E + experts_touched * 3 * d * F + 2 * T * d) + 4.0 * T * E + 4.0 * T * k
+
+
+def zipf_bias(E):
+    return (-ZIPF_S * np.log(np.arange(1, E + 1, dtype=np.float64))).astype(np.float32)
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return {"hbm_gbs": j["hbm_gbs"], "bf16": j["bf16_tflops"],
+                "bf16_sustained": j.get("bf16_tflops_sustained", j["bf16_tflops"]),
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# CPU: the reference's own moe_forward on a bounded sample of the workload
+# ----------------------------------------------------------------------------
+def reference_sample(c, budget_s, threads):
+    """Time llm.c's moe_forward (oracle/_ref, the unmodified reference
+    sources) on S tokens of the config, S sized to ~budget_s seconds.
+
+    Every token costs the same k expert FFNs, so tokens/s of a sample is
+    the workload's.  For large expert sets only the weights of 8 experts
+    are materialised on the host and the sample is drawn from tokens whose
+    top-k (by the reference's bias-free router, with a clear logit margin)
+    stays inside them; the other experts' weights are never read.
+    Returns (tokens_per_s, S, kind, description)."""
+    sys.path.insert(0, str(REPO / "tests"))
+    import oracle_lib as O
+
+    T, d, E, k, F, seed = c["T"], c["d"], c["E"], c["k"], c["F"], c["seed"]
+    kind = "reference" if O.ref_available() else "port"
+    R = min(T, 8192)
+    x = O.synth(seed, O.stream_x(), R * d, 1.0).reshape(R, d)
+    wr = O.synth(seed, O.stream_router(), d * E, W_STD).reshape(d, E)
+    logits = np.empty((R, E), np.float32)
+    ids = np.empty((R, k), np.int32)
+    O.oracle().oracle_router(O._f(x), R, d, O._f(wr), None, E, k, O._f(logits), None,
+                             O._i(ids), None)
+    weight_bytes = 3 * d * F * 4
+    if E * weight_bytes <= 8e9:
+        U = list(range(E))
+        cand = np.arange(R)
+    else:
+        U = list(np.argsort(-np.bincount(ids.ravel(), minlength=E), kind="stable")[:8])
+        srt = -np.sort(-logits, axis=1)
+        margin = srt[:, k - 1] - srt[:, k]
+        ok = np.all(np.isin(ids, U), axis=1) & (margin > 1e-3)
+        cand = np.nonzero(ok)[0]
+    dummy = np.zeros(1, np.float32)
+    g, u, dn = [dummy] * E, [dummy] * E, [dummy] * E
+    for e in U:
+        g[e] = O.synth(seed, O.stream_expert(e, 0), d * F, W_STD).reshape(d, F)
+        u[e] = O.synth(seed, O.stream_expert(e, 1), d * F, W_STD).reshape(d, F)
+        dn[e] = O.synth(seed, O.stream_expert(e, 2), F * d, W_STD).reshape(F, d)
+    gp = O._ptr_array(g)
+    up = O._ptr_array(u)
+    dp = O._ptr_array(dn)
+
+    def run(rows):
+        xs = np.ascontiguousarray(x[rows])
+        n = len(rows)
+        out = np.empty((n, d), np.float32)
+        probs = np.empty((n, E), np.float32)
+        idr = np.empty((n, k), np.int32)
+        t0 = time.perf_counter()
+        if kind == "reference":
+            O.ref().ref_moe_forward(O._f(xs), n, d, O._f(wr), E, k, gp, up, dp, F, O._f(out),
+                                    O._f(probs), O._i(idr))
+        else:
+            O.oracle().oracle_moe_forward(O._f(xs), n, d, O._f(wr), None, E, k, gp, up, dp, F,
+                                          None, n, None, O._f(out), O._f(probs), O._i(idr),
+                                          threads)
+        return time.perf_counter() - t0
+
+    if kind == "reference":
+        O.ref().ref_set_threads(threads)
+    probe = cand[: max(1, min(len(cand), 4))]
+    t_probe = run(probe) / len(probe)
+    S = int(max(1, min(len(cand), budget_s / max(t_probe, 1e-9))))
+    rows = cand[:S]
+    dt = run(rows)
+    desc = (f"{S} of the config's tokens (first {R} rows, experts {len(U)} of {E} resident"
+            f"{'' if len(U) == E else ', tokens routed inside them'}), {threads} threads, "
+            f"router without bias (the reference has none; per-token cost is unchanged)")
+    return S / dt, S, kind, desc, run, rows
+
+
+def run_reference_arm(args, c):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = len(os.sched_getaffinity(0))
+    tps, S, kind, desc, run, rows = reference_sample(c, budget_s=args.ref_budget, threads=threads)
+    for _ in range(args.warmup):
+        run(rows)
+    times = [run(rows) for _ in range(args.steps)]
+    ms = 1000.0 * statistics.mean(times)
+    value = S / (ms / 1000.0)
+    line = {
+        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
+        "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config, **{kk: c[kk] for kk in ("T", "d", "E", "k", "F")},
+                   "sample_tokens": S},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# GPU
+# ----------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c5", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--path", default="auto", choices=["auto", "tf32", "fp32"])
+    ap.add_argument("--ref-budget", type=float, default=6.0,
+                    help="seconds of CPU work per reference sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    c = CONFIGS[args.config]
+
+    if args.impl == "reference":
+        run_reference_arm(args, c)
+        return
+
+    import torch
+    import moe_b200 as M
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        raise SystemExit("expert-parallel runs need the EP build (not in this library yet)")
+
+    M.init(local)
+    path = {"auto": M.PATH_AUTO, "tf32": M.PATH_TF32, "fp32": M.PATH_FP32}[args.path]
+    T, d, E, k, F, seed = c["T"], c["d"], c["E"], c["k"], c["F"], c["seed"]
+    w = M.MoEWeights.synth(seed, W_STD, d, F, E, k)
+    stream = torch.cuda.current_stream()
+    x = torch.empty((T, d), dtype=torch.float32, device="cuda")
+    M.synth_fill(x.data_ptr(), T * d, seed, M.STREAM_X, 1.0, cuda_stream=stream.cuda_stream)
+    bias = None
+    if c["bias"] == "zipf":
+        bias = torch.from_numpy(zipf_bias(E)).cuda()
+    elif c["bias"] == "normal":
+        bias = torch.empty(E, device="cuda")
+        M.synth_fill(bias.data_ptr(), E, seed, M.STREAM_BIAS, 1.0, cuda_stream=stream.cuda_stream)
+    out = torch.empty((T, d), dtype=torch.float32, device="cuda")
+    probs = torch.empty((T, E), dtype=torch.float32, device="cuda")
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    bptr = bias.data_ptr() if bias is not None else None
+
+    def step():
+        M.moe_forward_device(w, x.data_ptr(), T, out.data_ptr(), probs.data_ptr(), ids.data_ptr(),
+                             bias_ptr=bptr, path=path, stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches_per_step = M.last_launches()
+    counts = M.last_counts(w)
+
+    # ---- device-resident timed region
+    M.profile_enable(True)
+    M.profile_read()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    M.profile_enable(False)
+    stage_ms, n_fw = M.profile_read()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    value = T / (ms / 1000.0)
+
+    # ---- end to end through the public host-buffer C-ABI (pinned buffers,
+    # H2D of x and D2H of out/probs/ids inside every step)
+    hx = torch.empty((T, d), dtype=torch.float32, pin_memory=True)
+    hx.copy_(x.cpu())
+    hout = torch.empty((T, d), dtype=torch.float32, pin_memory=True)
+    hprobs = torch.empty((T, E), dtype=torch.float32, pin_memory=True)
+    hids = torch.empty((T, k), dtype=torch.int32, pin_memory=True)
+    hbias = bias.cpu().contiguous() if bias is not None else None
+
+    def e2e_step():
+        M.moe_forward_host_ptr(w, hx.data_ptr(), T, hout.data_ptr(), hprobs.data_ptr(),
+                               hids.data_ptr(), hbias.data_ptr() if hbias is not None else None,
+                               path=path)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ms = 1000.0 * (time.perf_counter() - t0) / args.steps
+    assert torch.equal(hout, out.cpu()), "e2e output differs from the device-resident run"
+
+    # ---- roofline of the dominant kernel (expert up/gate GEMM)
+    peaks = measured_peaks()
+    tf32_peak = peaks["bf16_sustained"] / 2.0
+    stage_avg = {s: v / max(n_fw, 1) for s, v in stage_ms.items()}
+    up_flops = 4.0 * T * k * d * F
+    up_ms = stage_avg["upgate"]
+    achieved = up_flops / (up_ms / 1000.0) / 1e12
+    traffic = None
+    tfile = REPO / "profiles" / "traffic.json"
+    if tfile.exists():
+        tj = json.loads(tfile.read_text())
+        traffic = tj.get(args.config, {}).get("upgate_bytes_per_launch")
+    touched = int(np.count_nonzero(counts))
+    t_roof = max(flops_per_step(c) / (tf32_peak * 1e12),
+                 min_bytes_per_step(c, touched) / (peaks["hbm_gbs"] * 1e9))
+
+    line = {
+        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": args.config, "T": T, "d_model": d, "n_experts": E, "top_k": k,
+                   "d_ff": F, "router_bias": c["bias"], "path": args.path,
+                   "parallelism": f"ep{world}", "l2": "inputs larger than L2"
+                   if 4 * T * d > 126e6 else "inputs smaller than L2 (no flush)"},
+        "e2e": {"value": T / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": 4 * T * d + (4 * E if bias is not None else 0),
+                "d2h_bytes_per_step": 4 * T * d + 4 * T * E + 4 * T * k,
+                "timing": "host wall clock around synchronous moe_b200_forward calls"},
+        "roofline": {"bound": "tensor", "kernel": "tc_grouped_gemm<256,swiglu> (expert up/gate)",
+                     "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+                     "frac": achieved / tf32_peak, "traffic": traffic,
+                     "peak_src": f"{peaks['src']} bf16 sustained / 2 (TF32 rate)",
+                     "layer_frac": t_roof / (ms / 1000.0)},
+        "stages_ms": stage_avg,
+        "expert_counts_max_over_mean": float(counts.max() / counts.mean()),
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = len(os.sched_getaffinity(0))
+        tps, S, kind, desc, _, _ = reference_sample(c, budget_s=12.0, threads=threads)
+        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": kind,
+                                "sample": desc}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    w.free()
+
+
+if __name__ == "__main__":
+    main()

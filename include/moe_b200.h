@@ -1,0 +1,176 @@
+/*
+ * moe_b200.h — C-ABI of the B200-native Mixture-of-Experts feed-forward
+ * hot path of llm.c.
+ *
+ * Every entry point is plain C: host or device pointers, sizes and status
+ * codes.  No CUDA or PyTorch type appears in a signature (streams are
+ * passed as `void *` holding a cudaStream_t, NULL = the library's stream).
+ *
+ * The computation is the reference's moe_forward (llm.c
+ * src/transformer.c:287-366): router logits x·W_router (+ optional bias),
+ * row softmax, per-token top-k by probability with ties to the lower
+ * expert index, weights renormalised over the selected k, SwiGLU experts
+ * y = (silu(x·W_gate) ⊙ (x·W_up))·W_down, and the weighted combine in
+ * rank order.  Outputs are overwritten, never accumulated into.
+ *
+ * All calls return MOE_B200_OK (0) or a negative status; there is no CPU
+ * fallback: without a usable sm_100 device every compute call fails with
+ * MOE_B200_E_NODEV.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MOE_B200_OK          0
+#define MOE_B200_E_INVALID  (-1)  /* bad argument or unsupported shape      */
+#define MOE_B200_E_CUDA     (-2)  /* a CUDA runtime call failed             */
+#define MOE_B200_E_NOMEM    (-3)  /* device or pinned allocation failed      */
+#define MOE_B200_E_NCCL     (-4)  /* NCCL failure (expert parallel)          */
+#define MOE_B200_E_TIMEOUT  (-5)  /* a bounded device wait ran out           */
+#define MOE_B200_E_NODEV    (-6)  /* no usable sm_100 device                 */
+#define MOE_B200_E_STATE    (-7)  /* call made in the wrong state            */
+
+/* ---- expert arithmetic path ------------------------------------------- */
+#define MOE_B200_PATH_AUTO  0  /* TF32 tensor cores for prefill-sized expert
+                                  groups, FP32 weight streaming for decode  */
+#define MOE_B200_PATH_TF32  1  /* tcgen05 TF32 grouped GEMMs (tol 2e-3)     */
+#define MOE_B200_PATH_FP32  2  /* FP32 FFMA everywhere (tol 1e-5)           */
+
+typedef struct {
+    int path;            /* MOE_B200_PATH_*                                   */
+    int reserved[7];     /* zero                                              */
+} moe_b200_opts;
+
+/* Opaque device-resident expert set (router + E SwiGLU experts). */
+typedef struct moe_b200_weights moe_b200_weights;
+
+/* ---- library ----------------------------------------------------------- */
+
+/* Version string of the library build. */
+const char *moe_b200_version(void);
+
+/* Human-readable name of a status code. */
+const char *moe_b200_strerror(int status);
+
+/* Detail text of the last failure on this host thread ("" if none). */
+const char *moe_b200_last_error(void);
+
+/* Select and initialise a CUDA device for this host thread (creates the
+ * library stream and workspace lazily).  device < 0 keeps the current one. */
+int moe_b200_init(int device);
+
+/* Release every device resource the library holds on all devices. */
+void moe_b200_shutdown(void);
+
+/* ---- weights ----------------------------------------------------------- */
+
+/* Upload an expert set from the reference's host layout (row-major fp32):
+ *   W_router [d×E]; W_gate[e], W_up[e] [d×F]; W_down[e] [F×d].
+ * Replaces llm.c's implicit use of host MoEWeights (include/transformer.h
+ * :53-58).  The library repacks the experts once on the device into its
+ * K-major, gate/up-interleaved layout; the host arrays are not retained. */
+int moe_b200_weights_upload(const float *W_router,
+                            const float *const *W_gate,
+                            const float *const *W_up,
+                            const float *const *W_down,
+                            int d, int F, int E, int top_k,
+                            moe_b200_weights **out);
+
+/* Build an expert set directly on the device from the seeded synthetic
+ * generator (every weight ~N(0, w_std), streams as in
+ * moe_b200_synth_fill), for benchmarks whose weights would not fit in
+ * host memory.  Equivalent to generating the host arrays and calling
+ * moe_b200_weights_upload. */
+int moe_b200_weights_synth(uint64_t seed, float w_std, int d, int F, int E,
+                           int top_k, moe_b200_weights **out);
+
+/* Free a weight set (synchronises the device). */
+int moe_b200_weights_free(moe_b200_weights *w);
+
+/* Shape of a weight set. */
+int moe_b200_weights_shape(const moe_b200_weights *w, int *d, int *F, int *E,
+                           int *top_k);
+
+/* Copy the device weights back into the reference host layout (for
+ * checkpoint round trips and tests).  Any output pointer may be NULL. */
+int moe_b200_weights_download(const moe_b200_weights *w, float *W_router,
+                              float *const *W_gate, float *const *W_up,
+                              float *const *W_down);
+
+/* ---- forward ----------------------------------------------------------- */
+
+/* MoE forward on HOST buffers; synchronous, like llm.c's moe_forward.
+ *   x            [T×d] input rows (cache->x_norm_ffn in llm.c)
+ *   router_bias  [E] added to the logits before the softmax, or NULL
+ *                (NULL is the reference's behaviour)
+ *   out          [T×d] overwritten
+ *   router_probs [T×E] full softmax, or NULL   (cache->router_probs)
+ *   expert_ids   [T×k] rank-ordered ids, or NULL (cache->expert_ids)
+ * T = 0 is a no-op.  opts may be NULL (MOE_B200_PATH_AUTO). */
+int moe_b200_forward(const moe_b200_weights *w, const float *router_bias,
+                     const float *x, int T, float *out, float *router_probs,
+                     int *expert_ids, const moe_b200_opts *opts);
+
+/* Same computation on DEVICE buffers, asynchronous on `stream`
+ * (a cudaStream_t, or NULL for the library stream).  No host
+ * synchronisation and no allocation once the workspace has grown to T, so
+ * the call can be captured in a CUDA graph after one warm-up call at the
+ * largest T. */
+int moe_b200_forward_device(const moe_b200_weights *w, const float *d_bias,
+                            const float *d_x, int T, float *d_out,
+                            float *d_router_probs, int *d_expert_ids,
+                            const moe_b200_opts *opts, void *stream);
+
+/* Per-expert token counts of the last forward on this device (host array
+ * of E ints); synchronises the library stream. */
+int moe_b200_last_counts(const moe_b200_weights *w, int *counts);
+
+/* Number of kernel launches the last forward issued on this device. */
+int moe_b200_last_launches(void);
+
+/* ---- stage timing ------------------------------------------------------ */
+
+/* Stages of one forward, in launch order. */
+#define MOE_B200_STAGE_ROUTER    0   /* logits, softmax, top-k, tile histogram */
+#define MOE_B200_STAGE_DISPATCH  1   /* scan + permutation/gather              */
+#define MOE_B200_STAGE_UPGATE    2   /* expert x·[W_gate|W_up] + SwiGLU        */
+#define MOE_B200_STAGE_DOWN      3   /* expert h·W_down                        */
+#define MOE_B200_STAGE_COMBINE   4   /* weighted rank-order combine            */
+#define MOE_B200_NUM_STAGES      5
+
+/* Enable (1) or disable (0) per-stage CUDA-event timing of every forward
+ * on this device.  Events are recorded on the stream the kernels run on. */
+int moe_b200_profile_enable(int enable);
+
+/* Sum of each stage's device time in ms (stage_ms[MOE_B200_NUM_STAGES])
+ * and the number of forwards timed since the last read; resets both.
+ * Synchronises the timed streams. */
+int moe_b200_profile_read(double *stage_ms, int *n_forwards);
+
+/* ---- synthetic inputs (benchmark plumbing) ----------------------------- */
+
+/* Fill d_dst[0..n) on the device with the seeded approximately-N(0,std)
+ * generator: element i is the Irwin–Hall sum of twelve 16-bit uniforms
+ * from three splitmix64 hashes of (seed, stream, first + i), minus 6,
+ * times std — bit-identical to the host generator of the test oracle. */
+int moe_b200_synth_fill(float *d_dst, size_t n, uint64_t seed,
+                        uint64_t stream, uint64_t first, float std,
+                        void *cuda_stream);
+
+/* Stream ids used by moe_b200_weights_synth and the benchmarks. */
+#define MOE_B200_STREAM_X       1ULL
+#define MOE_B200_STREAM_ROUTER  2ULL
+#define MOE_B200_STREAM_BIAS    3ULL
+#define MOE_B200_STREAM_EXPERT(e, which) (0x100ULL + 4ULL * (uint64_t)(e) + (uint64_t)(which))
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_B200_H */

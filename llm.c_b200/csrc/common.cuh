@@ -1,0 +1,112 @@
+// common.cuh — shared device helpers of the MoE hot path.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define MOE_DEV __device__ __forceinline__
+
+namespace moe {
+
+constexpr int kMaxExperts = 128;   // router/dispatch limit (configs use <= 64)
+constexpr int kMaxTopK = 8;
+
+template <typename T>
+__host__ __device__ __forceinline__ T ceil_div(T a, T b) { return (a + b - 1) / b; }
+
+template <typename T>
+__host__ __device__ __forceinline__ T round_up(T a, T b) { return ceil_div(a, b) * b; }
+
+// ---------------------------------------------------------------------
+// exp as llm.c's softmax and SwiGLU compute it (src/matrix.c:82-116):
+// clamp to [-88, 88], split v*log2(e) = n + f with n = floor, evaluate
+// 2^f with the reference's degree-6 polynomial table in Horner form with
+// fused multiply-adds, and scale by 2^n built in the exponent field.
+// Using the same table keeps router probabilities bit-identical to the
+// reference's for identical logits.
+// ---------------------------------------------------------------------
+MOE_DEV float exp_ref(float v) {
+    v = fminf(fmaxf(v, -88.0f), 88.0f);
+    const float z = __fmul_rn(v, 1.4426950408f);
+    const float n = floorf(z);
+    const float f = __fsub_rn(z, n);
+    float p = 0.0001540353f;
+    p = __fmaf_rn(p, f, 0.0013333558f);
+    p = __fmaf_rn(p, f, 0.0096181292f);
+    p = __fmaf_rn(p, f, 0.0555041086f);
+    p = __fmaf_rn(p, f, 0.2402265069f);
+    p = __fmaf_rn(p, f, 0.6931471806f);
+    p = __fmaf_rn(p, f, 1.0000000000f);
+    const int ni = __float2int_rn(n);
+    const float scale = __int_as_float((ni + 127) << 23);
+    return __fmul_rn(p, scale);
+}
+
+// silu(g) * u as llm.c's swiglu computes it (src/matrix.c:618-655):
+// sigmoid = 1 / (1 + exp(-g)), silu = g * sigmoid, h = silu * u.
+MOE_DEV float swiglu_ref(float g, float u) {
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_ref(-g)));
+    return __fmul_rn(__fmul_rn(g, sig), u);
+}
+
+// Round an fp32 value to the nearest TF32 (10-bit mantissa, ties away
+// from zero), returned as fp32 bits with the low 13 mantissa bits zero.
+// tcgen05 kind::tf32 reads only the TF32 bits of its fp32 operands, i.e.
+// truncates; rounding the activations first removes that one-sided bias.
+MOE_DEV float round_tf32(float v) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return __uint_as_float(r);
+}
+
+// ---------------------------------------------------------------------
+// Seeded synthetic generator (bit-identical to the oracle's host copy).
+// ---------------------------------------------------------------------
+__host__ __device__ __forceinline__ uint64_t sm64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ULL;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    return z ^ (z >> 31);
+}
+
+__host__ __device__ __forceinline__ uint64_t synth_key(uint64_t seed, uint64_t stream) {
+    return sm64(sm64(seed) ^ (stream * 0xD6E8FEB86659FD93ULL));
+}
+
+__host__ __device__ __forceinline__ float synth_value(uint64_t key, uint64_t idx, float std) {
+    uint32_t s = 0;
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        const uint64_t h = sm64(key + 3ULL * idx + (uint64_t)j);
+        s += (uint32_t)(h & 0xFFFF) + (uint32_t)((h >> 16) & 0xFFFF) +
+             (uint32_t)((h >> 32) & 0xFFFF) + (uint32_t)(h >> 48);
+    }
+#ifdef __CUDA_ARCH__
+    const float z = __fmul_rn((float)((int32_t)s - 393210), 1.0f / 65536.0f);
+    return __fmul_rn(z, std);
+#else
+    const float z = (float)((int32_t)s - 393210) * (1.0f / 65536.0f);
+    return z * std;
+#endif
+}
+
+// ---------------------------------------------------------------------
+// Bounded waits: every spin in this library gives up after kWaitNs
+// nanoseconds of %globaltimer, records a timeout and lets the kernel
+// leave cleanly instead of hanging the GPU.
+// ---------------------------------------------------------------------
+constexpr uint64_t kWaitNs = 2000000000ULL;   // 2 s
+
+MOE_DEV uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Error word written by kernels (device-global, read by the host).
+struct DeviceStatus {
+    int timeout;       // nonzero: a bounded wait ran out (code = site id)
+    int bad_index;     // nonzero: a bounds check rejected an index
+};
+
+}  // namespace moe

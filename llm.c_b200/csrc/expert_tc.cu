@@ -1,0 +1,413 @@
+// expert_tc.cu — tcgen05 TF32 grouped expert GEMMs for prefill-sized
+// expert groups (llm.c src/transformer.c:157-165, batched over all tokens
+// routed to each expert).
+//
+// One persistent CTA per SM walks a static round-robin list of output
+// tiles (expert, 128-row m-tile, BN-column n-tile).  Warp roles:
+//   warp 0      TMA producer: 128B-swizzled K-major tiles of activations
+//               (128×32 fp32) and weights (BN×32 fp32) into a 4-stage
+//               shared-memory ring (plain loads, no cluster multicast)
+//   warp 1      TMEM allocator and MMA issuer: tcgen05.mma kind::tf32,
+//               M=128, N=BN, K=8, four per stage, accumulating in TMEM;
+//               tcgen05.commit frees the smem stage / publishes the tile
+//   warps 2..5  epilogue: tcgen05.ld 32x32b rows out of TMEM (two
+//               accumulator buffers, so the epilogue of tile i overlaps
+//               the main loop of tile i+1), fused SwiGLU for up/gate,
+//               row-masked stores.
+// Tile order inside an expert is grouped by GM m-tiles so that the CTAs
+// running together share a few weight tiles and a few activation row
+// blocks in L2.
+//
+// Every mbarrier wait is bounded (kWaitNs of %globaltimer); a timeout
+// sets an abort flag that all roles observe, records the site in the
+// device status word, and the CTA drains its in-flight MMAs and TMA loads
+// before it frees TMEM and exits.
+#include "kernels.cuh"
+
+namespace moe {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 32;          // fp32 elements per K step = 128 bytes
+constexpr int STAGES = 4;
+constexpr int GM = 8;           // m-tiles per raster group
+constexpr int kThreads = 192;
+constexpr int A_BYTES = BM * BK * 4;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait.  Returns false on timeout or when another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          volatile int *abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (abort_flag && *abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row core
+// groups 1024 bytes apart (SBO), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) |
+           ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::tf32: D=F32, A=B=TF32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes; the wait is in
+// the same asm statement so no use of the registers can precede it.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+struct TileCoord {
+    int e, ml, ni;
+};
+
+// tile -> (expert, m-tile within expert, n-tile); tiles of expert e are
+// [mt128[e]*NT, mt128[e+1]*NT), grouped by GM m-tiles, n-tiles inside.
+__device__ __forceinline__ TileCoord decode_tile(int tile, const int *mt, int E, int NT) {
+    int lo = 0, hi = E;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(mt + mid) * NT <= tile) lo = mid; else hi = mid - 1;
+    }
+    TileCoord c;
+    c.e = lo;
+    const int m0 = __ldg(mt + lo);
+    const int mcount = __ldg(mt + lo + 1) - m0;
+    const int l = tile - m0 * NT;
+    const int g = l / (GM * NT);
+    const int rem = l - g * GM * NT;
+    const int gcount = min(GM, mcount - g * GM);
+    c.ni = rem / gcount;
+    c.ml = g * GM + (rem - c.ni * gcount);
+    return c;
+}
+
+template <int BN, bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1)
+tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const int *__restrict__ plan, int E, int num_kb, int b_rows_per_expert,
+                int NT, float *__restrict__ out, int ldo, DeviceStatus *status)
+{
+    constexpr int B_BYTES = BN * BK * 4;
+    constexpr uint32_t TMEM_COLS = 2 * BN;        // two accumulator buffers
+    constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                ~static_cast<uintptr_t>(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * A_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + STAGES;
+    uint64_t *tfull = bars + 2 * STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *fin = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        mbar_init(fin, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+    }
+    __syncwarp();
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int *cnt = plan;
+    const int *off = plan + E;
+    const int *mt = off + E + 1;
+    const int total = __ldg(mt + E) * NT;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int issued[STAGES];
+            uint32_t issued_phase[STAGES];
+            for (int s = 0; s < STAGES; s++) issued[s] = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                const TileCoord c = decode_tile(tile, mt, E, NT);
+                const int a_row = __ldg(off + c.e) + c.ml * BM;
+                const int b_row = c.e * b_rows_per_expert + c.ni * BN;
+                for (int kb = 0; kb < num_kb; kb++) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+                    mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+                    tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, a_row, &full[stage]);
+                    tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, b_row, &full[stage]);
+                    issued[stage] = 1;
+                    issued_phase[stage] = phase;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+            }
+            if (!ok || *abort_flag) {
+                if (!*abort_flag) { *abort_flag = 1; atomicExch(&status->timeout, 1); }
+                // drain TMA loads still in flight into this CTA's smem
+                for (int s = 0; s < STAGES; s++)
+                    if (issued[s]) mbar_wait(&full[s], issued_phase[s], nullptr);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < num_kb; kb++) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+                    const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; kk++)
+                        mma_tf32(d_tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), IDESC,
+                                 (kb | kk) ? 1u : 0u);
+                    mma_commit(&empty[stage]);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                }
+                if (!ok) break;
+                mma_commit(&tfull[acc]);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1;
+            }
+            if (!ok && !*abort_flag) { *abort_flag = 1; atomicExch(&status->timeout, 2); }
+            // all MMAs issued by this CTA complete before TMEM is released
+            mma_commit(fin);
+            mbar_wait(fin, 0, nullptr);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int row_in_tile = q * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+            const TileCoord c = decode_tile(tile, mt, E, NT);
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+                if (!*abort_flag) { *abort_flag = 1; atomicExch(&status->timeout, 3); }
+                break;
+            }
+            tc_fence_after();
+            const int nvalid = __ldg(cnt + c.e) - c.ml * BM;
+            const bool valid = row_in_tile < nvalid;
+            const size_t grow = (size_t)(__ldg(off + c.e) + c.ml * BM + row_in_tile);
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+            if (SWIGLU) {
+                float *dst = out + grow * ldo + (size_t)c.ni * (BN / 2);
+#pragma unroll 1
+                for (int col = 0; col < BN / 2; col += 32) {
+                    float g[32], u[32];
+                    tmem_ld32(taddr + col, g);
+                    tmem_ld32(taddr + BN / 2 + col, u);
+                    if (valid) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 h;
+                            // h feeds the TF32 down GEMM: store it rounded
+                            h.x = round_tf32(swiglu_ref(g[j + 0], u[j + 0]));
+                            h.y = round_tf32(swiglu_ref(g[j + 1], u[j + 1]));
+                            h.z = round_tf32(swiglu_ref(g[j + 2], u[j + 2]));
+                            h.w = round_tf32(swiglu_ref(g[j + 3], u[j + 3]));
+                            *reinterpret_cast<float4 *>(dst + col + j) = h;
+                        }
+                    }
+                }
+            } else {
+                float *dst = out + grow * ldo + (size_t)c.ni * BN;
+#pragma unroll 1
+                for (int col = 0; col < BN; col += 32) {
+                    float v[32];
+                    tmem_ld32(taddr + col, v);
+                    if (valid) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4 *>(dst + col + j) =
+                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+    }
+
+    __syncwarp();          // lanes 1..31 of warps 0/1 wait for their lane 0
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+template <int BN>
+constexpr int smem_bytes() {
+    return STAGES * (A_BYTES + BN * BK * 4) + 1024 /*align slack*/ + 256 /*barriers*/;
+}
+
+}  // namespace tc
+
+cudaError_t tc_set_attributes() {
+    cudaError_t e;
+    e = cudaFuncSetAttribute(tc::tc_grouped_gemm<256, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, tc::smem_bytes<256>());
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(tc::tc_grouped_gemm<256, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, tc::smem_bytes<256>());
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(tc::tc_grouped_gemm<128, false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, tc::smem_bytes<128>());
+    return e;
+}
+
+static int tile_bound(int rows_bound, int E) { return ceil_div(rows_bound, tc::BM) + E; }
+
+cudaError_t launch_tc_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, const int *plan,
+                             int E, int rows_bound, int num_sms, DeviceStatus *status,
+                             cudaStream_t s)
+{
+    const int NT = F_pad / 128;               // 256 weight rows (128 gate + 128 up) per tile
+    const int bound = tile_bound(rows_bound, E) * NT;
+    const int grid = max(1, min(num_sms, bound));
+    tc::tc_grouped_gemm<256, true><<<grid, tc::kThreads, tc::smem_bytes<256>(), s>>>(
+        g.tmA, g.tmB, plan, E, d_pad / tc::BK, 2 * F_pad, NT, h, F_pad, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float *y,
+                           const int *plan, int E, int rows_bound, int num_sms,
+                           DeviceStatus *status, cudaStream_t s)
+{
+    const int NT = d_pad / bn;
+    const int bound = tile_bound(rows_bound, E) * NT;
+    const int grid = max(1, min(num_sms, bound));
+    if (bn == 256)
+        tc::tc_grouped_gemm<256, false><<<grid, tc::kThreads, tc::smem_bytes<256>(), s>>>(
+            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status);
+    else
+        tc::tc_grouped_gemm<128, false><<<grid, tc::kThreads, tc::smem_bytes<128>(), s>>>(
+            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status);
+    return cudaGetLastError();
+}
+
+}  // namespace moe

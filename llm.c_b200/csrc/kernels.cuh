@@ -1,0 +1,60 @@
+// kernels.cuh — kernel launchers of the MoE hot path (internal).
+#pragma once
+#include "common.cuh"
+#include <cuda.h>
+
+namespace moe {
+
+constexpr int kRouterTile = 32;   // tokens per router CTA
+
+// Plan (ints, device): cnt[E] | off[E+1] | mt128[E+1] | mt64[E+1]
+__host__ __device__ inline int plan_ints(int E) { return E + 3 * (E + 1); }
+
+cudaError_t launch_router(const float *x, int T, int d, const float *w_router,
+                          const float *bias, int E, int k, float *probs, int *ids,
+                          float *wts, int *loc, int *tile_cnt, cudaStream_t s);
+
+cudaError_t launch_dispatch(const float *x, int T, int d, int d_pad, int E, int k,
+                            const int *ids, const int *loc, const int *tile_cnt,
+                            int *tile_pref, int *plan, int *pos_of, float *x_perm,
+                            int round_to_tf32, DeviceStatus *status, cudaStream_t s);
+
+cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
+                           const int *pos_of, const float *wts, float *out, cudaStream_t s);
+
+// FP32 FFMA grouped expert GEMMs (64-row tiles scheduled on mt64).
+//   upgate: H[rows×F_pad] = swiglu(X_perm·Wg^T, X_perm·Wu^T)
+//   down:   Y[rows×d_pad] = H·Wd^T
+cudaError_t launch_ffma_upgate(const float *x_perm, int d_pad, const float *w_ug, int F_pad,
+                               float *h, const int *plan, int E, int rows_bound, cudaStream_t s);
+cudaError_t launch_ffma_down(const float *h, int F_pad, const float *w_d, int d_pad,
+                             float *y, const int *plan, int E, int rows_bound, cudaStream_t s);
+
+// tcgen05 TF32 grouped GEMMs (128-row tiles scheduled on mt128), persistent.
+struct TcGemm {
+    CUtensorMap tmA;   // activations [rows × K_pad], box {32, 128}, SW128
+    CUtensorMap tmB;   // weights [E*NB × K_pad], box {32, BN}, SW128
+};
+cudaError_t launch_tc_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, const int *plan,
+                             int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s);
+cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float *y, const int *plan,
+                           int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s);
+cudaError_t tc_set_attributes();
+
+// weight repack: src row-major [R × C] (one expert matrix) -> dst rows of
+// the K-major layout, see moe_b200.cu.
+cudaError_t launch_repack_upgate(const float *wg, const float *wu, int d, int F, int d_pad,
+                                 int F_pad, float *dst, cudaStream_t s);
+cudaError_t launch_repack_down(const float *wd, int d, int F, int d_pad, int F_pad, float *dst,
+                               cudaStream_t s);
+cudaError_t launch_unpack_upgate(const float *src, int d, int F, int d_pad, int F_pad,
+                                 float *wg, float *wu, cudaStream_t s);
+cudaError_t launch_unpack_down(const float *src, int d, int F, int d_pad, int F_pad, float *wd,
+                               cudaStream_t s);
+cudaError_t launch_synth(float *dst, size_t n, uint64_t seed, uint64_t stream, uint64_t first,
+                         float std, cudaStream_t s);
+cudaError_t launch_synth_pack_expert(float *ug, float *dn, int d, int F, int d_pad, int F_pad,
+                                     uint64_t seed, uint64_t stream_g, uint64_t stream_u,
+                                     uint64_t stream_d, float std, cudaStream_t s);
+
+}  // namespace moe

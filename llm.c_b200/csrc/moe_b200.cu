@@ -1,0 +1,621 @@
+// moe_b200.cu — host side of the C-ABI (include/moe_b200.h): device
+// contexts, workspace, weight residency, and the forward orchestration
+//   router -> scan -> gather -> expert up/gate(+SwiGLU) -> expert down -> combine
+// all on one stream with no host synchronisation in between (every grid
+// that depends on routing reads its tile counts from the device plan).
+#include "../../include/moe_b200.h"
+#include "kernels.cuh"
+
+#include <cuda.h>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+using namespace moe;
+
+// ---------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+#define CK(call)                                                                              \
+    do {                                                                                      \
+        cudaError_t _e = (call);                                                              \
+        if (_e != cudaSuccess)                                                                \
+            return fail(_e == cudaErrorMemoryAllocation ? MOE_B200_E_NOMEM : MOE_B200_E_CUDA, \
+                        "%s failed: %s (%s:%d)", #call, cudaGetErrorString(_e), __FILE__,     \
+                        __LINE__);                                                            \
+    } while (0)
+
+// ---------------------------------------------------------------------
+// tensor maps (driver entry point fetched through the runtime, so the
+// library does not link libcuda directly)
+// ---------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D fp32 row-major [rows × cols] tensor, box {32, box_rows}, 128B swizzle.
+static int make_tmap(CUtensorMap *m, const float *ptr, int64_t rows, int64_t cols, int box_rows) {
+    EncodeTiledFn enc = get_encode();
+    if (!enc) return fail(MOE_B200_E_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MOE_B200_E_CUDA, "cuTensorMapEncodeTiled error %d", (int)r);
+    return MOE_B200_OK;
+}
+
+// ---------------------------------------------------------------------
+// per-device context and workspace
+// ---------------------------------------------------------------------
+namespace {
+
+struct Buf {
+    void *p = nullptr;
+    size_t cap = 0;
+};
+
+static int grow(Buf &b, size_t bytes) {
+    if (bytes <= b.cap) return MOE_B200_OK;
+    if (b.p) CK(cudaFree(b.p));
+    b.p = nullptr;
+    b.cap = 0;
+    size_t want = bytes + bytes / 8 + 256;
+    CK(cudaMalloc(&b.p, want));
+    b.cap = want;
+    return MOE_B200_OK;
+}
+
+struct Ctx {
+    int device = -1;
+    int num_sms = 0;
+    int cc_major = 0, cc_minor = 0;
+    cudaStream_t stream = nullptr;
+    DeviceStatus *status = nullptr;      // device
+    bool attrs_set = false;
+    // workspace
+    Buf probs, ids, wts, loc, tile_cnt, tile_pref, plan, pos_of, x_perm, h, y;
+    Buf io_x, io_out, io_bias;
+    int last_E = 0;
+    int last_launches = 0;
+    // stage timing: ring of event sets, folded into the sums when read or
+    // when the ring wraps
+    bool prof = false;
+    static constexpr int kSlots = 64;
+    cudaEvent_t ev[kSlots][MOE_B200_NUM_STAGES + 1] = {};
+    bool pending[kSlots] = {};
+    int next_slot = 0;
+    double stage_ms[MOE_B200_NUM_STAGES] = {};
+    int n_timed = 0;
+};
+
+std::mutex g_mu;
+Ctx *g_ctx[64] = {nullptr};
+
+}  // namespace
+
+struct moe_b200_weights {
+    int device;
+    int d, F, E, k, d_pad, F_pad;
+    float *router;   // [d × E] row-major (host layout)
+    float *ug;       // [E][2F_pad × d_pad]
+    float *dn;       // [E][d_pad × F_pad]
+    CUtensorMap tm_ug;        // box {32, 256}
+    CUtensorMap tm_dn;        // box {32, 256 or 128}
+    int down_bn;
+};
+
+static int get_ctx(int device, Ctx **out) {
+    if (device < 0) CK(cudaGetDevice(&device));
+    if (device >= 64) return fail(MOE_B200_E_INVALID, "device %d out of range", device);
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx *c = g_ctx[device];
+    if (!c) {
+        int n = 0;
+        cudaError_t e = cudaGetDeviceCount(&n);
+        if (e != cudaSuccess || n == 0)
+            return fail(MOE_B200_E_NODEV, "no CUDA device: %s", cudaGetErrorString(e));
+        if (device >= n) return fail(MOE_B200_E_NODEV, "device %d not present (%d)", device, n);
+        CK(cudaSetDevice(device));
+        cudaDeviceProp prop;
+        CK(cudaGetDeviceProperties(&prop, device));
+        if (prop.major != 10)
+            return fail(MOE_B200_E_NODEV, "device %d is sm_%d%d; this build needs sm_100",
+                        device, prop.major, prop.minor);
+        c = new Ctx();
+        c->device = device;
+        c->num_sms = prop.multiProcessorCount;
+        c->cc_major = prop.major;
+        c->cc_minor = prop.minor;
+        CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+        CK(cudaMalloc(&c->status, sizeof(DeviceStatus)));
+        CK(cudaMemset(c->status, 0, sizeof(DeviceStatus)));
+        CK(tc_set_attributes());
+        c->attrs_set = true;
+        g_ctx[device] = c;
+    }
+    CK(cudaSetDevice(device));
+    *out = c;
+    return MOE_B200_OK;
+}
+
+// ---------------------------------------------------------------------
+// library
+// ---------------------------------------------------------------------
+extern "C" const char *moe_b200_version(void) { return "moe_b200 0.1 (sm_100a)"; }
+
+extern "C" const char *moe_b200_strerror(int s) {
+    switch (s) {
+    case MOE_B200_OK: return "ok";
+    case MOE_B200_E_INVALID: return "invalid argument";
+    case MOE_B200_E_CUDA: return "CUDA error";
+    case MOE_B200_E_NOMEM: return "out of memory";
+    case MOE_B200_E_NCCL: return "NCCL error";
+    case MOE_B200_E_TIMEOUT: return "device wait timed out";
+    case MOE_B200_E_NODEV: return "no usable sm_100 device";
+    case MOE_B200_E_STATE: return "bad state";
+    default: return "unknown status";
+    }
+}
+
+extern "C" const char *moe_b200_last_error(void) { return g_err; }
+
+extern "C" int moe_b200_init(int device) {
+    Ctx *c;
+    return get_ctx(device, &c);
+}
+
+static void free_buf(Buf &b) {
+    if (b.p) cudaFree(b.p);
+    b.p = nullptr;
+    b.cap = 0;
+}
+
+extern "C" void moe_b200_shutdown(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (int i = 0; i < 64; i++) {
+        Ctx *c = g_ctx[i];
+        if (!c) continue;
+        cudaSetDevice(i);
+        cudaStreamSynchronize(c->stream);
+        Buf *bufs[] = {&c->probs, &c->ids, &c->wts, &c->loc, &c->tile_cnt, &c->tile_pref,
+                       &c->plan, &c->pos_of, &c->x_perm, &c->h, &c->y, &c->io_x, &c->io_out,
+                       &c->io_bias};
+        for (Buf *b : bufs) free_buf(*b);
+        cudaFree(c->status);
+        cudaStreamDestroy(c->stream);
+        delete c;
+        g_ctx[i] = nullptr;
+    }
+}
+
+// ---------------------------------------------------------------------
+// weights
+// ---------------------------------------------------------------------
+static int check_shape(int d, int F, int E, int k) {
+    if (d <= 0 || F <= 0) return fail(MOE_B200_E_INVALID, "d=%d F=%d must be positive", d, F);
+    if (E < 1 || E > kMaxExperts)
+        return fail(MOE_B200_E_INVALID, "n_experts=%d outside [1, %d]", E, kMaxExperts);
+    if (k < 1 || k > E || k > kMaxTopK)
+        return fail(MOE_B200_E_INVALID, "top_k=%d outside [1, min(E, %d)]", k, kMaxTopK);
+    if ((int64_t)d * F > (int64_t)1 << 31)
+        return fail(MOE_B200_E_INVALID, "d*F too large");
+    return MOE_B200_OK;
+}
+
+static int weights_alloc(Ctx *c, int d, int F, int E, int k, moe_b200_weights **out) {
+    moe_b200_weights *w = new moe_b200_weights();
+    w->device = c->device;
+    w->d = d; w->F = F; w->E = E; w->k = k;
+    w->d_pad = round_up(d, 128);
+    w->F_pad = round_up(F, 128);
+    w->down_bn = (w->d_pad % 256 == 0) ? 256 : 128;
+    const size_t ug = (size_t)E * 2 * w->F_pad * w->d_pad, dn = (size_t)E * w->d_pad * w->F_pad;
+    cudaError_t e1 = cudaMalloc(&w->router, (size_t)d * E * 4);
+    cudaError_t e2 = cudaMalloc(&w->ug, ug * 4);
+    cudaError_t e3 = cudaMalloc(&w->dn, dn * 4);
+    if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
+        cudaFree(w->router); cudaFree(w->ug); cudaFree(w->dn);
+        delete w;
+        cudaGetLastError();
+        return fail(MOE_B200_E_NOMEM, "weights (%.2f GB) do not fit on device %d",
+                    (double)(ug + dn) * 4 / 1e9, c->device);
+    }
+    int rc = make_tmap(&w->tm_ug, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 256);
+    if (rc == 0) rc = make_tmap(&w->tm_dn, w->dn, (int64_t)E * w->d_pad, w->F_pad, w->down_bn);
+    if (rc) {
+        cudaFree(w->router); cudaFree(w->ug); cudaFree(w->dn);
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_weights_upload(const float *W_router, const float *const *W_gate,
+                                       const float *const *W_up, const float *const *W_down,
+                                       int d, int F, int E, int top_k, moe_b200_weights **out) {
+    if (!out || !W_router || !W_gate || !W_up || !W_down)
+        return fail(MOE_B200_E_INVALID, "null argument");
+    int rc = check_shape(d, F, E, top_k);
+    if (rc) return rc;
+    Ctx *c;
+    if ((rc = get_ctx(-1, &c))) return rc;
+    moe_b200_weights *w;
+    if ((rc = weights_alloc(c, d, F, E, top_k, &w))) return rc;
+    float *stage = nullptr;
+    const size_t dF = (size_t)d * F;
+    cudaError_t e = cudaMalloc(&stage, 3 * dF * 4);
+    if (e != cudaSuccess) {
+        moe_b200_weights_free(w);
+        return fail(MOE_B200_E_NOMEM, "upload staging: %s", cudaGetErrorString(e));
+    }
+    rc = MOE_B200_OK;
+    do {
+        if (cudaMemcpy(w->router, W_router, (size_t)d * E * 4, cudaMemcpyHostToDevice)) {
+            rc = fail(MOE_B200_E_CUDA, "router upload failed");
+            break;
+        }
+        for (int ex = 0; ex < E && !rc; ex++) {
+            if (!W_gate[ex] || !W_up[ex] || !W_down[ex]) {
+                rc = fail(MOE_B200_E_INVALID, "expert %d has a null matrix", ex);
+                break;
+            }
+            if (cudaMemcpyAsync(stage, W_gate[ex], dF * 4, cudaMemcpyHostToDevice, c->stream) ||
+                cudaMemcpyAsync(stage + dF, W_up[ex], dF * 4, cudaMemcpyHostToDevice, c->stream) ||
+                cudaMemcpyAsync(stage + 2 * dF, W_down[ex], dF * 4, cudaMemcpyHostToDevice,
+                                c->stream)) {
+                rc = fail(MOE_B200_E_CUDA, "expert %d upload failed", ex);
+                break;
+            }
+            float *ug = w->ug + (size_t)ex * 2 * w->F_pad * w->d_pad;
+            float *dn = w->dn + (size_t)ex * w->d_pad * w->F_pad;
+            if (launch_repack_upgate(stage, stage + dF, d, F, w->d_pad, w->F_pad, ug, c->stream) ||
+                launch_repack_down(stage + 2 * dF, d, F, w->d_pad, w->F_pad, dn, c->stream)) {
+                rc = fail(MOE_B200_E_CUDA, "repack launch failed");
+                break;
+            }
+            // staging is reused by the next expert
+            if (cudaStreamSynchronize(c->stream)) {
+                rc = fail(MOE_B200_E_CUDA, "repack failed: %s", cudaGetErrorString(cudaGetLastError()));
+                break;
+            }
+        }
+    } while (0);
+    cudaFree(stage);
+    if (rc) {
+        moe_b200_weights_free(w);
+        return rc;
+    }
+    *out = w;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_weights_synth(uint64_t seed, float w_std, int d, int F, int E,
+                                      int top_k, moe_b200_weights **out) {
+    if (!out) return fail(MOE_B200_E_INVALID, "null argument");
+    int rc = check_shape(d, F, E, top_k);
+    if (rc) return rc;
+    Ctx *c;
+    if ((rc = get_ctx(-1, &c))) return rc;
+    moe_b200_weights *w;
+    if ((rc = weights_alloc(c, d, F, E, top_k, &w))) return rc;
+    CK(launch_synth(w->router, (size_t)d * E, seed, MOE_B200_STREAM_ROUTER, 0, w_std, c->stream));
+    for (int ex = 0; ex < E; ex++) {
+        float *ug = w->ug + (size_t)ex * 2 * w->F_pad * w->d_pad;
+        float *dn = w->dn + (size_t)ex * w->d_pad * w->F_pad;
+        CK(launch_synth_pack_expert(ug, dn, d, F, w->d_pad, w->F_pad, seed,
+                                    MOE_B200_STREAM_EXPERT(ex, 0), MOE_B200_STREAM_EXPERT(ex, 1),
+                                    MOE_B200_STREAM_EXPERT(ex, 2), w_std, c->stream));
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    *out = w;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_weights_free(moe_b200_weights *w) {
+    if (!w) return MOE_B200_OK;
+    cudaSetDevice(w->device);
+    cudaDeviceSynchronize();
+    cudaFree(w->router);
+    cudaFree(w->ug);
+    cudaFree(w->dn);
+    delete w;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_weights_shape(const moe_b200_weights *w, int *d, int *F, int *E,
+                                      int *top_k) {
+    if (!w) return fail(MOE_B200_E_INVALID, "null weights");
+    if (d) *d = w->d;
+    if (F) *F = w->F;
+    if (E) *E = w->E;
+    if (top_k) *top_k = w->k;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_weights_download(const moe_b200_weights *w, float *W_router,
+                                         float *const *W_gate, float *const *W_up,
+                                         float *const *W_down) {
+    if (!w) return fail(MOE_B200_E_INVALID, "null weights");
+    Ctx *c;
+    int rc = get_ctx(w->device, &c);
+    if (rc) return rc;
+    const int d = w->d, F = w->F;
+    const size_t dF = (size_t)d * F;
+    if (W_router) CK(cudaMemcpy(W_router, w->router, (size_t)d * w->E * 4, cudaMemcpyDeviceToHost));
+    if (!W_gate && !W_up && !W_down) return MOE_B200_OK;
+    float *stage = nullptr;
+    CK(cudaMalloc(&stage, 3 * dF * 4));
+    for (int ex = 0; ex < w->E; ex++) {
+        const float *ug = w->ug + (size_t)ex * 2 * w->F_pad * w->d_pad;
+        const float *dn = w->dn + (size_t)ex * w->d_pad * w->F_pad;
+        CK(launch_unpack_upgate(ug, d, F, w->d_pad, w->F_pad, stage, stage + dF, c->stream));
+        CK(launch_unpack_down(dn, d, F, w->d_pad, w->F_pad, stage + 2 * dF, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+        if (W_gate && W_gate[ex]) CK(cudaMemcpy(W_gate[ex], stage, dF * 4, cudaMemcpyDeviceToHost));
+        if (W_up && W_up[ex]) CK(cudaMemcpy(W_up[ex], stage + dF, dF * 4, cudaMemcpyDeviceToHost));
+        if (W_down && W_down[ex])
+            CK(cudaMemcpy(W_down[ex], stage + 2 * dF, dF * 4, cudaMemcpyDeviceToHost));
+    }
+    cudaFree(stage);
+    return MOE_B200_OK;
+}
+
+// ---------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------
+static int pick_path(const moe_b200_weights *w, int T, const moe_b200_opts *opts) {
+    int path = opts ? opts->path : MOE_B200_PATH_AUTO;
+    if (path == MOE_B200_PATH_AUTO) {
+        // tensor-core tiles are 128 rows: use them once the average expert
+        // group fills half a tile; smaller (decode-sized) groups stream the
+        // weights through FP32 FFMA.
+        const double avg = (double)T * w->k / w->E;
+        path = avg >= 64.0 ? MOE_B200_PATH_TF32 : MOE_B200_PATH_FP32;
+    }
+    return path;
+}
+
+static int ensure_workspace(Ctx *c, const moe_b200_weights *w, int T) {
+    const size_t Tk = (size_t)T * w->k, tiles = ceil_div(T, kRouterTile);
+    int rc;
+    if ((rc = grow(c->probs, (size_t)T * w->E * 4))) return rc;
+    if ((rc = grow(c->ids, Tk * 4))) return rc;
+    if ((rc = grow(c->wts, Tk * 4))) return rc;
+    if ((rc = grow(c->loc, Tk * 4))) return rc;
+    if ((rc = grow(c->tile_cnt, tiles * w->E * 4))) return rc;
+    if ((rc = grow(c->tile_pref, tiles * w->E * 4))) return rc;
+    if ((rc = grow(c->plan, (size_t)plan_ints(w->E) * 4))) return rc;
+    if ((rc = grow(c->pos_of, Tk * 4))) return rc;
+    if ((rc = grow(c->x_perm, Tk * w->d_pad * 4))) return rc;
+    if ((rc = grow(c->h, Tk * w->F_pad * 4))) return rc;
+    if ((rc = grow(c->y, Tk * w->d_pad * 4))) return rc;
+    return MOE_B200_OK;
+}
+
+static int fold_slot(Ctx *c, int slot) {
+    if (!c->pending[slot]) return MOE_B200_OK;
+    CK(cudaEventSynchronize(c->ev[slot][MOE_B200_NUM_STAGES]));
+    for (int i = 0; i < MOE_B200_NUM_STAGES; i++) {
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, c->ev[slot][i], c->ev[slot][i + 1]));
+        c->stage_ms[i] += ms;
+    }
+    c->n_timed++;
+    c->pending[slot] = false;
+    return MOE_B200_OK;
+}
+
+// returns the event set to record into for this forward, or nullptr
+static cudaEvent_t *prof_slot(Ctx *c) {
+    if (!c->prof) return nullptr;
+    const int slot = c->next_slot;
+    if (fold_slot(c, slot)) return nullptr;
+    if (!c->ev[slot][0])
+        for (int i = 0; i <= MOE_B200_NUM_STAGES; i++)
+            if (cudaEventCreate(&c->ev[slot][i]) != cudaSuccess) return nullptr;
+    c->pending[slot] = true;
+    c->next_slot = (slot + 1) % Ctx::kSlots;
+    return c->ev[slot];
+}
+
+static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, const float *d_x,
+                      int T, float *d_out, float *d_probs, int *d_ids,
+                      const moe_b200_opts *opts, cudaStream_t s) {
+    int rc = ensure_workspace(c, w, T);
+    if (rc) return rc;
+    const int E = w->E, k = w->k, d = w->d;
+    const int rows = T * k;
+    float *probs = d_probs ? d_probs : (float *)c->probs.p;
+    int *ids = d_ids ? d_ids : (int *)c->ids.p;
+    float *wts = (float *)c->wts.p;
+    int *loc = (int *)c->loc.p, *tile_cnt = (int *)c->tile_cnt.p, *tile_pref = (int *)c->tile_pref.p;
+    int *plan = (int *)c->plan.p, *pos_of = (int *)c->pos_of.p;
+    float *x_perm = (float *)c->x_perm.p, *h = (float *)c->h.p, *y = (float *)c->y.p;
+    int launches = 0;
+    cudaEvent_t *ev = prof_slot(c);
+#define MARK(i) \
+    if (ev) CK(cudaEventRecord(ev[i], s))
+
+    MARK(0);
+    CK(launch_router(d_x, T, d, w->router, d_bias, E, k, probs, ids, wts, loc, tile_cnt, s));
+    launches += 1;
+    MARK(1);
+    const int path = pick_path(w, T, opts);
+    CK(launch_dispatch(d_x, T, d, w->d_pad, E, k, ids, loc, tile_cnt, tile_pref, plan, pos_of,
+                       x_perm, path == MOE_B200_PATH_TF32, c->status, s));
+    launches += 2;
+    MARK(2);
+    if (path == MOE_B200_PATH_TF32) {
+        TcGemm up, dn;
+        if ((rc = make_tmap(&up.tmA, x_perm, rows, w->d_pad, 128))) return rc;
+        up.tmB = w->tm_ug;
+        if ((rc = make_tmap(&dn.tmA, h, rows, w->F_pad, 128))) return rc;
+        dn.tmB = w->tm_dn;
+        CK(launch_tc_upgate(up, w->d_pad, w->F_pad, h, plan, E, rows, c->num_sms, c->status, s));
+        MARK(3);
+        CK(launch_tc_down(dn, w->F_pad, w->d_pad, w->down_bn, y, plan, E, rows, c->num_sms,
+                          c->status, s));
+    } else if (path == MOE_B200_PATH_FP32) {
+        CK(launch_ffma_upgate(x_perm, w->d_pad, w->ug, w->F_pad, h, plan, E, rows, s));
+        MARK(3);
+        CK(launch_ffma_down(h, w->F_pad, w->dn, w->d_pad, y, plan, E, rows, s));
+    } else {
+        return fail(MOE_B200_E_INVALID, "unknown path %d", path);
+    }
+    launches += 2;
+    MARK(4);
+    CK(launch_combine(y, d, w->d_pad, T, k, pos_of, wts, d_out, s));
+    launches += 1;
+    MARK(5);
+#undef MARK
+    c->last_E = E;
+    c->last_launches = launches;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_forward_device(const moe_b200_weights *w, const float *d_bias,
+                                       const float *d_x, int T, float *d_out,
+                                       float *d_router_probs, int *d_expert_ids,
+                                       const moe_b200_opts *opts, void *stream) {
+    if (!w) return fail(MOE_B200_E_INVALID, "null weights");
+    if (T < 0) return fail(MOE_B200_E_INVALID, "T=%d", T);
+    if (T == 0) return MOE_B200_OK;
+    if (!d_x || !d_out) return fail(MOE_B200_E_INVALID, "null x/out");
+    if ((int64_t)T * w->k > (int64_t)1 << 30) return fail(MOE_B200_E_INVALID, "T too large");
+    Ctx *c;
+    int rc = get_ctx(w->device, &c);
+    if (rc) return rc;
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    return forward_on(c, w, d_bias, d_x, T, d_out, d_router_probs, d_expert_ids, opts, s);
+}
+
+static int check_status(Ctx *c) {
+    DeviceStatus st;
+    CK(cudaMemcpy(&st, c->status, sizeof st, cudaMemcpyDeviceToHost));
+    if (st.timeout || st.bad_index) {
+        CK(cudaMemset(c->status, 0, sizeof st));
+        if (st.timeout)
+            return fail(MOE_B200_E_TIMEOUT, "device wait timed out (site %d)", st.timeout);
+        return fail(MOE_B200_E_CUDA, "device bounds check rejected an index");
+    }
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_forward(const moe_b200_weights *w, const float *router_bias,
+                                const float *x, int T, float *out, float *router_probs,
+                                int *expert_ids, const moe_b200_opts *opts) {
+    if (!w) return fail(MOE_B200_E_INVALID, "null weights");
+    if (T < 0) return fail(MOE_B200_E_INVALID, "T=%d", T);
+    if (T == 0) return MOE_B200_OK;
+    if (!x || !out) return fail(MOE_B200_E_INVALID, "null x/out");
+    if ((int64_t)T * w->k > (int64_t)1 << 30) return fail(MOE_B200_E_INVALID, "T too large");
+    Ctx *c;
+    int rc = get_ctx(w->device, &c);
+    if (rc) return rc;
+    const size_t xb = (size_t)T * w->d * 4;
+    if ((rc = grow(c->io_x, xb))) return rc;
+    if ((rc = grow(c->io_out, xb))) return rc;
+    if ((rc = grow(c->io_bias, (size_t)w->E * 4))) return rc;
+    if ((rc = ensure_workspace(c, w, T))) return rc;
+    cudaStream_t s = c->stream;
+    CK(cudaMemcpyAsync(c->io_x.p, x, xb, cudaMemcpyHostToDevice, s));
+    const float *d_bias = nullptr;
+    if (router_bias) {
+        CK(cudaMemcpyAsync(c->io_bias.p, router_bias, (size_t)w->E * 4, cudaMemcpyHostToDevice, s));
+        d_bias = (const float *)c->io_bias.p;
+    }
+    rc = forward_on(c, w, d_bias, (const float *)c->io_x.p, T, (float *)c->io_out.p,
+                    (float *)c->probs.p, (int *)c->ids.p, opts, s);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(out, c->io_out.p, xb, cudaMemcpyDeviceToHost, s));
+    if (router_probs)
+        CK(cudaMemcpyAsync(router_probs, c->probs.p, (size_t)T * w->E * 4, cudaMemcpyDeviceToHost, s));
+    if (expert_ids)
+        CK(cudaMemcpyAsync(expert_ids, c->ids.p, (size_t)T * w->k * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return check_status(c);
+}
+
+extern "C" int moe_b200_last_counts(const moe_b200_weights *w, int *counts) {
+    if (!w || !counts) return fail(MOE_B200_E_INVALID, "null argument");
+    Ctx *c;
+    int rc = get_ctx(w->device, &c);
+    if (rc) return rc;
+    if (!c->plan.p || c->last_E != w->E) return fail(MOE_B200_E_STATE, "no forward on record");
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(counts, c->plan.p, (size_t)w->E * 4, cudaMemcpyDeviceToHost));
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_last_launches(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64 || !g_ctx[dev]) return 0;
+    return g_ctx[dev]->last_launches;
+}
+
+extern "C" int moe_b200_synth_fill(float *d_dst, size_t n, uint64_t seed, uint64_t stream,
+                                   uint64_t first, float std, void *cuda_stream) {
+    if (!d_dst && n) return fail(MOE_B200_E_INVALID, "null destination");
+    Ctx *c;
+    int rc = get_ctx(-1, &c);
+    if (rc) return rc;
+    cudaStream_t s = cuda_stream ? (cudaStream_t)cuda_stream : c->stream;
+    CK(launch_synth(d_dst, n, seed, stream, first, std, s));
+    if (!cuda_stream) CK(cudaStreamSynchronize(s));
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_profile_enable(int enable) {
+    Ctx *c;
+    int rc = get_ctx(-1, &c);
+    if (rc) return rc;
+    c->prof = enable != 0;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_profile_read(double *stage_ms, int *n_forwards) {
+    Ctx *c;
+    int rc = get_ctx(-1, &c);
+    if (rc) return rc;
+    for (int i = 0; i < Ctx::kSlots; i++)
+        if ((rc = fold_slot(c, i))) return rc;
+    if (stage_ms)
+        for (int i = 0; i < MOE_B200_NUM_STAGES; i++) stage_ms[i] = c->stage_ms[i];
+    if (n_forwards) *n_forwards = c->n_timed;
+    for (int i = 0; i < MOE_B200_NUM_STAGES; i++) c->stage_ms[i] = 0.0;
+    c->n_timed = 0;
+    return MOE_B200_OK;
+}

@@ -1,0 +1,320 @@
+"""Python host binding of libmoe_b200.so (the B200 MoE feed-forward path).
+
+Mirrors llm.c's MoE operator interface: `MoEWeights` holds the router and
+the E SwiGLU experts in the reference's host layout (W_router [d×E],
+W_gate/W_up [d×F], W_down [F×d]), and `moe_forward` returns what llm.c's
+moe_forward (src/transformer.c:287-366) writes: the layer output [T×d],
+cache->router_probs [T×E] and cache->expert_ids [T×k].
+
+All arithmetic runs in the CUDA library; there is no CPU fallback.  If the
+library is missing or no sm_100 device is usable the calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libmoe_b200.so"
+
+OK = 0
+E_INVALID, E_CUDA, E_NOMEM, E_NCCL, E_TIMEOUT, E_NODEV, E_STATE = -1, -2, -3, -4, -5, -6, -7
+PATH_AUTO, PATH_TF32, PATH_FP32 = 0, 1, 2
+STREAM_X, STREAM_ROUTER, STREAM_BIAS = 1, 2, 3
+
+
+def stream_expert(e: int, which: int) -> int:
+    return 0x100 + 4 * e + which
+
+
+class MoEError(RuntimeError):
+    def __init__(self, status: int, what: str, detail: str):
+        super().__init__(f"{what}: status {status} ({detail})")
+        self.status = status
+
+
+_fp = C.POINTER(C.c_float)
+_ip = C.POINTER(C.c_int)
+_vp = C.c_void_p
+
+
+class Opts(C.Structure):
+    _fields_ = [("path", C.c_int), ("reserved", C.c_int * 7)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load libmoe_b200.so once (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise FileNotFoundError(f"{LIB_PATH} missing: build it with `make -C {HERE}` "
+                                "or __graft_entry__.build()")
+    L = C.CDLL(str(LIB_PATH))
+    L.moe_b200_version.restype = C.c_char_p
+    L.moe_b200_strerror.restype = C.c_char_p
+    L.moe_b200_strerror.argtypes = [C.c_int]
+    L.moe_b200_last_error.restype = C.c_char_p
+    L.moe_b200_init.argtypes = [C.c_int]
+    L.moe_b200_shutdown.restype = None
+    L.moe_b200_weights_upload.argtypes = [_fp, C.POINTER(_fp), C.POINTER(_fp), C.POINTER(_fp),
+                                          C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.moe_b200_weights_synth.argtypes = [C.c_uint64, C.c_float, C.c_int, C.c_int, C.c_int,
+                                         C.c_int, C.POINTER(_vp)]
+    L.moe_b200_weights_free.argtypes = [_vp]
+    L.moe_b200_weights_shape.argtypes = [_vp, _ip, _ip, _ip, _ip]
+    L.moe_b200_weights_download.argtypes = [_vp, _fp, C.POINTER(_fp), C.POINTER(_fp),
+                                            C.POINTER(_fp)]
+    L.moe_b200_forward.argtypes = [_vp, _fp, _fp, C.c_int, _fp, _fp, _ip, C.POINTER(Opts)]
+    L.moe_b200_forward_device.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp,
+                                          C.POINTER(Opts), _vp]
+    L.moe_b200_last_counts.argtypes = [_vp, _ip]
+    L.moe_b200_last_launches.restype = C.c_int
+    L.moe_b200_profile_enable.argtypes = [C.c_int]
+    L.moe_b200_profile_read.argtypes = [C.POINTER(C.c_double), _ip]
+    L.moe_b200_synth_fill.argtypes = [_vp, C.c_size_t, C.c_uint64, C.c_uint64, C.c_uint64,
+                                      C.c_float, _vp]
+    _lib = L
+    return L
+
+
+def _check(rc: int, what: str):
+    if rc != OK:
+        L = lib()
+        raise MoEError(rc, what, f"{L.moe_b200_strerror(rc).decode()}: "
+                                 f"{L.moe_b200_last_error().decode()}")
+
+
+def _f(a):
+    if a is None:
+        return None
+    if not (a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]):
+        raise TypeError("expected a C-contiguous float32 array")
+    return a.ctypes.data_as(_fp)
+
+
+def _i(a):
+    if a is None:
+        return None
+    if not (a.dtype == np.int32 and a.flags["C_CONTIGUOUS"]):
+        raise TypeError("expected a C-contiguous int32 array")
+    return a.ctypes.data_as(_ip)
+
+
+def _opts(path: int) -> Opts:
+    o = Opts()
+    o.path = path
+    return o
+
+
+def version() -> str:
+    return lib().moe_b200_version().decode()
+
+
+def init(device: int = -1):
+    _check(lib().moe_b200_init(device), "moe_b200_init")
+
+
+def shutdown():
+    lib().moe_b200_shutdown()
+
+
+class MoEWeights:
+    """A device-resident expert set (llm.c MoEWeights, include/transformer.h:53-58)."""
+
+    def __init__(self, handle: int, d: int, F: int, E: int, k: int):
+        self.handle, self.d, self.F, self.E, self.top_k = handle, d, F, E, k
+
+    @classmethod
+    def upload(cls, W_router, W_gate, W_up, W_down, top_k: int) -> "MoEWeights":
+        W_router = np.ascontiguousarray(W_router, np.float32)
+        d, E = W_router.shape
+        F = np.asarray(W_gate[0]).shape[1]
+        keep = [np.ascontiguousarray(a, np.float32) for a in (*W_gate, *W_up, *W_down)]
+        g = (_fp * E)(*[_f(a) for a in keep[0:E]])
+        u = (_fp * E)(*[_f(a) for a in keep[E:2 * E]])
+        dn = (_fp * E)(*[_f(a) for a in keep[2 * E:3 * E]])
+        h = _vp()
+        _check(lib().moe_b200_weights_upload(_f(W_router), g, u, dn, d, F, E, top_k,
+                                             C.byref(h)), "moe_b200_weights_upload")
+        return cls(h.value, d, F, E, top_k)
+
+    @classmethod
+    def synth(cls, seed: int, w_std: float, d: int, F: int, E: int, top_k: int) -> "MoEWeights":
+        h = _vp()
+        _check(lib().moe_b200_weights_synth(seed, w_std, d, F, E, top_k, C.byref(h)),
+               "moe_b200_weights_synth")
+        return cls(h.value, d, F, E, top_k)
+
+    def download(self, experts: bool = True):
+        d, F, E = self.d, self.F, self.E
+        wr = np.empty((d, E), np.float32)
+        if not experts:
+            _check(lib().moe_b200_weights_download(self.handle, _f(wr), None, None, None),
+                   "moe_b200_weights_download")
+            return wr, None, None, None
+        g = [np.empty((d, F), np.float32) for _ in range(E)]
+        u = [np.empty((d, F), np.float32) for _ in range(E)]
+        dn = [np.empty((F, d), np.float32) for _ in range(E)]
+        _check(lib().moe_b200_weights_download(self.handle, _f(wr), (_fp * E)(*[_f(a) for a in g]),
+                                                (_fp * E)(*[_f(a) for a in u]),
+                                                (_fp * E)(*[_f(a) for a in dn])),
+               "moe_b200_weights_download")
+        return wr, g, u, dn
+
+    def free(self):
+        if self.handle:
+            lib().moe_b200_weights_free(self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def moe_forward(w: MoEWeights, x: np.ndarray, bias: np.ndarray | None = None,
+                path: int = PATH_AUTO):
+    """Host-buffer forward (synchronous): returns (out [T×d], probs [T×E], ids [T×k])."""
+    x = np.ascontiguousarray(x, np.float32)
+    T = x.shape[0]
+    out = np.empty((T, w.d), np.float32)
+    probs = np.empty((T, w.E), np.float32)
+    ids = np.empty((T, w.top_k), np.int32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    o = _opts(path)
+    _check(lib().moe_b200_forward(w.handle, _f(b), _f(x), T, _f(out), _f(probs), _i(ids),
+                                  C.byref(o)), "moe_b200_forward")
+    return out, probs, ids
+
+
+def moe_forward_host_ptr(w: MoEWeights, x_ptr: int, T: int, out_ptr: int, probs_ptr: int | None,
+                         ids_ptr: int | None, bias_ptr: int | None = None,
+                         path: int = PATH_AUTO):
+    """Host-buffer forward from raw host pointers (e.g. pinned torch tensors)."""
+    o = _opts(path)
+    _check(lib().moe_b200_forward(w.handle, C.cast(bias_ptr, _fp) if bias_ptr else None,
+                                  C.cast(x_ptr, _fp), T, C.cast(out_ptr, _fp),
+                                  C.cast(probs_ptr, _fp) if probs_ptr else None,
+                                  C.cast(ids_ptr, _ip) if ids_ptr else None, C.byref(o)),
+           "moe_b200_forward")
+
+
+def moe_forward_device(w: MoEWeights, x_ptr: int, T: int, out_ptr: int,
+                       probs_ptr: int | None = None, ids_ptr: int | None = None,
+                       bias_ptr: int | None = None, path: int = PATH_AUTO,
+                       stream: int | None = None):
+    """Device-buffer forward, asynchronous on `stream` (a cudaStream_t as int)."""
+    o = _opts(path)
+    _check(lib().moe_b200_forward_device(w.handle, bias_ptr, x_ptr, T, out_ptr, probs_ptr,
+                                         ids_ptr, C.byref(o), stream), "moe_b200_forward_device")
+
+
+def last_counts(w: MoEWeights) -> np.ndarray:
+    c = np.empty(w.E, np.int32)
+    _check(lib().moe_b200_last_counts(w.handle, _i(c)), "moe_b200_last_counts")
+    return c
+
+
+def last_launches() -> int:
+    return int(lib().moe_b200_last_launches())
+
+
+def synth_fill(dst_ptr: int, n: int, seed: int, stream_id: int, std: float, first: int = 0,
+               cuda_stream: int | None = None):
+    _check(lib().moe_b200_synth_fill(dst_ptr, n, seed, stream_id, first, std, cuda_stream),
+           "moe_b200_synth_fill")
+
+
+# ---------------------------------------------------------------- drop-in
+class LlmcMatrix(C.Structure):
+    _fields_ = [("data", _fp), ("grad", _fp), ("rows", C.c_int), ("cols", C.c_int)]
+
+
+class LlmcFFNWeights(C.Structure):
+    _fields_ = [("W_gate", LlmcMatrix), ("W_up", LlmcMatrix), ("W_down", LlmcMatrix)]
+
+
+class LlmcMoEWeights(C.Structure):
+    _fields_ = [("experts", C.POINTER(LlmcFFNWeights)), ("W_router", LlmcMatrix),
+                ("n_experts", C.c_int), ("top_k", C.c_int)]
+
+
+class LlmcModelConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("vocab_size", "max_seq_len", "d_model", "n_layers",
+                                       "n_heads", "n_kv_heads", "head_dim", "window_size",
+                                       "ffn_hidden", "n_experts", "top_k_experts")] + \
+               [("rms_norm_eps", C.c_float), ("rope_theta", C.c_float)]
+
+
+class LlmcForwardCache(C.Structure):
+    _fields_ = [(n, LlmcMatrix) for n in ("x_norm_attn", "x_norm_ffn", "attn_out", "ffn_out",
+                                          "Q", "K", "V", "attn_scores", "attn_weighted",
+                                          "gate_buf", "up_buf")] + \
+               [("router_probs", _fp), ("expert_ids", _ip)]
+
+
+def _mat(a):
+    return LlmcMatrix(_f(a), None, a.shape[0], a.shape[1])
+
+
+class LlmcMoE:
+    """llm.c's own MoEWeights struct built over numpy arrays, for calling the
+    exported drop-in `moe_forward` exactly as block_forward does
+    (src/transformer.c:761-764)."""
+
+    def __init__(self, W_router, W_gate, W_up, W_down, top_k: int):
+        self._keep = [np.ascontiguousarray(a, np.float32) for a in (W_router, *W_gate, *W_up, *W_down)]
+        E = len(W_gate)
+        wr, g, u, dn = self._keep[0], self._keep[1:1 + E], self._keep[1 + E:1 + 2 * E], self._keep[1 + 2 * E:]
+        self.experts = (LlmcFFNWeights * E)(*[LlmcFFNWeights(_mat(g[e]), _mat(u[e]), _mat(dn[e]))
+                                             for e in range(E)])
+        self.moe = LlmcMoEWeights(self.experts, _mat(wr), E, top_k)
+        self.d, self.E, self.k, self.F = wr.shape[0], E, top_k, g[0].shape[1]
+
+    def forward(self, x: np.ndarray):
+        L = lib()
+        L.moe_forward.argtypes = [C.POINTER(LlmcMatrix), C.POINTER(LlmcMoEWeights),
+                                  C.POINTER(LlmcModelConfig), C.POINTER(LlmcForwardCache),
+                                  C.POINTER(LlmcMatrix)]
+        L.moe_forward.restype = None
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[0]
+        out = np.empty((T, self.d), np.float32)
+        probs = np.empty((T, self.E), np.float32)
+        ids = np.empty((T, self.k), np.int32)
+        cfg = LlmcModelConfig()
+        cfg.d_model, cfg.ffn_hidden, cfg.n_experts, cfg.top_k_experts = self.d, self.F, self.E, self.k
+        cache = LlmcForwardCache()
+        cache.router_probs = _f(probs)
+        cache.expert_ids = _i(ids)
+        xm, om = _mat(x), _mat(out)
+        L.moe_forward(C.byref(xm), C.byref(self.moe), C.byref(cfg), C.byref(cache), C.byref(om))
+        return out, probs, ids
+
+    def invalidate(self):
+        L = lib()
+        L.moe_b200_invalidate.argtypes = [_vp]
+        _check(L.moe_b200_invalidate(C.addressof(self.moe)), "moe_b200_invalidate")
+
+
+STAGES = ("router", "dispatch", "upgate", "down", "combine")
+
+
+def profile_enable(on: bool = True):
+    _check(lib().moe_b200_profile_enable(1 if on else 0), "moe_b200_profile_enable")
+
+
+def profile_read():
+    """(dict stage -> summed device ms, number of forwards) since the last read."""
+    ms = (C.c_double * len(STAGES))()
+    n = C.c_int()
+    _check(lib().moe_b200_profile_read(ms, C.byref(n)), "moe_b200_profile_read")
+    return {k: float(ms[i]) for i, k in enumerate(STAGES)}, int(n.value)

@@ -1,0 +1,224 @@
+"""ctypes bindings for the CPU test oracle (oracle/liboracle.so) and for the
+reference build (oracle/_ref/libllmref.so).
+
+Test infrastructure only: tests/, __graft_entry__.smoke() and bench.py's
+CPU-baseline leg import this module; the product library never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent.parent
+ORACLE_SO = REPO / "oracle" / "liboracle.so"
+REF_SO = REPO / "oracle" / "_ref" / "libllmref.so"
+
+_fp = C.POINTER(C.c_float)
+_ip = C.POINTER(C.c_int)
+_fpp = C.POINTER(_fp)
+
+
+def _f(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_fp)
+
+
+def _i(a):
+    if a is None:
+        return None
+    assert a.dtype == np.int32 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_ip)
+
+
+def _ptr_array(arrs):
+    return (_fp * len(arrs))(*[_f(a) for a in arrs])
+
+
+_oracle = None
+_ref = None
+
+
+def oracle():
+    global _oracle
+    if _oracle is None:
+        lib = C.CDLL(str(ORACLE_SO))
+        lib.oracle_synth_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64,
+                                            C.c_size_t, C.c_float, _fp]
+        lib.oracle_stream_x.restype = C.c_uint64
+        lib.oracle_stream_router.restype = C.c_uint64
+        lib.oracle_stream_bias.restype = C.c_uint64
+        lib.oracle_stream_expert.restype = C.c_uint64
+        lib.oracle_stream_expert.argtypes = [C.c_int, C.c_int]
+        lib.oracle_exp_ref.restype = C.c_float
+        lib.oracle_exp_ref.argtypes = [C.c_float]
+        lib.oracle_softmax_rows.argtypes = [_fp, C.c_int, C.c_int]
+        lib.oracle_swiglu.argtypes = [_fp, _fp, _fp, C.c_int]
+        lib.oracle_router.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, C.c_int,
+                                      C.c_int, _fp, _fp, _ip, _fp]
+        lib.oracle_moe_forward.argtypes = [
+            _fp, C.c_int, C.c_int, _fp, _fp, C.c_int, C.c_int,
+            _fpp, _fpp, _fpp, C.c_int, _ip, C.c_int, _ip, _fp, _fp, _ip, C.c_int]
+        lib.oracle_moe_forward_synth.argtypes = [
+            _fp, C.c_int, C.c_int, _fp, _fp, C.c_int, C.c_int, C.c_int,
+            C.c_uint64, C.c_float, _ip, C.c_int, _ip, _fp, _fp, _ip, C.c_int]
+        lib.oracle_ffn_forward.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp,
+                                           C.c_int, _fp]
+        _oracle = lib
+    return _oracle
+
+
+def ref_available() -> bool:
+    return REF_SO.exists()
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        lib = C.CDLL(str(REF_SO))
+        lib.ref_set_threads.argtypes = [C.c_int]
+        lib.ref_moe_forward.argtypes = [_fp, C.c_int, C.c_int, _fp, C.c_int,
+                                        C.c_int, _fpp, _fpp, _fpp, C.c_int,
+                                        _fp, _fp, _ip]
+        lib.ref_moe_forward.restype = C.c_int
+        lib.ref_softmax_rows.argtypes = [_fp, C.c_int, C.c_int]
+        lib.ref_swiglu.argtypes = [_fp, _fp, _fp, C.c_int]
+        lib.ref_ffn_forward.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp,
+                                        C.c_int, _fp]
+        _ref = lib
+    return _ref
+
+
+# ---------------------------------------------------------------- generator
+
+def synth(seed: int, stream: int, n: int, std: float, first: int = 0) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    oracle().oracle_synth_normal(seed, stream, first, n, std, _f(out))
+    return out
+
+
+def stream_x():
+    return oracle().oracle_stream_x()
+
+
+def stream_router():
+    return oracle().oracle_stream_router()
+
+
+def stream_bias():
+    return oracle().oracle_stream_bias()
+
+
+def stream_expert(e, which):
+    return oracle().oracle_stream_expert(e, which)
+
+
+class MoEProblem:
+    """Seeded synthetic MoE layer in the reference's host layout.
+
+    x [T×d] ~ N(0, x_std); W_router [d×E], W_gate/W_up [d×F], W_down [F×d]
+    ~ N(0, w_std); bias: None, "normal" (b_e ~ N(0,1)) or "zipf" (b_e =
+    -s·ln(e+1), expert popularity ∝ (e+1)^-s).
+    """
+
+    def __init__(self, T, d, E, k, F, seed=0, w_std=0.02, x_std=1.0,
+                 bias=None, zipf_s=1.1, with_experts=True):
+        self.T, self.d, self.E, self.k, self.F = T, d, E, k, F
+        self.seed, self.w_std = seed, w_std
+        self.x = synth(seed, stream_x(), T * d, x_std).reshape(T, d)
+        self.W_router = synth(seed, stream_router(), d * E, w_std).reshape(d, E)
+        if bias is None:
+            self.bias = None
+        elif bias == "normal":
+            self.bias = synth(seed, stream_bias(), E, 1.0)
+        elif bias == "zipf":
+            self.bias = (-zipf_s * np.log(np.arange(1, E + 1, dtype=np.float64))).astype(np.float32)
+        else:
+            self.bias = np.ascontiguousarray(bias, dtype=np.float32)
+        self.experts = None
+        if with_experts:
+            self.experts = []
+            for e in range(E):
+                g = synth(seed, stream_expert(e, 0), d * F, w_std).reshape(d, F)
+                u = synth(seed, stream_expert(e, 1), d * F, w_std).reshape(d, F)
+                dn = synth(seed, stream_expert(e, 2), F * d, w_std).reshape(F, d)
+                self.experts.append((g, u, dn))
+
+    # ------------------------------------------------------------ oracle
+    def oracle_router(self):
+        T, E, k = self.T, self.E, self.k
+        logits = np.empty((T, E), np.float32)
+        probs = np.empty((T, E), np.float32)
+        ids = np.empty((T, k), np.int32)
+        wts = np.empty((T, k), np.float32)
+        oracle().oracle_router(_f(self.x), T, self.d, _f(self.W_router),
+                               _f(self.bias), E, k, _f(logits), _f(probs),
+                               _i(ids), _f(wts))
+        return logits, probs, ids, wts
+
+    def oracle_forward(self, rows=None, forced_ids=None, threads=0):
+        T, d, E, k, F = self.T, self.d, self.E, self.k, self.F
+        rows_arr = None if rows is None else np.ascontiguousarray(rows, np.int32)
+        nr = T if rows is None else len(rows_arr)
+        out = np.empty((nr, d), np.float32)
+        probs = np.empty((T, E), np.float32)
+        ids = np.empty((T, k), np.int32)
+        fid = None if forced_ids is None else np.ascontiguousarray(forced_ids, np.int32)
+        if self.experts is not None:
+            g = _ptr_array([e[0] for e in self.experts])
+            u = _ptr_array([e[1] for e in self.experts])
+            dn = _ptr_array([e[2] for e in self.experts])
+            oracle().oracle_moe_forward(_f(self.x), T, d, _f(self.W_router),
+                                        _f(self.bias), E, k, g, u, dn, F,
+                                        _i(rows_arr), nr, _i(fid), _f(out),
+                                        _f(probs), _i(ids), threads)
+        else:
+            oracle().oracle_moe_forward_synth(_f(self.x), T, d, _f(self.W_router),
+                                              _f(self.bias), E, k, F, self.seed,
+                                              self.w_std, _i(rows_arr), nr,
+                                              _i(fid), _f(out), _f(probs),
+                                              _i(ids), threads)
+        return out, probs, ids
+
+    # ------------------------------------------------------------ reference
+    def ref_forward(self, threads=0):
+        assert self.bias is None, "the reference router has no bias"
+        T, d, E, k, F = self.T, self.d, self.E, self.k, self.F
+        out = np.empty((T, d), np.float32)
+        probs = np.empty((T, E), np.float32)
+        ids = np.empty((T, k), np.int32)
+        lib = ref()
+        if threads > 0:
+            lib.ref_set_threads(threads)
+        g = _ptr_array([e[0] for e in self.experts])
+        u = _ptr_array([e[1] for e in self.experts])
+        dn = _ptr_array([e[2] for e in self.experts])
+        rc = lib.ref_moe_forward(_f(self.x), T, d, _f(self.W_router), E, k,
+                                 g, u, dn, F, _f(out), _f(probs), _i(ids))
+        assert rc == 0
+        return out, probs, ids
+
+
+def routing_mismatch_allowed(logits_row: np.ndarray, ids_a, ids_b, k: int,
+                             gap: float = 1e-6) -> bool:
+    """True when two top-k rankings of one token differ only where the
+    logits of the swapped experts lie within `gap` of each other (the
+    near-tie exemption for routing parity)."""
+    a, b = list(ids_a), list(ids_b)
+    for r in range(k):
+        if a[r] != b[r]:
+            if abs(float(logits_row[a[r]]) - float(logits_row[b[r]])) >= gap:
+                return False
+    return True
+
+
+def rel_err(got: np.ndarray, want: np.ndarray) -> float:
+    """max|got - want| / max|want| (the layer-output tolerance measure)."""
+    den = float(np.max(np.abs(want)))
+    if den == 0.0:
+        return float(np.max(np.abs(got)))
+    return float(np.max(np.abs(got.astype(np.float64) - want.astype(np.float64)))) / den
