@@ -258,7 +258,10 @@ def main():
     path = {"auto": M.PATH_AUTO, "tf32": M.PATH_TF32, "fp32": M.PATH_FP32}[args.path]
     T, d, E, k, F, seed = c["T"], c["d"], c["E"], c["k"], c["F"], c["seed"]
     w = M.MoEWeights.synth(seed, W_STD, d, F, E, k)
-    stream = torch.cuda.current_stream()
+    # a dedicated stream: the legacy default stream's handle is 0, which the
+    # library reads as "use the library stream"
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     x = torch.empty((T, d), dtype=torch.float32, device="cuda")
     M.synth_fill(x.data_ptr(), T * d, seed, M.STREAM_X, 1.0, cuda_stream=stream.cuda_stream)
     bias = None

@@ -5,7 +5,7 @@
 
 namespace moe {
 
-constexpr int kRouterTile = 32;   // tokens per router CTA
+constexpr int kRouterTile = 64;   // tokens per router CTA (dispatch tile granularity)
 
 // Plan (ints, device): cnt[E] | off[E+1] | mt128[E+1] | mt64[E+1]
 __host__ __device__ inline int plan_ints(int E) { return E + 3 * (E + 1); }
