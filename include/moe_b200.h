@@ -128,6 +128,37 @@ int moe_b200_forward_device(const moe_b200_weights *w, const float *d_bias,
                             float *d_router_probs, int *d_expert_ids,
                             const moe_b200_opts *opts, void *stream);
 
+/* Size of the static device array behind moe_b200_forward_noalloc. */
+#define MOE_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* MoE forward that allocates nothing: the same computation as
+ * moe_b200_forward_device on the FP32 FFMA expert path (tolerance 1e-5),
+ * with every intermediate buffer carved out of one fixed-size array that
+ * is compiled into the library (MOE_B200_NOALLOC_SCRATCH_BYTES, 16 MiB, held
+ * on every GPU that loads the library until the process exits).  This
+ * entry point has no counterpart in llm.c.
+ *
+ * It is for callers that cannot call cudaMalloc while they run: a serving
+ * or decode loop with a device-memory budget fixed at start-up, a program
+ * whose device memory is owned by another framework's caching allocator,
+ * or latency-critical code that must stay out of the CUDA allocator.  Such
+ * a caller creates the weights once beforehand (moe_b200_weights_upload
+ * allocates) and then passes only its own device buffers:
+ *   d_x [T×d] in; d_out [T×d] out (overwritten); d_router_probs [T×E] and
+ *   d_expert_ids [T×k] out, or NULL; d_bias [E] or NULL; `stream` a
+ *   cudaStream_t (NULL = the legacy default stream).
+ * The call is synchronous: it returns after the results are in d_out.
+ * Shapes whose intermediates do not fit the array (roughly T·k·(2·d + F)·4
+ * bytes plus router buffers) are rejected with MOE_B200_E_INVALID and a
+ * message from moe_b200_last_error(); split such a call into smaller T.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  Every call shares the one array,
+ * so calls that overlap on the GPU (two streams or two host threads on the
+ * same device) race; serialise them. */
+int moe_b200_forward_noalloc(const moe_b200_weights *w, const float *d_bias,
+                             const float *d_x, int T, float *d_out,
+                             float *d_router_probs, int *d_expert_ids, void *stream);
+
 /* Per-expert token counts of the last forward on this device (host array
  * of E ints); synchronises the library stream. */
 int moe_b200_last_counts(const moe_b200_weights *w, int *counts);

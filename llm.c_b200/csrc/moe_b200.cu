@@ -5,6 +5,7 @@
 // that depends on routing reads its tile counts from the device plan).
 #include "../../include/moe_b200.h"
 #include "kernels.cuh"
+#include "weights.cuh"
 
 #include <cuda.h>
 #include <cstdarg>
@@ -28,6 +29,8 @@ static int fail(int code, const char *fmt, ...) {
     va_end(ap);
     return code;
 }
+
+int moe::set_last_error(int code, const char *detail) { return fail(code, "%s", detail); }
 
 #define CK(call)                                                                              \
     do {                                                                                      \
@@ -125,16 +128,6 @@ Ctx *g_ctx[64] = {nullptr};
 
 }  // namespace
 
-struct moe_b200_weights {
-    int device;
-    int d, F, E, k, d_pad, F_pad;
-    float *router;   // [d × E] row-major (host layout)
-    float *ug;       // [E][2F_pad × d_pad]
-    float *dn;       // [E][d_pad × F_pad]
-    CUtensorMap tm_ug;        // box {32, 256}
-    CUtensorMap tm_dn;        // box {32, 256 or 128}
-    int down_bn;
-};
 
 static int get_ctx(int device, Ctx **out) {
     if (device < 0) CK(cudaGetDevice(&device));

@@ -1,0 +1,21 @@
+// weights.cuh — the device-resident expert set behind the opaque
+// moe_b200_weights handle (internal to the library).
+#pragma once
+#include <cuda.h>
+
+struct moe_b200_weights {
+    int device;
+    int d, F, E, k, d_pad, F_pad;
+    float *router;   // [d × E] row-major (host layout)
+    float *ug;       // [E][2F_pad × d_pad]
+    float *dn;       // [E][d_pad × F_pad]
+    CUtensorMap tm_ug;        // box {32, 256}
+    CUtensorMap tm_dn;        // box {32, 256 or 128}
+    int down_bn;
+};
+
+namespace moe {
+// Record a status and its detail text as this host thread's last error
+// (read back through moe_b200_last_error); returns `code`.
+__attribute__((visibility("hidden"))) int set_last_error(int code, const char *detail);
+}  // namespace moe

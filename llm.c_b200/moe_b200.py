@@ -318,3 +318,20 @@ def profile_read():
     n = C.c_int()
     _check(lib().moe_b200_profile_read(ms, C.byref(n)), "moe_b200_profile_read")
     return {k: float(ms[i]) for i, k in enumerate(STAGES)}, int(n.value)
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
+
+def moe_forward_noalloc(w: MoEWeights, x_ptr: int, T: int, out_ptr: int,
+                        probs_ptr: int | None = None, ids_ptr: int | None = None,
+                        bias_ptr: int | None = None, stream: int | None = None):
+    """Allocation-free forward on device buffers (FP32 expert path, synchronous).
+
+    For callers that may not allocate device memory while they run: all
+    intermediates live in a fixed 16 MiB array inside the library; shapes
+    that need more are rejected (MoEError with status E_INVALID)."""
+    L = lib()
+    L.moe_b200_forward_noalloc.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp]
+    _check(L.moe_b200_forward_noalloc(w.handle, bias_ptr, x_ptr, T, out_ptr, probs_ptr, ids_ptr,
+                                      stream), "moe_b200_forward_noalloc")

@@ -1,0 +1,76 @@
+"""GPU test of moe_b200_forward_noalloc, the entry point for callers that
+cannot allocate device memory while they run (a fixed-budget serving loop,
+a program whose device memory belongs to another framework's allocator).
+All of its intermediates live in a static 16 MiB array inside the library.
+
+It is checked through the C-ABI against the regular device entry point on
+the same FP32 expert path, on two calls in a row with different inputs, so
+that whatever the first call leaves in the shared array cannot leak into
+the second.  This file is named to be collected last.
+"""
+import numpy as np
+import pytest
+
+import moe_b200 as M
+import oracle_lib as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5   # the FP32 path's layer tolerance (max|Δ| / max|ref|)
+
+
+def _upload(p):
+    return M.MoEWeights.upload(p.W_router, [e[0] for e in p.experts], [e[1] for e in p.experts],
+                               [e[2] for e in p.experts], p.k)
+
+
+def _run_both(w, x_np, bias_np, E, k):
+    import torch
+    T, d = x_np.shape
+    s = torch.cuda.Stream()
+    x = torch.from_numpy(x_np).cuda()
+    bias = torch.from_numpy(bias_np).cuda() if bias_np is not None else None
+    bptr = bias.data_ptr() if bias is not None else None
+    outs = []
+    for noalloc in (False, True):
+        out = torch.full((T, d), float("nan"), device="cuda")
+        probs = torch.full((T, E), float("nan"), device="cuda")
+        ids = torch.full((T, k), -1, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        if noalloc:
+            M.moe_forward_noalloc(w, x.data_ptr(), T, out.data_ptr(), probs.data_ptr(),
+                                  ids.data_ptr(), bias_ptr=bptr, stream=s.cuda_stream)
+        else:
+            M.moe_forward_device(w, x.data_ptr(), T, out.data_ptr(), probs.data_ptr(),
+                                 ids.data_ptr(), bias_ptr=bptr, path=M.PATH_FP32,
+                                 stream=s.cuda_stream)
+        s.synchronize()
+        outs.append((out.cpu().numpy(), probs.cpu().numpy(), ids.cpu().numpy()))
+    return outs
+
+
+def test_noalloc_matches_device_entry_point_two_calls(moe):
+    p = O.MoEProblem(96, 384, 8, 2, 1536, seed=11)
+    w = _upload(p)
+    x2 = O.synth(12, O.stream_x(), 33 * 384, 1.0).reshape(33, 384)
+    bias2 = O.synth(12, O.stream_bias(), 8, 1.0)
+    for x, bias in ((p.x, None), (x2, bias2)):
+        (r_out, r_probs, r_ids), (n_out, n_probs, n_ids) = _run_both(w, x, bias, p.E, p.k)
+        assert np.isfinite(n_out).all()
+        assert np.array_equal(n_ids, r_ids)
+        assert np.max(np.abs(n_probs - r_probs)) <= 1e-7
+        assert O.rel_err(n_out, r_out) < TOL
+    w.free()
+
+
+def test_noalloc_rejects_oversized_call(moe):
+    import torch
+    w = M.MoEWeights.synth(3, 0.02, 1024, 4096, 8, 2)
+    T = 4096                       # needs ~200 MB of intermediates
+    x = torch.zeros((T, 1024), device="cuda")
+    out = torch.empty_like(x)
+    with pytest.raises(M.MoEError) as ei:
+        M.moe_forward_noalloc(w, x.data_ptr(), T, out.data_ptr())
+    assert ei.value.status == M.E_INVALID
+    assert "static array" in str(ei.value)
+    w.free()
