@@ -6,9 +6,11 @@
 
 A step is one forward of the MoE layer over the config's T tokens.  With N
 GPUs (torchrun) the layer runs expert-parallel: tokens are split across
-ranks, experts' work is balanced across ranks, and NCCL all-to-alls carry
-the dispatch and the combine; `value` is the whole job's tokens/s and the
-timing is the max over ranks.  Inputs are seeded synthetic tensors with
+ranks, the global expert-sorted rows are split into N equal slices (weights
+replicated), token rows reach their slice owner and results return by
+direct NVLink peer stores, and NCCL carries the counts and two barriers;
+`value` is the whole job's tokens/s (T fixed: strong scaling) and the timing
+is the max over ranks.  Inputs are seeded synthetic tensors with
 the config's shapes and distributions (no dataset is involved).
 
 Printed: one JSON line on rank 0 (see the keys in `main`).
@@ -248,98 +250,144 @@ def main():
     torch.cuda.set_device(local)
     dist = None
     if world > 1:
+        # the group's NCCL traffic is a few counts and barriers: keep it on
+        # plain NVLink transport (no NVLS multicast objects)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-        raise SystemExit("expert-parallel runs need the EP build (not in this library yet)")
 
     M.init(local)
     path = {"auto": M.PATH_AUTO, "tf32": M.PATH_TF32, "fp32": M.PATH_FP32}[args.path]
     T, d, E, k, F, seed = c["T"], c["d"], c["E"], c["k"], c["F"], c["seed"]
-    w = M.MoEWeights.synth(seed, W_STD, d, F, E, k)
+    if T % world:
+        raise SystemExit(f"T={T} is not divisible by {world} ranks")
+    Tl = T // world                      # this rank's tokens (strong scaling: T fixed)
+    w = M.MoEWeights.synth(seed, W_STD, d, F, E, k)   # every rank holds all experts
     # a dedicated stream: the legacy default stream's handle is 0, which the
     # library reads as "use the library stream"
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    x = torch.empty((T, d), dtype=torch.float32, device="cuda")
-    M.synth_fill(x.data_ptr(), T * d, seed, M.STREAM_X, 1.0, cuda_stream=stream.cuda_stream)
+    # rows [rank*Tl, (rank+1)*Tl) of the same global x the 1-GPU run sees
+    x = torch.empty((Tl, d), dtype=torch.float32, device="cuda")
+    M.synth_fill(x.data_ptr(), Tl * d, seed, M.STREAM_X, 1.0, first=rank * Tl * d,
+                 cuda_stream=stream.cuda_stream)
     bias = None
     if c["bias"] == "zipf":
         bias = torch.from_numpy(zipf_bias(E)).cuda()
     elif c["bias"] == "normal":
         bias = torch.empty(E, device="cuda")
         M.synth_fill(bias.data_ptr(), E, seed, M.STREAM_BIAS, 1.0, cuda_stream=stream.cuda_stream)
-    out = torch.empty((T, d), dtype=torch.float32, device="cuda")
-    probs = torch.empty((T, E), dtype=torch.float32, device="cuda")
-    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+    out = torch.empty((Tl, d), dtype=torch.float32, device="cuda")
+    probs = torch.empty((Tl, E), dtype=torch.float32, device="cuda")
+    ids = torch.empty((Tl, k), dtype=torch.int32, device="cuda")
     bptr = bias.data_ptr() if bias is not None else None
 
+    ep = None
+    if world > 1:
+        obj = [M.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ep = M.EP(obj[0], rank, world, Tl, w)
+
     def step():
-        M.moe_forward_device(w, x.data_ptr(), T, out.data_ptr(), probs.data_ptr(), ids.data_ptr(),
-                             bias_ptr=bptr, path=path, stream=stream.cuda_stream)
+        if ep is None:
+            M.moe_forward_device(w, x.data_ptr(), Tl, out.data_ptr(), probs.data_ptr(),
+                                 ids.data_ptr(), bias_ptr=bptr, path=path,
+                                 stream=stream.cuda_stream)
+        else:
+            ep.forward_device(x.data_ptr(), Tl, out.data_ptr(), probs.data_ptr(), ids.data_ptr(),
+                              bias_ptr=bptr, path=path, stream=stream.cuda_stream)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     for _ in range(args.warmup):
         step()
-    torch.cuda.synchronize()
+    barrier()
     launches_per_step = M.last_launches()
-    counts = M.last_counts(w)
+    if ep is None:
+        counts = M.last_counts(w)
+        slice_rows = Tl * k
+    else:
+        counts_all, slice_rows = ep.counts()
+        counts = counts_all.sum(axis=0)
 
-    # ---- device-resident timed region
+    # ---- device-resident timed region (CUDA events on the launch stream,
+    # barrier + synchronize on both sides, max over ranks)
     M.profile_enable(True)
     M.profile_read()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        torch.cuda.synchronize()
+        barrier()
         ev0.record(stream)
         for _ in range(args.steps):
             step()
         ev1.record(stream)
-        torch.cuda.synchronize()
+        barrier()
     M.profile_enable(False)
     stage_ms, n_fw = M.profile_read()
-    ms = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
     value = T / (ms / 1000.0)
 
     # ---- end to end through the public host-buffer C-ABI (pinned buffers,
     # H2D of x and D2H of out/probs/ids inside every step)
-    hx = torch.empty((T, d), dtype=torch.float32, pin_memory=True)
+    hx = torch.empty((Tl, d), dtype=torch.float32, pin_memory=True)
     hx.copy_(x.cpu())
-    hout = torch.empty((T, d), dtype=torch.float32, pin_memory=True)
-    hprobs = torch.empty((T, E), dtype=torch.float32, pin_memory=True)
-    hids = torch.empty((T, k), dtype=torch.int32, pin_memory=True)
+    hout = torch.empty((Tl, d), dtype=torch.float32, pin_memory=True)
+    hprobs = torch.empty((Tl, E), dtype=torch.float32, pin_memory=True)
+    hids = torch.empty((Tl, k), dtype=torch.int32, pin_memory=True)
     hbias = bias.cpu().contiguous() if bias is not None else None
+    hb = hbias.data_ptr() if hbias is not None else None
 
     def e2e_step():
-        M.moe_forward_host_ptr(w, hx.data_ptr(), T, hout.data_ptr(), hprobs.data_ptr(),
-                               hids.data_ptr(), hbias.data_ptr() if hbias is not None else None,
-                               path=path)
+        if ep is None:
+            M.moe_forward_host_ptr(w, hx.data_ptr(), Tl, hout.data_ptr(), hprobs.data_ptr(),
+                                   hids.data_ptr(), hb, path=path)
+        else:
+            ep.forward_host_ptr(hx.data_ptr(), Tl, hout.data_ptr(), hprobs.data_ptr(),
+                                hids.data_ptr(), hb, path=path)
 
     for _ in range(2):
         e2e_step()
-    torch.cuda.synchronize()
+    barrier()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         e2e_step()
     torch.cuda.synchronize()
-    e2e_ms = 1000.0 * (time.perf_counter() - t0) / args.steps
+    e2e_ms = max_over_ranks(1000.0 * (time.perf_counter() - t0) / args.steps)
+    barrier()
     assert torch.equal(hout, out.cpu()), "e2e output differs from the device-resident run"
 
-    # ---- roofline of the dominant kernel (expert up/gate GEMM)
+    # ---- roofline of the dominant kernel (expert up/gate GEMM on this rank)
     peaks = measured_peaks()
     tf32_peak = peaks["bf16_sustained"] / 2.0
     stage_avg = {s: v / max(n_fw, 1) for s, v in stage_ms.items()}
-    up_flops = 4.0 * T * k * d * F
+    up_flops = 4.0 * slice_rows * d * F          # this rank's slice of the global rows
     up_ms = stage_avg["upgate"]
     achieved = up_flops / (up_ms / 1000.0) / 1e12
     traffic = None
     tfile = REPO / "profiles" / "traffic.json"
-    if tfile.exists():
+    if tfile.exists() and world == 1:
         tj = json.loads(tfile.read_text())
         traffic = tj.get(args.config, {}).get("upgate_bytes_per_launch")
     touched = int(np.count_nonzero(counts))
-    t_roof = max(flops_per_step(c) / (tf32_peak * 1e12),
-                 min_bytes_per_step(c, touched) / (peaks["hbm_gbs"] * 1e9))
+    t_roof = max(flops_per_step(c) / (tf32_peak * 1e12 * world),
+                 min_bytes_per_step(c, touched) / (peaks["hbm_gbs"] * 1e9 * world))
+    if world > 1:
+        # rows crossing NVLink per rank and direction (dispatch, then return)
+        a2a = 4.0 * d * (T * k / world) * (world - 1) / world
+        t_roof += a2a / 770e9
 
     line = {
         "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
@@ -348,12 +396,14 @@ def main():
         "data": "synthetic",
         "config": {"workload": args.config, "T": T, "d_model": d, "n_experts": E, "top_k": k,
                    "d_ff": F, "router_bias": c["bias"], "path": args.path,
-                   "parallelism": f"ep{world}", "l2": "inputs larger than L2"
+                   "parallelism": f"ep{world}" + (" (balanced slices, replicated weights)"
+                                                  if world > 1 else ""),
+                   "l2": "inputs larger than L2"
                    if 4 * T * d > 126e6 else "inputs smaller than L2 (no flush)"},
         "e2e": {"value": T / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": 4 * T * d + (4 * E if bias is not None else 0),
+                "h2d_bytes_per_step": 4 * T * d + (4 * E * world if bias is not None else 0),
                 "d2h_bytes_per_step": 4 * T * d + 4 * T * E + 4 * T * k,
-                "timing": "host wall clock around synchronous moe_b200_forward calls"},
+                "timing": "host wall clock around synchronous forward calls, max over ranks"},
         "roofline": {"bound": "tensor", "kernel": "tc_grouped_gemm<256,swiglu> (expert up/gate)",
                      "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
                      "frac": achieved / tf32_peak, "traffic": traffic,
@@ -371,8 +421,11 @@ def main():
                                 "sample": desc}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if ep is not None:
+        ep.destroy()
+        dist.barrier()
+        dist.destroy_process_group()
     w.free()
-
 
 if __name__ == "__main__":
     main()

@@ -166,6 +166,56 @@ int moe_b200_last_counts(const moe_b200_weights *w, int *counts);
 /* Number of kernel launches the last forward issued on this device. */
 int moe_b200_last_launches(void);
 
+/* ---- expert parallel (one process per GPU, NVLink) --------------------- */
+/* llm.c has no multi-GPU path (README.md:379 lists it as a roadmap item);
+ * these entry points extend moe_forward to G GPUs of one node.
+ *
+ * Every rank holds the full expert set (replicated weights) and routes its
+ * own tokens.  The rows of all ranks, in global expert-sorted order, are
+ * split into G equal contiguous slices and rank q computes the expert
+ * products of slice q, so the load stays balanced however skewed expert
+ * popularity is.  Token rows and result rows move by direct peer stores
+ * over NVLink (CUDA IPC); NCCL carries only per-expert counts and two
+ * barriers.  All calls except moe_b200_ep_unique_id are collective: every
+ * rank makes them, in the same order. */
+#define MOE_B200_EP_ID_BYTES 128
+typedef struct moe_b200_ep moe_b200_ep;
+
+/* Create the NCCL id on one rank (id: MOE_B200_EP_ID_BYTES bytes); the
+ * caller broadcasts it to the other ranks by any host means. */
+int moe_b200_ep_unique_id(void *id);
+
+/* Join the group: rank in [0, world), at most max_tokens_per_rank tokens per
+ * forward on this rank, weights `w` (all E experts) on this rank's device. */
+int moe_b200_ep_create(const void *id, int rank, int world, int max_tokens_per_rank,
+                       const moe_b200_weights *w, moe_b200_ep **out);
+
+/* Leave the group and free its buffers (collective). */
+int moe_b200_ep_destroy(moe_b200_ep *ep);
+
+/* Forward of this rank's T tokens (device buffers, asynchronous on
+ * `stream`, NULL = the group's stream); same outputs as
+ * moe_b200_forward_device for these tokens. */
+int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, const float *d_x, int T,
+                               float *d_out, float *d_router_probs, int *d_expert_ids,
+                               const moe_b200_opts *opts, void *stream);
+
+/* Same with host buffers, synchronous (H2D of x, D2H of the outputs). */
+int moe_b200_ep_forward(moe_b200_ep *ep, const float *router_bias, const float *x, int T,
+                        float *out, float *router_probs, int *expert_ids,
+                        const moe_b200_opts *opts);
+
+/* Per-rank, per-expert counts of the last forward ([world × E]) and the
+ * number of rows this rank's slice held; synchronises the device. */
+int moe_b200_ep_counts(moe_b200_ep *ep, int *counts_all, int *slice_rows);
+
+/* The partition every rank derives from counts_all [world × E]: rows of
+ * expert e in `rank`'s slice (cnt_rank[E]), global position of `rank`'s
+ * first row of each expert (base_rank[E]), and the slice's start and size
+ * in the global expert-sorted order.  Host computation, no device. */
+int moe_b200_ep_partition(const int *counts_all, int world, int E, int rank, int *cnt_rank,
+                          int *base_rank, long long *slice_start, long long *slice_rows);
+
 /* ---- stage timing ------------------------------------------------------ */
 
 /* Stages of one forward, in launch order. */

@@ -53,7 +53,8 @@ template <bool SWIGLU>
 __global__ void __launch_bounds__(256)
 ffma_grouped_kernel(const float *__restrict__ A, int K,
                     const float *__restrict__ B, int b_rows_per_expert,
-                    float *__restrict__ C, int ldc, const int *__restrict__ plan, int E)
+                    float *__restrict__ C, int ldc, const int *__restrict__ plan, int E,
+                    float *const *__restrict__ out_ptrs, const int2 *__restrict__ ret)
 {
     __shared__ __align__(16) float As[BK][BM + 4];
     __shared__ __align__(16) float Bs[BK][BN + 4];
@@ -119,8 +120,14 @@ ffma_grouped_kernel(const float *__restrict__ A, int K,
         } else {
             o = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
         }
-        *reinterpret_cast<float4 *>(C + (size_t)(row0 + r) * ldc + n0 + tx * 4) = o;
+        float *dst = C + (size_t)(row0 + r) * ldc;
+        if (!SWIGLU && ret != nullptr) {          // expert-parallel return to the owner
+            const int2 rr = ret[row0 + r];
+            dst = out_ptrs[rr.x] + (size_t)rr.y * ldc;
+        }
+        *reinterpret_cast<float4 *>(dst + n0 + tx * 4) = o;
     }
+    if (!SWIGLU && ret != nullptr) __threadfence_system();
 }
 
 static int mtile_bound(int rows_bound, int E, int bm) { return ceil_div(rows_bound, bm) + E; }
@@ -129,15 +136,18 @@ cudaError_t launch_ffma_upgate(const float *x_perm, int d_pad, const float *w_ug
                                float *h, const int *plan, int E, int rows_bound, cudaStream_t s)
 {
     dim3 grid(mtile_bound(rows_bound, E, BM), F_pad / BN);
-    ffma_grouped_kernel<true><<<grid, 256, 0, s>>>(x_perm, d_pad, w_ug, 2 * F_pad, h, F_pad, plan, E);
+    ffma_grouped_kernel<true><<<grid, 256, 0, s>>>(x_perm, d_pad, w_ug, 2 * F_pad, h, F_pad, plan, E,
+                                                   nullptr, nullptr);
     return cudaGetLastError();
 }
 
 cudaError_t launch_ffma_down(const float *h, int F_pad, const float *w_d, int d_pad,
-                             float *y, const int *plan, int E, int rows_bound, cudaStream_t s)
+                             float *y, const int *plan, int E, int rows_bound, cudaStream_t s,
+                             float *const *y_ptrs, const int2 *ret)
 {
     dim3 grid(mtile_bound(rows_bound, E, BM), d_pad / BN);
-    ffma_grouped_kernel<false><<<grid, 256, 0, s>>>(h, F_pad, w_d, d_pad, y, d_pad, plan, E);
+    ffma_grouped_kernel<false><<<grid, 256, 0, s>>>(h, F_pad, w_d, d_pad, y, d_pad, plan, E,
+                                                    y_ptrs, ret);
     return cudaGetLastError();
 }
 

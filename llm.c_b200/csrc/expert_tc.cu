@@ -6,7 +6,7 @@
 // tiles (expert, 128-row m-tile, BN-column n-tile).  Warp roles:
 //   warp 0      TMA producer: 128B-swizzled K-major tiles of activations
 //               (128×32 fp32) and weights (BN×32 fp32) into a 4-stage
-//               shared-memory ring (plain loads, no cluster multicast)
+//               shared-memory ring (plain per-CTA loads)
 //   warp 1      TMEM allocator and MMA issuer: tcgen05.mma kind::tf32,
 //               M=128, N=BN, K=8, four per stage, accumulating in TMEM;
 //               tcgen05.commit frees the smem stage / publishes the tile
@@ -171,7 +171,8 @@ template <int BN, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1)
 tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const int *__restrict__ plan, int E, int num_kb, int b_rows_per_expert,
-                int NT, float *__restrict__ out, int ldo, DeviceStatus *status)
+                int NT, float *__restrict__ out, int ldo, DeviceStatus *status,
+                float *const *__restrict__ out_ptrs, const int2 *__restrict__ ret)
 {
     constexpr int B_BYTES = BN * BK * 4;
     constexpr uint32_t TMEM_COLS = 2 * BN;        // two accumulator buffers
@@ -329,7 +330,15 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     }
                 }
             } else {
-                float *dst = out + grow * ldo + (size_t)c.ni * BN;
+                // expert-parallel: a row of this rank's slice goes back to the
+                // rank that owns its token (peer memory over NVLink)
+                float *dst;
+                if (ret != nullptr && valid) {
+                    const int2 rr = ret[grow];
+                    dst = out_ptrs[rr.x] + (size_t)rr.y * ldo + (size_t)c.ni * BN;
+                } else {
+                    dst = out + grow * ldo + (size_t)c.ni * BN;
+                }
 #pragma unroll 1
                 for (int col = 0; col < BN; col += 32) {
                     float v[32];
@@ -347,6 +356,9 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             acc ^= 1;
             if (acc == 0) acc_phase ^= 1;
         }
+        // peer stores must be visible before the rank-wide barrier that
+        // follows this kernel on the stream
+        if (ret != nullptr) __threadfence_system();
     }
 
     __syncwarp();          // lanes 1..31 of warps 0/1 wait for their lane 0
@@ -390,23 +402,24 @@ cudaError_t launch_tc_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, co
     const int bound = tile_bound(rows_bound, E) * NT;
     const int grid = max(1, min(num_sms, bound));
     tc::tc_grouped_gemm<256, true><<<grid, tc::kThreads, tc::smem_bytes<256>(), s>>>(
-        g.tmA, g.tmB, plan, E, d_pad / tc::BK, 2 * F_pad, NT, h, F_pad, status);
+        g.tmA, g.tmB, plan, E, d_pad / tc::BK, 2 * F_pad, NT, h, F_pad, status, nullptr, nullptr);
     return cudaGetLastError();
 }
 
 cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float *y,
                            const int *plan, int E, int rows_bound, int num_sms,
-                           DeviceStatus *status, cudaStream_t s)
+                           DeviceStatus *status, cudaStream_t s, float *const *y_ptrs,
+                           const int2 *ret)
 {
     const int NT = d_pad / bn;
     const int bound = tile_bound(rows_bound, E) * NT;
     const int grid = max(1, min(num_sms, bound));
     if (bn == 256)
         tc::tc_grouped_gemm<256, false><<<grid, tc::kThreads, tc::smem_bytes<256>(), s>>>(
-            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status);
+            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status, y_ptrs, ret);
     else
         tc::tc_grouped_gemm<128, false><<<grid, tc::kThreads, tc::smem_bytes<128>(), s>>>(
-            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status);
+            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status, y_ptrs, ret);
     return cudaGetLastError();
 }
 

@@ -19,6 +19,10 @@ cudaError_t launch_dispatch(const float *x, int T, int d, int d_pad, int E, int 
                             int *tile_pref, int *plan, int *pos_of, float *x_perm,
                             int round_to_tf32, DeviceStatus *status, cudaStream_t s);
 
+// scan only (the expert-parallel path does its own gather)
+cudaError_t launch_dispatch_scan(const int *tile_cnt, int T, int E, int *tile_pref, int *plan,
+                                 cudaStream_t s);
+
 cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
                            const int *pos_of, const float *wts, float *out, cudaStream_t s);
 
@@ -28,7 +32,8 @@ cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
 cudaError_t launch_ffma_upgate(const float *x_perm, int d_pad, const float *w_ug, int F_pad,
                                float *h, const int *plan, int E, int rows_bound, cudaStream_t s);
 cudaError_t launch_ffma_down(const float *h, int F_pad, const float *w_d, int d_pad,
-                             float *y, const int *plan, int E, int rows_bound, cudaStream_t s);
+                             float *y, const int *plan, int E, int rows_bound, cudaStream_t s,
+                             float *const *y_ptrs = nullptr, const int2 *ret = nullptr);
 
 // tcgen05 TF32 grouped GEMMs (128-row tiles scheduled on mt128), persistent.
 struct TcGemm {
@@ -37,8 +42,10 @@ struct TcGemm {
 };
 cudaError_t launch_tc_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, const int *plan,
                              int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s);
+// y_ptrs/ret (expert parallel): output row i goes to y_ptrs[ret[i].x] + ret[i].y * d_pad
 cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float *y, const int *plan,
-                           int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s);
+                           int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s,
+                           float *const *y_ptrs = nullptr, const int2 *ret = nullptr);
 cudaError_t tc_set_attributes();
 
 // weight repack: src row-major [R × C] (one expert matrix) -> dst rows of

@@ -579,6 +579,27 @@ extern "C" int moe_b200_last_launches(void) {
     return g_ctx[dev]->last_launches;
 }
 
+// hooks for the expert-parallel forward (ep.cu): the same stage timing and
+// launch count as a single-GPU forward on this device
+cudaEvent_t *moe::profile_events(int device) {
+    Ctx *c;
+    if (get_ctx(device, &c)) return nullptr;
+    return prof_slot(c);
+}
+
+void moe::note_forward(int device, int E, int launches) {
+    Ctx *c;
+    if (get_ctx(device, &c)) return;
+    c->last_E = E;
+    c->last_launches = launches;
+}
+
+int moe::device_sms(int device) {
+    Ctx *c;
+    if (get_ctx(device, &c)) return 0;
+    return c->num_sms;
+}
+
 extern "C" int moe_b200_synth_fill(float *d_dst, size_t n, uint64_t seed, uint64_t stream,
                                    uint64_t first, float std, void *cuda_stream) {
     if (!d_dst && n) return fail(MOE_B200_E_INVALID, "null destination");

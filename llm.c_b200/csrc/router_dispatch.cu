@@ -172,3 +172,12 @@ cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
 }
 
 }  // namespace moe
+
+namespace moe {
+cudaError_t launch_dispatch_scan(const int *tile_cnt, int T, int E, int *tile_pref, int *plan,
+                                 cudaStream_t s)
+{
+    dispatch_scan_kernel<<<1, 1024, 0, s>>>(tile_cnt, ceil_div(T, kRouterTile), E, tile_pref, plan);
+    return cudaGetLastError();
+}
+}  // namespace moe

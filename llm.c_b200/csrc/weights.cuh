@@ -2,6 +2,7 @@
 // moe_b200_weights handle (internal to the library).
 #pragma once
 #include <cuda.h>
+#include <cuda_runtime.h>
 
 struct moe_b200_weights {
     int device;
@@ -18,4 +19,11 @@ namespace moe {
 // Record a status and its detail text as this host thread's last error
 // (read back through moe_b200_last_error); returns `code`.
 __attribute__((visibility("hidden"))) int set_last_error(int code, const char *detail);
+// Stage-timing events for one forward on `device` (nullptr when timing is
+// off): MOE_B200_NUM_STAGES + 1 events recorded between the stages.
+__attribute__((visibility("hidden"))) cudaEvent_t *profile_events(int device);
+// Record the expert count and kernel launches of the last forward.
+__attribute__((visibility("hidden"))) void note_forward(int device, int E, int launches);
+// Number of SMs of `device` (0 if the device is unusable).
+__attribute__((visibility("hidden"))) int device_sms(int device);
 }  // namespace moe

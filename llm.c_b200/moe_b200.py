@@ -335,3 +335,89 @@ def moe_forward_noalloc(w: MoEWeights, x_ptr: int, T: int, out_ptr: int,
     L.moe_b200_forward_noalloc.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp]
     _check(L.moe_b200_forward_noalloc(w.handle, bias_ptr, x_ptr, T, out_ptr, probs_ptr, ids_ptr,
                                       stream), "moe_b200_forward_noalloc")
+
+
+# ---------------------------------------------------------------- expert parallel
+EP_ID_BYTES = 128
+
+
+def ep_unique_id() -> bytes:
+    buf = C.create_string_buffer(EP_ID_BYTES)
+    _check(lib().moe_b200_ep_unique_id(buf), "moe_b200_ep_unique_id")
+    return buf.raw
+
+
+def ep_partition(counts_all: np.ndarray, rank: int):
+    """The slice plan of `rank` from the per-rank expert counts [world × E]:
+    (rows per expert in the slice, global base of rank's rows per expert,
+    slice start, slice size)."""
+    c = np.ascontiguousarray(counts_all, np.int32)
+    G, E = c.shape
+    cnt = np.empty(E, np.int32)
+    base = np.empty(E, np.int32)
+    lo, rows = C.c_longlong(), C.c_longlong()
+    L = lib()
+    L.moe_b200_ep_partition.argtypes = [_ip, C.c_int, C.c_int, C.c_int, _ip, _ip,
+                                        C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]
+    _check(L.moe_b200_ep_partition(_i(c), G, E, rank, _i(cnt), _i(base), C.byref(lo),
+                                   C.byref(rows)), "moe_b200_ep_partition")
+    return cnt, base, int(lo.value), int(rows.value)
+
+
+class EP:
+    """An expert-parallel group member (collective calls on every rank)."""
+
+    def __init__(self, uid: bytes, rank: int, world: int, max_tokens: int, w: MoEWeights):
+        L = lib()
+        L.moe_b200_ep_create.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, _vp,
+                                         C.POINTER(_vp)]
+        L.moe_b200_ep_destroy.argtypes = [_vp]
+        L.moe_b200_ep_forward_device.argtypes = [_vp, _vp, _vp, C.c_int, _vp, _vp, _vp,
+                                                 C.POINTER(Opts), _vp]
+        L.moe_b200_ep_forward.argtypes = [_vp, _fp, _fp, C.c_int, _fp, _fp, _ip,
+                                          C.POINTER(Opts)]
+        L.moe_b200_ep_counts.argtypes = [_vp, _ip, _ip]
+        h = _vp()
+        _check(L.moe_b200_ep_create(uid, rank, world, max_tokens, w.handle, C.byref(h)),
+               "moe_b200_ep_create")
+        self.handle, self.rank, self.world, self.w = h.value, rank, world, w
+
+    def forward_device(self, x_ptr, T, out_ptr, probs_ptr=None, ids_ptr=None, bias_ptr=None,
+                       path=PATH_AUTO, stream=None):
+        o = _opts(path)
+        _check(lib().moe_b200_ep_forward_device(self.handle, bias_ptr, x_ptr, T, out_ptr,
+                                                probs_ptr, ids_ptr, C.byref(o), stream),
+               "moe_b200_ep_forward_device")
+
+    def forward(self, x: np.ndarray, bias: np.ndarray | None = None, path=PATH_AUTO):
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[0]
+        w = self.w
+        out = np.empty((T, w.d), np.float32)
+        probs = np.empty((T, w.E), np.float32)
+        ids = np.empty((T, w.top_k), np.int32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        o = _opts(path)
+        _check(lib().moe_b200_ep_forward(self.handle, _f(b), _f(x), T, _f(out), _f(probs),
+                                         _i(ids), C.byref(o)), "moe_b200_ep_forward")
+        return out, probs, ids
+
+    def forward_host_ptr(self, x_ptr, T, out_ptr, probs_ptr, ids_ptr, bias_ptr=None,
+                         path=PATH_AUTO):
+        o = _opts(path)
+        _check(lib().moe_b200_ep_forward(self.handle, C.cast(bias_ptr, _fp) if bias_ptr else None,
+                                         C.cast(x_ptr, _fp), T, C.cast(out_ptr, _fp),
+                                         C.cast(probs_ptr, _fp) if probs_ptr else None,
+                                         C.cast(ids_ptr, _ip) if ids_ptr else None, C.byref(o)),
+               "moe_b200_ep_forward")
+
+    def counts(self):
+        c = np.empty((self.world, self.w.E), np.int32)
+        rows = C.c_int()
+        _check(lib().moe_b200_ep_counts(self.handle, _i(c), C.byref(rows)), "moe_b200_ep_counts")
+        return c, int(rows.value)
+
+    def destroy(self):
+        if self.handle:
+            lib().moe_b200_ep_destroy(self.handle)
+            self.handle = 0
