@@ -373,6 +373,10 @@ def main():
     peaks = measured_peaks()
     tf32_peak = peaks["bf16_sustained"] / 2.0
     stage_avg = {s: v / max(n_fw, 1) for s, v in stage_ms.items()}
+    stages_by_rank = None
+    if dist is not None:
+        stages_by_rank = [None] * world
+        dist.all_gather_object(stages_by_rank, {"stages": stage_avg, "slice_rows": slice_rows})
     up_flops = 4.0 * slice_rows * d * F          # this rank's slice of the global rows
     up_ms = stage_avg["upgate"]
     achieved = up_flops / (up_ms / 1000.0) / 1e12
@@ -410,6 +414,7 @@ def main():
                      "peak_src": f"{peaks['src']} bf16 sustained / 2 (TF32 rate)",
                      "layer_frac": t_roof / (ms / 1000.0)},
         "stages_ms": stage_avg,
+        "stages_ms_by_rank": stages_by_rank,
         "expert_counts_max_over_mean": float(counts.max() / counts.mean()),
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),

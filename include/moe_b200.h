@@ -186,7 +186,8 @@ typedef struct moe_b200_ep moe_b200_ep;
 int moe_b200_ep_unique_id(void *id);
 
 /* Join the group: rank in [0, world), at most max_tokens_per_rank tokens per
- * forward on this rank, weights `w` (all E experts) on this rank's device. */
+ * forward on each rank (the same value on every rank), weights `w` (all E
+ * experts) on this rank's device. */
 int moe_b200_ep_create(const void *id, int rank, int world, int max_tokens_per_rank,
                        const moe_b200_weights *w, moe_b200_ep **out);
 
@@ -209,12 +210,16 @@ int moe_b200_ep_forward(moe_b200_ep *ep, const float *router_bias, const float *
  * number of rows this rank's slice held; synchronises the device. */
 int moe_b200_ep_counts(moe_b200_ep *ep, int *counts_all, int *slice_rows);
 
-/* The partition every rank derives from counts_all [world × E]: rows of
- * expert e in `rank`'s slice (cnt_rank[E]), global position of `rank`'s
- * first row of each expert (base_rank[E]), and the slice's start and size
- * in the global expert-sorted order.  Host computation, no device. */
-int moe_b200_ep_partition(const int *counts_all, int world, int E, int rank, int *cnt_rank,
-                          int *base_rank, long long *slice_start, long long *slice_rows);
+/* The partition every rank derives from counts_all [world × E]: slices of
+ * the global expert-sorted rows balanced on estimated GEMM cost (2 units per
+ * 128-row tile of an expert in the slice, 1 per expert segment), cut at
+ * 128-row tile boundaries; equal rows instead if a slice would exceed
+ * `capacity` rows (0 = no limit).  Outputs: rows of expert e in `rank`'s
+ * slice (cnt_rank[E]), global position of `rank`'s first row of each expert
+ * (base_rank[E]), and the slice's start and size.  Host computation. */
+int moe_b200_ep_partition(const int *counts_all, int world, int E, int rank, long long capacity,
+                          int *cnt_rank, int *base_rank, long long *slice_start,
+                          long long *slice_rows);
 
 /* ---- stage timing ------------------------------------------------------ */
 

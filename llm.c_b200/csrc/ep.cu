@@ -38,16 +38,65 @@ using namespace moe;
 
 // ---------------------------------------------------------------------
 // partition (host copy: tests and diagnostics; device copy: the forward)
+//
+// Slices are balanced on estimated cost, not on rows: the grouped GEMMs
+// spend per 128-row m-tile, and each expert segment of a slice adds about
+// half an m-tile more (its partially filled last tile and its own pass over
+// the expert's weights).  So an expert with n rows costs 2·ceil(n/128) + 1
+// units, and slice boundaries fall on m-tile boundaries inside experts.  A
+// slice may then hold somewhat more rows than T·k/G; if any slice would
+// exceed the receive capacity, the partition falls back to equal rows.
+// Integer arithmetic throughout, so every rank (and the host copy) derives
+// the same boundaries.
 // ---------------------------------------------------------------------
-__host__ __device__ inline void ep_partition(const int *C, int G, int E, int rank, int *cnt_q,
-                                             int *base_r, long long *lo_out,
-                                             long long *chunk_out) {
-    long long M = 0;
-    for (int e = 0; e < E; e++)
-        for (int r = 0; r < G; r++) M += C[r * E + e];
-    const long long chunk = M > 0 ? (M + G - 1) / G : 1;
-    const long long lo = (long long)rank * chunk;
-    const long long hi = lo + chunk < M ? lo + chunk : M;
+__host__ __device__ inline void ep_slices(const int *C, int G, int E, long long capacity,
+                                          long long *S /* G+1 */) {
+    long long M = 0, U = 0;
+    for (int e = 0; e < E; e++) {
+        long long tot = 0;
+        for (int r = 0; r < G; r++) tot += C[r * E + e];
+        M += tot;
+        U += 2 * ((tot + 127) / 128) + (tot > 0 ? 1 : 0);
+    }
+    S[0] = 0;
+    int q = 1;
+    long long cum = 0, goff = 0;
+    for (int e = 0; e < E && q < G; e++) {
+        long long tot = 0;
+        for (int r = 0; r < G; r++) tot += C[r * E + e];
+        const long long tiles = (tot + 127) / 128;
+        const long long units = 2 * tiles + (tot > 0 ? 1 : 0);
+        // boundary q sits at cost q·U/G; place it inside this expert when the
+        // expert's cost range reaches it
+        while (q < G && (long long)q * U <= (long long)G * (cum + units)) {
+            const long long num = (long long)q * U - (long long)G * (cum + 1);   // 2t·G ≈ num
+            long long t = num <= 0 ? 0 : (num + G) / (2LL * G);
+            if (t > tiles) t = tiles;
+            const long long rows = 128 * t < tot ? 128 * t : tot;
+            S[q] = goff + rows;
+            q++;
+        }
+        cum += units;
+        goff += tot;
+    }
+    for (; q < G; q++) S[q] = M;
+    S[G] = M;
+    bool fits = true;
+    for (q = 1; q <= G; q++) {
+        if (S[q] < S[q - 1]) S[q] = S[q - 1];
+        if (capacity > 0 && S[q] - S[q - 1] > capacity) fits = false;
+    }
+    if (!fits) {                               // equal rows always fit
+        const long long chunk = M > 0 ? (M + G - 1) / G : 1;
+        for (q = 0; q <= G; q++) S[q] = (long long)q * chunk < M ? (long long)q * chunk : M;
+    }
+}
+
+__host__ __device__ inline void ep_partition(const int *C, int G, int E, int rank,
+                                             long long capacity, int *cnt_q, int *base_r,
+                                             long long *S /* G+1 */) {
+    ep_slices(C, G, E, capacity, S);
+    const long long lo = S[rank], hi = S[rank + 1];
     long long goff = 0;
     for (int e = 0; e < E; e++) {
         long long tot = 0, before = 0;
@@ -61,20 +110,18 @@ __host__ __device__ inline void ep_partition(const int *C, int G, int E, int ran
         if (base_r) base_r[e] = (int)(goff + before);
         goff += tot;
     }
-    if (lo_out) *lo_out = lo;
-    if (chunk_out) *chunk_out = chunk;
 }
 
 // One thread: this rank's slice plan (cnt | off | mt128 | mt64), the global
-// base of this rank's rows per expert, and the slice size.
+// base of this rank's rows per expert, and the slice boundaries.
 __global__ void ep_plan_kernel(const int *__restrict__ counts_all, int G, int E, int rank,
-                               int *__restrict__ plan, int *__restrict__ base_r,
-                               int *__restrict__ chunk_out)
+                               long long capacity, int *__restrict__ plan,
+                               int *__restrict__ base_r, int *__restrict__ slices)
 {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     int *cnt = plan, *off = plan + E, *mt128 = off + E + 1, *mt64 = mt128 + E + 1;
-    long long lo, chunk;
-    ep_partition(counts_all, G, E, rank, cnt, base_r, &lo, &chunk);
+    long long S[65];
+    ep_partition(counts_all, G, E, rank, capacity, cnt, base_r, S);
     int o = 0, m1 = 0, m2 = 0;
     for (int e = 0; e < E; e++) {
         off[e] = o; mt128[e] = m1; mt64[e] = m2;
@@ -83,7 +130,7 @@ __global__ void ep_plan_kernel(const int *__restrict__ counts_all, int G, int E,
         m2 += (cnt[e] + 63) / 64;
     }
     off[E] = o; mt128[E] = m1; mt64[E] = m2;
-    *chunk_out = (int)chunk;
+    for (int q = 0; q <= G; q++) slices[q] = (int)S[q];
 }
 
 // One warp per local (token, rank) entry: its local expert-sorted slot (for
@@ -93,7 +140,7 @@ __global__ void __launch_bounds__(256)
 ep_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad, int k, int E, int rank,
                  int G, int max_rows, const int *__restrict__ ids, const int *__restrict__ loc,
                  const int *__restrict__ tile_pref, const int *__restrict__ plan_local,
-                 const int *__restrict__ base_r, const int *__restrict__ chunk_p,
+                 const int *__restrict__ base_r, const int *__restrict__ slices,
                  float *const *__restrict__ recv_ptrs, int2 *const *__restrict__ ret_ptrs,
                  int *__restrict__ pos_of, int round_to_tf32, DeviceStatus *status)
 {
@@ -105,8 +152,12 @@ ep_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad, int k, in
         const int lr = tile_pref[(size_t)(t / kRouterTile) * E + e] + loc[warp];
         const int pos_local = plan_local[E + e] + lr;
         const int gp = base_r[e] + lr;
-        const int chunk = *chunk_p;
-        const int q = gp / chunk, p = gp - q * chunk;
+        int lo = 0, hi = G - 1;                 // slice q with slices[q] <= gp < slices[q+1]
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (slices[mid] <= gp) lo = mid; else hi = mid - 1;
+        }
+        const int q = lo, p = gp - slices[q];
         if (e < 0 || e >= E || q < 0 || q >= G || p < 0 || p >= max_rows || pos_local < 0 ||
             pos_local >= T * k) {
             if (lane == 0) atomicExch(&status->bad_index, 1);
@@ -143,24 +194,24 @@ ep_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad, int k, in
 // state
 // ---------------------------------------------------------------------
 struct moe_b200_ep {
-    int rank = 0, world = 1, device = 0, max_T = 0, max_rows = 0;
+    int rank = 0, world = 1, device = 0, max_T = 0, max_rows = 0, recv_rows = 0;
     const moe_b200_weights *w = nullptr;
     ncclComm_t comm = nullptr;
     cudaStream_t stream = nullptr;      // library stream for the host-buffer entry
     DeviceStatus *status = nullptr;
     // IPC-shared buffers (this rank's) and the peer tables
-    float *recv_x = nullptr;            // [max_rows × d_pad]
-    int2 *ret = nullptr;                // [max_rows]
+    float *recv_x = nullptr;            // [recv_rows × d_pad]
+    int2 *ret = nullptr;                // [recv_rows]
     float *y = nullptr;                 // [max_rows × d_pad] written by slice owners
     float **d_recv_ptrs = nullptr, **d_y_ptrs = nullptr;
     int2 **d_ret_ptrs = nullptr;
     std::vector<void *> opened;         // peer mappings to close
     // local work buffers
-    float *h = nullptr;                 // [max_rows × F_pad]
+    float *h = nullptr;                 // [recv_rows × F_pad]
     float *probs = nullptr, *wts = nullptr;
     int *ids = nullptr, *loc = nullptr, *tile_cnt = nullptr, *tile_pref = nullptr;
     int *plan_local = nullptr, *plan_q = nullptr, *pos_of = nullptr;
-    int *counts_all = nullptr, *base_r = nullptr, *chunk = nullptr, *bar = nullptr;
+    int *counts_all = nullptr, *base_r = nullptr, *slices = nullptr, *bar = nullptr;
     float *io_x = nullptr, *io_out = nullptr, *io_bias = nullptr;
     TcGemm up{}, dn{};
 };
@@ -221,7 +272,7 @@ void ep_release(moe_b200_ep *ep) {
     void *bufs[] = {ep->recv_x, ep->ret, ep->y, ep->d_recv_ptrs, ep->d_y_ptrs, ep->d_ret_ptrs,
                     ep->h, ep->probs, ep->wts, ep->ids, ep->loc, ep->tile_cnt, ep->tile_pref,
                     ep->plan_local, ep->plan_q, ep->pos_of, ep->counts_all, ep->base_r,
-                    ep->chunk, ep->bar, ep->io_x, ep->io_out, ep->io_bias, ep->status};
+                    ep->slices, ep->bar, ep->io_x, ep->io_out, ep->io_bias, ep->status};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (ep->stream) cudaStreamDestroy(ep->stream);
@@ -244,11 +295,14 @@ extern "C" int moe_b200_ep_unique_id(void *id_out) {
 }
 
 extern "C" int moe_b200_ep_partition(const int *counts_all, int world, int E, int rank,
-                                     int *cnt_rank, int *base_rank, long long *slice_start,
-                                     long long *slice_rows) {
-    if (!counts_all || world < 1 || E < 1 || rank < 0 || rank >= world)
+                                     long long capacity, int *cnt_rank, int *base_rank,
+                                     long long *slice_start, long long *slice_rows) {
+    if (!counts_all || world < 1 || world > 64 || E < 1 || rank < 0 || rank >= world)
         return ep_fail(MOE_B200_E_INVALID, "bad partition arguments%s%s");
-    ep_partition(counts_all, world, E, rank, cnt_rank, base_rank, slice_start, slice_rows);
+    long long S[65];
+    ep_partition(counts_all, world, E, rank, capacity, cnt_rank, base_rank, S);
+    if (slice_start) *slice_start = S[rank];
+    if (slice_rows) *slice_rows = S[rank + 1] - S[rank];
     return MOE_B200_OK;
 }
 
@@ -269,6 +323,9 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     ep->w = w;
     ep->max_T = max_tokens_per_rank;
     ep->max_rows = max_tokens_per_rank * w->k;
+    // cost-balanced slices may hold more rows than T·k: 25% headroom, beyond
+    // which the partition falls back to equal rows
+    ep->recv_rows = ep->max_rows + ep->max_rows / 4 + 256;
     int rc = MOE_B200_OK;
 #define TRY(x)                      \
     do {                            \
@@ -283,12 +340,12 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
             return ep_fail(MOE_B200_E_NOMEM, "expert-parallel buffers: %s%s", cudaGetErrorString(e));
         return MOE_B200_OK;
     };
-    const size_t R = ep->max_rows, T = ep->max_T, E = w->E, G = world;
+    const size_t R = ep->max_rows, RR = ep->recv_rows, T = ep->max_T, E = w->E, G = world;
     const size_t tiles = ceil_div<size_t>(T, kRouterTile);
-    TRY(alloc((void **)&ep->recv_x, R * w->d_pad * 4));
-    TRY(alloc((void **)&ep->ret, R * sizeof(int2)));
+    TRY(alloc((void **)&ep->recv_x, RR * w->d_pad * 4));
+    TRY(alloc((void **)&ep->ret, RR * sizeof(int2)));
     TRY(alloc((void **)&ep->y, R * w->d_pad * 4));
-    TRY(alloc((void **)&ep->h, R * w->F_pad * 4));
+    TRY(alloc((void **)&ep->h, RR * w->F_pad * 4));
     TRY(alloc((void **)&ep->probs, T * E * 4));
     TRY(alloc((void **)&ep->wts, R * 4));
     TRY(alloc((void **)&ep->ids, R * 4));
@@ -300,7 +357,7 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     TRY(alloc((void **)&ep->plan_q, plan_ints(E) * 4));
     TRY(alloc((void **)&ep->counts_all, G * E * 4));
     TRY(alloc((void **)&ep->base_r, E * 4));
-    TRY(alloc((void **)&ep->chunk, 4));
+    TRY(alloc((void **)&ep->slices, (G + 1) * 4));
     TRY(alloc((void **)&ep->bar, 4));
     TRY(alloc((void **)&ep->io_x, T * w->d * 4));
     TRY(alloc((void **)&ep->io_out, T * w->d * 4));
@@ -313,9 +370,9 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
         cudaMemset(ep->bar, 0, 4) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ep->stream, cudaStreamNonBlocking) != cudaSuccess)
         TRY(ep_fail(MOE_B200_E_CUDA, "expert-parallel set-up failed%s%s"));
-    TRY(ep_tmap(&ep->up.tmA, ep->recv_x, R, w->d_pad, 128));
+    TRY(ep_tmap(&ep->up.tmA, ep->recv_x, RR, w->d_pad, 128));
     ep->up.tmB = w->tm_ug;
-    TRY(ep_tmap(&ep->dn.tmA, ep->h, R, w->F_pad, 128));
+    TRY(ep_tmap(&ep->dn.tmA, ep->h, RR, w->F_pad, 128));
     ep->dn.tmB = w->tm_dn;
 
     // communicator
@@ -335,8 +392,18 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     y_ptrs[rank] = ep->y;
     ret_ptrs[rank] = ep->ret;
     if (world > 1) {
-        constexpr size_t HB = 3 * sizeof(cudaIpcMemHandle_t);
-        cudaIpcMemHandle_t mine[3];
+        // three IPC handles and this rank's max_tokens_per_rank (every rank
+        // must use the same capacity, or their partitions would differ)
+        constexpr size_t HB = 3 * sizeof(cudaIpcMemHandle_t) + 64;
+        struct {
+            cudaIpcMemHandle_t h[3];
+            long long max_t;
+            char pad[56];
+        } mine_blob;
+        static_assert(sizeof(mine_blob) == HB, "handle blob layout");
+        std::memset(&mine_blob, 0, sizeof mine_blob);
+        mine_blob.max_t = max_tokens_per_rank;
+        cudaIpcMemHandle_t *mine = mine_blob.h;
         if (cudaIpcGetMemHandle(&mine[0], ep->recv_x) != cudaSuccess ||
             cudaIpcGetMemHandle(&mine[1], ep->ret) != cudaSuccess ||
             cudaIpcGetMemHandle(&mine[2], ep->y) != cudaSuccess)
@@ -345,7 +412,7 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
         TRY(alloc((void **)&dh, HB * G));
         std::vector<unsigned char> all(HB * G);
         int step = MOE_B200_OK;
-        if (cudaMemcpy(dh + HB * rank, mine, HB, cudaMemcpyHostToDevice) != cudaSuccess)
+        if (cudaMemcpy(dh + HB * rank, &mine_blob, HB, cudaMemcpyHostToDevice) != cudaSuccess)
             step = ep_fail(MOE_B200_E_CUDA, "handle upload failed%s%s");
         if (!step) {
             ncclResult_t r = ncclAllGather(dh + HB * rank, dh, HB, ncclChar, ep->comm, ep->stream);
@@ -358,9 +425,16 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
         cudaFree(dh);
         TRY(step);
         for (int q = 0; q < world; q++) {
+            long long their_t = 0;
+            std::memcpy(&their_t, all.data() + HB * q + 3 * sizeof(cudaIpcMemHandle_t), 8);
+            if (their_t != max_tokens_per_rank)
+                TRY(ep_fail(MOE_B200_E_INVALID,
+                            "max_tokens_per_rank differs between ranks%s%s"));
+        }
+        for (int q = 0; q < world; q++) {
             if (q == rank) continue;
             cudaIpcMemHandle_t hq[3];
-            std::memcpy(hq, all.data() + HB * q, HB);
+            std::memcpy(hq, all.data() + HB * q, 3 * sizeof(cudaIpcMemHandle_t));
             void *p[3] = {nullptr, nullptr, nullptr};
             for (int i = 0; i < 3; i++) {
                 cudaError_t e = cudaIpcOpenMemHandle(&p[i], hq[i], cudaIpcMemLazyEnablePeerAccess);
@@ -421,19 +495,19 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
     }
     MARK(1);
     EP_NC(ncclAllGather(ep->plan_local, ep->counts_all, E, ncclInt32, ep->comm, s));
-    ep_plan_kernel<<<1, 32, 0, s>>>(ep->counts_all, G, E, ep->rank, ep->plan_q, ep->base_r,
-                                    ep->chunk);
+    ep_plan_kernel<<<1, 32, 0, s>>>(ep->counts_all, G, E, ep->rank, ep->recv_rows, ep->plan_q,
+                                    ep->base_r, ep->slices);
     EP_CK(cudaGetLastError());
     if (T > 0) {
         ep_gather_kernel<<<ceil_div(T * k, 8), 256, 0, s>>>(
-            d_x, T, w->d, w->d_pad, k, E, ep->rank, G, ep->max_rows, ids, ep->loc,
-            ep->tile_pref, ep->plan_local, ep->base_r, ep->chunk, ep->d_recv_ptrs,
+            d_x, T, w->d, w->d_pad, k, E, ep->rank, G, ep->recv_rows, ids, ep->loc,
+            ep->tile_pref, ep->plan_local, ep->base_r, ep->slices, ep->d_recv_ptrs,
             ep->d_ret_ptrs, ep->pos_of, path == MOE_B200_PATH_TF32, ep->status);
         EP_CK(cudaGetLastError());
     }
     EP_NC(ncclAllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s));
     MARK(2);
-    const int rows = ep->max_rows;
+    const int rows = ep->recv_rows;
     if (path == MOE_B200_PATH_TF32) {
         const int sms = device_sms(ep->device);
         EP_CK(launch_tc_upgate(ep->up, w->d_pad, w->F_pad, ep->h, ep->plan_q, E, rows, sms,
@@ -448,8 +522,8 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
         EP_CK(launch_ffma_down(ep->h, w->F_pad, w->dn, w->d_pad, ep->y, ep->plan_q, E, rows, s,
                                ep->d_y_ptrs, ep->ret));
     }
+    MARK(4);   // the wait for the other ranks counts under the combine stage
     EP_NC(ncclAllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s));
-    MARK(4);
     if (T > 0) EP_CK(launch_combine(ep->y, w->d, w->d_pad, T, k, ep->pos_of, ep->wts, d_out, s));
     MARK(5);
 #undef MARK

@@ -33,6 +33,7 @@ constexpr int STAGES = 4;
 constexpr int GM = 8;           // m-tiles per raster group
 constexpr int kThreads = 192;
 constexpr int A_BYTES = BM * BK * 4;
+constexpr int EPI_FLOATS = 32 * 33;   // per epilogue warp: 32×32 chunk, padded rows
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -183,7 +184,8 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                                 ~static_cast<uintptr_t>(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sB + STAGES * B_BYTES);
+    float *sEpi = reinterpret_cast<float *>(sB + STAGES * B_BYTES);   // [4 warps][32][33]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + 4 * EPI_FLOATS);
     uint64_t *full = bars;
     uint64_t *empty = bars + STAGES;
     uint64_t *tfull = bars + 2 * STAGES;
@@ -295,7 +297,6 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const int q = warp & 3;                 // TMEM lane quarter of this warp
-        const int row_in_tile = q * 32 + lane;
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -306,50 +307,59 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             }
             tc_fence_after();
             const int nvalid = __ldg(cnt + c.e) - c.ml * BM;
-            const bool valid = row_in_tile < nvalid;
-            const size_t grow = (size_t)(__ldg(off + c.e) + c.ml * BM + row_in_tile);
+            const int row0 = __ldg(off + c.e) + c.ml * BM + q * 32;   // this warp's first row
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-            if (SWIGLU) {
-                float *dst = out + grow * ldo + (size_t)c.ni * (BN / 2);
-#pragma unroll 1
-                for (int col = 0; col < BN / 2; col += 32) {
-                    float g[32], u[32];
-                    tmem_ld32(taddr + col, g);
-                    tmem_ld32(taddr + BN / 2 + col, u);
-                    if (valid) {
+            constexpr int NCOLS = SWIGLU ? BN / 2 : BN;
+            const size_t ncol0 = (size_t)c.ni * NCOLS;
+            // Stores go out row-contiguous: each 32×32 chunk is transposed
+            // through shared memory so that 8 lanes write one row's 128
+            // bytes and a warp instruction covers 4 whole row segments
+            // (full sectors locally, full-size packets over NVLink).
+            float *stage = sEpi + q * EPI_FLOATS;
+            const int sub = lane >> 3, c4 = (lane & 7) * 4;
+            float *rowdst[8];
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 h;
-                            // h feeds the TF32 down GEMM: store it rounded
-                            h.x = round_tf32(swiglu_ref(g[j + 0], u[j + 0]));
-                            h.y = round_tf32(swiglu_ref(g[j + 1], u[j + 1]));
-                            h.z = round_tf32(swiglu_ref(g[j + 2], u[j + 2]));
-                            h.w = round_tf32(swiglu_ref(g[j + 3], u[j + 3]));
-                            *reinterpret_cast<float4 *>(dst + col + j) = h;
-                        }
+            for (int pass = 0; pass < 8; pass++) {
+                const int r = pass * 4 + sub;
+                rowdst[pass] = nullptr;
+                if (q * 32 + r < nvalid) {
+                    const size_t grow = (size_t)(row0 + r);
+                    if (!SWIGLU && ret != nullptr) {
+                        // expert-parallel: the row goes back to the rank that
+                        // owns its token (peer memory over NVLink)
+                        const int2 rr = ret[grow];
+                        rowdst[pass] = out_ptrs[rr.x] + (size_t)rr.y * ldo + ncol0;
+                    } else {
+                        rowdst[pass] = out + grow * ldo + ncol0;
                     }
                 }
-            } else {
-                // expert-parallel: a row of this rank's slice goes back to the
-                // rank that owns its token (peer memory over NVLink)
-                float *dst;
-                if (ret != nullptr && valid) {
-                    const int2 rr = ret[grow];
-                    dst = out_ptrs[rr.x] + (size_t)rr.y * ldo + (size_t)c.ni * BN;
-                } else {
-                    dst = out + grow * ldo + (size_t)c.ni * BN;
-                }
+            }
 #pragma unroll 1
-                for (int col = 0; col < BN; col += 32) {
-                    float v[32];
+            for (int col = 0; col < NCOLS; col += 32) {
+                float v[32];
+                if (SWIGLU) {
+                    float u[32];
                     tmem_ld32(taddr + col, v);
-                    if (valid) {
+                    tmem_ld32(taddr + BN / 2 + col, u);
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4 *>(dst + col + j) =
-                                make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    for (int j = 0; j < 32; j++)   // h feeds the TF32 down GEMM: rounded
+                        v[j] = round_tf32(swiglu_ref(v[j], u[j]));
+                } else {
+                    tmem_ld32(taddr + col, v);
+                }
+#pragma unroll
+                for (int j = 0; j < 32; j++) stage[lane * 33 + j] = v[j];
+                __syncwarp();
+#pragma unroll
+                for (int pass = 0; pass < 8; pass++) {
+                    const int r = pass * 4 + sub;
+                    if (rowdst[pass] != nullptr) {
+                        const float *sr = stage + r * 33 + c4;
+                        *reinterpret_cast<float4 *>(rowdst[pass] + col + c4) =
+                            make_float4(sr[0], sr[1], sr[2], sr[3]);
                     }
                 }
+                __syncwarp();
             }
             tc_fence_before();
             mbar_arrive(&tempty[acc]);
@@ -374,7 +384,8 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 
 template <int BN>
 constexpr int smem_bytes() {
-    return STAGES * (A_BYTES + BN * BK * 4) + 1024 /*align slack*/ + 256 /*barriers*/;
+    return STAGES * (A_BYTES + BN * BK * 4) + 4 * EPI_FLOATS * 4 + 1024 /*align slack*/ +
+           256 /*barriers*/;
 }
 
 }  // namespace tc

@@ -347,20 +347,20 @@ def ep_unique_id() -> bytes:
     return buf.raw
 
 
-def ep_partition(counts_all: np.ndarray, rank: int):
+def ep_partition(counts_all: np.ndarray, rank: int, capacity: int = 0):
     """The slice plan of `rank` from the per-rank expert counts [world × E]:
     (rows per expert in the slice, global base of rank's rows per expert,
-    slice start, slice size)."""
+    slice start, slice size); `capacity` caps the rows of any slice."""
     c = np.ascontiguousarray(counts_all, np.int32)
     G, E = c.shape
     cnt = np.empty(E, np.int32)
     base = np.empty(E, np.int32)
     lo, rows = C.c_longlong(), C.c_longlong()
     L = lib()
-    L.moe_b200_ep_partition.argtypes = [_ip, C.c_int, C.c_int, C.c_int, _ip, _ip,
+    L.moe_b200_ep_partition.argtypes = [_ip, C.c_int, C.c_int, C.c_int, C.c_longlong, _ip, _ip,
                                         C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]
-    _check(L.moe_b200_ep_partition(_i(c), G, E, rank, _i(cnt), _i(base), C.byref(lo),
-                                   C.byref(rows)), "moe_b200_ep_partition")
+    _check(L.moe_b200_ep_partition(_i(c), G, E, rank, capacity, _i(cnt), _i(base),
+                                   C.byref(lo), C.byref(rows)), "moe_b200_ep_partition")
     return cnt, base, int(lo.value), int(rows.value)
 
 

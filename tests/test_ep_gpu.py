@@ -97,7 +97,9 @@ def test_ep_matches_single_gpu():
         for r in res:
             if "counts_total" in r:
                 assert r["counts_total"] == r["want_total"]
-                assert r["slice_rows"] <= r["want_total"] // world + 1
+                # cost-balanced slices: within the receive capacity (T·k/world + 25% + 256)
+                per = r["want_total"] // world
+                assert r["slice_rows"] <= per + per // 4 + 256
             else:
                 assert r["ids_equal"] and r["probs_equal"], r
                 assert r["out_equal"] or r["rel_err"] < 1e-6, r

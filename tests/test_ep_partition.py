@@ -11,21 +11,22 @@ import pytest
 import moe_b200 as M
 
 
-def simulate(counts):
+def simulate(counts, capacity=0):
     """Map every (source rank, expert, local rank-in-expert) row to its
     (slice, slot) the way the gather kernel does, and check the result."""
     G, E = counts.shape
-    plans = [M.ep_partition(counts, q) for q in range(G)]
-    chunk = plans[0][3]
+    plans = [M.ep_partition(counts, q, capacity) for q in range(G)]
+    starts = [p[2] for p in plans] + [plans[-1][2] + plans[-1][3]]
     M_rows = int(counts.sum())
-    assert all(p[3] == chunk for p in plans)
+    assert starts[0] == 0 and starts[-1] == M_rows and starts == sorted(starts)
     seen = {}
     for r in range(G):
         _, base_r, _, _ = plans[r]
         for e in range(E):
             for lr in range(counts[r, e]):
                 gp = int(base_r[e]) + lr
-                q, p = divmod(gp, chunk)
+                q = int(np.searchsorted(starts, gp, side="right")) - 1
+                p = gp - starts[q]
                 assert 0 <= q < G
                 cnt_q = plans[q][0]
                 off_q = np.concatenate([[0], np.cumsum(cnt_q)])
@@ -33,13 +34,18 @@ def simulate(counts):
                 assert (q, p) not in seen
                 seen[(q, p)] = (r, e, lr)
     sizes = [int(p[0].sum()) for p in plans]
+    assert sizes == [p[3] for p in plans]
     assert sum(sizes) == M_rows == len(seen)
-    assert max(sizes) <= chunk and max(sizes) - min(sizes) <= chunk
-    # every slice but the last is full: work is balanced to within one slice
-    assert all(s == chunk for s in sizes[:-1]) or M_rows < G
+    if capacity:
+        assert max(sizes) <= capacity
     for e in range(E):
         assert sum(int(p[0][e]) for p in plans) == counts[:, e].sum()
-    return sizes
+    return plans, sizes
+
+
+def cost(plan):
+    """Cost units of a slice: 2 per 128-row tile of each expert, 1 per expert."""
+    return sum(2 * ((int(n) + 127) // 128) + 1 for n in plan[0] if n > 0)
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
@@ -52,12 +58,34 @@ def test_partition_random(world):
 
 
 def test_partition_skewed_zipf():
-    # one expert holds most of the rows: it is split across slices
-    G, E = 8, 16
+    # Zipf(1.1) popularity: a few experts hold most rows, dozens hold a
+    # handful; the cost-balanced slices stay within a few percent of each
+    # other in cost, where equal-row slices would not
+    G, E = 8, 64
     p = np.arange(1, E + 1, dtype=np.float64) ** -1.1
-    counts = np.stack([np.random.default_rng(r).multinomial(400, p / p.sum()) for r in range(G)])
-    sizes = simulate(counts.astype(np.int32))
-    assert max(sizes) - min(sizes) <= 1 or len(set(sizes[:-1])) == 1
+    counts = np.stack([np.random.default_rng(r).multinomial(16384, p / p.sum())
+                       for r in range(G)]).astype(np.int32)
+    plans, sizes = simulate(counts)
+    costs = [cost(pl) for pl in plans]
+    assert max(costs) / np.mean(costs) < 1.03
+    # a slice boundary inside an expert falls on a 128-row tile boundary
+    # of that expert, except at the expert's end
+    tot = counts.sum(0)
+    goff = np.concatenate([[0], np.cumsum(tot)])
+    for pl in plans[1:]:
+        s = pl[2]
+        e = int(np.searchsorted(goff, s, side="right")) - 1
+        if e < E and goff[e] < s < goff[e + 1]:
+            assert (s - goff[e]) % 128 == 0
+
+
+def test_partition_capacity_fallback():
+    G, E = 4, 8
+    counts = np.zeros((G, E), np.int32)
+    counts[:, 0] = 1000                   # one huge expert, tiny others
+    counts[:, 1:] = 3
+    plans, sizes = simulate(counts, capacity=(counts.sum() + G - 1) // G)
+    assert max(sizes) - min(sizes) <= 1   # equal rows when cost slices would not fit
 
 
 def test_partition_empty():
