@@ -59,6 +59,12 @@ MOE_DEV float round_tf32(float v) {
     return __uint_as_float(r);
 }
 
+// v minus its TF32 truncation (the low 13 mantissa bits, as an fp32 value;
+// exact): what a tcgen05 kind::tf32 MMA drops when it reads v.
+MOE_DEV float tf32_residual(float v) {
+    return __fsub_rn(v, __uint_as_float(__float_as_uint(v) & 0xFFFFE000u));
+}
+
 // ---------------------------------------------------------------------
 // Seeded synthetic generator (bit-identical to the oracle's host copy).
 // ---------------------------------------------------------------------

@@ -48,6 +48,22 @@ cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float 
                            float *const *y_ptrs = nullptr, const int2 *ret = nullptr);
 cudaError_t tc_set_attributes();
 
+// 3xTF32 weight-streaming GEMMs for decode-sized expert groups
+struct DecMaps {
+    CUtensorMap tmW;    // weights, box {32, 64} (up/gate) or {32, 128} (down)
+    CUtensorMap tmXb;   // token operand big part  [rows × K], box {32, 64}
+    CUtensorMap tmXs;   // token operand small part [rows × K], box {32, 64}
+};
+cudaError_t dec_set_attributes();
+cudaError_t launch_split_tf32(float *big, float *small, size_t n, cudaStream_t s);
+cudaError_t launch_dec_upgate(const DecMaps &m, int d_pad, int F_pad, float *h_big, float *h_small,
+                              const int *plan, int E, int rows_bound, int num_sms,
+                              DeviceStatus *status, cudaStream_t s);
+cudaError_t launch_dec_down(const DecMaps &m, int F_pad, int d_pad, float *y, const int *plan,
+                            int E, int rows_bound, int num_sms, DeviceStatus *status,
+                            cudaStream_t s, float *const *y_ptrs = nullptr,
+                            const int2 *ret = nullptr);
+
 // weight repack: src row-major [R × C] (one expert matrix) -> dst rows of
 // the K-major layout, see moe_b200.cu.
 cudaError_t launch_repack_upgate(const float *wg, const float *wu, int d, int F, int d_pad,

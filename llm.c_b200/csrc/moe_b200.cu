@@ -109,6 +109,7 @@ struct Ctx {
     bool attrs_set = false;
     // workspace
     Buf probs, ids, wts, loc, tile_cnt, tile_pref, plan, pos_of, x_perm, h, y;
+    Buf xs, hs;                          // small parts of the 3xTF32 split
     Buf io_x, io_out, io_bias;
     int last_E = 0;
     int last_launches = 0;
@@ -155,6 +156,7 @@ static int get_ctx(int device, Ctx **out) {
         CK(cudaMalloc(&c->status, sizeof(DeviceStatus)));
         CK(cudaMemset(c->status, 0, sizeof(DeviceStatus)));
         CK(tc_set_attributes());
+        CK(dec_set_attributes());
         c->attrs_set = true;
         g_ctx[device] = c;
     }
@@ -203,8 +205,8 @@ extern "C" void moe_b200_shutdown(void) {
         cudaSetDevice(i);
         cudaStreamSynchronize(c->stream);
         Buf *bufs[] = {&c->probs, &c->ids, &c->wts, &c->loc, &c->tile_cnt, &c->tile_pref,
-                       &c->plan, &c->pos_of, &c->x_perm, &c->h, &c->y, &c->io_x, &c->io_out,
-                       &c->io_bias};
+                       &c->plan, &c->pos_of, &c->x_perm, &c->h, &c->y, &c->xs, &c->hs,
+                       &c->io_x, &c->io_out, &c->io_bias};
         for (Buf *b : bufs) free_buf(*b);
         cudaFree(c->status);
         cudaStreamDestroy(c->stream);
@@ -247,6 +249,8 @@ static int weights_alloc(Ctx *c, int d, int F, int E, int k, moe_b200_weights **
     }
     int rc = make_tmap(&w->tm_ug, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 256);
     if (rc == 0) rc = make_tmap(&w->tm_dn, w->dn, (int64_t)E * w->d_pad, w->F_pad, w->down_bn);
+    if (rc == 0) rc = make_tmap(&w->tm_ug64, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 64);
+    if (rc == 0) rc = make_tmap(&w->tm_dn128, w->dn, (int64_t)E * w->d_pad, w->F_pad, 128);
     if (rc) {
         cudaFree(w->router); cudaFree(w->ug); cudaFree(w->dn);
         delete w;
@@ -396,7 +400,7 @@ static int pick_path(const moe_b200_weights *w, int T, const moe_b200_opts *opts
         // group fills half a tile; smaller (decode-sized) groups stream the
         // weights through FP32 FFMA.
         const double avg = (double)T * w->k / w->E;
-        path = avg >= 64.0 ? MOE_B200_PATH_TF32 : MOE_B200_PATH_FP32;
+        path = avg >= 64.0 ? MOE_B200_PATH_TF32 : MOE_B200_PATH_TF32X3;
     }
     return path;
 }
@@ -481,6 +485,23 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
         MARK(3);
         CK(launch_tc_down(dn, w->F_pad, w->d_pad, w->down_bn, y, plan, E, rows, c->num_sms,
                           c->status, s));
+    } else if (path == MOE_B200_PATH_TF32X3) {
+        if ((rc = grow(c->xs, (size_t)rows * w->d_pad * 4))) return rc;
+        if ((rc = grow(c->hs, (size_t)rows * w->F_pad * 4))) return rc;
+        float *xs = (float *)c->xs.p, *hs = (float *)c->hs.p;
+        DecMaps up, dn;
+        up.tmW = w->tm_ug64;
+        if ((rc = make_tmap(&up.tmXb, x_perm, rows, w->d_pad, 64))) return rc;
+        if ((rc = make_tmap(&up.tmXs, xs, rows, w->d_pad, 64))) return rc;
+        dn.tmW = w->tm_dn128;
+        if ((rc = make_tmap(&dn.tmXb, h, rows, w->F_pad, 64))) return rc;
+        if ((rc = make_tmap(&dn.tmXs, hs, rows, w->F_pad, 64))) return rc;
+        CK(launch_split_tf32(x_perm, xs, (size_t)rows * w->d_pad, s));
+        CK(launch_dec_upgate(up, w->d_pad, w->F_pad, h, hs, plan, E, rows, c->num_sms, c->status,
+                             s));
+        MARK(3);
+        CK(launch_dec_down(dn, w->F_pad, w->d_pad, y, plan, E, rows, c->num_sms, c->status, s));
+        launches += 1;   // the split
     } else if (path == MOE_B200_PATH_FP32) {
         CK(launch_ffma_upgate(x_perm, w->d_pad, w->ug, w->F_pad, h, plan, E, rows, s));
         MARK(3);

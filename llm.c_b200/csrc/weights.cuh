@@ -12,6 +12,8 @@ struct moe_b200_weights {
     float *dn;       // [E][d_pad × F_pad]
     CUtensorMap tm_ug;        // box {32, 256}
     CUtensorMap tm_dn;        // box {32, 256 or 128}
+    CUtensorMap tm_ug64;      // box {32, 64}: decode up/gate (64 gate + 64 up rows)
+    CUtensorMap tm_dn128;     // box {32, 128}: decode down
     int down_bn;
 };
 

@@ -22,7 +22,7 @@ LIB_PATH = HERE / "libmoe_b200.so"
 
 OK = 0
 E_INVALID, E_CUDA, E_NOMEM, E_NCCL, E_TIMEOUT, E_NODEV, E_STATE = -1, -2, -3, -4, -5, -6, -7
-PATH_AUTO, PATH_TF32, PATH_FP32 = 0, 1, 2
+PATH_AUTO, PATH_TF32, PATH_FP32, PATH_TF32X3 = 0, 1, 2, 3
 STREAM_X, STREAM_ROUTER, STREAM_BIAS = 1, 2, 3
 
 

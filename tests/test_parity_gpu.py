@@ -2,8 +2,9 @@
 reference's own outputs (golden fixtures) and the CPU oracle.
 
 Tolerances (max|Δ| / max|ref| over the layer output):
-  FP32 FFMA path   1e-5
-  TF32 tcgen05     2e-3
+  FP32 FFMA path           1e-5
+  TF32 tcgen05             2e-3
+  3xTF32 tcgen05 decode    1e-5
 Routing: expert ids identical to the reference except where the swapped
 experts' logits lie within 1e-6 (near-ties); per-expert counts follow.
 """
@@ -16,7 +17,9 @@ from golden import make_golden as G
 
 pytestmark = pytest.mark.gpu
 
-TOL = {M.PATH_FP32: 1e-5, M.PATH_TF32: 2e-3}
+TOL = {M.PATH_FP32: 1e-5, M.PATH_TF32: 2e-3, M.PATH_TF32X3: 1e-5}
+PATHS = [M.PATH_FP32, M.PATH_TF32, M.PATH_TF32X3]
+PATH_IDS = ["fp32", "tf32", "tf32x3"]
 GOLDEN = sorted(G.HERE.glob("*.npz"))
 
 
@@ -52,7 +55,7 @@ def expected_rows(p, rows, gpu_ids, want_out, mism):
     return want
 
 
-@pytest.mark.parametrize("path", [M.PATH_FP32, M.PATH_TF32], ids=["fp32", "tf32"])
+@pytest.mark.parametrize("path", PATHS, ids=PATH_IDS)
 @pytest.mark.parametrize("case", GOLDEN, ids=lambda p: p.stem)
 def test_golden_parity(moe, case, path):
     p, z = load_case(case)
@@ -87,7 +90,7 @@ def test_drop_in_moe_forward_symbol(moe):
     llmc.invalidate()
 
 
-@pytest.mark.parametrize("path", [M.PATH_FP32, M.PATH_TF32], ids=["fp32", "tf32"])
+@pytest.mark.parametrize("path", PATHS, ids=PATH_IDS)
 def test_router_bias_vs_oracle(moe, path):
     """c3-shaped layer at reduced T with the per-expert N(0,1) bias."""
     p = O.MoEProblem(2048, 1024, 16, 2, 4096, seed=1, bias="normal")
