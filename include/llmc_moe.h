@@ -11,7 +11,7 @@
  *   llmc_FFNWeights    == FFNWeights    include/transformer.h:35-39
  *   llmc_MoEWeights    == MoEWeights    include/transformer.h:53-58
  *   llmc_ModelConfig   == ModelConfig   include/config.h:23-48
- *   llmc_ForwardCache  == ForwardCache  include/transformer.h:107-124
+ *   llmc_ForwardCache  == ForwardCache  include/transformer.h:108-124
  */
 #ifndef LLMC_MOE_H
 #define LLMC_MOE_H
@@ -69,6 +69,81 @@ typedef struct {
     float *router_probs;
     int *expert_ids;
 } llmc_ForwardCache;
+
+/* Decode-side types (for the drop-in inference_step below):
+ *   llmc_AttentionWeights == AttentionWeights  include/attention.h:40-45
+ *   llmc_RoPEBuffer       == RoPEBuffer        include/attention.h:75-80
+ *   llmc_BlockWeights     == BlockWeights      include/transformer.h:64-80
+ *   llmc_ModelWeights     == ModelWeights      include/transformer.h:86-98
+ *   llmc_Model            == Model             include/transformer.h:130-136
+ *   llmc_LayerKVCache     == LayerKVCache      include/inference.h:45-48
+ *   llmc_InferenceState   == InferenceState    include/inference.h:53-76 */
+typedef struct {
+    llmc_Matrix W_Q, W_K, W_V, W_O;
+} llmc_AttentionWeights;
+
+typedef struct {
+    float *cos_table;
+    float *sin_table;
+    int max_seq_len;
+    int head_dim;
+} llmc_RoPEBuffer;
+
+typedef struct {
+    float *rms_attn;
+    llmc_AttentionWeights attn;
+    float *rms_ffn;
+    int use_moe;
+    union {
+        llmc_FFNWeights ffn;
+        llmc_MoEWeights moe;
+    };
+} llmc_BlockWeights;
+
+typedef struct {
+    llmc_Matrix embed;
+    llmc_BlockWeights *blocks;
+    int n_layers;
+    float *rms_final;
+    llmc_Matrix lm_head;
+} llmc_ModelWeights;
+
+typedef struct {
+    llmc_ModelConfig cfg;
+    llmc_ModelWeights weights;
+    llmc_ForwardCache *caches;
+    llmc_RoPEBuffer rope;
+    void *train_scratch;
+} llmc_Model;
+
+typedef struct {
+    float *K;
+    float *V;
+} llmc_LayerKVCache;
+
+typedef struct {
+    llmc_LayerKVCache *kv_cache;
+    int n_layers;
+    int seq_pos;
+    int n_kv_heads;
+    int head_dim;
+    int kv_dim;
+    int max_seq_len;
+    float *x, *x_norm, *q, *k, *v, *attn_buf, *head_out, *logits;
+} llmc_InferenceState;
+
+/*
+ * inference_step — replaces llm.c's inference_step (src/inference.c:231-358,
+ * declared at include/inference.h:137) with the same signature and the same
+ * single-token KV-cache forward, and fills in the MoE branch that llm.c
+ * leaves as a TODO (src/inference.c:342-343): for a MoE block the pre-FFN
+ * normalised vector goes through the B200 MoE forward (T = 1) and is added
+ * to the residual, exactly as the dense branch adds its FFN output.  The
+ * non-MoE arithmetic (RMSNorm, Q/K/V/O projections, RoPE, KV-cache append,
+ * GQA attention over all cached positions, LM head) is a CPU restatement of
+ * the reference's.  Aborts on a device failure, like moe_forward.
+ */
+void inference_step(const llmc_Model *m, llmc_InferenceState *s, int token);
 
 /*
  * moe_forward — replaces llm.c's moe_forward (src/transformer.c:287-366,

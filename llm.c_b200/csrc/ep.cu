@@ -28,7 +28,7 @@
 #include "kernels.cuh"
 #include "weights.cuh"
 
-#include <nccl.h>
+#include "nccl_dyn.cuh"
 
 #include <cstdio>
 #include <cstring>
@@ -208,12 +208,16 @@ struct moe_b200_ep {
     std::vector<void *> opened;         // peer mappings to close
     // local work buffers
     float *h = nullptr;                 // [recv_rows × F_pad]
+    float *xs = nullptr, *hs = nullptr; // 3xTF32 small parts of recv_x and h
+    float *rpart = nullptr;             // split-K router partial logits (small T)
+    int rsplit = 1;
     float *probs = nullptr, *wts = nullptr;
     int *ids = nullptr, *loc = nullptr, *tile_cnt = nullptr, *tile_pref = nullptr;
     int *plan_local = nullptr, *plan_q = nullptr, *pos_of = nullptr;
     int *counts_all = nullptr, *base_r = nullptr, *slices = nullptr, *bar = nullptr;
     float *io_x = nullptr, *io_out = nullptr, *io_bias = nullptr;
     TcGemm up{}, dn{};
+    DecMaps dup{}, ddn{};
 };
 
 namespace {
@@ -236,7 +240,7 @@ int ep_fail(int code, const char *fmt, const char *a = "", const char *b = "") {
     do {                                                                                    \
         ncclResult_t _r = (call);                                                           \
         if (_r != ncclSuccess)                                                              \
-            return ep_fail(MOE_B200_E_NCCL, "%s: %s", #call, ncclGetErrorString(_r));       \
+            return ep_fail(MOE_B200_E_NCCL, "%s: %s", #call, nccl().GetErrorString(_r));       \
     } while (0)
 
 // encode a 2-D fp32 tensor map (same layout as the single-GPU path)
@@ -268,9 +272,9 @@ void ep_release(moe_b200_ep *ep) {
     cudaSetDevice(ep->device);
     cudaDeviceSynchronize();
     for (void *p : ep->opened) cudaIpcCloseMemHandle(p);
-    if (ep->comm) ncclCommDestroy(ep->comm);
+    if (ep->comm) nccl().CommDestroy(ep->comm);
     void *bufs[] = {ep->recv_x, ep->ret, ep->y, ep->d_recv_ptrs, ep->d_y_ptrs, ep->d_ret_ptrs,
-                    ep->h, ep->probs, ep->wts, ep->ids, ep->loc, ep->tile_cnt, ep->tile_pref,
+                    ep->h, ep->xs, ep->hs, ep->rpart, ep->probs, ep->wts, ep->ids, ep->loc, ep->tile_cnt, ep->tile_pref,
                     ep->plan_local, ep->plan_q, ep->pos_of, ep->counts_all, ep->base_r,
                     ep->slices, ep->bar, ep->io_x, ep->io_out, ep->io_bias, ep->status};
     for (void *b : bufs)
@@ -287,8 +291,9 @@ void ep_release(moe_b200_ep *ep) {
 extern "C" int moe_b200_ep_unique_id(void *id_out) {
     if (!id_out) return ep_fail(MOE_B200_E_INVALID, "null id buffer%s%s");
     static_assert(sizeof(ncclUniqueId) <= MOE_B200_EP_ID_BYTES, "NCCL id does not fit");
+    if (!nccl().ok) return ep_fail(MOE_B200_E_NCCL, "libnccl.so.2 not found%s%s");
     ncclUniqueId id;
-    EP_NC(ncclGetUniqueId(&id));
+    EP_NC(nccl().GetUniqueId(&id));
     std::memset(id_out, 0, MOE_B200_EP_ID_BYTES);
     std::memcpy(id_out, &id, sizeof id);
     return MOE_B200_OK;
@@ -314,6 +319,7 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
         return ep_fail(MOE_B200_E_INVALID, "bad arguments to moe_b200_ep_create%s%s");
     if ((int64_t)max_tokens_per_rank * w->k > (int64_t)1 << 30)
         return ep_fail(MOE_B200_E_INVALID, "max_tokens_per_rank too large%s%s");
+    if (!nccl().ok) return ep_fail(MOE_B200_E_NCCL, "libnccl.so.2 not found%s%s");
     EP_CK(cudaSetDevice(w->device));
     if (device_sms(w->device) == 0) return ep_fail(MOE_B200_E_NODEV, "device unusable%s%s");
     moe_b200_ep *ep = new moe_b200_ep();
@@ -346,6 +352,10 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     TRY(alloc((void **)&ep->ret, RR * sizeof(int2)));
     TRY(alloc((void **)&ep->y, R * w->d_pad * 4));
     TRY(alloc((void **)&ep->h, RR * w->F_pad * 4));
+    TRY(alloc((void **)&ep->xs, RR * w->d_pad * 4));
+    ep->rsplit = router_splits((int)T, w->d);
+    if (ep->rsplit > 1) TRY(alloc((void **)&ep->rpart, (size_t)ep->rsplit * T * E * 4));
+    TRY(alloc((void **)&ep->hs, RR * w->F_pad * 4));
     TRY(alloc((void **)&ep->probs, T * E * 4));
     TRY(alloc((void **)&ep->wts, R * 4));
     TRY(alloc((void **)&ep->ids, R * 4));
@@ -374,15 +384,21 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     ep->up.tmB = w->tm_ug;
     TRY(ep_tmap(&ep->dn.tmA, ep->h, RR, w->F_pad, 128));
     ep->dn.tmB = w->tm_dn;
+    ep->dup.tmW = w->tm_ug64;
+    TRY(ep_tmap(&ep->dup.tmXb, ep->recv_x, RR, w->d_pad, 64));
+    TRY(ep_tmap(&ep->dup.tmXs, ep->xs, RR, w->d_pad, 64));
+    ep->ddn.tmW = w->tm_dn128;
+    TRY(ep_tmap(&ep->ddn.tmXb, ep->h, RR, w->F_pad, 64));
+    TRY(ep_tmap(&ep->ddn.tmXs, ep->hs, RR, w->F_pad, 64));
 
     // communicator
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof id);
     {
-        ncclResult_t r = ncclCommInitRank(&ep->comm, world, id, rank);
+        ncclResult_t r = nccl().CommInitRank(&ep->comm, world, id, rank);
         if (r != ncclSuccess) {
             ep->comm = nullptr;
-            TRY(ep_fail(MOE_B200_E_NCCL, "ncclCommInitRank: %s%s", ncclGetErrorString(r)));
+            TRY(ep_fail(MOE_B200_E_NCCL, "ncclCommInitRank: %s%s", nccl().GetErrorString(r)));
         }
     }
     // exchange IPC handles of the three shared buffers (NCCL all-gather)
@@ -415,9 +431,9 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
         if (cudaMemcpy(dh + HB * rank, &mine_blob, HB, cudaMemcpyHostToDevice) != cudaSuccess)
             step = ep_fail(MOE_B200_E_CUDA, "handle upload failed%s%s");
         if (!step) {
-            ncclResult_t r = ncclAllGather(dh + HB * rank, dh, HB, ncclChar, ep->comm, ep->stream);
+            ncclResult_t r = nccl().AllGather(dh + HB * rank, dh, HB, ncclChar, ep->comm, ep->stream);
             if (r != ncclSuccess)
-                step = ep_fail(MOE_B200_E_NCCL, "ncclAllGather(handles): %s%s", ncclGetErrorString(r));
+                step = ep_fail(MOE_B200_E_NCCL, "nccl().AllGather(handles): %s%s", nccl().GetErrorString(r));
         }
         if (!step && (cudaStreamSynchronize(ep->stream) != cudaSuccess ||
                       cudaMemcpy(all.data(), dh, HB * G, cudaMemcpyDeviceToHost) != cudaSuccess))
@@ -471,30 +487,33 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
     const moe_b200_weights *w = ep->w;
     EP_CK(cudaSetDevice(ep->device));
     ncclResult_t async_err = ncclSuccess;
-    EP_NC(ncclCommGetAsyncError(ep->comm, &async_err));
+    EP_NC(nccl().CommGetAsyncError(ep->comm, &async_err));
     if (async_err != ncclSuccess)
-        return ep_fail(MOE_B200_E_NCCL, "communicator error: %s%s", ncclGetErrorString(async_err));
+        return ep_fail(MOE_B200_E_NCCL, "communicator error: %s%s", nccl().GetErrorString(async_err));
     cudaStream_t s = stream ? (cudaStream_t)stream : ep->stream;
     const int E = w->E, k = w->k, G = ep->world;
     float *probs = d_router_probs ? d_router_probs : ep->probs;
     int *ids = d_expert_ids ? d_expert_ids : ep->ids;
     int path = opts ? opts->path : MOE_B200_PATH_AUTO;
     if (path == MOE_B200_PATH_AUTO)
-        path = ((double)T * G * k / E >= 64.0) ? MOE_B200_PATH_TF32 : MOE_B200_PATH_FP32;
+        path = ((double)T * G * k / E >= 64.0) ? MOE_B200_PATH_TF32 : MOE_B200_PATH_TF32X3;
     cudaEvent_t *ev = profile_events(ep->device);
 #define MARK(i) \
     if (ev) EP_CK(cudaEventRecord(ev[i], s))
 
     MARK(0);
     if (T > 0) {
+        // the split-K router only when its buffer (sized for max_tokens) covers T
+        const int ns = router_splits(T, w->d);
+        const bool split = ns > 1 && ns <= ep->rsplit && ep->rpart != nullptr;
         EP_CK(launch_router(d_x, T, w->d, w->router, d_bias, E, k, probs, ids, ep->wts, ep->loc,
-                            ep->tile_cnt, s));
+                            ep->tile_cnt, s, split ? ep->rpart : nullptr, split ? ns : 1));
         EP_CK(launch_dispatch_scan(ep->tile_cnt, T, E, ep->tile_pref, ep->plan_local, s));
     } else {
         EP_CK(cudaMemsetAsync(ep->plan_local, 0, E * sizeof(int), s));
     }
     MARK(1);
-    EP_NC(ncclAllGather(ep->plan_local, ep->counts_all, E, ncclInt32, ep->comm, s));
+    EP_NC(nccl().AllGather(ep->plan_local, ep->counts_all, E, ncclInt32, ep->comm, s));
     ep_plan_kernel<<<1, 32, 0, s>>>(ep->counts_all, G, E, ep->rank, ep->recv_rows, ep->plan_q,
                                     ep->base_r, ep->slices);
     EP_CK(cudaGetLastError());
@@ -505,7 +524,7 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
             ep->d_ret_ptrs, ep->pos_of, path == MOE_B200_PATH_TF32, ep->status);
         EP_CK(cudaGetLastError());
     }
-    EP_NC(ncclAllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s));
+    EP_NC(nccl().AllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s));
     MARK(2);
     const int rows = ep->recv_rows;
     if (path == MOE_B200_PATH_TF32) {
@@ -515,6 +534,14 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
         MARK(3);
         EP_CK(launch_tc_down(ep->dn, w->F_pad, w->d_pad, w->down_bn, ep->y, ep->plan_q, E, rows,
                              sms, ep->status, s, ep->d_y_ptrs, ep->ret));
+    } else if (path == MOE_B200_PATH_TF32X3) {
+        const int sms = device_sms(ep->device);
+        EP_CK(launch_split_tf32(ep->recv_x, ep->xs, (size_t)rows * w->d_pad, s));
+        EP_CK(launch_dec_upgate(ep->dup, w->d_pad, w->F_pad, ep->h, ep->hs, ep->plan_q, E, rows,
+                                sms, ep->status, s));
+        MARK(3);
+        EP_CK(launch_dec_down(ep->ddn, w->F_pad, w->d_pad, ep->y, ep->plan_q, E, rows, sms,
+                              ep->status, s, ep->d_y_ptrs, ep->ret));
     } else {
         EP_CK(launch_ffma_upgate(ep->recv_x, w->d_pad, w->ug, w->F_pad, ep->h, ep->plan_q, E, rows,
                                  s));
@@ -523,11 +550,12 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
                                ep->d_y_ptrs, ep->ret));
     }
     MARK(4);   // the wait for the other ranks counts under the combine stage
-    EP_NC(ncclAllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s));
+    EP_NC(nccl().AllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s));
     if (T > 0) EP_CK(launch_combine(ep->y, w->d, w->d_pad, T, k, ep->pos_of, ep->wts, d_out, s));
     MARK(5);
 #undef MARK
-    note_forward(ep->device, E, T > 0 ? 7 : 3);
+    note_forward(ep->device, E,
+                 T > 0 ? 7 + (path == MOE_B200_PATH_TF32X3) + (router_splits(T, w->d) > 1) : 3);
     return MOE_B200_OK;
 }
 

@@ -10,9 +10,13 @@ constexpr int kRouterTile = 64;   // tokens per router CTA (dispatch tile granul
 // Plan (ints, device): cnt[E] | off[E+1] | mt128[E+1] | mt64[E+1]
 __host__ __device__ inline int plan_ints(int E) { return E + 3 * (E + 1); }
 
+// part/nsplit: optional [nsplit × T × E] buffer for the split-K variant used
+// when T is too small to fill the GPU (router_splits gives nsplit)
 cudaError_t launch_router(const float *x, int T, int d, const float *w_router,
                           const float *bias, int E, int k, float *probs, int *ids,
-                          float *wts, int *loc, int *tile_cnt, cudaStream_t s);
+                          float *wts, int *loc, int *tile_cnt, cudaStream_t s,
+                          float *part = nullptr, int nsplit = 1);
+int router_splits(int T, int d);
 
 cudaError_t launch_dispatch(const float *x, int T, int d, int d_pad, int E, int k,
                             const int *ids, const int *loc, const int *tile_cnt,

@@ -1,4 +1,7 @@
-// llmc_compat.cpp — llm.c's moe_forward entry point over the C-ABI.
+// llmc_compat.cpp — llm.c's own entry points over the C-ABI:
+//   moe_forward     (src/transformer.c:287-366)  block / prefill MoE
+//   inference_step  (src/inference.c:231-358)    single-token decode step,
+//                                                 with the MoE branch filled in
 //
 // Residency cache: one device expert set per MoEWeights pointer, uploaded
 // on first sight from the host matrices (include/transformer.h:53-58) and
@@ -6,6 +9,7 @@
 #include "../../include/llmc_moe.h"
 #include "../../include/moe_b200.h"
 
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -22,51 +26,61 @@ int env_path() {
     if (!p || !*p || !std::strcmp(p, "auto")) return MOE_B200_PATH_AUTO;
     if (!std::strcmp(p, "tf32")) return MOE_B200_PATH_TF32;
     if (!std::strcmp(p, "fp32")) return MOE_B200_PATH_FP32;
+    if (!std::strcmp(p, "tf32x3")) return MOE_B200_PATH_TF32X3;
     return MOE_B200_PATH_AUTO;
 }
 
-[[noreturn]] void die(const char *what, int rc) {
-    std::fprintf(stderr, "[moe_b200] moe_forward: %s: %s (%s)\n", what, moe_b200_strerror(rc),
+[[noreturn]] void die(const char *where, const char *what, int rc) {
+    std::fprintf(stderr, "[moe_b200] %s: %s: %s (%s)\n", where, what, moe_b200_strerror(rc),
                  moe_b200_last_error());
     std::abort();
+}
+
+// Device expert set of `mw`, uploaded on first sight.
+moe_b200_weights *resident(const llmc_MoEWeights *mw, int d, int F, const char *where) {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    auto it = g_cache.find(mw);
+    if (it != g_cache.end()) return it->second;
+    const int E = mw->n_experts, k = mw->top_k;
+    if (mw->W_router.rows != d || mw->W_router.cols != E)
+        die(where, "router shape mismatch", MOE_B200_E_INVALID);
+    std::vector<const float *> g(E), u(E), dn(E);
+    for (int e = 0; e < E; e++) {
+        const llmc_FFNWeights &fw = mw->experts[e];
+        if (fw.W_gate.rows != d || fw.W_gate.cols != F || fw.W_up.rows != d ||
+            fw.W_up.cols != F || fw.W_down.rows != F || fw.W_down.cols != d)
+            die(where, "expert shape mismatch", MOE_B200_E_INVALID);
+        g[e] = fw.W_gate.data;
+        u[e] = fw.W_up.data;
+        dn[e] = fw.W_down.data;
+    }
+    moe_b200_weights *w = nullptr;
+    int rc = moe_b200_weights_upload(mw->W_router.data, g.data(), u.data(), dn.data(), d, F, E,
+                                     k, &w);
+    if (rc) die(where, "weight upload", rc);
+    g_cache[mw] = w;
+    return w;
+}
+
+// The forward shared by both entry points: host buffers in, host buffers out.
+void run_moe(const llmc_MoEWeights *mw, int F, const float *x, int T, int d, float *out,
+             float *probs, int *ids, const char *where) {
+    moe_b200_weights *w = resident(mw, d, F, where);
+    moe_b200_opts opts;
+    std::memset(&opts, 0, sizeof opts);
+    opts.path = env_path();
+    const int rc = moe_b200_forward(w, nullptr, x, T, out, probs, ids, &opts);
+    if (rc) die(where, "forward", rc);
 }
 }  // namespace
 
 extern "C" void moe_forward(const llmc_Matrix *x, const llmc_MoEWeights *mw,
                             const llmc_ModelConfig *cfg, llmc_ForwardCache *cache,
                             llmc_Matrix *out) {
-    const int T = x->rows, d = x->cols, E = mw->n_experts, k = mw->top_k, F = cfg->ffn_hidden;
-    if (out->rows != T || out->cols != d || mw->W_router.rows != d || mw->W_router.cols != E)
-        die("shape mismatch", MOE_B200_E_INVALID);
-    moe_b200_weights *w = nullptr;
-    {
-        std::lock_guard<std::mutex> lk(g_cache_mu);
-        auto it = g_cache.find(mw);
-        if (it != g_cache.end()) {
-            w = it->second;
-        } else {
-            std::vector<const float *> g(E), u(E), dn(E);
-            for (int e = 0; e < E; e++) {
-                const llmc_FFNWeights &fw = mw->experts[e];
-                if (fw.W_gate.rows != d || fw.W_gate.cols != F || fw.W_up.rows != d ||
-                    fw.W_up.cols != F || fw.W_down.rows != F || fw.W_down.cols != d)
-                    die("expert shape mismatch", MOE_B200_E_INVALID);
-                g[e] = fw.W_gate.data;
-                u[e] = fw.W_up.data;
-                dn[e] = fw.W_down.data;
-            }
-            int rc = moe_b200_weights_upload(mw->W_router.data, g.data(), u.data(), dn.data(), d,
-                                             F, E, k, &w);
-            if (rc) die("weight upload", rc);
-            g_cache[mw] = w;
-        }
-    }
-    moe_b200_opts opts;
-    std::memset(&opts, 0, sizeof opts);
-    opts.path = env_path();
-    int rc = moe_b200_forward(w, nullptr, x->data, T, out->data, cache ? cache->router_probs : nullptr,
-                              cache ? cache->expert_ids : nullptr, &opts);
-    if (rc) die("forward", rc);
+    const int T = x->rows, d = x->cols;
+    if (out->rows != T || out->cols != d) die("moe_forward", "shape mismatch", MOE_B200_E_INVALID);
+    run_moe(mw, cfg->ffn_hidden, x->data, T, d, out->data, cache ? cache->router_probs : nullptr,
+            cache ? cache->expert_ids : nullptr, "moe_forward");
 }
 
 extern "C" int moe_b200_invalidate(const void *moe_weights) {
@@ -76,4 +90,126 @@ extern "C" int moe_b200_invalidate(const void *moe_weights) {
     int rc = moe_b200_weights_free(it->second);
     g_cache.erase(it);
     return rc;
+}
+
+// ---------------------------------------------------------------------------
+// inference_step: CPU restatement of the reference's single-token forward
+// (src/inference.c:161-228 helpers, 231-358 body) with the MoE branch added.
+// ---------------------------------------------------------------------------
+namespace {
+
+// out[N] = vec[M]ᵀ · mat[M×N], rows with vec[i] == 0 skipped
+// (matvec, src/inference.c:174-182)
+void matvec(const float *mat, const float *vec, float *out, int M, int N) {
+    std::memset(out, 0, (size_t)N * sizeof(float));
+    for (int i = 0; i < M; i++) {
+        const float vi = vec[i];
+        if (vi == 0.0f) continue;
+        const float *row = mat + (size_t)i * N;
+        for (int j = 0; j < N; j++) out[j] += vi * row[j];
+    }
+}
+
+// RMSNorm of one vector (rmsnorm_vec, src/inference.c:209-215)
+void rmsnorm_vec(const float *x, const float *w, float eps, float *out, int d) {
+    float ss = 0.0f;
+    for (int i = 0; i < d; i++) ss += x[i] * x[i];
+    const float inv = 1.0f / std::sqrt(ss / (float)d + eps);
+    for (int i = 0; i < d; i++) out[i] = x[i] * inv * w[i];
+}
+
+// RoPE at absolute position pos (rope_apply_pos, src/inference.c:189-203)
+void rope_apply_pos(float *qk, const llmc_RoPEBuffer *rb, int n_heads, int head_dim, int pos) {
+    const int half = head_dim / 2;
+    const float *cr = rb->cos_table + (size_t)pos * half;
+    const float *sr = rb->sin_table + (size_t)pos * half;
+    for (int h = 0; h < n_heads; h++) {
+        float *v = qk + (size_t)h * head_dim;
+        for (int i = 0; i < half; i++) {
+            const float v0 = v[2 * i] * cr[i] - v[2 * i + 1] * sr[i];
+            const float v1 = v[2 * i] * sr[i] + v[2 * i + 1] * cr[i];
+            v[2 * i] = v0;
+            v[2 * i + 1] = v1;
+        }
+    }
+}
+
+// softmax of one vector (softmax_vec, src/inference.c:218-225)
+void softmax_vec(float *v, int n) {
+    float mx = v[0];
+    for (int i = 1; i < n; i++) if (v[i] > mx) mx = v[i];
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) { v[i] = std::exp(v[i] - mx); sum += v[i]; }
+    const float inv = 1.0f / sum;
+    for (int i = 0; i < n; i++) v[i] *= inv;
+}
+
+}  // namespace
+
+extern "C" void inference_step(const llmc_Model *m, llmc_InferenceState *s, int token) {
+    const llmc_ModelConfig *cfg = &m->cfg;
+    const int d = cfg->d_model, nh = cfg->n_heads, nkv = cfg->n_kv_heads, hd = cfg->head_dim;
+    const int kv_dim = s->kv_dim, gqa = nh / nkv, pos = s->seq_pos;
+    const float scale = 1.0f / std::sqrt((float)hd);
+    if (pos >= s->max_seq_len) die("inference_step", "KV cache full", MOE_B200_E_INVALID);
+
+    std::memcpy(s->x, m->weights.embed.data + (size_t)token * d, (size_t)d * sizeof(float));
+    std::vector<float> ffn_scratch;
+    for (int l = 0; l < cfg->n_layers; l++) {
+        const llmc_BlockWeights *bw = &m->weights.blocks[l];
+        llmc_LayerKVCache *kvc = &s->kv_cache[l];
+
+        rmsnorm_vec(s->x, bw->rms_attn, cfg->rms_norm_eps, s->x_norm, d);
+        matvec(bw->attn.W_Q.data, s->x_norm, s->q, d, nh * hd);
+        matvec(bw->attn.W_K.data, s->x_norm, s->k, d, kv_dim);
+        matvec(bw->attn.W_V.data, s->x_norm, s->v, d, kv_dim);
+        rope_apply_pos(s->q, &m->rope, nh, hd, pos);
+        rope_apply_pos(s->k, &m->rope, nkv, hd, pos);
+        std::memcpy(kvc->K + (size_t)pos * kv_dim, s->k, (size_t)kv_dim * sizeof(float));
+        std::memcpy(kvc->V + (size_t)pos * kv_dim, s->v, (size_t)kv_dim * sizeof(float));
+
+        std::memset(s->head_out, 0, (size_t)nh * hd * sizeof(float));
+        for (int qh = 0; qh < nh; qh++) {
+            const int kvh = qh / gqa;
+            const float *qv = s->q + (size_t)qh * hd;
+            float *oh = s->head_out + (size_t)qh * hd;
+            for (int j = 0; j <= pos; j++) {
+                const float *kj = kvc->K + (size_t)j * kv_dim + (size_t)kvh * hd;
+                float dot = 0.0f;
+                for (int i = 0; i < hd; i++) dot += qv[i] * kj[i];
+                s->attn_buf[j] = dot * scale;
+            }
+            softmax_vec(s->attn_buf, pos + 1);
+            for (int j = 0; j <= pos; j++) {
+                const float *vj = kvc->V + (size_t)j * kv_dim + (size_t)kvh * hd;
+                const float a = s->attn_buf[j];
+                for (int i = 0; i < hd; i++) oh[i] += a * vj[i];
+            }
+        }
+        float *attn_out = s->x_norm;      // scratch reuse, as the reference does
+        matvec(bw->attn.W_O.data, s->head_out, attn_out, nh * hd, d);
+        for (int i = 0; i < d; i++) s->x[i] += attn_out[i];
+
+        rmsnorm_vec(s->x, bw->rms_ffn, cfg->rms_norm_eps, s->x_norm, d);
+        const int F = cfg->ffn_hidden;
+        if (!bw->use_moe) {
+            ffn_scratch.resize((size_t)3 * F);
+            float *gate = ffn_scratch.data(), *up = gate + F, *h = up + F;
+            float *ffn_out = s->q;
+            matvec(bw->ffn.W_gate.data, s->x_norm, gate, d, F);
+            matvec(bw->ffn.W_up.data, s->x_norm, up, d, F);
+            for (int i = 0; i < F; i++) h[i] = (gate[i] / (1.0f + std::exp(-gate[i]))) * up[i];
+            matvec(bw->ffn.W_down.data, h, ffn_out, F, d);
+            for (int i = 0; i < d; i++) s->x[i] += ffn_out[i];
+        } else {
+            // the MoE branch the reference leaves out (src/inference.c:342-343)
+            ffn_scratch.resize((size_t)d);
+            float *ffn_out = ffn_scratch.data();
+            run_moe(&bw->moe, F, s->x_norm, 1, d, ffn_out, nullptr, nullptr, "inference_step");
+            for (int i = 0; i < d; i++) s->x[i] += ffn_out[i];
+        }
+    }
+    rmsnorm_vec(s->x, m->weights.rms_final, cfg->rms_norm_eps, s->x_norm, d);
+    matvec(m->weights.lm_head.data, s->x_norm, s->logits, d, cfg->vocab_size);
+    s->seq_pos++;
 }

@@ -110,6 +110,7 @@ struct Ctx {
     // workspace
     Buf probs, ids, wts, loc, tile_cnt, tile_pref, plan, pos_of, x_perm, h, y;
     Buf xs, hs;                          // small parts of the 3xTF32 split
+    Buf rpart;                           // split-K router partial logits (small T)
     Buf io_x, io_out, io_bias;
     int last_E = 0;
     int last_launches = 0;
@@ -206,7 +207,7 @@ extern "C" void moe_b200_shutdown(void) {
         cudaStreamSynchronize(c->stream);
         Buf *bufs[] = {&c->probs, &c->ids, &c->wts, &c->loc, &c->tile_cnt, &c->tile_pref,
                        &c->plan, &c->pos_of, &c->x_perm, &c->h, &c->y, &c->xs, &c->hs,
-                       &c->io_x, &c->io_out, &c->io_bias};
+                       &c->rpart, &c->io_x, &c->io_out, &c->io_bias};
         for (Buf *b : bufs) free_buf(*b);
         cudaFree(c->status);
         cudaStreamDestroy(c->stream);
@@ -467,8 +468,11 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
     if (ev) CK(cudaEventRecord(ev[i], s))
 
     MARK(0);
-    CK(launch_router(d_x, T, d, w->router, d_bias, E, k, probs, ids, wts, loc, tile_cnt, s));
-    launches += 1;
+    const int nsplit = router_splits(T, d);
+    if (nsplit > 1 && (rc = grow(c->rpart, (size_t)nsplit * T * E * 4))) return rc;
+    CK(launch_router(d_x, T, d, w->router, d_bias, E, k, probs, ids, wts, loc, tile_cnt, s,
+                     (float *)c->rpart.p, nsplit));
+    launches += nsplit > 1 ? 2 : 1;
     MARK(1);
     const int path = pick_path(w, T, opts);
     CK(launch_dispatch(d_x, T, d, w->d_pad, E, k, ids, loc, tile_cnt, tile_pref, plan, pos_of,

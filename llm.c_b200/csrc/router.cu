@@ -34,43 +34,21 @@ template <> struct RouterShape<128> { static constexpr int TPT = 4, EPT = 8; };
 
 }  // namespace
 
+// FFMA dot products of this CTA's 64 tokens with W_router over K range
+// [d0, d1): acc[i][j] += x[t0 + ty*TPT + i][k] * W[k][tx*EPT + j].
 template <int EB>
-__global__ void __launch_bounds__(256)
-router_topk_kernel(const float *__restrict__ x, int T, int d,
-                   const float *__restrict__ w_router,   // [d×E]
-                   const float *__restrict__ bias,       // [E] or null
-                   int E, int k,
-                   float *__restrict__ probs,            // [T×E]
-                   int *__restrict__ ids,                // [T×k]
-                   float *__restrict__ wts,              // [T×k]
-                   int *__restrict__ loc,                // [T×k]
-                   int *__restrict__ tile_cnt)           // [tiles×E]
+__device__ __forceinline__ void router_dot(const float *__restrict__ x, int T, int d,
+                                           const float *__restrict__ w_router, int E, int t0,
+                                           int d0, int d1, float *smem,
+                                           float (&acc)[RouterShape<EB>::TPT][RouterShape<EB>::EPT])
 {
     constexpr int TPT = RouterShape<EB>::TPT, EPT = RouterShape<EB>::EPT;
-    constexpr int NTX = EB / EPT;                 // threads along experts
-    static_assert((TT / TPT) * NTX == 256, "thread tile must cover 256 threads");
-    constexpr int MAIN_FLOATS = TT * XS + DC * EB;
-    constexpr int LG_FLOATS = TT * (EB + 1);
-    __shared__ __align__(16) float smem[MAIN_FLOATS > LG_FLOATS ? MAIN_FLOATS : LG_FLOATS];
-    __shared__ int sid[TT][kMaxTopK];
-    __shared__ float swt[TT][kMaxTopK];
+    constexpr int NTX = EB / EPT;
     float *xs = smem;                 // [TT][XS]
     float *ws = smem + TT * XS;       // [DC][EB]
-    float *lg = smem;                 // [TT][EB+1] (after the main loop)
-
-    const int tile = blockIdx.x;
-    const int t0 = tile * TT;
     const int tid = threadIdx.x;
     const int tx = tid % NTX, ty = tid / NTX;
     const bool vec_x = (d & 3) == 0;
-
-    float acc[TPT][EPT];
-#pragma unroll
-    for (int i = 0; i < TPT; i++)
-#pragma unroll
-        for (int j = 0; j < EPT; j++) acc[i][j] = 0.0f;
-
-    // register staging of one chunk: x as float4 (2 per thread), W scalar
     constexpr int XV = TT * DC / 4 / 256;        // float4 of x per thread = 2
     constexpr int WN = DC * EB / 256;            // W floats per thread
     float4 xr[XV];
@@ -85,13 +63,13 @@ router_topk_kernel(const float *__restrict__ x, int T, int d,
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (t < T) {
                 const float *p = x + (size_t)t * d + i;
-                if (vec_x && i + 3 < d) {
+                if (vec_x && i + 3 < d1) {
                     v = __ldg(reinterpret_cast<const float4 *>(p));
                 } else {
-                    if (i + 0 < d) v.x = __ldg(p + 0);
-                    if (i + 1 < d) v.y = __ldg(p + 1);
-                    if (i + 2 < d) v.z = __ldg(p + 2);
-                    if (i + 3 < d) v.w = __ldg(p + 3);
+                    if (i + 0 < d1) v.x = __ldg(p + 0);
+                    if (i + 1 < d1) v.y = __ldg(p + 1);
+                    if (i + 2 < d1) v.z = __ldg(p + 2);
+                    if (i + 3 < d1) v.w = __ldg(p + 3);
                 }
             }
             xr[q] = v;
@@ -101,7 +79,7 @@ router_topk_kernel(const float *__restrict__ x, int T, int d,
             const int idx = tid + q * 256;
             const int r = idx / EB, c = idx % EB;
             const int i = i0 + r;
-            wr[q] = (i < d && c < E) ? __ldg(w_router + (size_t)i * E + c) : 0.0f;
+            wr[q] = (i < d1 && c < E) ? __ldg(w_router + (size_t)i * E + c) : 0.0f;
         }
     };
     auto store_chunk = [&]() {
@@ -115,12 +93,12 @@ router_topk_kernel(const float *__restrict__ x, int T, int d,
         for (int q = 0; q < WN; q++) ws[tid + q * 256] = wr[q];
     };
 
-    load_chunk(0);
-    for (int i0 = 0; i0 < d; i0 += DC) {
+    load_chunk(d0);
+    for (int i0 = d0; i0 < d1; i0 += DC) {
         __syncthreads();                 // previous chunk fully consumed
         store_chunk();
         __syncthreads();
-        if (i0 + DC < d) load_chunk(i0 + DC);   // overlaps the FMAs below
+        if (i0 + DC < d1) load_chunk(i0 + DC);   // overlaps the FMAs below
 #pragma unroll 8
         for (int c = 0; c < DC; c++) {
             float xv[TPT], wv[EPT];
@@ -145,18 +123,20 @@ router_topk_kernel(const float *__restrict__ x, int T, int d,
                 for (int j = 0; j < EPT; j++) acc[i][j] = __fmaf_rn(xv[i], wv[j], acc[i][j]);
         }
     }
-    __syncthreads();                     // xs/ws are reused as lg below
-#pragma unroll
-    for (int i = 0; i < TPT; i++)
-#pragma unroll
-        for (int j = 0; j < EPT; j++) {
-            const int e = tx * EPT + j;
-            if (e < E)
-                lg[(ty * TPT + i) * (EB + 1) + e] =
-                    bias ? __fadd_rn(acc[i][j], __ldg(bias + e)) : acc[i][j];
-        }
-    __syncthreads();
+    __syncthreads();                     // smem is reused by the caller
+}
 
+// Softmax, top-k, renormalisation, tile writes and the tile histogram for
+// the logits in lg [TT][EB+1] (bias already added).
+template <int EB>
+__device__ __forceinline__ void router_tail(float *lg, int T, int E, int k, int tile,
+                                            float *__restrict__ probs, int *__restrict__ ids,
+                                            float *__restrict__ wts, int *__restrict__ loc,
+                                            int *__restrict__ tile_cnt,
+                                            int (*sid)[kMaxTopK], float (*swt)[kMaxTopK])
+{
+    const int tid = threadIdx.x;
+    const int t0 = tile * TT;
     if (tid < TT && t0 + tid < T) {
         float *row = lg + tid * (EB + 1);
         // softmax_rows, AVX2+FMA branch: 8-wide part then scalar tail.
@@ -227,21 +207,147 @@ router_topk_kernel(const float *__restrict__ x, int T, int d,
     }
 }
 
-cudaError_t launch_router(const float *x, int T, int d, const float *w_router,
-                          const float *bias, int E, int k, float *probs, int *ids,
-                          float *wts, int *loc, int *tile_cnt, cudaStream_t s)
+template <int EB>
+__global__ void __launch_bounds__(256)
+router_topk_kernel(const float *__restrict__ x, int T, int d,
+                   const float *__restrict__ w_router,   // [d×E]
+                   const float *__restrict__ bias,       // [E] or null
+                   int E, int k,
+                   float *__restrict__ probs,            // [T×E]
+                   int *__restrict__ ids,                // [T×k]
+                   float *__restrict__ wts,              // [T×k]
+                   int *__restrict__ loc,                // [T×k]
+                   int *__restrict__ tile_cnt)           // [tiles×E]
+{
+    constexpr int TPT = RouterShape<EB>::TPT, EPT = RouterShape<EB>::EPT;
+    constexpr int NTX = EB / EPT;
+    static_assert((TT / TPT) * NTX == 256, "thread tile must cover 256 threads");
+    constexpr int MAIN_FLOATS = TT * XS + DC * EB;
+    constexpr int LG_FLOATS = TT * (EB + 1);
+    __shared__ __align__(16) float smem[MAIN_FLOATS > LG_FLOATS ? MAIN_FLOATS : LG_FLOATS];
+    __shared__ int sid[TT][kMaxTopK];
+    __shared__ float swt[TT][kMaxTopK];
+
+    const int tile = blockIdx.x;
+    const int tx = threadIdx.x % NTX, ty = threadIdx.x / NTX;
+    float acc[TPT][EPT];
+#pragma unroll
+    for (int i = 0; i < TPT; i++)
+#pragma unroll
+        for (int j = 0; j < EPT; j++) acc[i][j] = 0.0f;
+    router_dot<EB>(x, T, d, w_router, E, tile * TT, 0, d, smem, acc);
+    float *lg = smem;                 // [TT][EB+1]
+#pragma unroll
+    for (int i = 0; i < TPT; i++)
+#pragma unroll
+        for (int j = 0; j < EPT; j++) {
+            const int e = tx * EPT + j;
+            if (e < E)
+                lg[(ty * TPT + i) * (EB + 1) + e] =
+                    bias ? __fadd_rn(acc[i][j], __ldg(bias + e)) : acc[i][j];
+        }
+    __syncthreads();
+    router_tail<EB>(lg, T, E, k, tile, probs, ids, wts, loc, tile_cnt, sid, swt);
+}
+
+// Small T: the K range is split over blockIdx.y so that enough CTAs run;
+// each writes its partial logits, and router_reduce_topk_kernel sums the
+// splits in a fixed order (deterministic) before the same tail.
+template <int EB>
+__global__ void __launch_bounds__(256)
+router_partial_kernel(const float *__restrict__ x, int T, int d,
+                      const float *__restrict__ w_router, int E, int dsplit,
+                      float *__restrict__ part)             // [nsplit][T][E]
+{
+    constexpr int TPT = RouterShape<EB>::TPT, EPT = RouterShape<EB>::EPT;
+    constexpr int NTX = EB / EPT;
+    __shared__ __align__(16) float smem[TT * XS + DC * EB];
+    const int tile = blockIdx.x, split = blockIdx.y;
+    const int d0 = split * dsplit, d1 = min(d, d0 + dsplit);
+    const int tx = threadIdx.x % NTX, ty = threadIdx.x / NTX;
+    float acc[TPT][EPT];
+#pragma unroll
+    for (int i = 0; i < TPT; i++)
+#pragma unroll
+        for (int j = 0; j < EPT; j++) acc[i][j] = 0.0f;
+    router_dot<EB>(x, T, d, w_router, E, tile * TT, d0, d1, smem, acc);
+    float *dst = part + (size_t)split * T * E;
+#pragma unroll
+    for (int i = 0; i < TPT; i++) {
+        const int t = tile * TT + ty * TPT + i;
+        if (t >= T) continue;
+#pragma unroll
+        for (int j = 0; j < EPT; j++) {
+            const int e = tx * EPT + j;
+            if (e < E) dst[(size_t)t * E + e] = acc[i][j];
+        }
+    }
+}
+
+template <int EB>
+__global__ void __launch_bounds__(256)
+router_reduce_topk_kernel(const float *__restrict__ part, int nsplit, int T,
+                          const float *__restrict__ bias, int E, int k,
+                          float *__restrict__ probs, int *__restrict__ ids,
+                          float *__restrict__ wts, int *__restrict__ loc,
+                          int *__restrict__ tile_cnt)
+{
+    __shared__ __align__(16) float lg[TT * (EB + 1)];
+    __shared__ int sid[TT][kMaxTopK];
+    __shared__ float swt[TT][kMaxTopK];
+    const int tile = blockIdx.x, t0 = tile * TT;
+    for (int q = threadIdx.x; q < TT * E; q += 256) {
+        const int r = q / E, e = q % E, t = t0 + r;
+        if (t >= T) continue;
+        float v = 0.0f;
+        for (int sp = 0; sp < nsplit; sp++) v = __fadd_rn(v, part[((size_t)sp * T + t) * E + e]);
+        lg[r * (EB + 1) + e] = bias ? __fadd_rn(v, __ldg(bias + e)) : v;
+    }
+    __syncthreads();
+    router_tail<EB>(lg, T, E, k, tile, probs, ids, wts, loc, tile_cnt, sid, swt);
+}
+
+int router_splits(int T, int d) {
+    const int tiles = ceil_div(T, TT);
+    if (tiles >= 64 || d < 256) return 1;
+    int ns = ceil_div(256, tiles);
+    ns = min(ns, d / 128);
+    return max(ns, 1);
+}
+
+template <int EB>
+static void launch_router_eb(const float *x, int T, int d, const float *w_router, const float *bias,
+                             int E, int k, float *probs, int *ids, float *wts, int *loc,
+                             int *tile_cnt, float *part, int nsplit, cudaStream_t s)
 {
     const int tiles = ceil_div(T, TT);
+    if (nsplit <= 1 || part == nullptr) {
+        router_topk_kernel<EB><<<tiles, 256, 0, s>>>(x, T, d, w_router, bias, E, k, probs, ids, wts,
+                                                     loc, tile_cnt);
+        return;
+    }
+    const int dsplit = round_up(ceil_div(d, nsplit), DC);
+    nsplit = ceil_div(d, dsplit);
+    router_partial_kernel<EB><<<dim3(tiles, nsplit), 256, 0, s>>>(x, T, d, w_router, E, dsplit, part);
+    router_reduce_topk_kernel<EB><<<tiles, 256, 0, s>>>(part, nsplit, T, bias, E, k, probs, ids, wts,
+                                                        loc, tile_cnt);
+}
+
+cudaError_t launch_router(const float *x, int T, int d, const float *w_router,
+                          const float *bias, int E, int k, float *probs, int *ids,
+                          float *wts, int *loc, int *tile_cnt, cudaStream_t s,
+                          float *part, int nsplit)
+{
     if (E <= 8)
-        router_topk_kernel<8><<<tiles, 256, 0, s>>>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt);
+        launch_router_eb<8>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt, part, nsplit, s);
     else if (E <= 16)
-        router_topk_kernel<16><<<tiles, 256, 0, s>>>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt);
+        launch_router_eb<16>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt, part, nsplit, s);
     else if (E <= 32)
-        router_topk_kernel<32><<<tiles, 256, 0, s>>>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt);
+        launch_router_eb<32>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt, part, nsplit, s);
     else if (E <= 64)
-        router_topk_kernel<64><<<tiles, 256, 0, s>>>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt);
+        launch_router_eb<64>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt, part, nsplit, s);
     else
-        router_topk_kernel<128><<<tiles, 256, 0, s>>>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt);
+        launch_router_eb<128>(x, T, d, w_router, bias, E, k, probs, ids, wts, loc, tile_cnt, part, nsplit, s);
     return cudaGetLastError();
 }
 

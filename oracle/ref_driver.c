@@ -10,6 +10,9 @@
  *   ref_softmax_rows  -> softmax_rows     (src/matrix.c:529-586)
  *   ref_swiglu        -> swiglu           (src/matrix.c:618-655)
  *   ref_ffn_forward   -> ffn_forward      (src/transformer.c:157-165)
+ *   ref_model_*       -> model_init / model_forward / model_free
+ *                        (src/transformer.c:475-802), with srand(seed)
+ *   ref_inference_*   -> inference_init / inference_step (src/inference.c)
  */
 #include <stdlib.h>
 #include <string.h>
@@ -89,3 +92,40 @@ void ref_ffn_forward(const float *x, int n, int d, const float *Wg,
     mat_free(&gb);
     mat_free(&ub);
 }
+
+/* ---- whole-model entry points for the decode (config 2) oracle --------- */
+#include "inference.h"
+
+void *ref_model_init(int vocab, int max_seq, int d, int n_layers, int n_heads, int n_kv,
+                     int head_dim, int window, int ffn, int n_experts, int top_k, float eps,
+                     float theta, unsigned seed) {
+    ModelConfig cfg;
+    memset(&cfg, 0, sizeof cfg);
+    cfg.vocab_size = vocab; cfg.max_seq_len = max_seq; cfg.d_model = d;
+    cfg.n_layers = n_layers; cfg.n_heads = n_heads; cfg.n_kv_heads = n_kv;
+    cfg.head_dim = head_dim; cfg.window_size = window; cfg.ffn_hidden = ffn;
+    cfg.n_experts = n_experts; cfg.top_k_experts = top_k; cfg.rms_norm_eps = eps;
+    cfg.rope_theta = theta;
+    srand(seed);
+    return model_init(&cfg);
+}
+
+void ref_model_free(void *m) { model_free((Model *)m); }
+
+/* logits of the last position of model_forward over tokens[0..n) */
+void ref_model_forward_last(void *mp, const int *tokens, int n, float *logits_last) {
+    Model *m = (Model *)mp;
+    int V = m->cfg.vocab_size;
+    Matrix lg = mat_alloc(n, V, 0);
+    model_forward(m, tokens, n, &lg);
+    memcpy(logits_last, lg.data + (size_t)(n - 1) * V, (size_t)V * sizeof(float));
+    mat_free(&lg);
+}
+
+void *ref_inference_init(void *m) { return inference_init((const Model *)m); }
+void ref_inference_free(void *s) { inference_free((InferenceState *)s); }
+void ref_inference_step(void *m, void *s, int token) {
+    inference_step((const Model *)m, (InferenceState *)s, token);
+}
+float *ref_inference_logits(void *s) { return ((InferenceState *)s)->logits; }
+int ref_inference_pos(void *s) { return ((InferenceState *)s)->seq_pos; }

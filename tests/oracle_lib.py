@@ -89,6 +89,18 @@ def ref():
         lib.ref_swiglu.argtypes = [_fp, _fp, _fp, C.c_int]
         lib.ref_ffn_forward.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp,
                                         C.c_int, _fp]
+        lib.ref_model_init.restype = C.c_void_p
+        lib.ref_model_init.argtypes = [C.c_int] * 11 + [C.c_float, C.c_float, C.c_uint]
+        lib.ref_model_free.argtypes = [C.c_void_p]
+        lib.ref_model_forward_last.argtypes = [C.c_void_p, _ip, C.c_int, _fp]
+        lib.ref_inference_init.restype = C.c_void_p
+        lib.ref_inference_init.argtypes = [C.c_void_p]
+        lib.ref_inference_free.argtypes = [C.c_void_p]
+        lib.ref_inference_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        lib.ref_inference_logits.restype = _fp
+        lib.ref_inference_logits.argtypes = [C.c_void_p]
+        lib.ref_inference_pos.restype = C.c_int
+        lib.ref_inference_pos.argtypes = [C.c_void_p]
         _ref = lib
     return _ref
 

@@ -61,3 +61,13 @@ def test_built_for_sm100a_only():
         pytest.skip("build log absent")
     text = log.read_text()
     assert "sm_100a" in text and "sm_90" not in text
+
+
+def test_loading_library_before_torch_keeps_torch_importable():
+    # the library resolves NCCL only when an expert-parallel group is made,
+    # so loading it first must not pin an NCCL that torch cannot use
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, 'llm.c_b200'); import moe_b200; "
+            "moe_b200.lib(); import torch; print(torch.__version__)")
+    subprocess.run([sys.executable, "-c", code], cwd=str(REPO), check=True, timeout=600)

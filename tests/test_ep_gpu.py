@@ -54,7 +54,7 @@ def _worker(rank, world, port, q):
             Tl = T // world
             ep = M.EP(obj[0], rank, world, Tl, w)
             xs = np.ascontiguousarray(p.x[rank * Tl:(rank + 1) * Tl])
-            for path in (M.PATH_FP32, M.PATH_TF32):
+            for path in (M.PATH_FP32, M.PATH_TF32, M.PATH_TF32X3):
                 for rep in range(2):
                     out, probs, ids = ep.forward(xs, p.bias, path=path)
                     r_out, r_probs, r_ids = M.moe_forward(w, xs, p.bias, path=path)

@@ -179,5 +179,5 @@ def test_device_entry_point_with_torch_buffers(moe):
     h_out, h_probs, h_ids = M.moe_forward(w, p.x, path=M.PATH_TF32)
     assert np.array_equal(out.cpu().numpy(), h_out)
     assert np.array_equal(ids.cpu().numpy(), h_ids)
-    assert M.last_launches() == 6
+    assert M.last_launches() in (6, 7)     # 7 when the router runs split-K
     w.free()

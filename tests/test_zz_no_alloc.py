@@ -6,7 +6,10 @@ All of its intermediates live in a static 16 MiB array inside the library.
 It is checked through the C-ABI against the regular device entry point on
 the same FP32 expert path, on two calls in a row with different inputs, so
 that whatever the first call leaves in the shared array cannot leak into
-the second.  This file is named to be collected last.
+the second.  The tolerances are the parity tests' own: probabilities within
+2e-6 (the regular entry point may sum the router logits in another order),
+routing identical except where two experts' logits lie within 1e-6, layer
+output within 1e-5.  This file is named to be collected last.
 """
 import numpy as np
 import pytest
@@ -16,7 +19,8 @@ import oracle_lib as O
 
 pytestmark = pytest.mark.gpu
 
-TOL = 1e-5   # the FP32 path's layer tolerance (max|Δ| / max|ref|)
+TOL = 1e-5        # the FP32 path's layer tolerance (max|Δ| / max|ref|)
+PROBS_TOL = 2e-6  # router probabilities
 
 
 def _upload(p):
@@ -57,8 +61,13 @@ def test_noalloc_matches_device_entry_point_two_calls(moe):
     for x, bias in ((p.x, None), (x2, bias2)):
         (r_out, r_probs, r_ids), (n_out, n_probs, n_ids) = _run_both(w, x, bias, p.E, p.k)
         assert np.isfinite(n_out).all()
-        assert np.array_equal(n_ids, r_ids)
-        assert np.max(np.abs(n_probs - r_probs)) <= 1e-7
+        logits = np.empty((x.shape[0], p.E), np.float32)
+        O.oracle().oracle_router(O._f(np.ascontiguousarray(x)), x.shape[0], x.shape[1],
+                                 O._f(p.W_router), O._f(bias), p.E, p.k, O._f(logits),
+                                 None, None, None)
+        for t in np.nonzero(np.any(n_ids != r_ids, axis=1))[0]:
+            assert O.routing_mismatch_allowed(logits[t], n_ids[t], r_ids[t], p.k)
+        assert np.max(np.abs(n_probs - r_probs)) <= PROBS_TOL
         assert O.rel_err(n_out, r_out) < TOL
     w.free()
 
