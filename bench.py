@@ -31,8 +31,11 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "llm.c_b200"))
 
+DECODE_PREFILL = 512        # c2: KV cache prefilled with 512 random tokens
+
 CONFIGS = {
-    # name: T, d, E, k, F, seed, bias
+    # name: T, d, E, k, F, seed, bias (c2 is the 6-layer decode step, run_decode)
+    "c2": dict(T=1, d=384, E=8, k=2, F=1536, seed=0, bias=None),
     "c1": dict(T=2048, d=256, E=8, k=2, F=1024, seed=0, bias=None),
     "c3": dict(T=16384, d=1024, E=16, k=2, F=4096, seed=1, bias="normal"),
     "c4": dict(T=256, d=2048, E=32, k=4, F=5632, seed=0, bias=None),
@@ -220,6 +223,133 @@ def run_reference_arm(args, c):
 
 
 # ----------------------------------------------------------------------------
+# c2: the single-token decode step of a 6-layer llm.c model with MoE FFNs
+# ----------------------------------------------------------------------------
+def reference_decode_ms(dec, steps, threads):
+    """The reference's own pieces for one decode step on the same model:
+    llm.c's inference_step (which leaves the MoE FFN out, src/inference.c:
+    342-343) plus, per MoE layer, llm.c's moe_forward on one token."""
+    sys.path.insert(0, str(REPO / "tests"))
+    import oracle_lib as O
+    import ctypes as C
+    R = O.ref()
+    R.ref_set_threads(threads)
+    R.ref_inference_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    m_ptr, s_ptr = C.addressof(dec.model), C.addressof(dec.state)
+    c = dec.c
+    t0 = time.perf_counter()
+    for i in range(steps):
+        R.ref_inference_step(m_ptr, s_ptr, i % c.vocab)
+    step_ms = 1000.0 * (time.perf_counter() - t0) / steps
+    x = np.random.default_rng(3).standard_normal((1, c.d)).astype(np.float32)
+    moe_ms = 0.0
+    for layer, mw in dec.moe_weight_structs():
+        E = mw.n_experts
+        ex = [mw.experts[e] for e in range(E)]
+        g = (O._fp * E)(*[e.W_gate.data for e in ex])
+        u = (O._fp * E)(*[e.W_up.data for e in ex])
+        dn = (O._fp * E)(*[e.W_down.data for e in ex])
+        out = np.empty((1, c.d), np.float32)
+        probs = np.empty((1, E), np.float32)
+        ids = np.empty((1, mw.top_k), np.int32)
+        reps = 20
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            R.ref_moe_forward(O._f(x), 1, c.d, mw.W_router.data, E, mw.top_k, g, u, dn, c.ffn,
+                              O._f(out), O._f(probs), O._i(ids))
+        moe_ms += 1000.0 * (time.perf_counter() - t0) / reps
+    return step_ms, moe_ms
+
+
+def run_decode(args):
+    import torch  # noqa: F401  (CUDA context before the library, as in the other arms)
+    import moe_b200 as M
+    import llmc_model as LM
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    M.init(0)
+    cfg = LM.DecodeConfig(max_seq=DECODE_PREFILL + args.warmup + args.steps + 8)
+    dec = LM.LlmcDecoder(cfg, seed=0)
+    rng = np.random.default_rng(1)
+    if args.impl == "reference":
+        threads = len(os.sched_getaffinity(0))
+        for t in rng.integers(0, cfg.vocab, DECODE_PREFILL):
+            dec.step(int(t))          # fill the KV cache (B200 path; not timed)
+        step_ms, moe_ms = reference_decode_ms(dec, max(args.steps, 3), threads)
+        value = 1000.0 / (step_ms + moe_ms)
+        line = {"metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
+                "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": step_ms + moe_ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "c2", "layers": cfg.n_layers, "d_model": cfg.d,
+                           "n_experts": cfg.n_experts, "top_k": cfg.top_k, "d_ff": cfg.ffn,
+                           "kv_cached_tokens": DECODE_PREFILL},
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads,
+                                 "kind": "reference",
+                                 "sample": f"inference_step {step_ms:.3f} ms (MoE left out by "
+                                           f"the reference) + 6 x moe_forward(T=1) {moe_ms:.3f} ms"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    for t in rng.integers(0, cfg.vocab, DECODE_PREFILL):
+        dec.step(int(t))
+    toks = rng.integers(0, cfg.vocab, args.warmup + args.steps)
+    for t in toks[:args.warmup]:
+        dec.step(int(t))
+    M.profile_enable(True)
+    M.profile_read()
+    with ClockSampler(0) as clk:
+        t0 = time.perf_counter()
+        for t in toks[args.warmup:]:
+            dec.step(int(t))
+        ms = 1000.0 * (time.perf_counter() - t0) / args.steps
+    M.profile_enable(False)
+    stage_ms, n_fw = M.profile_read()
+    stage_avg = {s: v / max(n_fw, 1) for s, v in stage_ms.items()}
+    moe_dev_ms = cfg.n_layers * sum(stage_avg.values())
+    peaks = measured_peaks()
+    # dominant kernel: expert up/gate (3xTF32 weight streaming); algorithmic
+    # bytes = the gate and up weights of the k experts a token touches
+    up_bytes = cfg.top_k * 2 * cfg.d * cfg.ffn * 4
+    up_gbs = up_bytes / (stage_avg["upgate"] / 1000.0) / 1e9
+    launches = M.last_launches()
+    line = {
+        "metric": "moe_layer_tokens_per_s", "value": 1000.0 / ms, "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "c2", "layers": cfg.n_layers, "d_model": cfg.d,
+                   "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads, "d_ff": cfg.ffn,
+                   "n_experts": cfg.n_experts, "top_k": cfg.top_k,
+                   "kv_cached_tokens": DECODE_PREFILL, "batch": 1,
+                   "parallelism": "single GPU (MoE); attention on the host as in llm.c"},
+        "e2e": {"value": 1000.0 / ms, "unit": "tokens/s", "ms_per_step": ms,
+                "h2d_bytes_per_step": cfg.n_layers * cfg.d * 4,
+                "d2h_bytes_per_step": cfg.n_layers * (cfg.d + cfg.n_experts + cfg.top_k) * 4,
+                "timing": "host wall clock around synchronous inference_step calls"},
+        "moe_device_ms_per_step": moe_dev_ms,
+        "roofline": {"bound": "hbm", "kernel": "dec_gemm<up/gate> (3xTF32 weight streaming)",
+                     "achieved": up_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": up_gbs / peaks["hbm_gbs"], "traffic": None,
+                     "peak_src": peaks["src"] + " HBM copy bandwidth"},
+        "stages_ms": stage_avg,
+        "gpu_launches": launches * cfg.n_layers * args.steps,
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline and (REPO / "oracle" / "_ref" / "libllmref.so").exists():
+        threads = len(os.sched_getaffinity(0))
+        step_ms, moe_ms = reference_decode_ms(dec, 5, threads)
+        line["cpu_baseline"] = {"value": 1000.0 / (step_ms + moe_ms), "unit": "tokens/s",
+                                "cores": threads, "kind": "reference",
+                                "sample": f"5 steps: inference_step {step_ms:.3f} ms (MoE left "
+                                          f"out by the reference) + 6 x moe_forward(T=1) "
+                                          f"{moe_ms:.3f} ms"}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
 # GPU
 # ----------------------------------------------------------------------------
 def main():
@@ -237,6 +367,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     c = CONFIGS[args.config]
 
+    if args.config == "c2":
+        run_decode(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args, c)
         return

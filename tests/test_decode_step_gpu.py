@@ -68,3 +68,28 @@ def test_dense_decode_matches_reference_inference_step(moe):
     R.ref_inference_free(s_ref)
     R.ref_inference_free(s_ours)
     R.ref_model_free(m)
+
+
+def test_python_model_builder_layout_matches_reference(moe):
+    """llm.c_b200/llmc_model.py builds llm.c's structs from Python: two
+    identical dense models stepped by llm.c's own inference_step and by the
+    drop-in must agree, which checks every mirrored struct layout."""
+    import llmc_model as LM
+    R = O.ref()
+    cfg = LM.DecodeConfig(n_experts=1, top_k=1, max_seq=16)
+    a, b = LM.LlmcDecoder(cfg, seed=3), LM.LlmcDecoder(cfg, seed=3)
+    R.ref_inference_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    for t in np.random.default_rng(7).integers(0, cfg.vocab, 8):
+        R.ref_inference_step(C.addressof(a.model), C.addressof(a.state), int(t))
+        b.step(int(t))
+        assert O.rel_err(b.logits(), a.logits()) < 1e-5
+    assert a.pos == b.pos == 8
+
+
+def test_python_model_builder_moe_decode_runs(moe):
+    import llmc_model as LM
+    dec = LM.LlmcDecoder(LM.DecodeConfig(max_seq=8), seed=4)
+    for t in (1, 2, 3):
+        dec.step(t)
+    lg = dec.logits()
+    assert np.isfinite(lg).all() and dec.pos == 3
