@@ -134,6 +134,19 @@ void rope_apply_pos(float *qk, const llmc_RoPEBuffer *rb, int n_heads, int head_
     }
 }
 
+// dot product with eight interleaved partial sums (a fixed order, so the
+// result is deterministic; the reference's vec_dot, src/inference.c:133-155,
+// likewise sums in vector lanes)
+float dot8(const float *a, const float *b, int n) {
+    float p[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int i = 0;
+    for (; i + 8 <= n; i += 8)
+        for (int l = 0; l < 8; l++) p[l] += a[i + l] * b[i + l];
+    float s = ((p[0] + p[4]) + (p[1] + p[5])) + ((p[2] + p[6]) + (p[3] + p[7]));
+    for (; i < n; i++) s += a[i] * b[i];
+    return s;
+}
+
 // softmax of one vector (softmax_vec, src/inference.c:218-225)
 void softmax_vec(float *v, int n) {
     float mx = v[0];
@@ -175,9 +188,7 @@ extern "C" void inference_step(const llmc_Model *m, llmc_InferenceState *s, int 
             float *oh = s->head_out + (size_t)qh * hd;
             for (int j = 0; j <= pos; j++) {
                 const float *kj = kvc->K + (size_t)j * kv_dim + (size_t)kvh * hd;
-                float dot = 0.0f;
-                for (int i = 0; i < hd; i++) dot += qv[i] * kj[i];
-                s->attn_buf[j] = dot * scale;
+                s->attn_buf[j] = dot8(qv, kj, hd) * scale;
             }
             softmax_vec(s->attn_buf, pos + 1);
             for (int j = 0; j <= pos; j++) {
