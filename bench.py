@@ -363,6 +363,8 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=6.0,
                     help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cta-pair", action="store_true",
+                    help="TF32 path on the CTA-pair (cta_group::2) GEMM kernels")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     c = CONFIGS[args.config]
@@ -427,7 +429,7 @@ def main():
         if ep is None:
             M.moe_forward_device(w, x.data_ptr(), Tl, out.data_ptr(), probs.data_ptr(),
                                  ids.data_ptr(), bias_ptr=bptr, path=path,
-                                 stream=stream.cuda_stream)
+                                 stream=stream.cuda_stream, cta_pair=args.cta_pair)
         else:
             ep.forward_device(x.data_ptr(), Tl, out.data_ptr(), probs.data_ptr(), ids.data_ptr(),
                               bias_ptr=bptr, path=path, stream=stream.cuda_stream)
@@ -486,7 +488,7 @@ def main():
     def e2e_step():
         if ep is None:
             M.moe_forward_host_ptr(w, hx.data_ptr(), Tl, hout.data_ptr(), hprobs.data_ptr(),
-                                   hids.data_ptr(), hb, path=path)
+                                   hids.data_ptr(), hb, path=path, cta_pair=args.cta_pair)
         else:
             ep.forward_host_ptr(hx.data_ptr(), Tl, hout.data_ptr(), hprobs.data_ptr(),
                                 hids.data_ptr(), hb, path=path)

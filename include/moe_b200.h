@@ -48,7 +48,12 @@ extern "C" {
 
 typedef struct {
     int path;            /* MOE_B200_PATH_*                                   */
-    int reserved[7];     /* zero                                              */
+    int cta_pair;        /* TF32 path only: 0 = single-SM GEMMs (128-row
+                            tiles; fastest measured at the 1000 W power cap),
+                            1 = CTA-pair GEMMs (tcgen05 cta_group::2, 256x256
+                            tiles over two SMs; down only when d is padded
+                            to a multiple of 256)                            */
+    int reserved[6];     /* zero                                              */
 } moe_b200_opts;
 
 /* Opaque device-resident expert set (router + E SwiGLU experts). */
@@ -168,6 +173,12 @@ int moe_b200_last_counts(const moe_b200_weights *w, int *counts);
 
 /* Number of kernel launches the last forward issued on this device. */
 int moe_b200_last_launches(void);
+
+/* SM count of `device` (-1 = current) and the number of CTA pairs (two-SM
+ * clusters) of the TF32 pair GEMM that can be resident at once; either
+ * output may be NULL.  No counterpart in llm.c (a diagnostic of this
+ * library's launch sizing). */
+int moe_b200_device_info(int device, int *num_sms, int *cta_pairs);
 
 /* ---- expert parallel (one process per GPU, NVLink) --------------------- */
 /* llm.c has no multi-GPU path (README.md:379 lists it as a roadmap item);

@@ -112,7 +112,7 @@ __host__ __device__ inline void ep_partition(const int *C, int G, int E, int ran
     }
 }
 
-// One thread: this rank's slice plan (cnt | off | mt128 | mt64), the global
+// One thread: this rank's slice plan (cnt | off | mt128 | mt64 | mt256), the global
 // base of this rank's rows per expert, and the slice boundaries.
 __global__ void ep_plan_kernel(const int *__restrict__ counts_all, int G, int E, int rank,
                                long long capacity, int *__restrict__ plan,
@@ -120,16 +120,18 @@ __global__ void ep_plan_kernel(const int *__restrict__ counts_all, int G, int E,
 {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     int *cnt = plan, *off = plan + E, *mt128 = off + E + 1, *mt64 = mt128 + E + 1;
+    int *mt256 = mt64 + E + 1;
     long long S[65];
     ep_partition(counts_all, G, E, rank, capacity, cnt, base_r, S);
-    int o = 0, m1 = 0, m2 = 0;
+    int o = 0, m1 = 0, m2 = 0, m3 = 0;
     for (int e = 0; e < E; e++) {
-        off[e] = o; mt128[e] = m1; mt64[e] = m2;
+        off[e] = o; mt128[e] = m1; mt64[e] = m2; mt256[e] = m3;
         o += cnt[e];
         m1 += (cnt[e] + 127) / 128;
         m2 += (cnt[e] + 63) / 64;
+        m3 += (cnt[e] + 255) / 256;
     }
-    off[E] = o; mt128[E] = m1; mt64[E] = m2;
+    off[E] = o; mt128[E] = m1; mt64[E] = m2; mt256[E] = m3;
     for (int q = 0; q <= G; q++) slices[q] = (int)S[q];
 }
 

@@ -7,8 +7,10 @@ namespace moe {
 
 constexpr int kRouterTile = 64;   // tokens per router CTA (dispatch tile granularity)
 
-// Plan (ints, device): cnt[E] | off[E+1] | mt128[E+1] | mt64[E+1]
-__host__ __device__ inline int plan_ints(int E) { return E + 3 * (E + 1); }
+// Plan (ints, device): cnt[E] | off[E+1] | mt128[E+1] | mt64[E+1] | mt256[E+1]
+// (mtN = prefix over experts of ceil(cnt/N): the N-row m-tiles the grouped
+// GEMMs schedule on)
+__host__ __device__ inline int plan_ints(int E) { return E + 4 * (E + 1); }
 
 // part/nsplit: optional [nsplit × T × E] buffer for the split-K variant used
 // when T is too small to fill the GPU (router_splits gives nsplit)
@@ -51,6 +53,18 @@ cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float 
                            int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s,
                            float *const *y_ptrs = nullptr, const int2 *ret = nullptr);
 cudaError_t tc_set_attributes();
+// The same GEMMs on CTA pairs (tcgen05 cta_group::2): 256×256 output tiles
+// scheduled on mt256; tmB has box {32, 128} (each CTA loads half of the
+// weight tile).  Down needs d_pad % 256 == 0.
+cudaError_t launch_tc2_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, const int *plan,
+                              int E, int rows_bound, int max_pairs, DeviceStatus *status,
+                              cudaStream_t s);
+cudaError_t launch_tc2_down(const TcGemm &g, int F_pad, int d_pad, float *y, const int *plan,
+                            int E, int rows_bound, int max_pairs, DeviceStatus *status,
+                            cudaStream_t s, float *const *y_ptrs = nullptr,
+                            const int2 *ret = nullptr);
+cudaError_t tc2_set_attributes();
+int tc2_max_pairs(int num_sms);
 
 // 3xTF32 weight-streaming GEMMs for decode-sized expert groups
 struct DecMaps {

@@ -103,6 +103,7 @@ static int grow(Buf &b, size_t bytes) {
 struct Ctx {
     int device = -1;
     int num_sms = 0;
+    int tc2_pairs = 0;                   // co-resident CTA pairs of the 2-SM GEMM
     int cc_major = 0, cc_minor = 0;
     cudaStream_t stream = nullptr;
     DeviceStatus *status = nullptr;      // device
@@ -158,6 +159,8 @@ static int get_ctx(int device, Ctx **out) {
         CK(cudaMemset(c->status, 0, sizeof(DeviceStatus)));
         CK(tc_set_attributes());
         CK(dec_set_attributes());
+        CK(tc2_set_attributes());
+        c->tc2_pairs = tc2_max_pairs(c->num_sms);
         c->attrs_set = true;
         g_ctx[device] = c;
     }
@@ -252,6 +255,7 @@ static int weights_alloc(Ctx *c, int d, int F, int E, int k, moe_b200_weights **
     if (rc == 0) rc = make_tmap(&w->tm_dn, w->dn, (int64_t)E * w->d_pad, w->F_pad, w->down_bn);
     if (rc == 0) rc = make_tmap(&w->tm_ug64, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 64);
     if (rc == 0) rc = make_tmap(&w->tm_dn128, w->dn, (int64_t)E * w->d_pad, w->F_pad, 128);
+    if (rc == 0) rc = make_tmap(&w->tm_ug128, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 128);
     if (rc) {
         cudaFree(w->router); cudaFree(w->ug); cudaFree(w->dn);
         delete w;
@@ -481,14 +485,28 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
     MARK(2);
     if (path == MOE_B200_PATH_TF32) {
         TcGemm up, dn;
+        const bool pair = opts && opts->cta_pair && c->tc2_pairs > 0;
         if ((rc = make_tmap(&up.tmA, x_perm, rows, w->d_pad, 128))) return rc;
-        up.tmB = w->tm_ug;
         if ((rc = make_tmap(&dn.tmA, h, rows, w->F_pad, 128))) return rc;
-        dn.tmB = w->tm_dn;
-        CK(launch_tc_upgate(up, w->d_pad, w->F_pad, h, plan, E, rows, c->num_sms, c->status, s));
+        if (pair) {
+            up.tmB = w->tm_ug128;
+            CK(launch_tc2_upgate(up, w->d_pad, w->F_pad, h, plan, E, rows, c->tc2_pairs,
+                                 c->status, s));
+        } else {
+            up.tmB = w->tm_ug;
+            CK(launch_tc_upgate(up, w->d_pad, w->F_pad, h, plan, E, rows, c->num_sms, c->status,
+                                s));
+        }
         MARK(3);
-        CK(launch_tc_down(dn, w->F_pad, w->d_pad, w->down_bn, y, plan, E, rows, c->num_sms,
-                          c->status, s));
+        if (pair && w->d_pad % 256 == 0) {
+            dn.tmB = w->tm_dn128;
+            CK(launch_tc2_down(dn, w->F_pad, w->d_pad, y, plan, E, rows, c->tc2_pairs, c->status,
+                               s));
+        } else {
+            dn.tmB = w->tm_dn;
+            CK(launch_tc_down(dn, w->F_pad, w->d_pad, w->down_bn, y, plan, E, rows, c->num_sms,
+                              c->status, s));
+        }
     } else if (path == MOE_B200_PATH_TF32X3) {
         if ((rc = grow(c->xs, (size_t)rows * w->d_pad * 4))) return rc;
         if ((rc = grow(c->hs, (size_t)rows * w->F_pad * 4))) return rc;
@@ -617,6 +635,15 @@ void moe::note_forward(int device, int E, int launches) {
     if (get_ctx(device, &c)) return;
     c->last_E = E;
     c->last_launches = launches;
+}
+
+extern "C" int moe_b200_device_info(int device, int *num_sms, int *cta_pairs) {
+    Ctx *c;
+    int rc = get_ctx(device, &c);
+    if (rc) return rc;
+    if (num_sms) *num_sms = c->num_sms;
+    if (cta_pairs) *cta_pairs = c->tc2_pairs;
+    return MOE_B200_OK;
 }
 
 int moe::device_sms(int device) {

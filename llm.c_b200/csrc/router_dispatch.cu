@@ -11,7 +11,7 @@ namespace moe {
 // K4a  dispatch_scan — one CTA.  For every expert: exclusive prefix of
 // the tile histograms (tile_pref), total count, expert row offset in the
 // permuted buffer, and the m-tile prefixes the grouped GEMMs schedule on.
-// Plan layout (ints): cnt[E] | off[E+1] | mt128[E+1] | mt64[E+1]
+// Plan layout (ints): cnt[E] | off[E+1] | mt128[E+1] | mt64[E+1] | mt256[E+1]
 // ---------------------------------------------------------------------
 __global__ void __launch_bounds__(1024)
 dispatch_scan_kernel(const int *__restrict__ tile_cnt, int n_tiles, int E,
@@ -39,15 +39,17 @@ dispatch_scan_kernel(const int *__restrict__ tile_cnt, int n_tiles, int E,
     __syncthreads();
     if (threadIdx.x == 0) {
         int *cnt = plan, *off = plan + E, *mt128 = off + E + 1, *mt64 = mt128 + E + 1;
-        int o = 0, m1 = 0, m2 = 0;
+        int *mt256 = mt64 + E + 1;
+        int o = 0, m1 = 0, m2 = 0, m3 = 0;
         for (int e = 0; e < E; e++) {
             cnt[e] = cnt_s[e];
-            off[e] = o; mt128[e] = m1; mt64[e] = m2;
+            off[e] = o; mt128[e] = m1; mt64[e] = m2; mt256[e] = m3;
             o += cnt_s[e];
             m1 += (cnt_s[e] + 127) / 128;
             m2 += (cnt_s[e] + 63) / 64;
+            m3 += (cnt_s[e] + 255) / 256;
         }
-        off[E] = o; mt128[E] = m1; mt64[E] = m2;
+        off[E] = o; mt128[E] = m1; mt64[E] = m2; mt256[E] = m3;
     }
 }
 

@@ -14,6 +14,7 @@ struct moe_b200_weights {
     CUtensorMap tm_dn;        // box {32, 256 or 128}
     CUtensorMap tm_ug64;      // box {32, 64}: decode up/gate (64 gate + 64 up rows)
     CUtensorMap tm_dn128;     // box {32, 128}: decode down
+    CUtensorMap tm_ug128;     // box {32, 128}: CTA-pair up/gate (one 128-row gate or up block per CTA)
     int down_bn;
 };
 

@@ -42,7 +42,7 @@ _vp = C.c_void_p
 
 
 class Opts(C.Structure):
-    _fields_ = [("path", C.c_int), ("reserved", C.c_int * 7)]
+    _fields_ = [("path", C.c_int), ("cta_pair", C.c_int), ("reserved", C.c_int * 6)]
 
 
 _lib = None
@@ -107,9 +107,10 @@ def _i(a):
     return a.ctypes.data_as(_ip)
 
 
-def _opts(path: int) -> Opts:
+def _opts(path: int, cta_pair: bool = False) -> Opts:
     o = Opts()
     o.path = path
+    o.cta_pair = int(bool(cta_pair))
     return o
 
 
@@ -181,7 +182,7 @@ class MoEWeights:
 
 
 def moe_forward(w: MoEWeights, x: np.ndarray, bias: np.ndarray | None = None,
-                path: int = PATH_AUTO):
+                path: int = PATH_AUTO, cta_pair: bool = False):
     """Host-buffer forward (synchronous): returns (out [T×d], probs [T×E], ids [T×k])."""
     x = np.ascontiguousarray(x, np.float32)
     T = x.shape[0]
@@ -189,7 +190,7 @@ def moe_forward(w: MoEWeights, x: np.ndarray, bias: np.ndarray | None = None,
     probs = np.empty((T, w.E), np.float32)
     ids = np.empty((T, w.top_k), np.int32)
     b = None if bias is None else np.ascontiguousarray(bias, np.float32)
-    o = _opts(path)
+    o = _opts(path, cta_pair)
     _check(lib().moe_b200_forward(w.handle, _f(b), _f(x), T, _f(out), _f(probs), _i(ids),
                                   C.byref(o)), "moe_b200_forward")
     return out, probs, ids
@@ -197,9 +198,9 @@ def moe_forward(w: MoEWeights, x: np.ndarray, bias: np.ndarray | None = None,
 
 def moe_forward_host_ptr(w: MoEWeights, x_ptr: int, T: int, out_ptr: int, probs_ptr: int | None,
                          ids_ptr: int | None, bias_ptr: int | None = None,
-                         path: int = PATH_AUTO):
+                         path: int = PATH_AUTO, cta_pair: bool = False):
     """Host-buffer forward from raw host pointers (e.g. pinned torch tensors)."""
-    o = _opts(path)
+    o = _opts(path, cta_pair)
     _check(lib().moe_b200_forward(w.handle, C.cast(bias_ptr, _fp) if bias_ptr else None,
                                   C.cast(x_ptr, _fp), T, C.cast(out_ptr, _fp),
                                   C.cast(probs_ptr, _fp) if probs_ptr else None,
@@ -210,9 +211,9 @@ def moe_forward_host_ptr(w: MoEWeights, x_ptr: int, T: int, out_ptr: int, probs_
 def moe_forward_device(w: MoEWeights, x_ptr: int, T: int, out_ptr: int,
                        probs_ptr: int | None = None, ids_ptr: int | None = None,
                        bias_ptr: int | None = None, path: int = PATH_AUTO,
-                       stream: int | None = None):
+                       stream: int | None = None, cta_pair: bool = False):
     """Device-buffer forward, asynchronous on `stream` (a cudaStream_t as int)."""
-    o = _opts(path)
+    o = _opts(path, cta_pair)
     _check(lib().moe_b200_forward_device(w.handle, bias_ptr, x_ptr, T, out_ptr, probs_ptr,
                                          ids_ptr, C.byref(o), stream), "moe_b200_forward_device")
 
@@ -310,6 +311,13 @@ STAGES = ("router", "dispatch", "upgate", "down", "combine")
 
 def profile_enable(on: bool = True):
     _check(lib().moe_b200_profile_enable(1 if on else 0), "moe_b200_profile_enable")
+
+
+def device_info(device: int = -1):
+    """(SM count, co-resident CTA pairs of the TF32 pair GEMM) of a device."""
+    n, pairs = C.c_int(), C.c_int()
+    _check(lib().moe_b200_device_info(device, C.byref(n), C.byref(pairs)), "moe_b200_device_info")
+    return int(n.value), int(pairs.value)
 
 
 def profile_read():
