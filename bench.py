@@ -365,9 +365,18 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cta-pair", action="store_true",
                     help="TF32 path on the CTA-pair (cta_group::2) GEMM kernels")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="override T (small profiling cases; the JSON config records it)")
+    ap.add_argument("--d-ff", type=int, default=None,
+                    help="override d_ff (profiling cases for the router, dispatch and combine "
+                         "kernels, which do not depend on it)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    c = CONFIGS[args.config]
+    c = dict(CONFIGS[args.config])
+    if args.tokens:
+        c["T"] = args.tokens
+    if args.d_ff:
+        c["F"] = args.d_ff
 
     if args.config == "c2":
         run_decode(args)
@@ -533,7 +542,8 @@ def main():
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": args.config, "T": T, "d_model": d, "n_experts": E, "top_k": k,
+        "config": {"workload": args.config + ("-profile" if (args.tokens or args.d_ff) else ""),
+                   "T": T, "d_model": d, "n_experts": E, "top_k": k,
                    "d_ff": F, "router_bias": c["bias"], "path": args.path,
                    "parallelism": f"ep{world}" + (" (balanced slices, replicated weights)"
                                                   if world > 1 else ""),

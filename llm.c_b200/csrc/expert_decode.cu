@@ -20,22 +20,41 @@
 // relative).  Token operands arrive with their small part precomputed in
 // global memory (split kernel after the gather; the up/gate epilogue writes
 // H's small part); weight tiles get theirs from a converter warpgroup as
-// they land.  X_big and X_small sit back to back in shared memory, so one
-// N=128 MMA computes W·[X_big | X_small] and a second (N=64) adds
-// W_small·X_big into the first half: 2 MMAs per K step.
+// they land, written straight into tensor memory (one thread per weight
+// row, tcgen05.st), where the MMA takes it as its A operand.  X_big and
+// X_small sit back to back in shared memory, so one N=128 MMA computes
+// W·[X_big | X_small] and a second (N=64, A from TMEM) adds W_small·X_big
+// into the first half: 2 MMAs per 8-wide K slice.
 //
-// Warp roles (10 warps): 0 TMA producer, 1 TMEM allocator + MMA issuer,
-// 2-5 converter (weight tile -> big in place + small beside it, then a
-// proxy fence), 6-9 epilogue.  4-stage ring of 48 KB (W, W_small, X_big,
-// X_small).  The tensor core's own accumulation truncates, and over a long
-// K that alone costs ~1e-5, so each 32-wide K stage is multiplied into a
-// FRESH 128×64 TMEM partial (an 8-slot ring) and the epilogue warps add the
-// partials in registers with IEEE round-to-nearest — the long sum over K is
-// ordinary fp32 arithmetic, as on the FFMA path.  Up/gate
-// tiles hold 64 gate rows and the 64 matching up rows, so the SwiGLU runs
-// in the epilogue: the warps holding the up half hand their values to the
-// gate-half warps through shared memory, under an mbarrier pair.  Every
-// wait is bounded; a timeout aborts the CTA cleanly.
+// Pipelining.  Every tcgen05 instruction and every mbarrier wait costs the
+// waiting thread tens of cycles, and the single MMA-issuing thread is the
+// long pole: so it does one wait, the 8 MMAs and ONE commit per K step, in
+// a loop unrolled over the ring period so that every ring position and
+// descriptor offset is a constant.
+//   * One commit per step arrives on done[step % R]; every consumer of
+//     "the MMAs of step m have finished" (ring-slot reuse by the producers
+//     and the converter, partial ready for the epilogue) waits on that
+//     barrier at its own lag.  R is at least every ring depth, so no waiter
+//     can fall a whole phase behind (no parity aliasing).
+//   * The converter warps wait for everything else the step needs — the
+//     weight tile, the token tile, a free TMEM partial slot, a free W_small
+//     slot — convert, and signal ready[step % NS] once.
+// Loads have long latencies under load (~2 us from HBM for the weights,
+// ~0.7 us from L2 for the token rows), so the shared-memory rings are as
+// deep as fits: weights W 8 × 16 KB (own producer warp, up to 8 steps
+// ahead) and tokens X_big|X_small 4 × 16 KB (own producer warp).  W_small
+// lives in TMEM (8 slots of 32 columns), not in shared memory.
+// Warp roles (11 warps): 0 weight producer, 10 token producer, 1 TMEM
+// allocator + MMA issuer, 2-5 converter, 6-9 epilogue.  The tensor core's
+// own accumulation truncates, and over a long K that alone costs ~1e-5, so
+// each 32-wide K step is multiplied into a FRESH 128×128 TMEM partial (a
+// 2-slot ring) and the epilogue warps add the partials in registers with
+// IEEE round-to-nearest — the long sum over K is ordinary fp32 arithmetic,
+// as on the FFMA path.  Up/gate tiles hold 64 gate rows and the 64
+// matching up rows, so the SwiGLU runs in the epilogue: the warps holding
+// the up half hand their values to the gate-half warps through shared
+// memory, under an mbarrier pair.  Every wait is bounded; a timeout aborts
+// the CTA cleanly.
 #include "tc_common.cuh"
 
 namespace moe {
@@ -45,20 +64,32 @@ using namespace tc;
 
 constexpr int MW = 128;                 // weight rows per tile (MMA M)
 constexpr int NTOK = 64;                // tokens per tile (MMA N)
-constexpr int BK = 32;                  // K per stage (128 bytes of fp32)
-constexpr int STAGES = 4;
+constexpr int BK = 32;                  // K per step (128 bytes of fp32)
+constexpr int NW = 8;                   // weight ring stages
+constexpr int NX = 4;                   // token-operand ring stages
+constexpr int NS = 8;                   // W_small ring slots (TMEM, 32 columns each)
+constexpr int NSLOT = 2;                // TMEM ring of per-step partial products
+constexpr int R = 8;                    // done[] ring: >= NW, NX, NS, NSLOT
+static_assert(R >= NW && R >= NX && R >= NS && R >= NSLOT, "done ring too short");
+// the MMA loop is unrolled over R steps with every ring position a constant
+static_assert(NW == R && NS == R && R % NX == 0 && R % NSLOT == 0, "ring sizes");
 constexpr int A_BYTES = MW * BK * 4;    // 16 KB
 constexpr int B_BYTES = NTOK * BK * 4;  // 8 KB
-constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;   // W, W_small, X_big, X_small
-constexpr int kThreads = 320;
-constexpr int NSLOT = 4;                // TMEM ring of per-stage partial products
-constexpr int SLOT_COLS = 2 * NTOK;     // [W·X_big + W_small·X_big | W·X_small]
-constexpr uint32_t TMEM_COLS = NSLOT * SLOT_COLS;   // 512
+constexpr int X_BYTES = 2 * B_BYTES;    // X_big | X_small
+constexpr int kThreads = 352;
+// TMEM columns: partial slot s at s*128 ([W·X_big + W_small·X_big |
+// W·X_small]), then the W_small operand slots
+constexpr int SLOT_COLS = 2 * NTOK;
+constexpr uint32_t WS_COL0 = NSLOT * SLOT_COLS;
+constexpr uint32_t TMEM_COLS = 512;
+static_assert(WS_COL0 + NS * BK <= TMEM_COLS, "TMEM columns");
 constexpr int UPS_LD = NTOK + 1;        // padded row of the up hand-off buffer
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 64 * UPS_LD * 4 + 1024 + 512;
+constexpr int RING_BYTES = NW * A_BYTES + NX * X_BYTES;
+constexpr int SMEM_BYTES = RING_BYTES + 64 * UPS_LD * 4 + 1024 + 512;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 
 struct DecArgs {
-    const int *plan;        // cnt | off | mt128 | mt64 (token tiles of 64 use mt64)
+    const int *plan;        // cnt | off | mt128 | mt64 | mt256 (token tiles of 64 use mt64)
     int E;
     int num_kb;             // K / 32
     int NB;                 // weight blocks per expert (F_pad/64 or d_pad/128)
@@ -94,6 +125,23 @@ __device__ __forceinline__ DecTile dec_decode(int tile, const int *plan, int E, 
     return t;
 }
 
+// Position in a ring of N entries: index and the parity of its current use
+// (incremental: the hot loops do no division).
+template <int N>
+struct Ring {
+    int i = 0;
+    uint32_t ph = 0;
+    __device__ __forceinline__ void next() {
+        if (++i == N) { i = 0; ph ^= 1; }
+    }
+};
+
+// Wait until the MMAs of step m have finished (done[m % R], its (m / R)-th
+// phase).
+__device__ __forceinline__ bool wait_done(uint64_t *done, int m, volatile int *abort_flag) {
+    return mbar_wait(&done[m % R], (uint32_t)((m / R) & 1), abort_flag);
+}
+
 template <bool UPGATE>
 __global__ void __launch_bounds__(kThreads, 1)
 dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
@@ -104,25 +152,23 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~static_cast<uintptr_t>(1023));
-    float *ups = reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES);   // [64][UPS_LD]
+    uint8_t *sW = smem;                                  // [NW][16 KB]
+    uint8_t *sX = sW + NW * A_BYTES;                     // [NX][X_big 8 KB | X_small 8 KB]
+    float *ups = reinterpret_cast<float *>(smem + RING_BYTES);   // [64][UPS_LD]
     uint64_t *bars = reinterpret_cast<uint64_t *>(ups + 64 * UPS_LD);
-    uint64_t *full = bars, *conv = bars + STAGES, *empty = bars + 2 * STAGES;
-    uint64_t *pfull = bars + 3 * STAGES, *pempty = pfull + NSLOT;
+    uint64_t *wfull = bars, *xfull = wfull + NW, *ready = xfull + NX, *done = ready + NS;
+    uint64_t *pempty = done + R;
     uint64_t *ups_ready = pempty + NSLOT, *ups_free = ups_ready + 1, *fin = ups_free + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&conv[s], 128);
-            mbar_init(&empty[s], 1);
-        }
-        for (int i = 0; i < NSLOT; i++) {
-            mbar_init(&pfull[i], 1);
-            mbar_init(&pempty[i], 128);
-        }
+        for (int s = 0; s < NW; s++) mbar_init(&wfull[s], 1);
+        for (int s = 0; s < NX; s++) mbar_init(&xfull[s], 1);
+        for (int s = 0; s < NS; s++) mbar_init(&ready[s], 128);
+        for (int s = 0; s < R; s++) mbar_init(&done[s], 1);
+        for (int s = 0; s < NSLOT; s++) mbar_init(&pempty[s], 128);
         mbar_init(ups_ready, 64);
         mbar_init(ups_free, 64);
         mbar_init(fin, 1);
@@ -140,8 +186,11 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
     const uint32_t tmem_base = *tmem_slot;
 
     const int total = __ldg(a.plan + a.E + 2 * (a.E + 1) + a.E) * a.NB;   // mt64[E] * NB
+    // this CTA's tiles are blockIdx.x, blockIdx.x + gridDim.x, ...; K steps
+    // are numbered across them
+    const int my_tiles = blockIdx.x < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int nsteps = my_tiles * a.num_kb;
 
-    auto stage_ptr = [&](int s) { return smem + s * STAGE_BYTES; };
     auto set_abort = [&](int site) {
         if (!*abort_flag) {
             *abort_flag = 1;
@@ -149,14 +198,13 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
         }
     };
 
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
+    if (warp == 0 || warp == 10) {
+        // ---------------- TMA producers: weights (warp 0), tokens (warp 10) ----------------
         if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            int issued[STAGES];
-            uint32_t issued_phase[STAGES];
-            for (int s = 0; s < STAGES; s++) issued[s] = 0;
+            const bool weights = warp == 0;
+            const int depth = weights ? NW : NX;
+            uint64_t *full = weights ? wfull : xfull;
+            int n = 0;                                   // K step
             bool ok = true;
             for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
                 const DecTile t = dec_decode(tile, a.plan, a.E, a.NB);
@@ -168,54 +216,65 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                 } else {
                     wrow = t.e * a.w_rows_per_expert + t.nb * MW;
                 }
-                for (int kb = 0; kb < a.num_kb; kb++) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
-                    uint8_t *sp = stage_ptr(stage);
-                    mbar_expect_tx(&full[stage], A_BYTES + 2 * B_BYTES);
-                    if (UPGATE) {
-                        tma_load_2d(sp, &tmW, kb * BK, wrow, &full[stage]);
-                        tma_load_2d(sp + A_BYTES / 2, &tmW, kb * BK, wrow2, &full[stage]);
+                for (int kb = 0; kb < a.num_kb; kb++, n++) {
+                    // the stage's previous contents (step n - depth) are consumed
+                    if (n >= depth && !wait_done(done, n - depth, abort_flag)) { ok = false; break; }
+                    const int st = n % depth;
+                    if (weights) {
+                        uint8_t *dst = sW + st * A_BYTES;
+                        mbar_expect_tx(&full[st], A_BYTES);
+                        if (UPGATE) {
+                            tma_load_2d(dst, &tmW, kb * BK, wrow, &full[st]);
+                            tma_load_2d(dst + A_BYTES / 2, &tmW, kb * BK, wrow2, &full[st]);
+                        } else {
+                            tma_load_2d(dst, &tmW, kb * BK, wrow, &full[st]);
+                        }
                     } else {
-                        tma_load_2d(sp, &tmW, kb * BK, wrow, &full[stage]);
+                        uint8_t *dst = sX + st * X_BYTES;
+                        mbar_expect_tx(&full[st], X_BYTES);
+                        tma_load_2d(dst, &tmXb, kb * BK, t.row0, &full[st]);
+                        tma_load_2d(dst + B_BYTES, &tmXs, kb * BK, t.row0, &full[st]);
                     }
-                    tma_load_2d(sp + 2 * A_BYTES, &tmXb, kb * BK, t.row0, &full[stage]);
-                    tma_load_2d(sp + 2 * A_BYTES + B_BYTES, &tmXs, kb * BK, t.row0, &full[stage]);
-                    issued[stage] = 1;
-                    issued_phase[stage] = phase;
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
             }
-            if (!ok) set_abort(11);
-            if (*abort_flag)
-                for (int s = 0; s < STAGES; s++)
-                    if (issued[s]) mbar_wait(&full[s], issued_phase[s], nullptr);
+            if (!ok) set_abort(weights ? 11 : 17);
+            if (*abort_flag) {
+                // loads still in flight (the last `depth` steps issued) land
+                // before the CTA winds down
+                for (int m = n - 1; m >= 0 && m >= n - depth; m--)
+                    mbar_wait(&full[m % depth], (uint32_t)((m / depth) & 1), nullptr);
+            }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+        // ---------------- MMA issuer: one wait, 8 MMAs, one commit per step ----------------
         if (lane == 0) {
-            int stage = 0, slot = 0;
-            uint32_t phase = 0, sphase = 0;
+            // descriptors of ring entry 0; entry j is +j*(bytes >> 4) in the
+            // start-address field, and +2 there is the next 8-wide K slice
+            const uint64_t dw0 = sw128_desc(smem_u32(sW));
+            const uint64_t dx0 = sw128_desc(smem_u32(sX));   // X_small follows X_big
+            const uint32_t ts0 = tmem_base + WS_COL0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-                for (int kb = 0; kb < a.num_kb; kb++) {
-                    if (!mbar_wait(&conv[stage], phase, abort_flag)) { ok = false; break; }
-                    if (!mbar_wait(&pempty[slot], sphase ^ 1, abort_flag)) { ok = false; break; }
+            uint32_t ph = 0;                      // parity of ready[] in this round of R steps
+            for (int n0 = 0; n0 < nsteps && ok; n0 += R, ph ^= 1) {
+#pragma unroll
+                for (int j = 0; j < R; j++) {
+                    if (n0 + j >= nsteps) break;
+                    // ready: W_small written, and (checked by the converter)
+                    // the weight and token tiles landed, the TMEM slot free.
+                    if (!mbar_wait(&ready[j], ph, abort_flag)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t d = tmem_base + (uint32_t)(slot * SLOT_COLS);
-                    const uint32_t w = smem_u32(stage_ptr(stage));
-                    const uint32_t ws = w + A_BYTES, xb = w + 2 * A_BYTES;   // X_small follows X_big
+                    const uint32_t d = tmem_base + (uint32_t)((j % NSLOT) * SLOT_COLS);
+                    const uint64_t dw = dw0 + (uint64_t)(j * (A_BYTES >> 4));
+                    const uint64_t dx = dx0 + (uint64_t)((j % NX) * (X_BYTES >> 4));
+                    const uint32_t ts = ts0 + (uint32_t)(j * BK);
 #pragma unroll
                     for (int kk = 0; kk < BK / 8; kk++) {
-                        const uint32_t o = kk * 32;
                         // cols 0..63: W·X_big, cols 64..127: W·X_small (X_big|X_small as one 128-row B)
-                        mma_tf32(d, sw128_desc(w + o), sw128_desc(xb + o), IDESC_N128, kk ? 1u : 0u);
-                        // cols 0..63 += W_small·X_big
-                        mma_tf32(d, sw128_desc(ws + o), sw128_desc(xb + o), IDESC_N64, 1u);
+                        mma_tf32(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
+                        // cols 0..63 += W_small·X_big (A: 8 columns of W_small in TMEM)
+                        mma_tf32_ts(d, ts + 8 * kk, dx + 2 * kk, IDESC_N64, 1u);
                     }
-                    mma_commit(&empty[stage]);     // smem stage free once these finish
-                    mma_commit(&pfull[slot]);      // partial ready for the epilogue
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
-                    if (++slot == NSLOT) { slot = 0; sphase ^= 1; }
+                    mma_commit(&done[j]);
                 }
             }
             if (!ok) set_abort(12);
@@ -224,54 +283,75 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
         }
     } else if (warp < 6) {
         // ---------------- converter (warps 2..5) ----------------
-        const int ct = threadIdx.x - 64;          // 0..127
-        int stage = 0;
-        uint32_t phase = 0;
+        // waits for what the step needs, W stage -> W_small slot, one
+        // arrive on ready.  Every warp needs the weight tile and the
+        // W_small slot; the token tile and the TMEM slot, which only the
+        // MMA needs, are vouched for by one warp each (their arrives on
+        // ready carry the acquire on to the MMA thread).
+        const int cw = warp - 2;                  // converter warp 0..3
+        const int crow = (warp & 3) * 32 + lane;  // weight row = TMEM lane this thread writes
+        const uint32_t ws_lane = tmem_base + ((uint32_t)((warp & 3) * 32) << 16);
+        Ring<NW> rw;
+        Ring<NS> rs;
+        Ring<NX> rx;
+        Ring<NSLOT> rp;
+        Ring<R> rlag;                             // step n - NS of the done ring
         bool ok = true;
-        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-            for (int kb = 0; kb < a.num_kb; kb++) {
-                if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
-                const float4 *w4 = reinterpret_cast<const float4 *>(stage_ptr(stage));
-                float4 *s4 = reinterpret_cast<float4 *>(stage_ptr(stage) + A_BYTES);
-#pragma unroll 4
-                for (int i = ct; i < A_BYTES / 16; i += 128) {
-                    const float4 v = w4[i];
-                    s4[i] = make_float4(tf32_residual(v.x), tf32_residual(v.y),
-                                        tf32_residual(v.z), tf32_residual(v.w));
-                }
-                fence_proxy_async_smem();   // st.shared -> visible to tcgen05.mma
-                mbar_arrive(&conv[stage]);
-                if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        for (int n = 0; n < nsteps; n++) {
+            if (!mbar_wait(&wfull[rw.i], rw.ph, abort_flag) ||
+                (cw == 2 && !mbar_wait(&xfull[rx.i], rx.ph, abort_flag)) ||
+                (cw == 3 && !mbar_wait(&pempty[rp.i], rp.ph ^ 1, abort_flag))) {
+                ok = false;
+                break;
             }
+            if (n >= NS) {                        // the W_small slot's last reader finished
+                if (!mbar_wait(&done[rlag.i], rlag.ph, abort_flag)) { ok = false; break; }
+                rlag.next();
+            }
+            // this thread's weight row: its 128 bytes, 16-byte chunks
+            // permuted by the 128-byte swizzle (chunk c sits at c ^ (row % 8))
+            const uint8_t *wrow = sW + rw.i * A_BYTES + crow * 128;
+            float ws[BK];
+#pragma unroll
+            for (int c = 0; c < BK / 4; c++) {
+                const float4 v = *reinterpret_cast<const float4 *>(wrow + ((c ^ (crow & 7)) << 4));
+                ws[4 * c + 0] = tf32_residual(v.x);
+                ws[4 * c + 1] = tf32_residual(v.y);
+                ws[4 * c + 2] = tf32_residual(v.z);
+                ws[4 * c + 3] = tf32_residual(v.w);
+            }
+            tmem_st32(ws_lane + WS_COL0 + (uint32_t)(rs.i * BK), ws);
+            tc_fence_before();
+            mbar_arrive(&ready[rs.i]);
+            rw.next(); rs.next(); rx.next(); rp.next();
         }
         if (!ok) set_abort(13);
     } else {
         // ---------------- epilogue (warps 6..9) ----------------
         const int q = warp & 3;                   // TMEM lane quarter
-        int slot = 0;
-        uint32_t sphase = 0, ups_phase = 0;
+        uint32_t ups_phase = 0;
         bool ok = true;
+        int n = 0;
+        const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
         for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
             const DecTile t = dec_decode(tile, a.plan, a.E, a.NB);
             float v[NTOK];
 #pragma unroll
             for (int j = 0; j < NTOK; j++) v[j] = 0.0f;
-            for (int kb = 0; kb < a.num_kb; kb++) {
-                if (!mbar_wait(&pfull[slot], sphase, abort_flag)) { set_abort(14); ok = false; break; }
+            for (int kb = 0; kb < a.num_kb; kb++, n++) {
+                if (!wait_done(done, n, abort_flag)) { set_abort(14); ok = false; break; }
                 tc_fence_after();
-                const uint32_t taddr =
-                    tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * SLOT_COLS);
+                const uint32_t taddr = lane_base + (uint32_t)((n % NSLOT) * SLOT_COLS);
 #pragma unroll
                 for (int c = 0; c < NTOK; c += 32) {
                     float pb[32], ps[32];
-                    tmem_ld32(taddr + c, pb);             // W·X_big + W_small·X_big
-                    tmem_ld32(taddr + NTOK + c, ps);      // W·X_small
+                    // W·X_big + W_small·X_big, and W·X_small
+                    tmem_ld32x2(taddr + c, taddr + NTOK + c, pb, ps);
 #pragma unroll
                     for (int j = 0; j < 32; j++) v[c + j] = __fadd_rn(v[c + j], __fadd_rn(pb[j], ps[j]));
                 }
                 tc_fence_before();
-                mbar_arrive(&pempty[slot]);
-                if (++slot == NSLOT) { slot = 0; sphase ^= 1; }
+                mbar_arrive(&pempty[n % NSLOT]);
             }
             if (!ok) break;
             if (UPGATE) {

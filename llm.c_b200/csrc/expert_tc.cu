@@ -127,9 +127,7 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            int issued[STAGES];
-            uint32_t issued_phase[STAGES];
-            for (int s = 0; s < STAGES; s++) issued[s] = 0;
+            uint32_t issued = 0, issued_phase = 0;    // bit s: stage s loaded / its phase
             bool ok = true;
             for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
                 const TileCoord c = decode_tile(tile, mt, E, NT);
@@ -140,8 +138,8 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
                     tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, a_row, &full[stage]);
                     tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, b_row, &full[stage]);
-                    issued[stage] = 1;
-                    issued_phase[stage] = phase;
+                    issued |= 1u << stage;
+                    issued_phase = (issued_phase & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) { stage = 0; phase ^= 1; }
                 }
             }
@@ -149,7 +147,7 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 if (!*abort_flag) { *abort_flag = 1; atomicExch(&status->timeout, 1); }
                 // drain TMA loads still in flight into this CTA's smem
                 for (int s = 0; s < STAGES; s++)
-                    if (issued[s]) mbar_wait(&full[s], issued_phase[s], nullptr);
+                    if ((issued >> s) & 1u) mbar_wait(&full[s], (issued_phase >> s) & 1u, nullptr);
             }
         }
     } else if (warp == 1) {
