@@ -460,6 +460,7 @@ def main():
         step()
     barrier()
     launches_per_step = M.last_launches()
+    path_used = M.last_path()
     if ep is None:
         counts = M.last_counts(w)
         slice_rows = Tl * k
@@ -521,15 +522,33 @@ def main():
     if dist is not None:
         stages_by_rank = [None] * world
         dist.all_gather_object(stages_by_rank, {"stages": stage_avg, "slice_rows": slice_rows})
-    up_flops = 4.0 * slice_rows * d * F          # this rank's slice of the global rows
     up_ms = stage_avg["upgate"]
-    achieved = up_flops / (up_ms / 1000.0) / 1e12
+    touched = int(np.count_nonzero(counts))
     traffic = None
     tfile = REPO / "profiles" / "traffic.json"
     if tfile.exists() and world == 1:
         tj = json.loads(tfile.read_text())
         traffic = tj.get(args.config, {}).get("upgate_bytes_per_launch")
-    touched = int(np.count_nonzero(counts))
+    if path_used == M.PATH_TF32:
+        # tensor-bound grouped GEMM: 2 GEMMs (gate, up) of this rank's rows
+        up_flops = 4.0 * slice_rows * d * F
+        achieved = up_flops / (up_ms / 1000.0) / 1e12
+        roof = {"bound": "tensor", "kernel": "tc_grouped_gemm<256,swiglu> (expert up/gate)",
+                "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+                "frac": achieved / tf32_peak, "traffic": traffic,
+                "peak_src": f"{peaks['src']} bf16 sustained / 2 (TF32 rate)"}
+    else:
+        # weight-streaming (3xTF32 / FP32 FFMA): HBM-bound on the gate and up
+        # weights of the experts this rank's rows touch (each read once);
+        # under expert parallelism a rank's slice covers about 1/world of them
+        w_bytes = 2.0 * d * F * 4 * touched / world
+        achieved = w_bytes / (up_ms / 1000.0) / 1e9
+        roof = {"bound": "hbm",
+                "kernel": ("dec_gemm<up/gate> (3xTF32 weight streaming)"
+                           if path_used == M.PATH_TF32X3 else "ffma_grouped<up/gate> (FP32)"),
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                "peak_src": peaks["src"] + " HBM copy bandwidth"}
     t_roof = max(flops_per_step(c) / (tf32_peak * 1e12 * world),
                  min_bytes_per_step(c, touched) / (peaks["hbm_gbs"] * 1e9 * world))
     if world > 1:
@@ -545,6 +564,8 @@ def main():
         "config": {"workload": args.config + ("-profile" if (args.tokens or args.d_ff) else ""),
                    "T": T, "d_model": d, "n_experts": E, "top_k": k,
                    "d_ff": F, "router_bias": c["bias"], "path": args.path,
+                   "path_run": {M.PATH_TF32: "tf32", M.PATH_FP32: "fp32",
+                                M.PATH_TF32X3: "tf32x3"}.get(path_used, "?"),
                    "parallelism": f"ep{world}" + (" (balanced slices, replicated weights)"
                                                   if world > 1 else ""),
                    "l2": "inputs larger than L2"
@@ -553,11 +574,7 @@ def main():
                 "h2d_bytes_per_step": 4 * T * d + (4 * E * world if bias is not None else 0),
                 "d2h_bytes_per_step": 4 * T * d + 4 * T * E + 4 * T * k,
                 "timing": "host wall clock around synchronous forward calls, max over ranks"},
-        "roofline": {"bound": "tensor", "kernel": "tc_grouped_gemm<256,swiglu> (expert up/gate)",
-                     "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
-                     "frac": achieved / tf32_peak, "traffic": traffic,
-                     "peak_src": f"{peaks['src']} bf16 sustained / 2 (TF32 rate)",
-                     "layer_frac": t_roof / (ms / 1000.0)},
+        "roofline": {**roof, "layer_frac": t_roof / (ms / 1000.0)},
         "stages_ms": stage_avg,
         "stages_ms_by_rank": stages_by_rank,
         "expert_counts_max_over_mean": float(counts.max() / counts.mean()),

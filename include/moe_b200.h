@@ -174,6 +174,10 @@ int moe_b200_last_counts(const moe_b200_weights *w, int *counts);
 /* Number of kernel launches the last forward issued on this device. */
 int moe_b200_last_launches(void);
 
+/* Expert arithmetic path (MOE_B200_PATH_TF32, _FP32 or _TF32X3) the last
+ * forward on this device ran, after AUTO was resolved; 0 before any. */
+int moe_b200_last_path(void);
+
 /* SM count of `device` (-1 = current) and the number of CTA pairs (two-SM
  * clusters) of the TF32 pair GEMM that can be resident at once; either
  * output may be NULL.  No counterpart in llm.c (a diagnostic of this

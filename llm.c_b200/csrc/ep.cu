@@ -557,7 +557,8 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
     MARK(5);
 #undef MARK
     note_forward(ep->device, E,
-                 T > 0 ? 7 + (path == MOE_B200_PATH_TF32X3) + (router_splits(T, w->d) > 1) : 3);
+                 T > 0 ? 7 + (path == MOE_B200_PATH_TF32X3) + (router_splits(T, w->d) > 1) : 3,
+                 path);
     return MOE_B200_OK;
 }
 

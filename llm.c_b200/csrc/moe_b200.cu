@@ -115,6 +115,7 @@ struct Ctx {
     Buf io_x, io_out, io_bias;
     int last_E = 0;
     int last_launches = 0;
+    int last_path = 0;
     // stage timing: ring of event sets, folded into the sums when read or
     // when the ring wraps
     bool prof = false;
@@ -539,6 +540,7 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
 #undef MARK
     c->last_E = E;
     c->last_launches = launches;
+    c->last_path = path;
     return MOE_B200_OK;
 }
 
@@ -616,6 +618,12 @@ extern "C" int moe_b200_last_counts(const moe_b200_weights *w, int *counts) {
     return MOE_B200_OK;
 }
 
+extern "C" int moe_b200_last_path(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64 || !g_ctx[dev]) return 0;
+    return g_ctx[dev]->last_path;
+}
+
 extern "C" int moe_b200_last_launches(void) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64 || !g_ctx[dev]) return 0;
@@ -630,11 +638,12 @@ cudaEvent_t *moe::profile_events(int device) {
     return prof_slot(c);
 }
 
-void moe::note_forward(int device, int E, int launches) {
+void moe::note_forward(int device, int E, int launches, int path) {
     Ctx *c;
     if (get_ctx(device, &c)) return;
     c->last_E = E;
     c->last_launches = launches;
+    c->last_path = path;
 }
 
 extern "C" int moe_b200_device_info(int device, int *num_sms, int *cta_pairs) {

@@ -299,8 +299,19 @@ router_reduce_topk_kernel(const float *__restrict__ part, int nsplit, int T,
     for (int q = threadIdx.x; q < TT * E; q += 256) {
         const int r = q / E, e = q % E, t = t0 + r;
         if (t >= T) continue;
+        // splits summed in ascending order; their loads issued 8 at a time
+        const float *pp = part + (size_t)t * E + e;
+        const size_t stride = (size_t)T * E;
         float v = 0.0f;
-        for (int sp = 0; sp < nsplit; sp++) v = __fadd_rn(v, part[((size_t)sp * T + t) * E + e]);
+        int sp = 0;
+        for (; sp + 8 <= nsplit; sp += 8) {
+            float a[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) a[i] = __ldg(pp + (size_t)(sp + i) * stride);
+#pragma unroll
+            for (int i = 0; i < 8; i++) v = __fadd_rn(v, a[i]);
+        }
+        for (; sp < nsplit; sp++) v = __fadd_rn(v, __ldg(pp + (size_t)sp * stride));
         lg[r * (EB + 1) + e] = bias ? __fadd_rn(v, __ldg(bias + e)) : v;
     }
     __syncthreads();

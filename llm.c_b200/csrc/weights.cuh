@@ -26,7 +26,7 @@ __attribute__((visibility("hidden"))) int set_last_error(int code, const char *d
 // off): MOE_B200_NUM_STAGES + 1 events recorded between the stages.
 __attribute__((visibility("hidden"))) cudaEvent_t *profile_events(int device);
 // Record the expert count and kernel launches of the last forward.
-__attribute__((visibility("hidden"))) void note_forward(int device, int E, int launches);
+__attribute__((visibility("hidden"))) void note_forward(int device, int E, int launches, int path);
 // Number of SMs of `device` (0 if the device is unusable).
 __attribute__((visibility("hidden"))) int device_sms(int device);
 }  // namespace moe

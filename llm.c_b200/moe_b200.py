@@ -76,6 +76,7 @@ def lib() -> C.CDLL:
                                           C.POINTER(Opts), _vp]
     L.moe_b200_last_counts.argtypes = [_vp, _ip]
     L.moe_b200_last_launches.restype = C.c_int
+    L.moe_b200_last_path.restype = C.c_int
     L.moe_b200_profile_enable.argtypes = [C.c_int]
     L.moe_b200_profile_read.argtypes = [C.POINTER(C.c_double), _ip]
     L.moe_b200_synth_fill.argtypes = [_vp, C.c_size_t, C.c_uint64, C.c_uint64, C.c_uint64,
@@ -222,6 +223,11 @@ def last_counts(w: MoEWeights) -> np.ndarray:
     c = np.empty(w.E, np.int32)
     _check(lib().moe_b200_last_counts(w.handle, _i(c)), "moe_b200_last_counts")
     return c
+
+
+def last_path() -> int:
+    """MOE_B200_PATH_* the last forward on this device ran (AUTO resolved)."""
+    return int(lib().moe_b200_last_path())
 
 
 def last_launches() -> int:
