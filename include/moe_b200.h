@@ -48,11 +48,10 @@ extern "C" {
 
 typedef struct {
     int path;            /* MOE_B200_PATH_*                                   */
-    int cta_pair;        /* TF32 path only: 0 = single-SM GEMMs (128-row
-                            tiles; fastest measured at the 1000 W power cap),
-                            1 = CTA-pair GEMMs (tcgen05 cta_group::2, 256x256
-                            tiles over two SMs; down only when d is padded
-                            to a multiple of 256)                            */
+    int cta_pair;        /* tensor-core paths: 0 = single-SM kernels (the
+                            fastest measured), 1 = CTA-pair kernels (tcgen05
+                            cta_group::2, M=256 over two SMs; down only when
+                            d is padded to a multiple of 256)               */
     int reserved[6];     /* zero                                              */
 } moe_b200_opts;
 

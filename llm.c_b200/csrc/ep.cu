@@ -389,9 +389,11 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     ep->dup.tmW = w->tm_ug64;
     TRY(ep_tmap(&ep->dup.tmXb, ep->recv_x, RR, w->d_pad, 64));
     TRY(ep_tmap(&ep->dup.tmXs, ep->xs, RR, w->d_pad, 64));
+    ep->dup.tmXb32 = ep->dup.tmXb;       // CTA-pair map, unused by the single-CTA kernels
     ep->ddn.tmW = w->tm_dn128;
     TRY(ep_tmap(&ep->ddn.tmXb, ep->h, RR, w->F_pad, 64));
     TRY(ep_tmap(&ep->ddn.tmXs, ep->hs, RR, w->F_pad, 64));
+    ep->ddn.tmXb32 = ep->ddn.tmXb;
 
     // communicator
     ncclUniqueId id;
@@ -540,9 +542,9 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
         const int sms = device_sms(ep->device);
         EP_CK(launch_split_tf32(ep->recv_x, ep->xs, (size_t)rows * w->d_pad, s));
         EP_CK(launch_dec_upgate(ep->dup, w->d_pad, w->F_pad, ep->h, ep->hs, ep->plan_q, E, rows,
-                                sms, ep->status, s));
+                                sms, 0, ep->status, s));
         MARK(3);
-        EP_CK(launch_dec_down(ep->ddn, w->F_pad, w->d_pad, ep->y, ep->plan_q, E, rows, sms,
+        EP_CK(launch_dec_down(ep->ddn, w->F_pad, w->d_pad, ep->y, ep->plan_q, E, rows, sms, 0,
                               ep->status, s, ep->d_y_ptrs, ep->ret));
     } else {
         EP_CK(launch_ffma_upgate(ep->recv_x, w->d_pad, w->ug, w->F_pad, ep->h, ep->plan_q, E, rows,

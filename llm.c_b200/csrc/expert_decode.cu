@@ -142,18 +142,33 @@ __device__ __forceinline__ bool wait_done(uint64_t *done, int m, volatile int *a
     return mbar_wait(&done[m % R], (uint32_t)((m / R) & 1), abort_flag);
 }
 
-template <bool UPGATE>
+// PAIR: a 2-CTA cluster computes a 256-row weight block (128 rows per CTA)
+// with tcgen05 cta_group::2 MMAs (M=256) issued by the rank-0 CTA, so each
+// MMA instruction carries twice the weight bytes.  Each CTA streams its own
+// weight rows and writes its own W_small into its own TMEM; the token
+// operand B is split by columns between the CTAs (MMA1's N=128 =
+// [X_big | X_small]: X_big in rank 0, X_small in rank 1; MMA2's N=64 =
+// X_big: tokens 0..31 in rank 0, 32..63 in rank 1).  Both CTAs' converter
+// warps arrive on rank 0's ready barrier (cluster-scope release); rank 0's
+// single commit per step arrives on both CTAs' done rings (multicast
+// commit, not a load).
+template <bool UPGATE, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
 dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
-         const __grid_constant__ CUtensorMap tmXs, DecArgs a)
+         const __grid_constant__ CUtensorMap tmXs, const __grid_constant__ CUtensorMap tmXb32,
+         DecArgs a)
 {
-    constexpr uint32_t IDESC_N128 = idesc_tf32(MW, 2 * NTOK);
-    constexpr uint32_t IDESC_N64 = idesc_tf32(MW, NTOK);
+    constexpr int MM = PAIR ? 2 * MW : MW;                  // MMA M (weight rows per block)
+    constexpr uint32_t IDESC_N128 = idesc_tf32(MM, 2 * NTOK);
+    constexpr uint32_t IDESC_N64 = idesc_tf32(MM, NTOK);
+    // token stage: single [X_big 8 KB | X_small 8 KB]; pair [MMA1 half 8 KB | MMA2 half 4 KB]
+    constexpr int XB = PAIR ? B_BYTES + B_BYTES / 2 : X_BYTES;
+    constexpr int XB2 = PAIR ? B_BYTES : 0;                 // offset of MMA2's B in a stage
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                 ~static_cast<uintptr_t>(1023));
     uint8_t *sW = smem;                                  // [NW][16 KB]
-    uint8_t *sX = sW + NW * A_BYTES;                     // [NX][X_big 8 KB | X_small 8 KB]
+    uint8_t *sX = sW + NW * A_BYTES;                     // [NX][XB]
     float *ups = reinterpret_cast<float *>(smem + RING_BYTES);   // [64][UPS_LD]
     uint64_t *bars = reinterpret_cast<uint64_t *>(ups + 64 * UPS_LD);
     uint64_t *wfull = bars, *xfull = wfull + NW, *ready = xfull + NX, *done = ready + NS;
@@ -163,10 +178,13 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = PAIR ? cluster_rank() : 0;
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;     // CTA or CTA pair
+    const int nunits = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     if (threadIdx.x == 0) {
         for (int s = 0; s < NW; s++) mbar_init(&wfull[s], 1);
         for (int s = 0; s < NX; s++) mbar_init(&xfull[s], 1);
-        for (int s = 0; s < NS; s++) mbar_init(&ready[s], 128);
+        for (int s = 0; s < NS; s++) mbar_init(&ready[s], PAIR ? 256 : 128);
         for (int s = 0; s < R; s++) mbar_init(&done[s], 1);
         for (int s = 0; s < NSLOT; s++) mbar_init(&pempty[s], 128);
         mbar_init(ups_ready, 64);
@@ -177,18 +195,25 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmXb)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmXs)) : "memory");
+        if (PAIR)
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmXb32))
+                         : "memory");
     }
     __syncwarp();
-    if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
+    if (warp == 1) {
+        if (PAIR) tmem_alloc_pair(tmem_slot, TMEM_COLS);
+        else tmem_alloc(tmem_slot, TMEM_COLS);
+    }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();            // the peer's barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     const int total = __ldg(a.plan + a.E + 2 * (a.E + 1) + a.E) * a.NB;   // mt64[E] * NB
-    // this CTA's tiles are blockIdx.x, blockIdx.x + gridDim.x, ...; K steps
-    // are numbered across them
-    const int my_tiles = blockIdx.x < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    // this unit's tiles are unit, unit + nunits, ...; K steps are numbered
+    // across them
+    const int my_tiles = unit < total ? (total - 1 - unit) / nunits + 1 : 0;
     const int nsteps = my_tiles * a.num_kb;
 
     auto set_abort = [&](int site) {
@@ -206,15 +231,16 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
             uint64_t *full = weights ? wfull : xfull;
             int n = 0;                                   // K step
             bool ok = true;
-            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            for (int tile = unit; tile < total && ok; tile += nunits) {
                 const DecTile t = dec_decode(tile, a.plan, a.E, a.NB);
                 int wrow, wrow2 = 0;
                 if (UPGATE) {
-                    const int f0 = t.nb * 64;
+                    // this CTA's 64 gate rows f0.. (and, 128 rows on, the matching up rows)
+                    const int f0 = t.nb * (PAIR ? 128 : 64) + (int)rank * 64;
                     wrow = t.e * a.w_rows_per_expert + (f0 / 128) * 256 + (f0 % 128);
-                    wrow2 = wrow + 128;                   // the matching up rows
+                    wrow2 = wrow + 128;
                 } else {
-                    wrow = t.e * a.w_rows_per_expert + t.nb * MW;
+                    wrow = t.e * a.w_rows_per_expert + t.nb * MM + (int)rank * MW;
                 }
                 for (int kb = 0; kb < a.num_kb; kb++, n++) {
                     // the stage's previous contents (step n - depth) are consumed
@@ -229,11 +255,17 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                         } else {
                             tma_load_2d(dst, &tmW, kb * BK, wrow, &full[st]);
                         }
-                    } else {
-                        uint8_t *dst = sX + st * X_BYTES;
-                        mbar_expect_tx(&full[st], X_BYTES);
+                    } else if (!PAIR) {
+                        uint8_t *dst = sX + st * XB;
+                        mbar_expect_tx(&full[st], XB);
                         tma_load_2d(dst, &tmXb, kb * BK, t.row0, &full[st]);
                         tma_load_2d(dst + B_BYTES, &tmXs, kb * BK, t.row0, &full[st]);
+                    } else {
+                        // this CTA's column halves of the two B operands
+                        uint8_t *dst = sX + st * XB;
+                        mbar_expect_tx(&full[st], XB);
+                        tma_load_2d(dst, rank ? &tmXs : &tmXb, kb * BK, t.row0, &full[st]);
+                        tma_load_2d(dst + XB2, &tmXb32, kb * BK, t.row0 + (int)rank * 32, &full[st]);
                     }
                 }
             }
@@ -247,11 +279,11 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer: one wait, 8 MMAs, one commit per step ----------------
-        if (lane == 0) {
+        if (lane == 0 && rank == 0) {
             // descriptors of ring entry 0; entry j is +j*(bytes >> 4) in the
             // start-address field, and +2 there is the next 8-wide K slice
             const uint64_t dw0 = sw128_desc(smem_u32(sW));
-            const uint64_t dx0 = sw128_desc(smem_u32(sX));   // X_small follows X_big
+            const uint64_t dx0 = sw128_desc(smem_u32(sX));   // single: X_small follows X_big
             const uint32_t ts0 = tmem_base + WS_COL0;
             bool ok = true;
             uint32_t ph = 0;                      // parity of ready[] in this round of R steps
@@ -261,24 +293,36 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                     if (n0 + j >= nsteps) break;
                     // ready: W_small written, and (checked by the converter)
                     // the weight and token tiles landed, the TMEM slot free.
-                    if (!mbar_wait(&ready[j], ph, abort_flag)) { ok = false; break; }
+                    if (!(PAIR ? mbar_wait_cluster(&ready[j], ph, abort_flag)
+                               : mbar_wait(&ready[j], ph, abort_flag))) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t d = tmem_base + (uint32_t)((j % NSLOT) * SLOT_COLS);
                     const uint64_t dw = dw0 + (uint64_t)(j * (A_BYTES >> 4));
-                    const uint64_t dx = dx0 + (uint64_t)((j % NX) * (X_BYTES >> 4));
+                    const uint64_t dx = dx0 + (uint64_t)((j % NX) * (XB >> 4));
+                    const uint64_t dx2 = dx + (uint64_t)(XB2 >> 4);      // MMA2's B
                     const uint32_t ts = ts0 + (uint32_t)(j * BK);
 #pragma unroll
                     for (int kk = 0; kk < BK / 8; kk++) {
                         // cols 0..63: W·X_big, cols 64..127: W·X_small (X_big|X_small as one 128-row B)
-                        mma_tf32(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
-                        // cols 0..63 += W_small·X_big (A: 8 columns of W_small in TMEM)
-                        mma_tf32_ts(d, ts + 8 * kk, dx + 2 * kk, IDESC_N64, 1u);
+                        // then cols 0..63 += W_small·X_big (A: 8 columns of W_small in TMEM)
+                        if (PAIR) {
+                            mma_tf32_pair(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
+                            mma_tf32_ts_pair(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
+                        } else {
+                            mma_tf32(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
+                            mma_tf32_ts(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
+                        }
                     }
-                    mma_commit(&done[j]);
+                    if (PAIR) mma_commit_pair(&done[j]);
+                    else mma_commit(&done[j]);
                 }
             }
             if (!ok) set_abort(12);
-            mma_commit(fin);
+            if (PAIR) mma_commit_pair_local(fin);
+            else mma_commit(fin);
             mbar_wait(fin, 0, nullptr);
         }
     } else if (warp < 6) {
@@ -322,7 +366,8 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
             }
             tmem_st32(ws_lane + WS_COL0 + (uint32_t)(rs.i * BK), ws);
             tc_fence_before();
-            mbar_arrive(&ready[rs.i]);
+            if (PAIR) mbar_arrive_cluster(mapa(smem_u32(&ready[rs.i]), 0));
+            else mbar_arrive(&ready[rs.i]);
             rw.next(); rs.next(); rx.next(); rp.next();
         }
         if (!ok) set_abort(13);
@@ -333,7 +378,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
         bool ok = true;
         int n = 0;
         const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
-        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+        for (int tile = unit; tile < total && ok; tile += nunits) {
             const DecTile t = dec_decode(tile, a.plan, a.E, a.NB);
             float v[NTOK];
 #pragma unroll
@@ -364,7 +409,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                 } else {                           // gate rows: SwiGLU and store h split
                     const int f = q * 32 + lane;
                     if (!mbar_wait(ups_ready, ups_phase, abort_flag)) { set_abort(16); break; }
-                    const size_t col = (size_t)t.nb * 64 + f;
+                    const size_t col = (size_t)t.nb * (PAIR ? 128 : 64) + rank * 64 + f;
 #pragma unroll
                     for (int j = 0; j < NTOK; j++) {
                         if (j >= t.ntok) break;
@@ -377,7 +422,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                 }
                 ups_phase ^= 1;
             } else {
-                const int jcol = t.nb * MW + q * 32 + lane;   // output column of y
+                const int jcol = t.nb * MM + (int)rank * MW + q * 32 + lane;   // output column of y
 #pragma unroll
                 for (int j = 0; j < NTOK; j++) {
                     if (j >= t.ntok) break;
@@ -399,8 +444,12 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
     __syncwarp();
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();            // neither CTA leaves while the pair still works
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+    if (warp == 1) {
+        if (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+        else tmem_dealloc(tmem_base, TMEM_COLS);
+    }
 }
 
 // small = v - trunc_tf32(v) beside the unchanged v (the big part is v
@@ -419,12 +468,35 @@ __global__ void split_tf32_kernel(const float4 *__restrict__ big, float4 *__rest
 }  // namespace dec
 
 cudaError_t dec_set_attributes() {
-    cudaError_t e = cudaFuncSetAttribute(dec::dec_gemm<true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         dec::SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(dec::dec_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                dec::SMEM_BYTES);
+    const void *fns[4] = {(const void *)dec::dec_gemm<true, false>, (const void *)dec::dec_gemm<false, false>,
+                          (const void *)dec::dec_gemm<true, true>, (const void *)dec::dec_gemm<false, true>};
+    for (const void *f : fns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             dec::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+// CTA pairs of the decode kernel that can be resident at once (0 if none)
+int dec_max_pairs(int num_sms) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+    cfg.blockDim = dim3(dec::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = dec::SMEM_BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, dec::dec_gemm<true, true>, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n < num_sms / 2 ? n : num_sms / 2;
 }
 
 cudaError_t launch_split_tf32(float *big, float *small, size_t n, cudaStream_t s) {
@@ -435,35 +507,57 @@ cudaError_t launch_split_tf32(float *big, float *small, size_t n, cudaStream_t s
     return cudaGetLastError();
 }
 
-static int dec_grid(int rows_bound, int E, int NB, int num_sms) {
+// persistent units (CTAs, or CTA pairs) for a grid of (token tiles × NB) tiles
+static int dec_units(int rows_bound, int E, int NB, int cap) {
     const int bound = (ceil_div(rows_bound, dec::NTOK) + E) * NB;
-    return bound < num_sms ? (bound > 0 ? bound : 1) : num_sms;
+    return bound < cap ? (bound > 0 ? bound : 1) : cap;
+}
+
+template <bool UPGATE>
+static cudaError_t dec_launch(const DecMaps &m, const dec::DecArgs &a, int units, bool pair,
+                              cudaStream_t s) {
+    if (!pair) {
+        dec::dec_gemm<UPGATE, false><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
+            m.tmW, m.tmXb, m.tmXs, m.tmXb, a);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * units, 1, 1);
+    cfg.blockDim = dim3(dec::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = dec::SMEM_BYTES;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, dec::dec_gemm<UPGATE, true>, m.tmW, m.tmXb, m.tmXs, m.tmXb32, a);
 }
 
 cudaError_t launch_dec_upgate(const DecMaps &m, int d_pad, int F_pad, float *h_big, float *h_small,
-                              const int *plan, int E, int rows_bound, int num_sms,
+                              const int *plan, int E, int rows_bound, int num_sms, int max_pairs,
                               DeviceStatus *status, cudaStream_t s)
 {
+    const bool pair = max_pairs > 0;
     dec::DecArgs a{};
-    a.plan = plan; a.E = E; a.num_kb = d_pad / dec::BK; a.NB = F_pad / 64;
+    a.plan = plan; a.E = E; a.num_kb = d_pad / dec::BK; a.NB = F_pad / (pair ? 128 : 64);
     a.w_rows_per_expert = 2 * F_pad; a.h_big = h_big; a.h_small = h_small; a.ldh = F_pad;
     a.status = status;
-    dec::dec_gemm<true><<<dec_grid(rows_bound, E, a.NB, num_sms), dec::kThreads, dec::SMEM_BYTES, s>>>(
-        m.tmW, m.tmXb, m.tmXs, a);
-    return cudaGetLastError();
+    return dec_launch<true>(m, a, dec_units(rows_bound, E, a.NB, pair ? max_pairs : num_sms), pair, s);
 }
 
 cudaError_t launch_dec_down(const DecMaps &m, int F_pad, int d_pad, float *y, const int *plan,
-                            int E, int rows_bound, int num_sms, DeviceStatus *status,
+                            int E, int rows_bound, int num_sms, int max_pairs, DeviceStatus *status,
                             cudaStream_t s, float *const *y_ptrs, const int2 *ret)
 {
+    const bool pair = max_pairs > 0 && d_pad % (2 * dec::MW) == 0;
     dec::DecArgs a{};
-    a.plan = plan; a.E = E; a.num_kb = F_pad / dec::BK; a.NB = d_pad / dec::MW;
+    a.plan = plan; a.E = E; a.num_kb = F_pad / dec::BK; a.NB = d_pad / (pair ? 2 * dec::MW : dec::MW);
     a.w_rows_per_expert = d_pad; a.y = y; a.ldy = d_pad; a.y_ptrs = y_ptrs; a.ret = ret;
     a.status = status;
-    dec::dec_gemm<false><<<dec_grid(rows_bound, E, a.NB, num_sms), dec::kThreads, dec::SMEM_BYTES, s>>>(
-        m.tmW, m.tmXb, m.tmXs, a);
-    return cudaGetLastError();
+    return dec_launch<false>(m, a, dec_units(rows_bound, E, a.NB, pair ? max_pairs : num_sms), pair, s);
 }
 
 }  // namespace moe

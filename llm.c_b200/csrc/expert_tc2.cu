@@ -43,29 +43,6 @@ constexpr int EPI_FLOATS = 32 * 33;
 constexpr uint32_t TMEM_COLS = 2 * BN;   // two accumulator buffers
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 4 * EPI_FLOATS * 4 + 1024 + 256;
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-// shared::cluster address of the same shared-memory location in CTA `rank`
-__device__ __forceinline__ uint32_t mapa(uint32_t cta_addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(cta_addr), "r"(rank));
-    return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-                 : "memory");
-}
-
 // Load into this CTA's shared memory; the byte count completes on the
 // barrier at `mbar_cluster` (the rank-0 CTA's).
 __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, int x, int y,
@@ -75,29 +52,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m
         " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar_cluster)
         : "memory");
-}
-
-__device__ __forceinline__ void mma_tf32_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                              uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-
-// one arrive on `bar` (same offset) in both CTAs of the pair
-__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%0], %1;" ::"r"(smem_u32(bar)), "h"((uint16_t)0x3)
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_commit_local2(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_u32(bar))
-                 : "memory");
 }
 
 struct PairTile {
@@ -239,7 +193,7 @@ tc_grouped_gemm_pair(const __grid_constant__ CUtensorMap tmA, const __grid_const
                 if (acc == 0) acc_phase ^= 1;
             }
             if (!ok) set_abort(22);
-            mma_commit_local2(fin);
+            mma_commit_pair_local(fin);
             mbar_wait(fin, 0, nullptr);
         }
     } else {

@@ -71,14 +71,18 @@ struct DecMaps {
     CUtensorMap tmW;    // weights, box {32, 64} (up/gate) or {32, 128} (down)
     CUtensorMap tmXb;   // token operand big part  [rows × K], box {32, 64}
     CUtensorMap tmXs;   // token operand small part [rows × K], box {32, 64}
+    CUtensorMap tmXb32; // big part again, box {32, 32} (CTA-pair kernels)
 };
 cudaError_t dec_set_attributes();
+// max_pairs > 0: run on CTA pairs (M=256 per MMA), at most max_pairs of them
+// (down only when d_pad % 256 == 0); 0: single CTAs
+int dec_max_pairs(int num_sms);
 cudaError_t launch_split_tf32(float *big, float *small, size_t n, cudaStream_t s);
 cudaError_t launch_dec_upgate(const DecMaps &m, int d_pad, int F_pad, float *h_big, float *h_small,
-                              const int *plan, int E, int rows_bound, int num_sms,
+                              const int *plan, int E, int rows_bound, int num_sms, int max_pairs,
                               DeviceStatus *status, cudaStream_t s);
 cudaError_t launch_dec_down(const DecMaps &m, int F_pad, int d_pad, float *y, const int *plan,
-                            int E, int rows_bound, int num_sms, DeviceStatus *status,
+                            int E, int rows_bound, int num_sms, int max_pairs, DeviceStatus *status,
                             cudaStream_t s, float *const *y_ptrs = nullptr,
                             const int2 *ret = nullptr);
 

@@ -104,6 +104,7 @@ struct Ctx {
     int device = -1;
     int num_sms = 0;
     int tc2_pairs = 0;                   // co-resident CTA pairs of the 2-SM GEMM
+    int dec_pairs = 0;                   // co-resident CTA pairs of the 2-SM decode kernel
     int cc_major = 0, cc_minor = 0;
     cudaStream_t stream = nullptr;
     DeviceStatus *status = nullptr;      // device
@@ -162,6 +163,7 @@ static int get_ctx(int device, Ctx **out) {
         CK(dec_set_attributes());
         CK(tc2_set_attributes());
         c->tc2_pairs = tc2_max_pairs(c->num_sms);
+        c->dec_pairs = dec_max_pairs(c->num_sms);
         c->attrs_set = true;
         g_ctx[device] = c;
     }
@@ -516,14 +518,18 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
         up.tmW = w->tm_ug64;
         if ((rc = make_tmap(&up.tmXb, x_perm, rows, w->d_pad, 64))) return rc;
         if ((rc = make_tmap(&up.tmXs, xs, rows, w->d_pad, 64))) return rc;
+        if ((rc = make_tmap(&up.tmXb32, x_perm, rows, w->d_pad, 32))) return rc;
         dn.tmW = w->tm_dn128;
         if ((rc = make_tmap(&dn.tmXb, h, rows, w->F_pad, 64))) return rc;
         if ((rc = make_tmap(&dn.tmXs, hs, rows, w->F_pad, 64))) return rc;
+        if ((rc = make_tmap(&dn.tmXb32, h, rows, w->F_pad, 32))) return rc;
+        const int dpairs = (opts && opts->cta_pair) ? c->dec_pairs : 0;
         CK(launch_split_tf32(x_perm, xs, (size_t)rows * w->d_pad, s));
-        CK(launch_dec_upgate(up, w->d_pad, w->F_pad, h, hs, plan, E, rows, c->num_sms, c->status,
-                             s));
+        CK(launch_dec_upgate(up, w->d_pad, w->F_pad, h, hs, plan, E, rows, c->num_sms, dpairs,
+                             c->status, s));
         MARK(3);
-        CK(launch_dec_down(dn, w->F_pad, w->d_pad, y, plan, E, rows, c->num_sms, c->status, s));
+        CK(launch_dec_down(dn, w->F_pad, w->d_pad, y, plan, E, rows, c->num_sms, dpairs,
+                           c->status, s));
         launches += 1;   // the split
     } else if (path == MOE_B200_PATH_FP32) {
         CK(launch_ffma_upgate(x_perm, w->d_pad, w->ug, w->F_pad, h, plan, E, rows, s));

@@ -78,3 +78,41 @@ def test_pair_deterministic(moe):
     w.free()
     for u, v in zip(a, b):
         assert np.array_equal(u, v)
+
+
+# 3xTF32 decode-sized path on CTA pairs: the same products in the same order
+# as the single-CTA kernel, so the outputs agree to fp32 rounding; each is
+# checked against the oracle at the FP32-path tolerance.
+DEC_SHAPES = [
+    # T,   d,    E,  k,  F,    bias
+    (256, 512, 16, 4, 640, None),        # d_pad 512: down on pairs too; ~64 rows per expert
+    (96, 320, 8, 2, 384, "normal"),      # d_pad 384: down on single CTAs, up/gate on pairs
+    (1, 256, 8, 2, 512, None),           # one token
+    (700, 256, 64, 1, 256, None),        # ~11 rows per expert, many experts
+]
+
+
+@pytest.mark.parametrize("shape", DEC_SHAPES, ids=lambda s: f"T{s[0]}_d{s[1]}_E{s[2]}_k{s[3]}_F{s[4]}")
+def test_decode_pair_matches_single_and_oracle(moe, shape):
+    T, d, E, k, F, bias = shape
+    p = O.MoEProblem(T, d, E, k, F, seed=11, bias=bias)
+    w = _upload(p)
+    a_out, a_probs, a_ids = M.moe_forward(w, p.x, p.bias, path=M.PATH_TF32X3, cta_pair=True)
+    b_out, b_probs, b_ids = M.moe_forward(w, p.x, p.bias, path=M.PATH_TF32X3, cta_pair=False)
+    w.free()
+    assert np.array_equal(a_ids, b_ids) and np.array_equal(a_probs, b_probs)
+    assert O.rel_err(a_out, b_out) < 1e-6
+    rows = np.arange(T, dtype=np.int32) if T <= 64 else \
+        np.sort(np.random.default_rng(2).choice(T, 64, replace=False)).astype(np.int32)
+    want, _, _ = p.oracle_forward(rows=rows, forced_ids=a_ids)
+    assert O.rel_err(a_out[rows], want) < 1e-5
+
+
+def test_decode_pair_deterministic(moe):
+    p = O.MoEProblem(256, 512, 16, 4, 640, seed=5)
+    w = _upload(p)
+    a = M.moe_forward(w, p.x, path=M.PATH_TF32X3, cta_pair=True)
+    b = M.moe_forward(w, p.x, path=M.PATH_TF32X3, cta_pair=True)
+    w.free()
+    for u, v in zip(a, b):
+        assert np.array_equal(u, v)
