@@ -183,6 +183,36 @@ int moe_b200_last_path(void);
  * library's launch sizing). */
 int moe_b200_device_info(int device, int *num_sms, int *cta_pairs);
 
+/* ---- device-resident decode (llm.c's inference_step on the B200) ------- */
+/* Replaces llm.c's single-token KV-cache forward (src/inference.c:231-358,
+ * declared at include/inference.h:137) with a device-resident one, MoE
+ * blocks included (llm.c leaves them as a TODO at src/inference.c:342-343).
+ * `model` is an llm.c Model (include/llmc_moe.h, llmc_Model); every weight
+ * it holds, the RoPE tables and a KV cache of `max_seq` positions
+ * (max_seq <= the model's RoPE table length) are copied to the current
+ * device once.  Dense blocks (use_moe = 0) are supported.  The caller's
+ * Model is only read during create; later changes to it need a new decoder.
+ * A step appends `token` at the current position and writes the vocab
+ * logits to host memory (if `logits` is not NULL); the position advances
+ * like InferenceState.seq_pos.  Steps run as one CUDA graph.  Returns
+ * MOE_B200_E_TIMEOUT if a bounded device wait ran out.  No counterpart in
+ * llm.c beyond inference_step itself. */
+typedef struct moe_b200_decoder moe_b200_decoder;
+/* flags: 0 = the whole step as ONE persistent cooperative kernel (one CTA
+ * per SM, stages separated by a bounded grid-wide barrier);
+ * MOE_B200_DECODER_STAGE_KERNELS = one kernel per stage (31 for six
+ * layers), the same arithmetic. */
+#define MOE_B200_DECODER_STAGE_KERNELS 1
+int moe_b200_decoder_create(const void *model, int max_seq, int flags, moe_b200_decoder **dec);
+int moe_b200_decoder_step(moe_b200_decoder *dec, int token, float *logits);
+/* Rewind to position `pos` (<= the current one); later steps overwrite the
+ * cache from there. */
+int moe_b200_decoder_set_pos(moe_b200_decoder *dec, int pos);
+int moe_b200_decoder_pos(const moe_b200_decoder *dec);
+/* Kernels in one step (the graph's launches). */
+int moe_b200_decoder_launches(const moe_b200_decoder *dec);
+int moe_b200_decoder_destroy(moe_b200_decoder *dec);
+
 /* ---- expert parallel (one process per GPU, NVLink) --------------------- */
 /* llm.c has no multi-GPU path (README.md:379 lists it as a roadmap item);
  * these entry points extend moe_forward to G GPUs of one node.

@@ -49,6 +49,50 @@ MOE_DEV float swiglu_ref(float g, float u) {
     return __fmul_rn(__fmul_rn(g, sig), u);
 }
 
+// One token's routing, in place on its logits row[0..E) (bias already
+// added): the reference's softmax (softmax_rows, src/matrix.c:529-586, AVX2
+// branch: 8-lane partial sums, hsum tree, scalar tail), its top-k
+// (src/transformer.c:312-332: k passes, strict '>', best = -1, best_e = 0,
+// e ascending, chosen experts skipped) and renormalisation (:334-337,350).
+// Leaves the probabilities in row and writes sel[k] (rank order) and w[k].
+MOE_DEV void route_token(float *row, int E, int k, int *sel, float *w) {
+    const int nv = E - E % 8;
+    float mx = -1e38f;
+    for (int e = 0; e < E; e++) mx = fmaxf(mx, row[e]);
+    float lane[8];
+#pragma unroll
+    for (int l = 0; l < 8; l++) lane[l] = 0.0f;
+    for (int e = 0; e < nv; e++) {
+        const float ex = exp_ref(__fsub_rn(row[e], mx));
+        row[e] = ex;
+        lane[e & 7] = __fadd_rn(lane[e & 7], ex);
+    }
+    const float a0 = __fadd_rn(lane[0], lane[4]), a1 = __fadd_rn(lane[1], lane[5]);
+    const float a2 = __fadd_rn(lane[2], lane[6]), a3 = __fadd_rn(lane[3], lane[7]);
+    float sum = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+    for (int e = nv; e < E; e++) {
+        row[e] = expf(__fsub_rn(row[e], mx));
+        sum = __fadd_rn(sum, row[e]);
+    }
+    const float inv = __fdiv_rn(1.0f, sum);
+    for (int e = 0; e < nv; e++) row[e] = __fmul_rn(row[e], inv);
+    for (int e = nv; e < E; e++) row[e] = __fdiv_rn(row[e], sum);
+    for (int r = 0; r < k; r++) {
+        float best = -1.0f;
+        int best_e = 0;
+        for (int e = 0; e < E; e++) {
+            bool taken = false;
+            for (int q = 0; q < r; q++) taken |= (sel[q] == e);
+            if (!taken && row[e] > best) { best = row[e]; best_e = e; }
+        }
+        sel[r] = best_e;
+    }
+    float s = 0.0f;
+    for (int r = 0; r < k; r++) s = __fadd_rn(s, row[sel[r]]);
+    const float winv = (s > 1e-9f) ? __fdiv_rn(1.0f, s) : 0.0f;
+    for (int r = 0; r < k; r++) w[r] = __fmul_rn(row[sel[r]], winv);
+}
+
 // Round an fp32 value to the nearest TF32 (10-bit mantissa, ties away
 // from zero), returned as fp32 bits with the low 13 mantissa bits zero.
 // tcgen05 kind::tf32 reads only the TF32 bits of its fp32 operands, i.e.

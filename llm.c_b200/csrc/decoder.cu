@@ -1,0 +1,780 @@
+// decoder.cu — llm.c's single-token KV-cache forward (src/inference.c:231-358,
+// with the MoE branch its TODO at :342-343 leaves out) run entirely on the
+// device, replayed as one CUDA graph per generated token.
+//
+// Everything the step touches stays in HBM: embeddings, per-layer norm and
+// attention weights, the experts (the library's packed, resident expert
+// sets), final norm, LM head, RoPE tables and the KV cache.  Per step the
+// host writes the token id (4 bytes) and reads the logits back.
+//
+// Per layer, six FP32 kernels (a decode step is latency-bound: ~45 MB of
+// weights for the configuration-2 model):
+//   1 qkv     RMSNorm (:209-215) + x·[W_Q | W_K | W_V] (:174-182), RoPE at
+//             the step's position on the q and k columns (:189-203), k and v
+//             appended to the KV cache (:279-281)
+//   2 attn    per (query head, 64-position chunk): scores q·k·(1/sqrt(hd)),
+//             chunk max, exp-sums and exp-weighted V (flash decoding); GQA
+//             head mapping kvh = qh / (n_heads / n_kv_heads) (:285-305)
+//   3 oproj   combines the chunks of every head into the softmax-weighted
+//             head outputs, then x += head_out·W_O (:307-309)
+//   4 router  RMSNorm (:311) + logits x_norm·W_router + the reference's
+//             softmax / top-k / renormalisation (src/transformer.c:299-337)
+//   5 upgate  per selected expert and hidden unit f: gate and up dot
+//             products and the reference's silu(gate)·up (:157-165)
+//   6 down    per output column: y_r = h_r·W_down[e_r] for each rank r and
+//             x += sum_r w_r·y_r in rank order (:355-358)
+// and after the last layer one kernel for the final RMSNorm and the LM head
+// (:350-356), which also advances the device-side position.  Dense blocks
+// (use_moe = 0) run as a one-expert MoE: probability 1, weight p/p = 1
+// exactly, so the FFN output is unchanged.
+//
+// Every reduction has a fixed order, so a step is deterministic.
+#include "kernels.cuh"
+#include "weights.cuh"
+#include "../../include/llmc_moe.h"
+#include "../../include/moe_b200.h"
+
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+namespace moe {
+namespace decs {
+
+constexpr int kThreads = 256;           // 8 warps
+constexpr int CH = 64;                  // attention positions per chunk
+constexpr int kMaxD = 8192;             // d_model limit (normalised vector in smem)
+
+struct Dims {
+    int d, d_pad, nh, nkv, hd, nq, kvd, qkv, vocab, max_seq, nchunk;
+    float eps, scale;
+};
+
+// per-layer device pointers (an array of these lives in device memory)
+struct LayerPtrs {
+    const float *rms_attn, *rms_ffn, *w_qkv, *w_o, *router, *ug, *dn;
+    int E, k, F, F_pad;
+};
+
+// every buffer a step reads or writes
+struct StepArgs {
+    Dims D;
+    int L;
+    const LayerPtrs *layers;
+    const float *embed, *rms_final, *lm_head, *rope_cos, *rope_sin;
+    float *kc, *vc;                    // [L][max_seq][kvd]
+    float *x, *q, *part, *h, *logits, *wts;
+    int *state, *ids;                  // state = {token, pos}
+    unsigned *bar;                     // grid barrier counter (zeroed before each step)
+    int *err;                          // barrier timeout flag
+};
+
+struct Smem {
+    float xn[kMaxD];                   // normalised vector / head outputs
+    float red[kThreads];
+    float qs[128];
+    float sc[CH];
+    float lg[kMaxExperts];
+    int sel[kMaxTopK];
+    float w[kMaxTopK];
+    int flag;
+};
+
+// Values written by other CTAs of the same launch are read through L2
+// (ld.global.cg): the persistent kernel has no kernel boundary to drop stale
+// L1 lines.  Weights, which no step writes, use the read-only path.
+__device__ __forceinline__ float ldcg(const float *p) { return __ldcg(p); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// S.xn[i] = x[i] * (1 / sqrt(mean(x²) + eps)) * w[i] for i < d, zero up to
+// d_pad (rmsnorm_vec, src/inference.c:209-215); every CTA sums the squares
+// in the same fixed order.
+__device__ __forceinline__ void rmsnorm_to_smem(const float *x, const float *__restrict__ w,
+                                                const Dims &D, Smem &S) {
+    constexpr int KEEP = 8;            // values kept in registers (d <= 2048)
+    float xv[KEEP];
+    float ss = 0.0f;
+#pragma unroll
+    for (int u = 0; u < KEEP; u++) {
+        const int i = threadIdx.x + u * kThreads;
+        xv[u] = i < D.d ? ldcg(x + i) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < KEEP; u++) ss = __fmaf_rn(xv[u], xv[u], ss);
+    for (int i = threadIdx.x + KEEP * kThreads; i < D.d; i += kThreads) {
+        const float v = ldcg(x + i);
+        ss = __fmaf_rn(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) S.red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kThreads / 32; q++) tot += S.red[q];
+    const float inv = 1.0f / sqrtf(tot / (float)D.d + D.eps);
+#pragma unroll
+    for (int u = 0; u < KEEP; u++) {
+        const int i = threadIdx.x + u * kThreads;
+        if (i < D.d_pad) S.xn[i] = i < D.d ? __fmul_rn(__fmul_rn(xv[u], inv), __ldg(w + i)) : 0.0f;
+    }
+    for (int i = threadIdx.x + KEEP * kThreads; i < D.d_pad; i += kThreads)
+        S.xn[i] = i < D.d ? __fmul_rn(__fmul_rn(ldcg(x + i), inv), __ldg(w + i)) : 0.0f;
+    __syncthreads();
+}
+
+// 32 output columns of v[0..n_in)·W[n_in × ld] (row-major, the reference's
+// matvec layout, src/inference.c:174-182): lane = column, warps split the
+// rows, partial sums added in warp order.  The value is valid in warp 0.
+__device__ __forceinline__ float matvec32(const float *v, const float *__restrict__ W, int n_in,
+                                          int ld, int col, bool valid, Smem &S) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rows = (n_in + 7) / 8, r0 = warp * rows, r1 = min(n_in, r0 + rows);
+    float acc = 0.0f;
+    if (valid) {
+        // 24 rows' loads in flight before their FMAs (a decode step is
+        // memory-latency bound); the sum still runs in row order
+        for (int i0 = r0; i0 < r1; i0 += 24) {
+            float wv[24];
+#pragma unroll
+            for (int u = 0; u < 24; u++)
+                wv[u] = i0 + u < r1 ? __ldg(W + (size_t)(i0 + u) * ld + col) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 24; u++)
+                if (i0 + u < r1) acc = __fmaf_rn(v[i0 + u], wv[u], acc);
+        }
+    }
+    S.red[warp * 32 + lane] = acc;
+    __syncthreads();
+    float out = 0.0f;
+    if (warp == 0) {
+#pragma unroll
+        for (int q = 0; q < 8; q++) out += S.red[q * 32 + lane];
+    }
+    __syncthreads();                   // S.red is reused by the next item
+    return out;
+}
+
+// ---- the stages; `item` is a unit of a stage's work ----
+
+// 1: RMSNorm, x·[W_Q | W_K | W_V] for 32 columns, RoPE, KV append.  Layer 0
+// starts from the token's embedding row; item 0 also stores it as the
+// residual stream.
+__device__ void qkv_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int token, int pos,
+                         int item, Smem &S) {
+    const Dims &D = A.D;
+    const float *src = layer == 0 ? A.embed + (size_t)token * D.d : A.x;
+    if (layer == 0 && item == 0)
+        for (int i = threadIdx.x; i < D.d; i += kThreads) A.x[i] = __ldg(src + i);
+    rmsnorm_to_smem(src, Lp.rms_attn, D, S);
+    const int lane = threadIdx.x & 31, col = item * 32 + lane;
+    const float v = matvec32(S.xn, Lp.w_qkv, D.d, D.qkv, col, col < D.qkv, S);
+    if (threadIdx.x < 32) {
+        // RoPE pairs (2i, 2i+1) of a head sit in adjacent lanes
+        const float other = __shfl_xor_sync(0xffffffffu, v, 1);
+        float *kc = A.kc + (size_t)layer * D.max_seq * D.kvd;
+        float *vc = A.vc + (size_t)layer * D.max_seq * D.kvd;
+        if (col < D.nq + D.kvd) {
+            const int c = col < D.nq ? col : col - D.nq;
+            const int half = D.hd / 2, pi = (c % D.hd) >> 1;
+            const float cr = __ldg(A.rope_cos + (size_t)pos * half + pi);
+            const float sr = __ldg(A.rope_sin + (size_t)pos * half + pi);
+            const bool even = (c & 1) == 0;
+            const float v0 = even ? v : other, v1 = even ? other : v;
+            const float r = even ? __fsub_rn(__fmul_rn(v0, cr), __fmul_rn(v1, sr))
+                                 : __fadd_rn(__fmul_rn(v0, sr), __fmul_rn(v1, cr));
+            if (col < D.nq) A.q[col] = r;
+            else kc[(size_t)pos * D.kvd + c] = r;
+        } else if (col < D.qkv) {
+            vc[(size_t)pos * D.kvd + (col - D.nq - D.kvd)] = v;
+        }
+    }
+}
+
+// 2: query head h, positions [chunk*CH, +CH) of 0..pos: chunk max m, sum of
+// exp(s - m) and the exp-weighted V sum, written to part[h][chunk] =
+// {m, l, o[hd]} (scores q·k / sqrt(hd), GQA kvh = h / (nh / nkv),
+// src/inference.c:285-305).
+__device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chunk, Smem &S) {
+    const Dims &D = A.D;
+    const int j0 = chunk * CH, n = min(CH, pos + 1 - j0);
+    const float *kc = A.kc + (size_t)layer * D.max_seq * D.kvd;
+    const float *vc = A.vc + (size_t)layer * D.max_seq * D.kvd;
+    float *dst = A.part + ((size_t)h * D.nchunk + chunk) * (D.hd + 2);
+    const int g = h / (D.nh / D.nkv);
+    for (int i = threadIdx.x; i < D.hd; i += kThreads) S.qs[i] = ldcg(A.q + h * D.hd + i);
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int PW = CH / (kThreads / 32);          // positions per warp
+    float kv[PW][4];                                  // hd <= 128: 4 values per lane
+#pragma unroll
+    for (int t = 0; t < PW; t++) {                    // every key load in flight first
+        const int jj = warp + t * (kThreads / 32);
+        const float *kr = kc + (size_t)(j0 + jj) * D.kvd + g * D.hd;
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+            kv[t][c] = (jj < n && lane + 32 * c < D.hd) ? ldcg(kr + lane + 32 * c) : 0.0f;
+    }
+#pragma unroll
+    for (int t = 0; t < PW; t++) {
+        const int jj = warp + t * (kThreads / 32);
+        float p = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+            if (lane + 32 * c < D.hd) p = __fmaf_rn(S.qs[lane + 32 * c], kv[t][c], p);
+        p = warp_sum(p);
+        if (lane == 0 && jj < n) S.sc[jj] = __fmul_rn(p, D.scale);
+    }
+    __syncthreads();
+    if (warp == 0) {                   // max, exp and sum over the chunk (CH = 64: 2 per lane)
+        const float s0 = lane < n ? S.sc[lane] : -INFINITY;
+        const float s1 = lane + 32 < n ? S.sc[lane + 32] : -INFINITY;
+        float m = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float e0 = lane < n ? expf(__fsub_rn(s0, m)) : 0.0f;
+        const float e1 = lane + 32 < n ? expf(__fsub_rn(s1, m)) : 0.0f;
+        if (lane < n) S.sc[lane] = e0;
+        if (lane + 32 < n) S.sc[lane + 32] = e1;
+        const float l = warp_sum(__fadd_rn(e0, e1));
+        if (lane == 0) { dst[0] = m; dst[1] = l; }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < D.hd; i += kThreads) {
+        const float *vcol = vc + (size_t)j0 * D.kvd + g * D.hd + i;
+        float o = 0.0f;
+        for (int jb = 0; jb < n; jb += 16) {          // 16 value loads in flight
+            float vv[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                vv[u] = jb + u < n ? ldcg(vcol + (size_t)(jb + u) * D.kvd) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 16; u++)
+                if (jb + u < n) o = __fmaf_rn(S.sc[jb + u], vv[u], o);
+        }
+        dst[2 + i] = o;
+    }
+    __syncthreads();                   // S.qs / S.sc are reused by the next item
+}
+
+// 3: softmax-weighted head outputs from the chunks, then x += head_out·W_O
+// for 32 columns (src/inference.c:307-309).
+__device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int item, Smem &S) {
+    const Dims &D = A.D;
+    const int nch = (pos + 1 + CH - 1) / CH;
+    for (int t = threadIdx.x; t < D.nq; t += kThreads) {
+        const int h = t / D.hd, i = t % D.hd;
+        const float *ph = A.part + (size_t)h * D.nchunk * (D.hd + 2);
+        float M = -INFINITY, L = 0.0f, O = 0.0f;
+        for (int c0 = 0; c0 < nch; c0 += 12) {         // 12 chunks' loads in flight
+            float mc[12], lc[12], oc[12];
+#pragma unroll
+            for (int u = 0; u < 12; u++) {
+                const float *pc = ph + (size_t)(c0 + u) * (D.hd + 2);
+                const bool ok = c0 + u < nch;
+                mc[u] = ok ? ldcg(pc) : -INFINITY;
+                lc[u] = ok ? ldcg(pc + 1) : 0.0f;
+                oc[u] = ok ? ldcg(pc + 2 + i) : 0.0f;
+            }
+            // running rescale, chunk by chunk in order
+#pragma unroll
+            for (int u = 0; u < 12; u++) {
+                if (c0 + u >= nch) break;
+                const float Mn = fmaxf(M, mc[u]);
+                const float a = expf(__fsub_rn(M, Mn)), b = expf(__fsub_rn(mc[u], Mn));
+                L = __fmaf_rn(lc[u], b, __fmul_rn(L, a));
+                O = __fmaf_rn(oc[u], b, __fmul_rn(O, a));
+                M = Mn;
+            }
+        }
+        S.xn[t] = __fdiv_rn(O, L);
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, col = item * 32 + lane;
+    const float v = matvec32(S.xn, Lp.w_o, D.nq, D.d, col, col < D.d, S);
+    if (threadIdx.x < 32 && col < D.d) A.x[col] = __fadd_rn(ldcg(A.x + col), v);
+}
+
+// 4 (once per CTA before its up/gate items): RMSNorm into S.xn, router
+// logits and the reference's routing of the token into S.sel / S.w
+// (src/inference.c:311; src/transformer.c:299-337).  `publish` also stores
+// the ids and weights for the down stage.
+__device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, bool publish, Smem &S) {
+    const Dims &D = A.D;
+    rmsnorm_to_smem(A.x, Lp.rms_ffn, D, S);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = warp; e < Lp.E; e += kThreads / 32) {
+        float p = 0.0f;
+        for (int i0 = lane; i0 < D.d; i0 += 32 * 16) {   // 16 loads in flight per lane
+            float wv[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                const int i = i0 + 32 * u;
+                wv[u] = i < D.d ? __ldg(Lp.router + (size_t)i * Lp.E + e) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                const int i = i0 + 32 * u;
+                if (i < D.d) p = __fmaf_rn(S.xn[i], wv[u], p);
+            }
+        }
+        p = warp_sum(p);
+        if (lane == 0) S.lg[e] = p;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        route_token(S.lg, Lp.E, Lp.k, S.sel, S.w);
+        if (publish)
+            for (int r = 0; r < Lp.k; r++) { A.ids[r] = S.sel[r]; A.wts[r] = S.w[r]; }
+    }
+    __syncthreads();
+}
+
+// 5: 8 hidden units of rank r: one warp per unit f, the gate and up rows of
+// expert S.sel[r] in the packed layout (128 gate rows, then the matching
+// 128 up rows), dot x_norm, the reference's silu(gate)·up into h[r][f].
+__device__ void upgate_item(const StepArgs &A, const LayerPtrs &Lp, int item, Smem &S) {
+    const Dims &D = A.D;
+    const int nfb = (Lp.F + 7) / 8;
+    const int r = item / nfb, f = (item % nfb) * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (f >= Lp.F) return;
+    const int e = S.sel[r];
+    const size_t grow = (size_t)e * 2 * Lp.F_pad + (size_t)(f / 128) * 256 + (f % 128);
+    const float4 *gw = reinterpret_cast<const float4 *>(Lp.ug + grow * D.d_pad);
+    const float4 *uw = reinterpret_cast<const float4 *>(Lp.ug + (grow + 128) * D.d_pad);
+    const float4 *x4 = reinterpret_cast<const float4 *>(S.xn);
+    float g = 0.0f, u = 0.0f;
+    for (int i = lane; i < D.d_pad / 4; i += 32) {
+        const float4 xv = x4[i], a = __ldg(gw + i), b = __ldg(uw + i);
+        g = __fmaf_rn(xv.x, a.x, g); g = __fmaf_rn(xv.y, a.y, g);
+        g = __fmaf_rn(xv.z, a.z, g); g = __fmaf_rn(xv.w, a.w, g);
+        u = __fmaf_rn(xv.x, b.x, u); u = __fmaf_rn(xv.y, b.y, u);
+        u = __fmaf_rn(xv.z, b.z, u); u = __fmaf_rn(xv.w, b.w, u);
+    }
+    g = warp_sum(g);
+    u = warp_sum(u);
+    if (lane == 0) A.h[(size_t)r * Lp.F_pad + f] = swiglu_ref(g, u);
+}
+
+// 6: 8 output columns, one warp each: y_r = h_r·W_down[ids[r]] row j
+// (packed [d_pad × F_pad]); x[j] += w_0·y_0 + w_1·y_1 + ... in rank order
+// (src/transformer.c:355-358).
+__device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int item) {
+    const Dims &D = A.D;
+    const int j = item * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (j >= D.d) return;
+    float out = 0.0f;
+    for (int r = 0; r < Lp.k; r++) {
+        const int e = __ldcg(A.ids + r);
+        const float4 *wr = reinterpret_cast<const float4 *>(Lp.dn + ((size_t)e * D.d_pad + j) * Lp.F_pad);
+        const float4 *hr = reinterpret_cast<const float4 *>(A.h + (size_t)r * Lp.F_pad);
+        float y = 0.0f;
+        for (int i0 = lane; i0 < Lp.F_pad / 4; i0 += 32 * 8) {   // 8 float4 pairs in flight
+            float4 a[8], hb[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + 32 * u;
+                const bool ok = i < Lp.F_pad / 4;
+                a[u] = ok ? __ldg(wr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                hb[u] = ok ? __ldcg(hr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                y = __fmaf_rn(hb[u].x, a[u].x, y); y = __fmaf_rn(hb[u].y, a[u].y, y);
+                y = __fmaf_rn(hb[u].z, a[u].z, y); y = __fmaf_rn(hb[u].w, a[u].w, y);
+            }
+        }
+        y = warp_sum(y);
+        out = __fmaf_rn(ldcg(A.wts + r), y, out);
+    }
+    if (lane == 0) A.x[j] = __fadd_rn(ldcg(A.x + j), out);
+}
+
+// 7: final RMSNorm and 32 columns of the LM head (x_norm·lm_head, [d × vocab]).
+__device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S) {
+    const Dims &D = A.D;
+    if (!normed) rmsnorm_to_smem(A.x, A.rms_final, D, S);
+    const int lane = threadIdx.x & 31, col = item * 32 + lane;
+    const float v = matvec32(S.xn, A.lm_head, D.d, D.vocab, col, col < D.vocab, S);
+    if (threadIdx.x < 32 && col < D.vocab) A.logits[col] = v;
+}
+
+// ---- one kernel per stage (the graph path) ----
+
+__global__ void __launch_bounds__(kThreads) qkv_kernel(StepArgs A, int layer) {
+    __shared__ Smem S;
+    const LayerPtrs Lp = A.layers[layer];
+    qkv_item(A, Lp, layer, A.state[0], A.state[1], blockIdx.x, S);
+}
+__global__ void __launch_bounds__(kThreads) attn_kernel(StepArgs A, int layer) {
+    __shared__ Smem S;
+    const int pos = A.state[1];
+    if ((int)blockIdx.y * CH > pos) return;
+    attn_item(A, layer, pos, blockIdx.x, blockIdx.y, S);
+}
+__global__ void __launch_bounds__(kThreads) oproj_kernel(StepArgs A, int layer) {
+    __shared__ Smem S;
+    oproj_item(A, A.layers[layer], A.state[1], blockIdx.x, S);
+}
+__global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer) {
+    __shared__ Smem S;
+    const LayerPtrs Lp = A.layers[layer];
+    route_cta(A, Lp, blockIdx.x == 0, S);
+    upgate_item(A, Lp, blockIdx.x, S);
+}
+__global__ void __launch_bounds__(kThreads) down_kernel(StepArgs A, int layer) {
+    down_item(A, A.layers[layer], blockIdx.x);
+}
+__global__ void __launch_bounds__(kThreads) lmhead_kernel(StepArgs A) {
+    __shared__ Smem S;
+    lmhead_item(A, blockIdx.x, false, S);
+    if (blockIdx.x == 0 && threadIdx.x == 0) A.state[1] += 1;
+}
+
+// ---- the whole step as one persistent cooperative kernel ----
+
+// Grid-wide barrier: every CTA arrives on one counter and waits, bounded by
+// kWaitNs of %globaltimer, until all gridDim.x CTAs of this phase arrived.
+// Returns false (and sets *err) if the wait ran out or another CTA gave up.
+__device__ __forceinline__ bool grid_barrier(const StepArgs &A, unsigned target, Smem &S) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(A.bar, 1u);
+        int good = 1;
+        const uint64_t t0 = globaltimer_ns();
+        while (true) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.bar) : "memory");
+            if (v >= target) break;
+            if (*(volatile int *)A.err) { good = 0; break; }
+            if (globaltimer_ns() - t0 > kWaitNs) { atomicExch(A.err, 1); good = 0; break; }
+        }
+        __threadfence();
+        S.flag = good;
+    }
+    __syncthreads();
+    return S.flag != 0;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs A) {
+    __shared__ Smem S;
+    const Dims &D = A.D;
+    const int token = A.state[0], pos = A.state[1];
+    const int G = gridDim.x, b = blockIdx.x;
+    unsigned phase = 0;
+    const int n_qkv = (D.qkv + 31) / 32, n_col = (D.d + 31) / 32, n_down = (D.d + 7) / 8;
+    const int nch = (pos + 1 + CH - 1) / CH;
+    for (int l = 0; l < A.L; l++) {
+        const LayerPtrs Lp = A.layers[l];
+        for (int it = b; it < n_qkv; it += G) qkv_item(A, Lp, l, token, pos, it, S);
+        if (!grid_barrier(A, ++phase * G, S)) return;
+        for (int it = b; it < D.nh * nch; it += G) attn_item(A, l, pos, it / nch, it % nch, S);
+        if (!grid_barrier(A, ++phase * G, S)) return;
+        for (int it = b; it < n_col; it += G) oproj_item(A, Lp, pos, it, S);
+        if (!grid_barrier(A, ++phase * G, S)) return;
+        const int n_ug = Lp.k * ((Lp.F + 7) / 8);
+        if (b < n_ug) {
+            route_cta(A, Lp, b == 0, S);
+            for (int it = b; it < n_ug; it += G) upgate_item(A, Lp, it, S);
+        }
+        if (!grid_barrier(A, ++phase * G, S)) return;
+        for (int it = b; it < n_down; it += G) down_item(A, Lp, it);
+        if (!grid_barrier(A, ++phase * G, S)) return;
+    }
+    const int n_lm = (D.vocab + 31) / 32;
+    bool normed = false;
+    for (int it = b; it < n_lm; it += G) {
+        lmhead_item(A, it, normed, S);
+        normed = true;                  // S.xn keeps the normalised vector across items
+    }
+    if (b == 0 && threadIdx.x == 0) A.state[1] = pos + 1;
+}
+
+}  // namespace decs
+}  // namespace moe
+
+using namespace moe;
+using namespace moe::decs;
+
+struct DecLayer {
+    float *rms_attn = nullptr, *rms_ffn = nullptr, *w_qkv = nullptr, *w_o = nullptr;
+    moe_b200_weights *ffn = nullptr;
+};
+
+struct moe_b200_decoder {
+    int device = 0;
+    Dims D{};
+    int L = 0, pos = 0, flags = 0, grid = 0;
+    float *embed = nullptr, *rms_final = nullptr, *lm_head = nullptr, *rope_cos = nullptr,
+          *rope_sin = nullptr;
+    std::vector<DecLayer> layers;
+    LayerPtrs *d_layers = nullptr;
+    float *kc = nullptr, *vc = nullptr;          // [L][max_seq][kvd]
+    float *x = nullptr, *q = nullptr, *part = nullptr, *h = nullptr, *logits = nullptr,
+          *wts = nullptr;
+    int *state = nullptr, *ids = nullptr;        // state = {token, pos}
+    unsigned *bar = nullptr;
+    int *err = nullptr;
+    int *h_token = nullptr;                      // pinned
+    int maxF_pad = 0;
+    cudaStream_t stream = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+};
+
+namespace {
+
+int dfail(int code, const char *msg) { return moe::set_last_error(code, msg); }
+
+#define DCK(call)                                                                          \
+    do {                                                                                   \
+        cudaError_t e_ = (call);                                                           \
+        if (e_ != cudaSuccess) return dfail(MOE_B200_E_CUDA, cudaGetErrorString(e_));       \
+    } while (0)
+
+int upload(float **dst, const float *src, size_t n) {
+    DCK(cudaMalloc(dst, n * sizeof(float)));
+    DCK(cudaMemcpy(*dst, src, n * sizeof(float), cudaMemcpyHostToDevice));
+    return MOE_B200_OK;
+}
+
+void free_all(moe_b200_decoder *m) {
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    for (DecLayer &l : m->layers) {
+        cudaFree(l.rms_attn); cudaFree(l.rms_ffn); cudaFree(l.w_qkv); cudaFree(l.w_o);
+        if (l.ffn) moe_b200_weights_free(l.ffn);
+    }
+    cudaFree(m->d_layers);
+    cudaFree(m->embed); cudaFree(m->rms_final); cudaFree(m->lm_head);
+    cudaFree(m->rope_cos); cudaFree(m->rope_sin); cudaFree(m->kc); cudaFree(m->vc);
+    cudaFree(m->x); cudaFree(m->q); cudaFree(m->part); cudaFree(m->h);
+    cudaFree(m->logits); cudaFree(m->wts); cudaFree(m->state); cudaFree(m->ids);
+    cudaFree(m->bar); cudaFree(m->err);
+    if (m->h_token) cudaFreeHost(m->h_token);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+StepArgs step_args(const moe_b200_decoder *m) {
+    StepArgs A{};
+    A.D = m->D;
+    A.L = m->L;
+    A.layers = m->d_layers;
+    A.embed = m->embed; A.rms_final = m->rms_final; A.lm_head = m->lm_head;
+    A.rope_cos = m->rope_cos; A.rope_sin = m->rope_sin;
+    A.kc = m->kc; A.vc = m->vc;
+    A.x = m->x; A.q = m->q; A.part = m->part; A.h = m->h; A.logits = m->logits; A.wts = m->wts;
+    A.state = m->state; A.ids = m->ids; A.bar = m->bar; A.err = m->err;
+    return A;
+}
+
+// the step's device work, in order, on m->stream
+int enqueue_step(moe_b200_decoder *m) {
+    const Dims &D = m->D;
+    cudaStream_t s = m->stream;
+    StepArgs A = step_args(m);
+    if (!(m->flags & MOE_B200_DECODER_STAGE_KERNELS)) {
+        DCK(cudaMemsetAsync(m->bar, 0, sizeof(unsigned), s));
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.gridDim = dim3(m->grid, 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        DCK(cudaLaunchKernelEx(&cfg, decode_step_kernel, A));
+        m->launches = 1;
+        return MOE_B200_OK;
+    }
+    int n = 0;
+    for (int l = 0; l < m->L; l++) {
+        const moe_b200_weights *w = m->layers[l].ffn;
+        qkv_kernel<<<ceil_div(D.qkv, 32), kThreads, 0, s>>>(A, l);
+        attn_kernel<<<dim3(D.nh, D.nchunk), kThreads, 0, s>>>(A, l);
+        oproj_kernel<<<ceil_div(D.d, 32), kThreads, 0, s>>>(A, l);
+        upgate_kernel<<<w->k * ceil_div(w->F, 8), kThreads, 0, s>>>(A, l);
+        down_kernel<<<ceil_div(D.d, 8), kThreads, 0, s>>>(A, l);
+        n += 5;
+    }
+    lmhead_kernel<<<ceil_div(D.vocab, 32), kThreads, 0, s>>>(A);
+    n += 1;
+    DCK(cudaGetLastError());
+    m->launches = n;
+    return MOE_B200_OK;
+}
+
+}  // namespace
+
+extern "C" int moe_b200_decoder_create(const void *model, int max_seq, int flags,
+                                       moe_b200_decoder **out) {
+    if (!model || !out) return dfail(MOE_B200_E_INVALID, "null argument");
+    *out = nullptr;
+    const llmc_Model *mp = static_cast<const llmc_Model *>(model);
+    const llmc_ModelConfig &c = mp->cfg;
+    const int d = c.d_model, nh = c.n_heads, nkv = c.n_kv_heads, hd = c.head_dim;
+    if (d <= 0 || d > kMaxD || nh <= 0 || nkv <= 0 || nh % nkv || hd <= 0 || hd > 128 ||
+        hd % 32 || nh * hd > kMaxD || c.vocab_size <= 0 || mp->weights.n_layers <= 0)
+        return dfail(MOE_B200_E_INVALID, "unsupported model shape for the device decoder");
+    if (max_seq <= 0 || max_seq > mp->rope.max_seq_len || mp->rope.head_dim != hd)
+        return dfail(MOE_B200_E_INVALID, "max_seq exceeds the model's RoPE table");
+    int rc = moe_b200_init(-1);
+    if (rc) return rc;
+    moe_b200_decoder *m = new moe_b200_decoder();
+    cudaGetDevice(&m->device);
+    m->flags = flags;
+    Dims &D = m->D;
+    D.d = d; D.d_pad = round_up(d, 128); D.nh = nh; D.nkv = nkv; D.hd = hd; D.nq = nh * hd;
+    D.kvd = nkv * hd; D.qkv = D.nq + 2 * D.kvd; D.vocab = c.vocab_size; D.max_seq = max_seq;
+    D.nchunk = ceil_div(max_seq, CH); D.eps = c.rms_norm_eps; D.scale = 1.0f / sqrtf((float)hd);
+    m->L = mp->weights.n_layers;
+    auto bail = [&](int r) { free_all(m); return r; };
+#define DTRY(x)                      \
+    do {                             \
+        int r_ = (x);                \
+        if (r_) return bail(r_);     \
+    } while (0)
+    const llmc_ModelWeights &W = mp->weights;
+    DTRY(upload(&m->embed, W.embed.data, (size_t)D.vocab * d));
+    DTRY(upload(&m->rms_final, W.rms_final, d));
+    DTRY(upload(&m->lm_head, W.lm_head.data, (size_t)d * D.vocab));
+    DTRY(upload(&m->rope_cos, mp->rope.cos_table, (size_t)max_seq * (hd / 2)));
+    DTRY(upload(&m->rope_sin, mp->rope.sin_table, (size_t)max_seq * (hd / 2)));
+    m->layers.resize(m->L);
+    std::vector<LayerPtrs> lp(m->L);
+    std::vector<float> qkv((size_t)d * D.qkv);
+    for (int l = 0; l < m->L; l++) {
+        const llmc_BlockWeights &b = W.blocks[l];
+        DecLayer &ly = m->layers[l];
+        DTRY(upload(&ly.rms_attn, b.rms_attn, d));
+        DTRY(upload(&ly.rms_ffn, b.rms_ffn, d));
+        for (int i = 0; i < d; i++) {           // [W_Q | W_K | W_V] columns per row
+            float *row = qkv.data() + (size_t)i * D.qkv;
+            std::memcpy(row, b.attn.W_Q.data + (size_t)i * D.nq, D.nq * sizeof(float));
+            std::memcpy(row + D.nq, b.attn.W_K.data + (size_t)i * D.kvd, D.kvd * sizeof(float));
+            std::memcpy(row + D.nq + D.kvd, b.attn.W_V.data + (size_t)i * D.kvd,
+                        D.kvd * sizeof(float));
+        }
+        DTRY(upload(&ly.w_qkv, qkv.data(), qkv.size()));
+        DTRY(upload(&ly.w_o, b.attn.W_O.data, (size_t)D.nq * d));
+        const int F = c.ffn_hidden;
+        if (b.use_moe) {
+            const llmc_MoEWeights &mw = b.moe;
+            if (mw.top_k > kMaxTopK) return bail(dfail(MOE_B200_E_INVALID, "top_k too large"));
+            std::vector<const float *> g(mw.n_experts), u(mw.n_experts), dn(mw.n_experts);
+            for (int e = 0; e < mw.n_experts; e++) {
+                g[e] = mw.experts[e].W_gate.data;
+                u[e] = mw.experts[e].W_up.data;
+                dn[e] = mw.experts[e].W_down.data;
+            }
+            DTRY(moe_b200_weights_upload(mw.W_router.data, g.data(), u.data(), dn.data(), d, F,
+                                         mw.n_experts, mw.top_k, &ly.ffn));
+        } else {                                   // dense FFN = one expert, weight 1
+            std::vector<float> zr(d, 0.0f);
+            const float *g = b.ffn.W_gate.data, *u = b.ffn.W_up.data, *dn = b.ffn.W_down.data;
+            DTRY(moe_b200_weights_upload(zr.data(), &g, &u, &dn, d, F, 1, 1, &ly.ffn));
+        }
+        const moe_b200_weights *w = ly.ffn;
+        lp[l] = LayerPtrs{ly.rms_attn, ly.rms_ffn, ly.w_qkv, ly.w_o, w->router, w->ug, w->dn,
+                          w->E, w->k, w->F, w->F_pad};
+        m->maxF_pad = m->maxF_pad > w->F_pad ? m->maxF_pad : w->F_pad;
+    }
+    const size_t cache = (size_t)m->L * max_seq * D.kvd;
+    if (cudaMalloc(&m->d_layers, lp.size() * sizeof(LayerPtrs)) != cudaSuccess ||
+        cudaMalloc(&m->kc, cache * 4) != cudaSuccess || cudaMalloc(&m->vc, cache * 4) != cudaSuccess ||
+        cudaMalloc(&m->x, (size_t)d * 4) != cudaSuccess ||
+        cudaMalloc(&m->q, (size_t)D.nq * 4) != cudaSuccess ||
+        cudaMalloc(&m->part, (size_t)nh * D.nchunk * (hd + 2) * 4) != cudaSuccess ||
+        cudaMalloc(&m->h, (size_t)kMaxTopK * m->maxF_pad * 4) != cudaSuccess ||
+        cudaMalloc(&m->logits, (size_t)D.vocab * 4) != cudaSuccess ||
+        cudaMalloc(&m->wts, kMaxTopK * 4) != cudaSuccess ||
+        cudaMalloc(&m->ids, kMaxTopK * 4) != cudaSuccess ||
+        cudaMalloc(&m->state, 2 * 4) != cudaSuccess ||
+        cudaMalloc(&m->bar, 4) != cudaSuccess || cudaMalloc(&m->err, 4) != cudaSuccess ||
+        cudaMallocHost(&m->h_token, 4) != cudaSuccess) {
+        cudaGetLastError();
+        return bail(dfail(MOE_B200_E_NOMEM, "decoder buffers do not fit"));
+    }
+    // h is zeroed once: the up/gate stage writes units [0, F), and the
+    // padding units [F, F_pad) meet zero weight columns in the down stage
+    if (cudaMemcpy(m->d_layers, lp.data(), lp.size() * sizeof(LayerPtrs),
+                   cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(m->state, 0, 8) != cudaSuccess || cudaMemset(m->err, 0, 4) != cudaSuccess ||
+        cudaMemset(m->h, 0, (size_t)kMaxTopK * m->maxF_pad * 4) != cudaSuccess ||
+        cudaMemset(m->kc, 0, cache * 4) != cudaSuccess || cudaMemset(m->vc, 0, cache * 4) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(dfail(MOE_B200_E_CUDA, "decoder set-up"));
+    if (!(flags & MOE_B200_DECODER_STAGE_KERNELS)) {
+        // one CTA per SM, all co-resident (cooperative launch)
+        int per_sm = 0, sms = moe::device_sms(m->device);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kThreads, 0) !=
+                cudaSuccess || per_sm < 1 || sms < 1)
+            return bail(dfail(MOE_B200_E_CUDA, "cooperative decode kernel cannot be resident"));
+        m->grid = sms;
+    }
+    // the step as one graph
+    if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return bail(dfail(MOE_B200_E_CUDA, "stream capture"));
+    rc = enqueue_step(m);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
+    if (rc) { if (g) cudaGraphDestroy(g); return bail(rc); }
+    if (ce != cudaSuccess) return bail(dfail(MOE_B200_E_CUDA, cudaGetErrorString(ce)));
+    m->graph = g;
+    if (cudaGraphInstantiate(&m->exec, g, 0) != cudaSuccess)
+        return bail(dfail(MOE_B200_E_CUDA, "graph instantiate"));
+    *out = m;
+    return MOE_B200_OK;
+#undef DTRY
+}
+
+extern "C" int moe_b200_decoder_step(moe_b200_decoder *m, int token, float *logits) {
+    if (!m) return dfail(MOE_B200_E_INVALID, "null decoder");
+    if (token < 0 || token >= m->D.vocab) return dfail(MOE_B200_E_INVALID, "token out of range");
+    if (m->pos >= m->D.max_seq) return dfail(MOE_B200_E_INVALID, "KV cache full");
+    DCK(cudaSetDevice(m->device));
+    *m->h_token = token;
+    DCK(cudaMemcpyAsync(m->state, m->h_token, 4, cudaMemcpyHostToDevice, m->stream));
+    DCK(cudaGraphLaunch(m->exec, m->stream));
+    if (logits)
+        DCK(cudaMemcpyAsync(logits, m->logits, (size_t)m->D.vocab * 4, cudaMemcpyDeviceToHost,
+                            m->stream));
+    DCK(cudaStreamSynchronize(m->stream));
+    int err = 0;
+    if (!(m->flags & MOE_B200_DECODER_STAGE_KERNELS)) {
+        DCK(cudaMemcpy(&err, m->err, 4, cudaMemcpyDeviceToHost));
+        if (err) return dfail(MOE_B200_E_TIMEOUT, "decode step: grid barrier wait ran out");
+    }
+    m->pos++;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_decoder_set_pos(moe_b200_decoder *m, int pos) {
+    if (!m) return dfail(MOE_B200_E_INVALID, "null decoder");
+    if (pos < 0 || pos > m->pos) return dfail(MOE_B200_E_INVALID, "position beyond the cache");
+    DCK(cudaSetDevice(m->device));
+    DCK(cudaStreamSynchronize(m->stream));
+    DCK(cudaMemcpy(m->state + 1, &pos, 4, cudaMemcpyHostToDevice));
+    m->pos = pos;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_decoder_pos(const moe_b200_decoder *m) { return m ? m->pos : -1; }
+
+extern "C" int moe_b200_decoder_launches(const moe_b200_decoder *m) { return m ? m->launches : 0; }
+
+extern "C" int moe_b200_decoder_destroy(moe_b200_decoder *m) {
+    if (!m) return MOE_B200_OK;
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    free_all(m);
+    return MOE_B200_OK;
+}

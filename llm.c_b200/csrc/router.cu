@@ -138,50 +138,12 @@ __device__ __forceinline__ void router_tail(float *lg, int T, int E, int k, int 
     const int tid = threadIdx.x;
     const int t0 = tile * TT;
     if (tid < TT && t0 + tid < T) {
-        float *row = lg + tid * (EB + 1);
-        // softmax_rows, AVX2+FMA branch: 8-wide part then scalar tail.
-        const int nv = E - E % 8;
-        float mx = -1e38f;
-        for (int e = 0; e < E; e++) mx = fmaxf(mx, row[e]);
-        float lane[8];
-#pragma unroll
-        for (int l = 0; l < 8; l++) lane[l] = 0.0f;
-        for (int e = 0; e < nv; e++) {
-            const float ex = exp_ref(__fsub_rn(row[e], mx));
-            row[e] = ex;
-            lane[e & 7] = __fadd_rn(lane[e & 7], ex);
-        }
-        const float a0 = __fadd_rn(lane[0], lane[4]), a1 = __fadd_rn(lane[1], lane[5]);
-        const float a2 = __fadd_rn(lane[2], lane[6]), a3 = __fadd_rn(lane[3], lane[7]);
-        float sum = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
-        for (int e = nv; e < E; e++) {
-            row[e] = expf(__fsub_rn(row[e], mx));
-            sum = __fadd_rn(sum, row[e]);
-        }
-        const float inv = __fdiv_rn(1.0f, sum);
-        for (int e = 0; e < nv; e++) row[e] = __fmul_rn(row[e], inv);
-        for (int e = nv; e < E; e++) row[e] = __fdiv_rn(row[e], sum);
-
-        // top-k (src/transformer.c:318-332): k passes, strict '>', best = -1,
-        // best_e = 0, e ascending, already-chosen experts skipped.
         int sel[kMaxTopK];
-        for (int r = 0; r < k; r++) {
-            float best = -1.0f;
-            int best_e = 0;
-            for (int e = 0; e < E; e++) {
-                bool taken = false;
-                for (int q = 0; q < r; q++) taken |= (sel[q] == e);
-                if (!taken && row[e] > best) { best = row[e]; best_e = e; }
-            }
-            sel[r] = best_e;
-        }
-        // renormalisation (src/transformer.c:334-337,350)
-        float s = 0.0f;
-        for (int r = 0; r < k; r++) s = __fadd_rn(s, row[sel[r]]);
-        const float winv = (s > 1e-9f) ? __fdiv_rn(1.0f, s) : 0.0f;
+        float wsel[kMaxTopK];
+        route_token(lg + tid * (EB + 1), E, k, sel, wsel);
         for (int r = 0; r < k; r++) {
             sid[tid][r] = sel[r];
-            swt[tid][r] = __fmul_rn(row[sel[r]], winv);
+            swt[tid][r] = wsel[r];
         }
     }
     __syncthreads();

@@ -435,3 +435,46 @@ class EP:
         if self.handle:
             lib().moe_b200_ep_destroy(self.handle)
             self.handle = 0
+
+
+class Decoder:
+    """Device-resident single-token decode of an llm.c Model (ctypes pointer
+    or address of an llmc_Model, e.g. from llmc_model.LlmcDecoder or the
+    reference's model_init): llm.c's inference_step on the B200."""
+
+    STAGE_KERNELS = 1      # one kernel per stage instead of one persistent kernel
+
+    def __init__(self, model_ptr, max_seq: int, flags: int = 0):
+        L = lib()
+        L.moe_b200_decoder_create.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp)]
+        L.moe_b200_decoder_step.argtypes = [_vp, C.c_int, _fp]
+        L.moe_b200_decoder_set_pos.argtypes = [_vp, C.c_int]
+        L.moe_b200_decoder_pos.argtypes = [_vp]
+        L.moe_b200_decoder_launches.argtypes = [_vp]
+        L.moe_b200_decoder_destroy.argtypes = [_vp]
+        h = _vp()
+        _check(L.moe_b200_decoder_create(model_ptr, int(max_seq), int(flags), C.byref(h)),
+               "moe_b200_decoder_create")
+        self.handle = h
+        self._vocab = None
+
+    def step(self, token: int, logits: np.ndarray | None = None):
+        """Run one step; fills `logits` (float32, vocab) when given."""
+        ptr = None if logits is None else _f(logits)
+        _check(lib().moe_b200_decoder_step(self.handle, int(token), ptr), "moe_b200_decoder_step")
+
+    def set_pos(self, pos: int):
+        _check(lib().moe_b200_decoder_set_pos(self.handle, int(pos)), "moe_b200_decoder_set_pos")
+
+    @property
+    def pos(self) -> int:
+        return int(lib().moe_b200_decoder_pos(self.handle))
+
+    @property
+    def launches(self) -> int:
+        return int(lib().moe_b200_decoder_launches(self.handle))
+
+    def free(self):
+        if self.handle:
+            lib().moe_b200_decoder_destroy(self.handle)
+            self.handle = None
