@@ -142,6 +142,12 @@ typedef struct {
  * non-MoE arithmetic (RMSNorm, Q/K/V/O projections, RoPE, KV-cache append,
  * GQA attention over all cached positions, LM head) is a CPU restatement of
  * the reference's.  Aborts on a device failure, like moe_forward.
+ * With the environment variable MOE_B200_DECODE=device the whole step runs
+ * on the B200 instead (moe_b200_decoder_* in moe_b200.h; one decoder per
+ * Model, created on first use): logits and seq_pos are updated as usual,
+ * but the KV cache lives on the device and s->kv_cache is not written.  A
+ * smaller seq_pos than the device's rewinds it; call moe_b200_invalidate(m)
+ * after changing the model's weights.
  */
 void inference_step(const llmc_Model *m, llmc_InferenceState *s, int token);
 
@@ -162,9 +168,11 @@ void moe_forward(const llmc_Matrix *x, const llmc_MoEWeights *w,
                  const llmc_ModelConfig *cfg, llmc_ForwardCache *cache,
                  llmc_Matrix *out);
 
-/* Drop the device copy of an expert set uploaded by moe_forward (no-op if
- * none).  Returns MOE_B200_OK or a negative status. */
-int moe_b200_invalidate(const void *moe_weights);
+/* Drop the device copy of an expert set uploaded by moe_forward, given its
+ * MoEWeights pointer, or the device decoder of inference_step's device mode,
+ * given its Model pointer (no-op if none).  Returns MOE_B200_OK or a
+ * negative status. */
+int moe_b200_invalidate(const void *weights_or_model);
 
 #ifdef __cplusplus
 }

@@ -18,8 +18,25 @@
 #include <vector>
 
 namespace {
+// a resident expert set and the host matrices it was uploaded from
+struct Resident {
+    moe_b200_weights *w = nullptr;
+    std::vector<const float *> src;      // W_router, then gate, up, down of each expert
+};
 std::mutex g_cache_mu;
-std::unordered_map<const void *, moe_b200_weights *> g_cache;
+std::unordered_map<const void *, Resident> g_cache;
+
+std::vector<const float *> host_sources(const llmc_MoEWeights *mw) {
+    std::vector<const float *> v;
+    v.reserve(1 + 3 * (size_t)mw->n_experts);
+    v.push_back(mw->W_router.data);
+    for (int e = 0; e < mw->n_experts; e++) {
+        v.push_back(mw->experts[e].W_gate.data);
+        v.push_back(mw->experts[e].W_up.data);
+        v.push_back(mw->experts[e].W_down.data);
+    }
+    return v;
+}
 
 int env_path() {
     const char *p = std::getenv("MOE_B200_PATH");
@@ -36,11 +53,17 @@ int env_path() {
     std::abort();
 }
 
-// Device expert set of `mw`, uploaded on first sight.
+// Device expert set of `mw`, uploaded on first sight.  An entry whose host
+// matrices moved (a different model reusing the MoEWeights address) is
+// uploaded again; same-address reuse needs moe_b200_invalidate.
 moe_b200_weights *resident(const llmc_MoEWeights *mw, int d, int F, const char *where) {
     std::lock_guard<std::mutex> lk(g_cache_mu);
     auto it = g_cache.find(mw);
-    if (it != g_cache.end()) return it->second;
+    if (it != g_cache.end()) {
+        if (it->second.src == host_sources(mw)) return it->second.w;
+        moe_b200_weights_free(it->second.w);
+        g_cache.erase(it);
+    }
     const int E = mw->n_experts, k = mw->top_k;
     if (mw->W_router.rows != d || mw->W_router.cols != E)
         die(where, "router shape mismatch", MOE_B200_E_INVALID);
@@ -58,7 +81,7 @@ moe_b200_weights *resident(const llmc_MoEWeights *mw, int d, int F, const char *
     int rc = moe_b200_weights_upload(mw->W_router.data, g.data(), u.data(), dn.data(), d, F, E,
                                      k, &w);
     if (rc) die(where, "weight upload", rc);
-    g_cache[mw] = w;
+    g_cache[mw] = Resident{w, host_sources(mw)};
     return w;
 }
 
@@ -83,12 +106,27 @@ extern "C" void moe_forward(const llmc_Matrix *x, const llmc_MoEWeights *mw,
             cache ? cache->expert_ids : nullptr, "moe_forward");
 }
 
-extern "C" int moe_b200_invalidate(const void *moe_weights) {
-    std::lock_guard<std::mutex> lk(g_cache_mu);
-    auto it = g_cache.find(moe_weights);
-    if (it == g_cache.end()) return MOE_B200_OK;
-    int rc = moe_b200_weights_free(it->second);
-    g_cache.erase(it);
+// device decoders of inference_step's device mode, one per Model
+std::mutex g_dec_mu;
+std::unordered_map<const void *, moe_b200_decoder *> g_decoders;
+
+extern "C" int moe_b200_invalidate(const void *ptr) {
+    int rc = MOE_B200_OK;
+    {
+        std::lock_guard<std::mutex> lk(g_cache_mu);
+        auto it = g_cache.find(ptr);
+        if (it != g_cache.end()) {
+            rc = moe_b200_weights_free(it->second.w);
+            g_cache.erase(it);
+        }
+    }
+    std::lock_guard<std::mutex> lk(g_dec_mu);
+    auto it = g_decoders.find(ptr);
+    if (it != g_decoders.end()) {
+        const int r2 = moe_b200_decoder_destroy(it->second);
+        g_decoders.erase(it);
+        if (!rc) rc = r2;
+    }
     return rc;
 }
 
@@ -159,7 +197,46 @@ void softmax_vec(float *v, int n) {
 
 }  // namespace
 
+// MOE_B200_DECODE=device: the whole step on the B200 (moe_b200_decoder),
+// one decoder per Model, created on first use with the state's max_seq_len.
+// The device keeps its own KV cache: s->kv_cache is not written; logits and
+// seq_pos are.  A rewound seq_pos rewinds the device cache; a seq_pos ahead
+// of it (steps taken on the host meanwhile) cannot be reconstructed.
+static bool device_mode() {
+    const char *p = std::getenv("MOE_B200_DECODE");
+    return p && !std::strcmp(p, "device");
+}
+
+static void device_step(const llmc_Model *m, llmc_InferenceState *s, int token) {
+    moe_b200_decoder *dec = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_dec_mu);
+        auto it = g_decoders.find(m);
+        if (it == g_decoders.end()) {
+            const int rc = moe_b200_decoder_create(m, s->max_seq_len, 0, &dec);
+            if (rc) die("inference_step", "device decoder", rc);
+            g_decoders[m] = dec;
+        } else {
+            dec = it->second;
+        }
+    }
+    const int dpos = moe_b200_decoder_pos(dec);
+    if (s->seq_pos != dpos) {
+        if (s->seq_pos > dpos)
+            die("inference_step", "state advanced past the device KV cache", MOE_B200_E_STATE);
+        const int rc = moe_b200_decoder_set_pos(dec, s->seq_pos);
+        if (rc) die("inference_step", "device decoder rewind", rc);
+    }
+    const int rc = moe_b200_decoder_step(dec, token, s->logits);
+    if (rc) die("inference_step", "device decode step", rc);
+    s->seq_pos++;
+}
+
 extern "C" void inference_step(const llmc_Model *m, llmc_InferenceState *s, int token) {
+    if (device_mode()) {
+        device_step(m, s, token);
+        return;
+    }
     const llmc_ModelConfig *cfg = &m->cfg;
     const int d = cfg->d_model, nh = cfg->n_heads, nkv = cfg->n_kv_heads, hd = cfg->head_dim;
     const int kv_dim = s->kv_dim, gqa = nh / nkv, pos = s->seq_pos;

@@ -234,3 +234,25 @@ def rel_err(got: np.ndarray, want: np.ndarray) -> float:
     if den == 0.0:
         return float(np.max(np.abs(got)))
     return float(np.max(np.abs(got.astype(np.float64) - want.astype(np.float64)))) / den
+
+
+def release_ref_model(m_ptr):
+    """Free a reference llm.c Model (from ref_model_init) after dropping the
+    device copies the B200 library keeps for it: the expert sets uploaded by
+    the drop-in moe_forward / inference_step (keyed by each block's
+    MoEWeights pointer) and inference_step's device decoder (keyed by the
+    Model pointer).  The library's residency cache is keyed by pointer, so
+    a later model allocated at the same addresses would otherwise meet the
+    stale copies (its contract: invalidate before changing or freeing)."""
+    import moe_b200 as M
+    import llmc_model as LM
+    L = M.lib()
+    L.moe_b200_invalidate.argtypes = [C.c_void_p]
+    model = LM.Model.from_address(m_ptr)
+    moe_off = LM.BlockWeights.u.offset        # the MoEWeights member of the union
+    for l in range(model.weights.n_layers):
+        blk = model.weights.blocks[l]
+        if blk.use_moe:
+            L.moe_b200_invalidate(C.addressof(blk) + moe_off)
+    L.moe_b200_invalidate(m_ptr)
+    ref().ref_model_free(m_ptr)

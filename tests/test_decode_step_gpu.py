@@ -49,7 +49,7 @@ def test_moe_decode_steps_match_reference_model_forward(moe):
     assert int(np.argmax(got)) == int(np.argmax(want))
     # the MoE weights were uploaded once per layer and reused across steps
     R.ref_inference_free(s)
-    R.ref_model_free(m)
+    O.release_ref_model(m)
 
 
 def test_dense_decode_matches_reference_inference_step(moe):
@@ -67,7 +67,7 @@ def test_dense_decode_matches_reference_inference_step(moe):
         assert O.rel_err(b, a) < 1e-5
     R.ref_inference_free(s_ref)
     R.ref_inference_free(s_ours)
-    R.ref_model_free(m)
+    O.release_ref_model(m)
 
 
 def test_python_model_builder_layout_matches_reference(moe):

@@ -73,7 +73,7 @@ def test_moe_device_decode_matches_reference(moe, flags):
     assert dec.launches == (1 if flags == 0 else 6 * 5 + 1)
     dec.free()
     R.ref_inference_free(s)
-    R.ref_model_free(m)
+    O.release_ref_model(m)
 
 
 @pytest.mark.parametrize("flags", MODES, ids=MODE_IDS)
@@ -91,7 +91,7 @@ def test_dense_device_decode_matches_reference_inference_step(moe, flags):
         assert O.rel_err(got, _logits(R, s)) < 5e-5
     dec.free()
     R.ref_inference_free(s)
-    R.ref_model_free(m)
+    O.release_ref_model(m)
 
 
 def test_device_decode_variants_agree_and_rewind_is_deterministic(moe):
@@ -114,7 +114,7 @@ def test_device_decode_variants_agree_and_rewind_is_deterministic(moe):
         dec.step(int(toks[i]), again)
         assert np.array_equal(again, first[i])
     dec.free()
-    R.ref_model_free(m)
+    O.release_ref_model(m)
 
 
 def test_device_decode_rejects_full_cache_and_bad_token(moe):
@@ -133,4 +133,29 @@ def test_device_decode_rejects_full_cache_and_bad_token(moe):
     dec.step(0)
     assert dec.pos == 2
     dec.free()
-    R.ref_model_free(m)
+    O.release_ref_model(m)
+
+
+def test_inference_step_device_mode(moe, monkeypatch):
+    """llm.c's inference_step symbol with MOE_B200_DECODE=device runs the
+    whole step on the B200 and gives the reference model_forward's logits."""
+    R = O.ref()
+    n = 20
+    m = _model(8, 2, max_seq=n + 4)
+    s = R.ref_inference_init(m)
+    step = _host_step()
+    monkeypatch.setenv("MOE_B200_DECODE", "device")
+    toks = np.random.default_rng(8).integers(0, V, n).astype(np.int32)
+    for t in toks:
+        step(m, s, int(t))
+    assert R.ref_inference_pos(s) == n
+    got = _logits(R, s)
+    want = np.empty(V, np.float32)
+    R.ref_model_forward_last(m, O._i(toks), n, O._f(want))
+    assert O.rel_err(got, want) < 1e-4
+    assert int(np.argmax(got)) == int(np.argmax(want))
+    L = M.lib()
+    L.moe_b200_invalidate.argtypes = [C.c_void_p]
+    assert L.moe_b200_invalidate(m) == 0          # drops the model's device decoder
+    R.ref_inference_free(s)
+    O.release_ref_model(m)
