@@ -42,7 +42,8 @@
 // Loads have long latencies under load (~2 us from HBM for the weights,
 // ~0.7 us from L2 for the token rows), so the shared-memory rings are as
 // deep as fits: weights W 8 × 16 KB (own producer warp, up to 8 steps
-// ahead) and tokens X_big|X_small 4 × 16 KB (own producer warp).  W_small
+// ahead) and tokens X_big|X_small 4 × 16 KB (own producer warp); 10 weight
+// and 2 token stages measured 1.6× slower (the token ring starves).  W_small
 // lives in TMEM (8 slots of 32 columns), not in shared memory.
 // Warp roles (11 warps): 0 weight producer, 10 token producer, 1 TMEM
 // allocator + MMA issuer, 2-5 converter, 6-9 epilogue.  The tensor core's
@@ -91,12 +92,14 @@ static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 struct DecArgs {
     const int *plan;        // cnt | off | mt128 | mt64 | mt256 (token tiles of 64 use mt64)
     int E;
-    int num_kb;             // K / 32
+    int num_kb;             // K steps of 32 per tile (K / 32 / ksplit)
+    int ksplit;             // down only: K halves per weight block (1 or 2), into y and y2
     int NB;                 // weight blocks per expert (F_pad/64 or d_pad/128)
     int w_rows_per_expert;  // 2*F_pad (up/gate) or d_pad (down)
     float *h_big, *h_small; // up/gate outputs [rows × F_pad]
     int ldh;
     float *y;               // down output [rows × d_pad] (local)
+    float *y2;              // down output of the second K half (ksplit = 2)
     int ldy;
     float *const *y_ptrs;   // expert parallel: per-rank output bases
     const int2 *ret;        // expert parallel: (rank, row) of each slice row
@@ -210,7 +213,8 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    const int total = __ldg(a.plan + a.E + 2 * (a.E + 1) + a.E) * a.NB;   // mt64[E] * NB
+    // mt64[E] * NB weight-block × token tiles, each split in ksplit K ranges
+    const int total = __ldg(a.plan + a.E + 2 * (a.E + 1) + a.E) * a.NB * a.ksplit;
     // this unit's tiles are unit, unit + nunits, ...; K steps are numbered
     // across them
     const int my_tiles = unit < total ? (total - 1 - unit) / nunits + 1 : 0;
@@ -232,7 +236,8 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
             int n = 0;                                   // K step
             bool ok = true;
             for (int tile = unit; tile < total && ok; tile += nunits) {
-                const DecTile t = dec_decode(tile, a.plan, a.E, a.NB);
+                const DecTile t = dec_decode(tile / a.ksplit, a.plan, a.E, a.NB);
+                const int kb0 = (tile % a.ksplit) * a.num_kb;
                 int wrow, wrow2 = 0;
                 if (UPGATE) {
                     // this CTA's 64 gate rows f0.. (and, 128 rows on, the matching up rows)
@@ -250,22 +255,22 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                         uint8_t *dst = sW + st * A_BYTES;
                         mbar_expect_tx(&full[st], A_BYTES);
                         if (UPGATE) {
-                            tma_load_2d(dst, &tmW, kb * BK, wrow, &full[st]);
-                            tma_load_2d(dst + A_BYTES / 2, &tmW, kb * BK, wrow2, &full[st]);
+                            tma_load_2d(dst, &tmW, (kb0 + kb) * BK, wrow, &full[st]);
+                            tma_load_2d(dst + A_BYTES / 2, &tmW, (kb0 + kb) * BK, wrow2, &full[st]);
                         } else {
-                            tma_load_2d(dst, &tmW, kb * BK, wrow, &full[st]);
+                            tma_load_2d(dst, &tmW, (kb0 + kb) * BK, wrow, &full[st]);
                         }
                     } else if (!PAIR) {
                         uint8_t *dst = sX + st * XB;
                         mbar_expect_tx(&full[st], XB);
-                        tma_load_2d(dst, &tmXb, kb * BK, t.row0, &full[st]);
-                        tma_load_2d(dst + B_BYTES, &tmXs, kb * BK, t.row0, &full[st]);
+                        tma_load_2d(dst, &tmXb, (kb0 + kb) * BK, t.row0, &full[st]);
+                        tma_load_2d(dst + B_BYTES, &tmXs, (kb0 + kb) * BK, t.row0, &full[st]);
                     } else {
                         // this CTA's column halves of the two B operands
                         uint8_t *dst = sX + st * XB;
                         mbar_expect_tx(&full[st], XB);
-                        tma_load_2d(dst, rank ? &tmXs : &tmXb, kb * BK, t.row0, &full[st]);
-                        tma_load_2d(dst + XB2, &tmXb32, kb * BK, t.row0 + (int)rank * 32, &full[st]);
+                        tma_load_2d(dst, rank ? &tmXs : &tmXb, (kb0 + kb) * BK, t.row0, &full[st]);
+                        tma_load_2d(dst + XB2, &tmXb32, (kb0 + kb) * BK, t.row0 + (int)rank * 32, &full[st]);
                     }
                 }
             }
@@ -379,7 +384,8 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
         int n = 0;
         const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
         for (int tile = unit; tile < total && ok; tile += nunits) {
-            const DecTile t = dec_decode(tile, a.plan, a.E, a.NB);
+            const DecTile t = dec_decode(tile / a.ksplit, a.plan, a.E, a.NB);
+            float *ydst = (tile % a.ksplit) ? a.y2 : a.y;
             float v[NTOK];
 #pragma unroll
             for (int j = 0; j < NTOK; j++) v[j] = 0.0f;
@@ -432,7 +438,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                         const int2 rr = a.ret[row];
                         dst = a.y_ptrs[rr.x] + (size_t)rr.y * a.ldy;
                     } else {
-                        dst = a.y + (size_t)row * a.ldy;
+                        dst = ydst + (size_t)row * a.ldy;
                     }
                     dst[jcol] = v[j];
                 }
@@ -542,22 +548,36 @@ cudaError_t launch_dec_upgate(const DecMaps &m, int d_pad, int F_pad, float *h_b
 {
     const bool pair = max_pairs > 0;
     dec::DecArgs a{};
-    a.plan = plan; a.E = E; a.num_kb = d_pad / dec::BK; a.NB = F_pad / (pair ? 128 : 64);
+    a.plan = plan; a.E = E; a.num_kb = d_pad / dec::BK; a.ksplit = 1; a.NB = F_pad / (pair ? 128 : 64);
     a.w_rows_per_expert = 2 * F_pad; a.h_big = h_big; a.h_small = h_small; a.ldh = F_pad;
     a.status = status;
     return dec_launch<true>(m, a, dec_units(rows_bound, E, a.NB, pair ? max_pairs : num_sms), pair, s);
 }
 
+// K halves for the down GEMM (1 or 2): halves when its weight blocks would
+// fill the SMs in few, unevenly filled waves (and K splits evenly).
+int dec_down_ksplit(int F_pad, int d_pad, int rows_bound, int E, int num_sms) {
+    const int kb = F_pad / dec::BK;
+    const int bound = (ceil_div(rows_bound, dec::NTOK) + E) * (d_pad / dec::MW);
+    return (kb % 2 == 0 && bound < 8 * num_sms) ? 2 : 1;
+}
+
 cudaError_t launch_dec_down(const DecMaps &m, int F_pad, int d_pad, float *y, const int *plan,
                             int E, int rows_bound, int num_sms, int max_pairs, DeviceStatus *status,
-                            cudaStream_t s, float *const *y_ptrs, const int2 *ret)
+                            cudaStream_t s, float *const *y_ptrs, const int2 *ret, float *y2)
 {
     const bool pair = max_pairs > 0 && d_pad % (2 * dec::MW) == 0;
+    const int kb = F_pad / dec::BK;
+    if (y2 != nullptr && (kb % 2 != 0 || ret != nullptr)) return cudaErrorInvalidValue;
     dec::DecArgs a{};
-    a.plan = plan; a.E = E; a.num_kb = F_pad / dec::BK; a.NB = d_pad / (pair ? 2 * dec::MW : dec::MW);
-    a.w_rows_per_expert = d_pad; a.y = y; a.ldy = d_pad; a.y_ptrs = y_ptrs; a.ret = ret;
+    a.plan = plan; a.E = E; a.NB = d_pad / (pair ? 2 * dec::MW : dec::MW);
+    a.ksplit = y2 != nullptr ? 2 : 1;       // second K half written to y2
+    a.num_kb = kb / a.ksplit;
+    a.w_rows_per_expert = d_pad; a.y = y; a.y2 = y2; a.ldy = d_pad; a.y_ptrs = y_ptrs; a.ret = ret;
     a.status = status;
-    return dec_launch<false>(m, a, dec_units(rows_bound, E, a.NB, pair ? max_pairs : num_sms), pair, s);
+    return dec_launch<false>(m, a,
+                             dec_units(rows_bound, E, a.NB * a.ksplit, pair ? max_pairs : num_sms),
+                             pair, s);
 }
 
 }  // namespace moe

@@ -30,7 +30,8 @@ cudaError_t launch_dispatch_scan(const int *tile_cnt, int T, int E, int *tile_pr
                                  cudaStream_t s);
 
 cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
-                           const int *pos_of, const float *wts, float *out, cudaStream_t s);
+                           const int *pos_of, const float *wts, float *out, cudaStream_t s,
+                           const float *y2 = nullptr);
 
 // FP32 FFMA grouped expert GEMMs (64-row tiles scheduled on mt64).
 //   upgate: H[rows×F_pad] = swiglu(X_perm·Wg^T, X_perm·Wu^T)
@@ -84,7 +85,10 @@ cudaError_t launch_dec_upgate(const DecMaps &m, int d_pad, int F_pad, float *h_b
 cudaError_t launch_dec_down(const DecMaps &m, int F_pad, int d_pad, float *y, const int *plan,
                             int E, int rows_bound, int num_sms, int max_pairs, DeviceStatus *status,
                             cudaStream_t s, float *const *y_ptrs = nullptr,
-                            const int2 *ret = nullptr);
+                            const int2 *ret = nullptr, float *y2 = nullptr);
+// 2 when the down GEMM should run in two K halves (into y and a second
+// buffer y2, summed by the combine), else 1
+int dec_down_ksplit(int F_pad, int d_pad, int rows_bound, int E, int num_sms);
 
 // weight repack: src row-major [R × C] (one expert matrix) -> dst rows of
 // the K-major layout, see moe_b200.cu.

@@ -112,6 +112,7 @@ struct Ctx {
     // workspace
     Buf probs, ids, wts, loc, tile_cnt, tile_pref, plan, pos_of, x_perm, h, y;
     Buf xs, hs;                          // small parts of the 3xTF32 split
+    Buf y2;                              // second K half of a split down GEMM
     Buf rpart;                           // split-K router partial logits (small T)
     Buf io_x, io_out, io_bias;
     int last_E = 0;
@@ -213,7 +214,7 @@ extern "C" void moe_b200_shutdown(void) {
         cudaStreamSynchronize(c->stream);
         Buf *bufs[] = {&c->probs, &c->ids, &c->wts, &c->loc, &c->tile_cnt, &c->tile_pref,
                        &c->plan, &c->pos_of, &c->x_perm, &c->h, &c->y, &c->xs, &c->hs,
-                       &c->rpart, &c->io_x, &c->io_out, &c->io_bias};
+                       &c->rpart, &c->y2, &c->io_x, &c->io_out, &c->io_bias};
         for (Buf *b : bufs) free_buf(*b);
         cudaFree(c->status);
         cudaStreamDestroy(c->stream);
@@ -470,6 +471,7 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
     int *plan = (int *)c->plan.p, *pos_of = (int *)c->pos_of.p;
     float *x_perm = (float *)c->x_perm.p, *h = (float *)c->h.p, *y = (float *)c->y.p;
     int launches = 0;
+    float *y2 = nullptr;                 // second K half of the down GEMM, when split
     cudaEvent_t *ev = prof_slot(c);
 #define MARK(i) \
     if (ev) CK(cudaEventRecord(ev[i], s))
@@ -524,12 +526,16 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
         if ((rc = make_tmap(&dn.tmXs, hs, rows, w->F_pad, 64))) return rc;
         if ((rc = make_tmap(&dn.tmXb32, h, rows, w->F_pad, 32))) return rc;
         const int dpairs = (opts && opts->cta_pair) ? c->dec_pairs : 0;
+        if (!dpairs && dec_down_ksplit(w->F_pad, w->d_pad, rows, E, c->num_sms) == 2) {
+            if ((rc = grow(c->y2, (size_t)rows * w->d_pad * 4))) return rc;
+            y2 = (float *)c->y2.p;
+        }
         CK(launch_split_tf32(x_perm, xs, (size_t)rows * w->d_pad, s));
         CK(launch_dec_upgate(up, w->d_pad, w->F_pad, h, hs, plan, E, rows, c->num_sms, dpairs,
                              c->status, s));
         MARK(3);
         CK(launch_dec_down(dn, w->F_pad, w->d_pad, y, plan, E, rows, c->num_sms, dpairs,
-                           c->status, s));
+                           c->status, s, nullptr, nullptr, y2));
         launches += 1;   // the split
     } else if (path == MOE_B200_PATH_FP32) {
         CK(launch_ffma_upgate(x_perm, w->d_pad, w->ug, w->F_pad, h, plan, E, rows, s));
@@ -540,7 +546,7 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
     }
     launches += 2;
     MARK(4);
-    CK(launch_combine(y, d, w->d_pad, T, k, pos_of, wts, d_out, s));
+    CK(launch_combine(y, d, w->d_pad, T, k, pos_of, wts, d_out, s, y2));
     launches += 1;
     MARK(5);
 #undef MARK

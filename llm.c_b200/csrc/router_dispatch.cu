@@ -112,8 +112,9 @@ dispatch_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad,
 __global__ void __launch_bounds__(256)
 combine_kernel(const float *__restrict__ y, int d, int d_pad, int T, int k,
                const int *__restrict__ pos_of, const float *__restrict__ wts,
-               float *__restrict__ out)
+               float *__restrict__ out, const float *__restrict__ y2)
 {
+    // y2 (optional): the second K half of the down GEMM, added to y first
     const int t = blockIdx.x;
     if (t >= T) return;
     int pos[kMaxTopK];
@@ -129,7 +130,12 @@ combine_kernel(const float *__restrict__ y, int d, int d_pad, int T, int k,
 #pragma unroll
             for (int r = 0; r < kMaxTopK; r++) {
                 if (r < k) {
-                    const float4 v = __ldg(reinterpret_cast<const float4 *>(y + (size_t)pos[r] * d_pad) + c);
+                    float4 v = __ldg(reinterpret_cast<const float4 *>(y + (size_t)pos[r] * d_pad) + c);
+                    if (y2) {
+                        const float4 v2 = __ldg(reinterpret_cast<const float4 *>(y2 + (size_t)pos[r] * d_pad) + c);
+                        v.x = __fadd_rn(v.x, v2.x); v.y = __fadd_rn(v.y, v2.y);
+                        v.z = __fadd_rn(v.z, v2.z); v.w = __fadd_rn(v.w, v2.w);
+                    }
                     acc.x = __fmaf_rn(w[r], v.x, acc.x);
                     acc.y = __fmaf_rn(w[r], v.y, acc.y);
                     acc.z = __fmaf_rn(w[r], v.z, acc.z);
@@ -141,7 +147,11 @@ combine_kernel(const float *__restrict__ y, int d, int d_pad, int T, int k,
     } else {
         for (int c = threadIdx.x; c < d; c += blockDim.x) {
             float acc = 0.0f;
-            for (int r = 0; r < k; r++) acc = __fmaf_rn(w[r], __ldg(y + (size_t)pos[r] * d_pad + c), acc);
+            for (int r = 0; r < k; r++) {
+                float v = __ldg(y + (size_t)pos[r] * d_pad + c);
+                if (y2) v = __fadd_rn(v, __ldg(y2 + (size_t)pos[r] * d_pad + c));
+                acc = __fmaf_rn(w[r], v, acc);
+            }
             o[c] = acc;
         }
     }
@@ -164,12 +174,13 @@ cudaError_t launch_dispatch(const float *x, int T, int d, int d_pad, int E, int 
 }
 
 cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
-                           const int *pos_of, const float *wts, float *out, cudaStream_t s)
+                           const int *pos_of, const float *wts, float *out, cudaStream_t s,
+                           const float *y2)
 {
     int threads = 256;
     const int work = (d & 3) == 0 ? d / 4 : d;
     if (work < 256) threads = max(32, round_up(work, 32));
-    combine_kernel<<<T, threads, 0, s>>>(y, d, d_pad, T, k, pos_of, wts, out);
+    combine_kernel<<<T, threads, 0, s>>>(y, d, d_pad, T, k, pos_of, wts, out, y2);
     return cudaGetLastError();
 }
 
