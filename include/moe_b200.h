@@ -213,6 +213,21 @@ int moe_b200_decoder_pos(const moe_b200_decoder *dec);
 int moe_b200_decoder_launches(const moe_b200_decoder *dec);
 int moe_b200_decoder_destroy(moe_b200_decoder *dec);
 
+/* ---- llm.c checkpoints straight to the device ----------------------------
+ * Files written by llm.c's model_save (src/transformer.c:573-617): the magic
+ * "CLLM", the ModelConfig, then every tensor as fp32 in a fixed order.
+ * Experts are streamed through double-buffered pinned staging, one expert
+ * at a time, so a checkpoint far larger than host memory loads; no llm.c
+ * Model is built on the host. */
+/* The checkpoint's ModelConfig (llmc_ModelConfig, include/llmc_moe.h). */
+int moe_b200_checkpoint_config(const char *path, void *cfg);
+/* The MoE block of `layer` (or its dense FFN, as one expert) as a device
+ * expert set, the same as moe_b200_weights_upload from the loaded Model. */
+int moe_b200_checkpoint_load_experts(const char *path, int layer, moe_b200_weights **w);
+/* A device decoder (moe_b200_decoder_create) straight from a checkpoint;
+ * the RoPE tables are built as llm.c's rope_buffer_init builds them. */
+int moe_b200_decoder_load(const char *path, int max_seq, int flags, moe_b200_decoder **dec);
+
 /* ---- expert parallel (one process per GPU, NVLink) --------------------- */
 /* llm.c has no multi-GPU path (README.md:379 lists it as a roadmap item);
  * these entry points extend moe_forward to G GPUs of one node.

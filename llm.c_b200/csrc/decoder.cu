@@ -614,20 +614,27 @@ int enqueue_step(moe_b200_decoder *m) {
 
 }  // namespace
 
-extern "C" int moe_b200_decoder_create(const void *model, int max_seq, int flags,
-                                       moe_b200_decoder **out) {
-    if (!model || !out) return dfail(MOE_B200_E_INVALID, "null argument");
+// Build a decoder from host tensors in llm.c's layouts and the blocks' FFNs
+// already on the device (ownership of every src.blocks[l].ffn passes to the
+// decoder, also on failure).
+int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decoder **out) {
     *out = nullptr;
-    const llmc_Model *mp = static_cast<const llmc_Model *>(model);
-    const llmc_ModelConfig &c = mp->cfg;
+    auto drop_ffns = [&]() {
+        for (const DecBlockSrc &b : src.blocks)
+            if (b.ffn) moe_b200_weights_free(b.ffn);
+    };
+    const llmc_ModelConfig &c = src.cfg;
     const int d = c.d_model, nh = c.n_heads, nkv = c.n_kv_heads, hd = c.head_dim;
+    const int L = (int)src.blocks.size();
     if (d <= 0 || d > kMaxD || nh <= 0 || nkv <= 0 || nh % nkv || hd <= 0 || hd > 128 ||
-        hd % 32 || nh * hd > kMaxD || c.vocab_size <= 0 || mp->weights.n_layers <= 0)
+        hd % 32 || nh * hd > kMaxD || c.vocab_size <= 0 || L <= 0) {
+        drop_ffns();
         return dfail(MOE_B200_E_INVALID, "unsupported model shape for the device decoder");
-    if (max_seq <= 0 || max_seq > mp->rope.max_seq_len || mp->rope.head_dim != hd)
+    }
+    if (max_seq <= 0 || max_seq > src.rope_len) {
+        drop_ffns();
         return dfail(MOE_B200_E_INVALID, "max_seq exceeds the model's RoPE table");
-    int rc = moe_b200_init(-1);
-    if (rc) return rc;
+    }
     moe_b200_decoder *m = new moe_b200_decoder();
     cudaGetDevice(&m->device);
     m->flags = flags;
@@ -635,54 +642,38 @@ extern "C" int moe_b200_decoder_create(const void *model, int max_seq, int flags
     D.d = d; D.d_pad = round_up(d, 128); D.nh = nh; D.nkv = nkv; D.hd = hd; D.nq = nh * hd;
     D.kvd = nkv * hd; D.qkv = D.nq + 2 * D.kvd; D.vocab = c.vocab_size; D.max_seq = max_seq;
     D.nchunk = ceil_div(max_seq, CH); D.eps = c.rms_norm_eps; D.scale = 1.0f / sqrtf((float)hd);
-    m->L = mp->weights.n_layers;
+    m->L = L;
+    m->layers.resize(L);
+    for (int l = 0; l < L; l++) m->layers[l].ffn = src.blocks[l].ffn;   // freed with m from here
     auto bail = [&](int r) { free_all(m); return r; };
 #define DTRY(x)                      \
     do {                             \
         int r_ = (x);                \
         if (r_) return bail(r_);     \
     } while (0)
-    const llmc_ModelWeights &W = mp->weights;
-    DTRY(upload(&m->embed, W.embed.data, (size_t)D.vocab * d));
-    DTRY(upload(&m->rms_final, W.rms_final, d));
-    DTRY(upload(&m->lm_head, W.lm_head.data, (size_t)d * D.vocab));
-    DTRY(upload(&m->rope_cos, mp->rope.cos_table, (size_t)max_seq * (hd / 2)));
-    DTRY(upload(&m->rope_sin, mp->rope.sin_table, (size_t)max_seq * (hd / 2)));
-    m->layers.resize(m->L);
-    std::vector<LayerPtrs> lp(m->L);
+    DTRY(upload(&m->embed, src.embed, (size_t)D.vocab * d));
+    DTRY(upload(&m->rms_final, src.rms_final, d));
+    DTRY(upload(&m->lm_head, src.lm_head, (size_t)d * D.vocab));
+    DTRY(upload(&m->rope_cos, src.rope_cos, (size_t)max_seq * (hd / 2)));
+    DTRY(upload(&m->rope_sin, src.rope_sin, (size_t)max_seq * (hd / 2)));
+    std::vector<LayerPtrs> lp(L);
     std::vector<float> qkv((size_t)d * D.qkv);
-    for (int l = 0; l < m->L; l++) {
-        const llmc_BlockWeights &b = W.blocks[l];
+    for (int l = 0; l < L; l++) {
+        const DecBlockSrc &b = src.blocks[l];
         DecLayer &ly = m->layers[l];
+        if (!ly.ffn || ly.ffn->d != d) return bail(dfail(MOE_B200_E_INVALID, "block FFN shape"));
         DTRY(upload(&ly.rms_attn, b.rms_attn, d));
         DTRY(upload(&ly.rms_ffn, b.rms_ffn, d));
         for (int i = 0; i < d; i++) {           // [W_Q | W_K | W_V] columns per row
             float *row = qkv.data() + (size_t)i * D.qkv;
-            std::memcpy(row, b.attn.W_Q.data + (size_t)i * D.nq, D.nq * sizeof(float));
-            std::memcpy(row + D.nq, b.attn.W_K.data + (size_t)i * D.kvd, D.kvd * sizeof(float));
-            std::memcpy(row + D.nq + D.kvd, b.attn.W_V.data + (size_t)i * D.kvd,
-                        D.kvd * sizeof(float));
+            std::memcpy(row, b.W_Q + (size_t)i * D.nq, D.nq * sizeof(float));
+            std::memcpy(row + D.nq, b.W_K + (size_t)i * D.kvd, D.kvd * sizeof(float));
+            std::memcpy(row + D.nq + D.kvd, b.W_V + (size_t)i * D.kvd, D.kvd * sizeof(float));
         }
         DTRY(upload(&ly.w_qkv, qkv.data(), qkv.size()));
-        DTRY(upload(&ly.w_o, b.attn.W_O.data, (size_t)D.nq * d));
-        const int F = c.ffn_hidden;
-        if (b.use_moe) {
-            const llmc_MoEWeights &mw = b.moe;
-            if (mw.top_k > kMaxTopK) return bail(dfail(MOE_B200_E_INVALID, "top_k too large"));
-            std::vector<const float *> g(mw.n_experts), u(mw.n_experts), dn(mw.n_experts);
-            for (int e = 0; e < mw.n_experts; e++) {
-                g[e] = mw.experts[e].W_gate.data;
-                u[e] = mw.experts[e].W_up.data;
-                dn[e] = mw.experts[e].W_down.data;
-            }
-            DTRY(moe_b200_weights_upload(mw.W_router.data, g.data(), u.data(), dn.data(), d, F,
-                                         mw.n_experts, mw.top_k, &ly.ffn));
-        } else {                                   // dense FFN = one expert, weight 1
-            std::vector<float> zr(d, 0.0f);
-            const float *g = b.ffn.W_gate.data, *u = b.ffn.W_up.data, *dn = b.ffn.W_down.data;
-            DTRY(moe_b200_weights_upload(zr.data(), &g, &u, &dn, d, F, 1, 1, &ly.ffn));
-        }
+        DTRY(upload(&ly.w_o, b.W_O, (size_t)D.nq * d));
         const moe_b200_weights *w = ly.ffn;
+        if (w->k > kMaxTopK) return bail(dfail(MOE_B200_E_INVALID, "top_k too large"));
         lp[l] = LayerPtrs{ly.rms_attn, ly.rms_ffn, ly.w_qkv, ly.w_o, w->router, w->ug, w->dn,
                           w->E, w->k, w->F, w->F_pad};
         m->maxF_pad = m->maxF_pad > w->F_pad ? m->maxF_pad : w->F_pad;
@@ -723,7 +714,7 @@ extern "C" int moe_b200_decoder_create(const void *model, int max_seq, int flags
     // the step as one graph
     if (cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
         return bail(dfail(MOE_B200_E_CUDA, "stream capture"));
-    rc = enqueue_step(m);
+    const int rc = enqueue_step(m);
     cudaGraph_t g = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
     if (rc) { if (g) cudaGraphDestroy(g); return bail(rc); }
@@ -734,6 +725,56 @@ extern "C" int moe_b200_decoder_create(const void *model, int max_seq, int flags
     *out = m;
     return MOE_B200_OK;
 #undef DTRY
+}
+
+extern "C" int moe_b200_decoder_create(const void *model, int max_seq, int flags,
+                                       moe_b200_decoder **out) {
+    if (!model || !out) return dfail(MOE_B200_E_INVALID, "null argument");
+    *out = nullptr;
+    const llmc_Model *mp = static_cast<const llmc_Model *>(model);
+    const llmc_ModelConfig &c = mp->cfg;
+    if (mp->weights.n_layers <= 0 || mp->rope.head_dim != c.head_dim)
+        return dfail(MOE_B200_E_INVALID, "unsupported model for the device decoder");
+    int rc = moe_b200_init(-1);
+    if (rc) return rc;
+    const llmc_ModelWeights &W = mp->weights;
+    DecSrc src;
+    src.cfg = c;
+    src.embed = W.embed.data;
+    src.rms_final = W.rms_final;
+    src.lm_head = W.lm_head.data;
+    src.rope_cos = mp->rope.cos_table;
+    src.rope_sin = mp->rope.sin_table;
+    src.rope_len = mp->rope.max_seq_len;
+    src.blocks.resize(W.n_layers);
+    const int d = c.d_model, F = c.ffn_hidden;
+    for (int l = 0; l < W.n_layers; l++) {
+        const llmc_BlockWeights &b = W.blocks[l];
+        DecBlockSrc &o = src.blocks[l];
+        o.rms_attn = b.rms_attn; o.rms_ffn = b.rms_ffn;
+        o.W_Q = b.attn.W_Q.data; o.W_K = b.attn.W_K.data; o.W_V = b.attn.W_V.data;
+        o.W_O = b.attn.W_O.data;
+        if (b.use_moe) {
+            const llmc_MoEWeights &mw = b.moe;
+            std::vector<const float *> g(mw.n_experts), u(mw.n_experts), dn(mw.n_experts);
+            for (int e = 0; e < mw.n_experts; e++) {
+                g[e] = mw.experts[e].W_gate.data;
+                u[e] = mw.experts[e].W_up.data;
+                dn[e] = mw.experts[e].W_down.data;
+            }
+            rc = moe_b200_weights_upload(mw.W_router.data, g.data(), u.data(), dn.data(), d, F,
+                                         mw.n_experts, mw.top_k, &o.ffn);
+        } else {                                   // dense FFN = one expert, weight 1
+            std::vector<float> zr(d, 0.0f);
+            const float *g = b.ffn.W_gate.data, *u = b.ffn.W_up.data, *dn = b.ffn.W_down.data;
+            rc = moe_b200_weights_upload(zr.data(), &g, &u, &dn, d, F, 1, 1, &o.ffn);
+        }
+        if (rc) {
+            for (int q = 0; q < l; q++) moe_b200_weights_free(src.blocks[q].ffn);
+            return rc;
+        }
+    }
+    return moe::decoder_build(src, max_seq, flags, out);
 }
 
 extern "C" int moe_b200_decoder_step(moe_b200_decoder *m, int token, float *logits) {

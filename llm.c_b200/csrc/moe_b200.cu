@@ -269,17 +269,39 @@ static int weights_alloc(Ctx *c, int d, int F, int E, int k, moe_b200_weights **
     return MOE_B200_OK;
 }
 
+int moe::weights_create(int d, int F, int E, int k, moe_b200_weights **out) {
+    int rc = check_shape(d, F, E, k);
+    if (rc) return rc;
+    Ctx *c;
+    if ((rc = get_ctx(-1, &c))) return rc;
+    return weights_alloc(c, d, F, E, k, out);
+}
+
+int moe::weights_put_expert(moe_b200_weights *w, int ex, const float *d_stage, cudaStream_t s) {
+    const size_t dF = (size_t)w->d * w->F;
+    float *ug = w->ug + (size_t)ex * 2 * w->F_pad * w->d_pad;
+    float *dn = w->dn + (size_t)ex * w->d_pad * w->F_pad;
+    if (launch_repack_upgate(d_stage, d_stage + dF, w->d, w->F, w->d_pad, w->F_pad, ug, s) ||
+        launch_repack_down(d_stage + 2 * dF, w->d, w->F, w->d_pad, w->F_pad, dn, s))
+        return fail(MOE_B200_E_CUDA, "repack launch failed");
+    return MOE_B200_OK;
+}
+
+cudaStream_t moe::current_stream() {
+    Ctx *c;
+    return get_ctx(-1, &c) ? nullptr : c->stream;
+}
+
 extern "C" int moe_b200_weights_upload(const float *W_router, const float *const *W_gate,
                                        const float *const *W_up, const float *const *W_down,
                                        int d, int F, int E, int top_k, moe_b200_weights **out) {
     if (!out || !W_router || !W_gate || !W_up || !W_down)
         return fail(MOE_B200_E_INVALID, "null argument");
-    int rc = check_shape(d, F, E, top_k);
+    moe_b200_weights *w;
+    int rc = moe::weights_create(d, F, E, top_k, &w);
     if (rc) return rc;
     Ctx *c;
-    if ((rc = get_ctx(-1, &c))) return rc;
-    moe_b200_weights *w;
-    if ((rc = weights_alloc(c, d, F, E, top_k, &w))) return rc;
+    if ((rc = get_ctx(-1, &c))) { moe_b200_weights_free(w); return rc; }
     float *stage = nullptr;
     const size_t dF = (size_t)d * F;
     cudaError_t e = cudaMalloc(&stage, 3 * dF * 4);
@@ -305,13 +327,7 @@ extern "C" int moe_b200_weights_upload(const float *W_router, const float *const
                 rc = fail(MOE_B200_E_CUDA, "expert %d upload failed", ex);
                 break;
             }
-            float *ug = w->ug + (size_t)ex * 2 * w->F_pad * w->d_pad;
-            float *dn = w->dn + (size_t)ex * w->d_pad * w->F_pad;
-            if (launch_repack_upgate(stage, stage + dF, d, F, w->d_pad, w->F_pad, ug, c->stream) ||
-                launch_repack_down(stage + 2 * dF, d, F, w->d_pad, w->F_pad, dn, c->stream)) {
-                rc = fail(MOE_B200_E_CUDA, "repack launch failed");
-                break;
-            }
+            if ((rc = moe::weights_put_expert(w, ex, stage, c->stream))) break;
             // staging is reused by the next expert
             if (cudaStreamSynchronize(c->stream)) {
                 rc = fail(MOE_B200_E_CUDA, "repack failed: %s", cudaGetErrorString(cudaGetLastError()));

@@ -4,6 +4,11 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <vector>
+
+#include "../../include/llmc_moe.h"
+#include "../../include/moe_b200.h"
+
 struct moe_b200_weights {
     int device;
     int d, F, E, k, d_pad, F_pad;
@@ -18,6 +23,7 @@ struct moe_b200_weights {
     int down_bn;
 };
 
+
 namespace moe {
 // Record a status and its detail text as this host thread's last error
 // (read back through moe_b200_last_error); returns `code`.
@@ -29,4 +35,34 @@ __attribute__((visibility("hidden"))) cudaEvent_t *profile_events(int device);
 __attribute__((visibility("hidden"))) void note_forward(int device, int E, int launches, int path);
 // Number of SMs of `device` (0 if the device is unusable).
 __attribute__((visibility("hidden"))) int device_sms(int device);
+
+// ---- building blocks shared by the upload, the checkpoint loader and the
+// device decoder ----
+// A device expert set of the given shape, weights not yet filled.
+__attribute__((visibility("hidden"))) int weights_create(int d, int F, int E, int k,
+                                                         moe_b200_weights **out);
+// Repack expert `ex` from a device staging buffer holding its W_gate, W_up
+// [d × F] and W_down [F × d] (llm.c's host layouts, back to back) into the
+// set's packed layout, on `s`.
+__attribute__((visibility("hidden"))) int weights_put_expert(moe_b200_weights *w, int ex,
+                                                             const float *d_stage, cudaStream_t s);
+// The library stream of the current device.
+__attribute__((visibility("hidden"))) cudaStream_t current_stream();
+
+// A device decoder from host tensors (llm.c layouts) and the blocks' FFNs
+// already on the device; owns every blocks[l].ffn afterwards.
+struct DecBlockSrc {
+    const float *rms_attn = nullptr, *rms_ffn = nullptr;
+    const float *W_Q = nullptr, *W_K = nullptr, *W_V = nullptr, *W_O = nullptr;
+    moe_b200_weights *ffn = nullptr;
+};
+struct DecSrc {
+    llmc_ModelConfig cfg;
+    const float *embed = nullptr, *rms_final = nullptr, *lm_head = nullptr;
+    const float *rope_cos = nullptr, *rope_sin = nullptr;   // [rope_len × head_dim/2]
+    int rope_len = 0;
+    std::vector<DecBlockSrc> blocks;
+};
+__attribute__((visibility("hidden"))) int decoder_build(const DecSrc &src, int max_seq, int flags,
+                                                        moe_b200_decoder **out);
 }  // namespace moe

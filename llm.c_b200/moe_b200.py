@@ -81,6 +81,15 @@ def lib() -> C.CDLL:
     L.moe_b200_profile_read.argtypes = [C.POINTER(C.c_double), _ip]
     L.moe_b200_synth_fill.argtypes = [_vp, C.c_size_t, C.c_uint64, C.c_uint64, C.c_uint64,
                                       C.c_float, _vp]
+    L.moe_b200_checkpoint_config.argtypes = [C.c_char_p, _vp]
+    L.moe_b200_checkpoint_load_experts.argtypes = [C.c_char_p, C.c_int, C.POINTER(_vp)]
+    L.moe_b200_decoder_create.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.moe_b200_decoder_load.argtypes = [C.c_char_p, C.c_int, C.c_int, C.POINTER(_vp)]
+    L.moe_b200_decoder_step.argtypes = [_vp, C.c_int, _fp]
+    L.moe_b200_decoder_set_pos.argtypes = [_vp, C.c_int]
+    L.moe_b200_decoder_pos.argtypes = [_vp]
+    L.moe_b200_decoder_launches.argtypes = [_vp]
+    L.moe_b200_decoder_destroy.argtypes = [_vp]
     _lib = L
     return L
 
@@ -153,6 +162,18 @@ class MoEWeights:
         _check(lib().moe_b200_weights_synth(seed, w_std, d, F, E, top_k, C.byref(h)),
                "moe_b200_weights_synth")
         return cls(h.value, d, F, E, top_k)
+
+    @classmethod
+    def from_checkpoint(cls, path, layer: int) -> "MoEWeights":
+        """Block `layer`'s experts (or dense FFN, as one expert) of an llm.c
+        checkpoint (model_save format), streamed straight to the device."""
+        cfg = checkpoint_config(path)
+        h = _vp()
+        _check(lib().moe_b200_checkpoint_load_experts(_path(path), int(layer), C.byref(h)),
+               "moe_b200_checkpoint_load_experts")
+        moe = cfg.n_experts > 1
+        return cls(h.value, cfg.d_model, cfg.ffn_hidden, cfg.n_experts if moe else 1,
+                   cfg.top_k_experts if moe else 1)
 
     def download(self, experts: bool = True):
         d, F, E = self.d, self.F, self.E
@@ -437,6 +458,18 @@ class EP:
             self.handle = 0
 
 
+def _path(path) -> bytes:
+    return str(path).encode()
+
+
+def checkpoint_config(path) -> "LlmcModelConfig":
+    """The ModelConfig stored in an llm.c checkpoint (model_save format)."""
+    cfg = LlmcModelConfig()
+    _check(lib().moe_b200_checkpoint_config(_path(path), C.byref(cfg)),
+           "moe_b200_checkpoint_config")
+    return cfg
+
+
 class Decoder:
     """Device-resident single-token decode of an llm.c Model (ctypes pointer
     or address of an llmc_Model, e.g. from llmc_model.LlmcDecoder or the
@@ -446,17 +479,23 @@ class Decoder:
 
     def __init__(self, model_ptr, max_seq: int, flags: int = 0):
         L = lib()
-        L.moe_b200_decoder_create.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp)]
-        L.moe_b200_decoder_step.argtypes = [_vp, C.c_int, _fp]
-        L.moe_b200_decoder_set_pos.argtypes = [_vp, C.c_int]
-        L.moe_b200_decoder_pos.argtypes = [_vp]
-        L.moe_b200_decoder_launches.argtypes = [_vp]
-        L.moe_b200_decoder_destroy.argtypes = [_vp]
         h = _vp()
         _check(L.moe_b200_decoder_create(model_ptr, int(max_seq), int(flags), C.byref(h)),
                "moe_b200_decoder_create")
         self.handle = h
         self._vocab = None
+
+    @classmethod
+    def from_checkpoint(cls, path, max_seq: int, flags: int = 0) -> "Decoder":
+        """A device decoder straight from an llm.c checkpoint file; no llm.c
+        Model is built on the host."""
+        h = _vp()
+        _check(lib().moe_b200_decoder_load(_path(path), int(max_seq), int(flags), C.byref(h)),
+               "moe_b200_decoder_load")
+        self = cls.__new__(cls)
+        self.handle = h
+        self._vocab = None
+        return self
 
     def step(self, token: int, logits: np.ndarray | None = None):
         """Run one step; fills `logits` (float32, vocab) when given."""

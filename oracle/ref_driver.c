@@ -129,3 +129,7 @@ void ref_inference_step(void *m, void *s, int token) {
 }
 float *ref_inference_logits(void *s) { return ((InferenceState *)s)->logits; }
 int ref_inference_pos(void *s) { return ((InferenceState *)s)->seq_pos; }
+
+/* llm.c's own checkpoint format (model_save / model_load, src/transformer.c:573-697) */
+int ref_model_save(void *m, const char *path) { return model_save((const Model *)m, path); }
+void *ref_model_load(const char *path) { return model_load(path); }

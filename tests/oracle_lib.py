@@ -101,6 +101,10 @@ def ref():
         lib.ref_inference_logits.argtypes = [C.c_void_p]
         lib.ref_inference_pos.restype = C.c_int
         lib.ref_inference_pos.argtypes = [C.c_void_p]
+        lib.ref_model_save.restype = C.c_int
+        lib.ref_model_save.argtypes = [C.c_void_p, C.c_char_p]
+        lib.ref_model_load.restype = C.c_void_p
+        lib.ref_model_load.argtypes = [C.c_char_p]
         _ref = lib
     return _ref
 
