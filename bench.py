@@ -405,6 +405,74 @@ def run_decode(args):
 # ----------------------------------------------------------------------------
 # GPU
 # ----------------------------------------------------------------------------
+def block_ffn_measure(args, M, w, x, bptr, host_bias_ptr, path, stream, stage_ms_moe, n_moe,
+                      moe_ms, T, d, E, k):
+    """Device and end-to-end timing of moe_b200_block_ffn (RMSNorm + MoE +
+    residual) on the bench workload, against the MoE-only step just timed."""
+    import torch
+    peaks = measured_peaks()
+    rms = torch.ones(d, device="cuda") + 0.1 * torch.randn(d, device="cuda",
+                                                           generator=torch.Generator("cuda").manual_seed(1))
+    xb = x.clone()
+    xn = torch.empty_like(x)
+    probs = torch.empty((T, E), device="cuda")
+    ids = torch.empty((T, k), dtype=torch.int32, device="cuda")
+
+    def step():
+        M.block_ffn_device(w, rms.data_ptr(), 1e-5, xb.data_ptr(), T, xn.data_ptr(),
+                           probs.data_ptr(), ids.data_ptr(), bias_ptr=bptr, path=path,
+                           stream=stream.cuda_stream, cta_pair=args.cta_pair)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches = M.last_launches()
+    M.profile_enable(True)
+    M.profile_read()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    M.profile_enable(False)
+    st, n = M.profile_read()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    # the RMSNorm runs inside the router stage: its time is the router stage's growth
+    norm_ms = st["router"] / max(n, 1) - stage_ms_moe["router"] / max(n_moe, 1)
+    norm_bytes = 2.0 * 4 * T * d                 # read x, write x_norm
+    # end to end through the host C-ABI: x up, x (and probs, ids) back
+    hx = torch.empty((T, d), dtype=torch.float32, pin_memory=True)
+    hx.copy_(x.cpu())
+    hrms = rms.cpu().contiguous()
+    hprobs = torch.empty((T, E), dtype=torch.float32, pin_memory=True)
+    hids = torch.empty((T, k), dtype=torch.int32, pin_memory=True)
+    hb = host_bias_ptr
+
+    def e2e():
+        M.block_ffn_host_ptr(w, hrms.data_ptr(), 1e-5, hx.data_ptr(), T, None, hprobs.data_ptr(),
+                             hids.data_ptr(), hb, path=path, cta_pair=args.cta_pair)
+
+    for _ in range(2):
+        e2e()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e()
+    e2e_ms = 1000.0 * (time.perf_counter() - t0) / args.steps
+    return {
+        "ms_per_step": ms, "tokens_per_s": T / (ms / 1000.0),
+        "overhead_vs_moe_ms": ms - moe_ms,
+        "rmsnorm_ms": norm_ms,
+        "rmsnorm_gbs": norm_bytes / (norm_ms / 1000.0) / 1e9 if norm_ms > 0 else None,
+        "rmsnorm_frac_of_hbm": (norm_bytes / (norm_ms / 1000.0) / 1e9 / peaks["hbm_gbs"]
+                                if norm_ms > 0 else None),
+        "launches_per_step": launches,
+        "e2e": {"value": T / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": 4 * T * d + 4 * d + (4 * E if hb is not None else 0),
+                "d2h_bytes_per_step": 4 * T * d + 4 * T * E + 4 * T * k},
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -567,6 +635,14 @@ def main():
     barrier()
     assert torch.equal(hout, out.cpu()), "e2e output differs from the device-resident run"
 
+    # ---- the FFN half of block_forward fused around the same MoE
+    # (src/transformer.c:752-767): RMSNorm in front, residual in the combine.
+    # x is updated in place step after step on a scratch copy.
+    block = None
+    if ep is None:
+        block = block_ffn_measure(args, M, w, x, bptr, hb, path, stream, stage_ms_moe=stage_ms,
+                                  n_moe=n_fw, moe_ms=ms, T=T, d=d, E=E, k=k)
+
     # ---- roofline of the dominant kernel (expert up/gate GEMM on this rank)
     peaks = measured_peaks()
     tf32_peak = peaks["bf16_sustained"] / 2.0
@@ -634,6 +710,8 @@ def main():
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    if block is not None:
+        line["block_ffn"] = block
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = len(os.sched_getaffinity(0))
         tps, S, kind, desc, _, _ = reference_sample(c, budget_s=12.0, threads=threads)

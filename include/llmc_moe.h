@@ -168,6 +168,22 @@ void moe_forward(const llmc_Matrix *x, const llmc_MoEWeights *w,
                  const llmc_ModelConfig *cfg, llmc_ForwardCache *cache,
                  llmc_Matrix *out);
 
+/*
+ * moe_b200_llmc_block_ffn — the FFN half of llm.c's block_forward
+ * (src/transformer.c:752-767) as one call, for a maintainer to put in place
+ * of those lines:
+ *     x_norm = rms_norm(x, bw->rms_ffn, eps); x += FFN_or_MoE(x_norm)
+ * x [rows × d_model] is updated in place.  MoE blocks write
+ * cache->router_probs and cache->expert_ids as moe_forward does; dense
+ * blocks run their FFN as one expert.  cache->x_norm_ffn and cache->ffn_out
+ * are not written: nothing in llm.c reads them after block_forward
+ * (model_backward recomputes the norms from its saved block inputs,
+ * src/transformer.c:986-996).  Weights stay resident as for moe_forward
+ * (moe_b200_invalidate with &bw->moe or &bw->ffn).  Aborts on failure.
+ */
+void moe_b200_llmc_block_ffn(llmc_Matrix *x, const llmc_BlockWeights *bw,
+                             llmc_ForwardCache *cache, const llmc_ModelConfig *cfg);
+
 /* Drop the device copy of an expert set uploaded by moe_forward, given its
  * MoEWeights pointer, or the device decoder of inference_step's device mode,
  * given its Model pointer (no-op if none).  Returns MOE_B200_OK or a

@@ -129,11 +129,35 @@ int moe_b200_forward(const moe_b200_weights *w, const float *router_bias,
  * (a cudaStream_t, or NULL for the library stream).  No host
  * synchronisation and no allocation once the workspace has grown to T, so
  * the call can be captured in a CUDA graph after one warm-up call at the
- * largest T. */
+ * largest T.  d_x and d_out must be 16-byte aligned. */
 int moe_b200_forward_device(const moe_b200_weights *w, const float *d_bias,
                             const float *d_x, int T, float *d_out,
                             float *d_router_probs, int *d_expert_ids,
                             const moe_b200_opts *opts, void *stream);
+
+/* The FFN half of llm.c's block_forward for a MoE block
+ * (src/transformer.c:752-767) in one call:
+ *   x_norm = rms_norm(x, rms_weight, eps)      (src/matrix.c:666-713)
+ *   x     += moe_forward(x_norm)               (mat_add_inplace)
+ * The RMSNorm runs on the device in front of the router, and the residual
+ * add is fused into the combine, so x goes up once and comes back once.
+ *   rms_weight [d]    block's rms_ffn
+ *   x [T×d]           residual stream, updated in place
+ *   x_norm [T×d]      receives the normalised rows (cache->x_norm_ffn), or
+ *                     NULL
+ *   router_bias, router_probs, expert_ids, opts as moe_b200_forward.
+ * The RMSNorm follows the reference's summation order with correctly rounded
+ * division and square root. */
+int moe_b200_block_ffn(const moe_b200_weights *w, const float *rms_weight, float eps,
+                       const float *router_bias, float *x, int T, float *x_norm,
+                       float *router_probs, int *expert_ids, const moe_b200_opts *opts);
+
+/* Same on DEVICE buffers, asynchronous on `stream` (NULL = library stream);
+ * d_x and d_x_norm 16-byte aligned. */
+int moe_b200_block_ffn_device(const moe_b200_weights *w, const float *d_rms_weight, float eps,
+                              const float *d_bias, float *d_x, int T, float *d_x_norm,
+                              float *d_router_probs, int *d_expert_ids,
+                              const moe_b200_opts *opts, void *stream);
 
 /* Size of the static device array behind moe_b200_forward_noalloc. */
 #define MOE_B200_NOALLOC_SCRATCH_BYTES (16u << 20)

@@ -486,6 +486,8 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
                                           int *d_expert_ids, const moe_b200_opts *opts,
                                           void *stream) {
     if (!ep || !d_x || !d_out) return ep_fail(MOE_B200_E_INVALID, "null argument%s%s");
+    if (((uintptr_t)d_x | (uintptr_t)d_out) & 15)
+        return ep_fail(MOE_B200_E_INVALID, "x and out must be 16-byte aligned%s%s");
     if (T < 0 || T > ep->max_T)
         return ep_fail(MOE_B200_E_INVALID, "T outside [0, max_tokens_per_rank]%s%s");
     const moe_b200_weights *w = ep->w;

@@ -31,7 +31,11 @@ cudaError_t launch_dispatch_scan(const int *tile_cnt, int T, int E, int *tile_pr
 
 cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
                            const int *pos_of, const float *wts, float *out, cudaStream_t s,
-                           const float *y2 = nullptr);
+                           const float *y2 = nullptr, const float *resid = nullptr);
+// block_forward's pre-FFN RMSNorm over rows of x[T × d] (block_ffn.cu)
+cudaError_t launch_rmsnorm(const float *x, int T, int d, const float *weight, float eps,
+                           float *out, cudaStream_t s);
+int rmsnorm_max_d();
 
 // FP32 FFMA grouped expert GEMMs (64-row tiles scheduled on mt64).
 //   upgate: H[rows×F_pad] = swiglu(X_perm·Wg^T, X_perm·Wu^T)

@@ -2,10 +2,14 @@
 //   moe_forward     (src/transformer.c:287-366)  block / prefill MoE
 //   inference_step  (src/inference.c:231-358)    single-token decode step,
 //                                                 with the MoE branch filled in
+//   moe_b200_llmc_block_ffn (src/transformer.c:752-767)  block_forward's
+//                                                 RMSNorm + FFN + residual
 //
-// Residency cache: one device expert set per MoEWeights pointer, uploaded
-// on first sight from the host matrices (include/transformer.h:53-58) and
-// kept until moe_b200_invalidate or shutdown.
+// Residency cache: one device expert set per MoEWeights pointer (and, for
+// dense blocks run through moe_b200_llmc_block_ffn, one single-expert set
+// per FFNWeights pointer), uploaded on first sight from the host matrices
+// (include/transformer.h:53-58) and kept until moe_b200_invalidate or
+// shutdown.
 #include "../../include/llmc_moe.h"
 #include "../../include/moe_b200.h"
 
@@ -25,6 +29,7 @@ struct Resident {
 };
 std::mutex g_cache_mu;
 std::unordered_map<const void *, Resident> g_cache;
+std::unordered_map<const void *, Resident> g_dense;   // keyed by FFNWeights pointer
 
 std::vector<const float *> host_sources(const llmc_MoEWeights *mw) {
     std::vector<const float *> v;
@@ -85,6 +90,29 @@ moe_b200_weights *resident(const llmc_MoEWeights *mw, int d, int F, const char *
     return w;
 }
 
+// A dense FFN (FFNWeights) as a one-expert set with a zero router: softmax
+// over one logit is 1, so the combine returns the expert's output exactly.
+moe_b200_weights *resident_dense(const llmc_FFNWeights *fw, int d, int F, const char *where) {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    const std::vector<const float *> src{fw->W_gate.data, fw->W_up.data, fw->W_down.data};
+    auto it = g_dense.find(fw);
+    if (it != g_dense.end()) {
+        if (it->second.src == src) return it->second.w;
+        moe_b200_weights_free(it->second.w);
+        g_dense.erase(it);
+    }
+    if (fw->W_gate.rows != d || fw->W_gate.cols != F || fw->W_up.rows != d ||
+        fw->W_up.cols != F || fw->W_down.rows != F || fw->W_down.cols != d)
+        die(where, "dense FFN shape mismatch", MOE_B200_E_INVALID);
+    const std::vector<float> zero_router((size_t)d, 0.0f);
+    const float *g = fw->W_gate.data, *u = fw->W_up.data, *dn = fw->W_down.data;
+    moe_b200_weights *w = nullptr;
+    const int rc = moe_b200_weights_upload(zero_router.data(), &g, &u, &dn, d, F, 1, 1, &w);
+    if (rc) die(where, "weight upload", rc);
+    g_dense[fw] = Resident{w, src};
+    return w;
+}
+
 // The forward shared by both entry points: host buffers in, host buffers out.
 void run_moe(const llmc_MoEWeights *mw, int F, const float *x, int T, int d, float *out,
              float *probs, int *ids, const char *where) {
@@ -96,6 +124,30 @@ void run_moe(const llmc_MoEWeights *mw, int F, const float *x, int T, int d, flo
     if (rc) die(where, "forward", rc);
 }
 }  // namespace
+
+// block_forward's FFN half (src/transformer.c:752-767): x_norm =
+// rms_norm(x, rms_ffn); FFN or MoE of x_norm; x += result — one device call.
+extern "C" void moe_b200_llmc_block_ffn(llmc_Matrix *x, const llmc_BlockWeights *bw,
+                                        llmc_ForwardCache *cache, const llmc_ModelConfig *cfg) {
+    const char *where = "moe_b200_llmc_block_ffn";
+    const int T = x->rows, d = x->cols;
+    if (d != cfg->d_model) die(where, "x width is not d_model", MOE_B200_E_INVALID);
+    moe_b200_opts opts;
+    std::memset(&opts, 0, sizeof opts);
+    opts.path = env_path();
+    int rc;
+    if (bw->use_moe) {
+        moe_b200_weights *w = resident(&bw->moe, d, cfg->ffn_hidden, where);
+        rc = moe_b200_block_ffn(w, bw->rms_ffn, cfg->rms_norm_eps, nullptr, x->data, T, nullptr,
+                                cache ? cache->router_probs : nullptr,
+                                cache ? cache->expert_ids : nullptr, &opts);
+    } else {
+        moe_b200_weights *w = resident_dense(&bw->ffn, d, cfg->ffn_hidden, where);
+        rc = moe_b200_block_ffn(w, bw->rms_ffn, cfg->rms_norm_eps, nullptr, x->data, T, nullptr,
+                                nullptr, nullptr, &opts);
+    }
+    if (rc) die(where, "block FFN", rc);
+}
 
 extern "C" void moe_forward(const llmc_Matrix *x, const llmc_MoEWeights *mw,
                             const llmc_ModelConfig *cfg, llmc_ForwardCache *cache,
@@ -114,10 +166,13 @@ extern "C" int moe_b200_invalidate(const void *ptr) {
     int rc = MOE_B200_OK;
     {
         std::lock_guard<std::mutex> lk(g_cache_mu);
-        auto it = g_cache.find(ptr);
-        if (it != g_cache.end()) {
-            rc = moe_b200_weights_free(it->second.w);
-            g_cache.erase(it);
+        for (auto *map : {&g_cache, &g_dense}) {
+            auto it = map->find(ptr);
+            if (it != map->end()) {
+                const int r = moe_b200_weights_free(it->second.w);
+                if (!rc) rc = r;
+                map->erase(it);
+            }
         }
     }
     std::lock_guard<std::mutex> lk(g_dec_mu);

@@ -115,6 +115,7 @@ struct Ctx {
     Buf y2;                              // second K half of a split down GEMM
     Buf rpart;                           // split-K router partial logits (small T)
     Buf io_x, io_out, io_bias;
+    Buf xn, io_rms;                      // block FFN: RMSNorm output, host-call norm weights
     int last_E = 0;
     int last_launches = 0;
     int last_path = 0;
@@ -214,7 +215,8 @@ extern "C" void moe_b200_shutdown(void) {
         cudaStreamSynchronize(c->stream);
         Buf *bufs[] = {&c->probs, &c->ids, &c->wts, &c->loc, &c->tile_cnt, &c->tile_pref,
                        &c->plan, &c->pos_of, &c->x_perm, &c->h, &c->y, &c->xs, &c->hs,
-                       &c->rpart, &c->y2, &c->io_x, &c->io_out, &c->io_bias};
+                       &c->rpart, &c->y2, &c->io_x, &c->io_out, &c->io_bias,
+                       &c->xn, &c->io_rms};
         for (Buf *b : bufs) free_buf(*b);
         cudaFree(c->status);
         cudaStreamDestroy(c->stream);
@@ -418,6 +420,8 @@ extern "C" int moe_b200_weights_download(const moe_b200_weights *w, float *W_rou
 // ---------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------
+static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
 static int pick_path(const moe_b200_weights *w, int T, const moe_b200_opts *opts) {
     int path = opts ? opts->path : MOE_B200_PATH_AUTO;
     if (path == MOE_B200_PATH_AUTO) {
@@ -473,9 +477,19 @@ static cudaEvent_t *prof_slot(Ctx *c) {
     return c->ev[slot];
 }
 
+// block_forward's FFN half around the MoE forward (src/transformer.c:752-767):
+// the input is the residual stream x, RMSNorm writes x_norm for the router
+// and the dispatch, and the combine adds the MoE output back onto x.
+struct BlockNorm {
+    const float *weight;   // device [d]
+    float eps;
+    float *x_norm;         // device [T × d]
+};
+
 static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, const float *d_x,
                       int T, float *d_out, float *d_probs, int *d_ids,
-                      const moe_b200_opts *opts, cudaStream_t s) {
+                      const moe_b200_opts *opts, cudaStream_t s,
+                      const BlockNorm *bn = nullptr) {
     int rc = ensure_workspace(c, w, T);
     if (rc) return rc;
     const int E = w->E, k = w->k, d = w->d;
@@ -493,6 +507,13 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
     if (ev) CK(cudaEventRecord(ev[i], s))
 
     MARK(0);
+    const float *resid = nullptr;
+    if (bn) {
+        CK(launch_rmsnorm(d_x, T, d, bn->weight, bn->eps, bn->x_norm, s));
+        launches += 1;
+        resid = d_x;
+        d_x = bn->x_norm;
+    }
     const int nsplit = router_splits(T, d);
     if (nsplit > 1 && (rc = grow(c->rpart, (size_t)nsplit * T * E * 4))) return rc;
     CK(launch_router(d_x, T, d, w->router, d_bias, E, k, probs, ids, wts, loc, tile_cnt, s,
@@ -562,7 +583,7 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
     }
     launches += 2;
     MARK(4);
-    CK(launch_combine(y, d, w->d_pad, T, k, pos_of, wts, d_out, s, y2));
+    CK(launch_combine(y, d, w->d_pad, T, k, pos_of, wts, d_out, s, y2, resid));
     launches += 1;
     MARK(5);
 #undef MARK
@@ -580,12 +601,44 @@ extern "C" int moe_b200_forward_device(const moe_b200_weights *w, const float *d
     if (T < 0) return fail(MOE_B200_E_INVALID, "T=%d", T);
     if (T == 0) return MOE_B200_OK;
     if (!d_x || !d_out) return fail(MOE_B200_E_INVALID, "null x/out");
+    if (!aligned16(d_x) || !aligned16(d_out))
+        return fail(MOE_B200_E_INVALID, "device x/out must be 16-byte aligned");
     if ((int64_t)T * w->k > (int64_t)1 << 30) return fail(MOE_B200_E_INVALID, "T too large");
     Ctx *c;
     int rc = get_ctx(w->device, &c);
     if (rc) return rc;
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     return forward_on(c, w, d_bias, d_x, T, d_out, d_router_probs, d_expert_ids, opts, s);
+}
+
+static int block_args_check(const moe_b200_weights *w, const void *rms_weight, const void *x,
+                            int T) {
+    if (!w) return fail(MOE_B200_E_INVALID, "null weights");
+    if (T < 0) return fail(MOE_B200_E_INVALID, "T=%d", T);
+    if (T > 0 && (!x || !rms_weight)) return fail(MOE_B200_E_INVALID, "null x/rms_weight");
+    if ((int64_t)T * w->k > (int64_t)1 << 30) return fail(MOE_B200_E_INVALID, "T too large");
+    if (w->d > rmsnorm_max_d()) return fail(MOE_B200_E_INVALID, "d=%d above the RMSNorm limit", w->d);
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_block_ffn_device(const moe_b200_weights *w, const float *d_rms_weight,
+                                         float eps, const float *d_bias, float *d_x, int T,
+                                         float *d_x_norm, float *d_router_probs,
+                                         int *d_expert_ids, const moe_b200_opts *opts,
+                                         void *stream) {
+    int rc = block_args_check(w, d_rms_weight, d_x, T);
+    if (rc || T == 0) return rc;
+    if (!aligned16(d_x) || (d_x_norm && !aligned16(d_x_norm)))
+        return fail(MOE_B200_E_INVALID, "device x/x_norm must be 16-byte aligned");
+    Ctx *c;
+    if ((rc = get_ctx(w->device, &c))) return rc;
+    if (!d_x_norm) {
+        if ((rc = grow(c->xn, (size_t)T * w->d * 4))) return rc;
+        d_x_norm = (float *)c->xn.p;
+    }
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    const BlockNorm bn{d_rms_weight, eps, d_x_norm};
+    return forward_on(c, w, d_bias, d_x, T, d_x, d_router_probs, d_expert_ids, opts, s, &bn);
 }
 
 static int check_status(Ctx *c) {
@@ -627,6 +680,42 @@ extern "C" int moe_b200_forward(const moe_b200_weights *w, const float *router_b
                     (float *)c->probs.p, (int *)c->ids.p, opts, s);
     if (rc) return rc;
     CK(cudaMemcpyAsync(out, c->io_out.p, xb, cudaMemcpyDeviceToHost, s));
+    if (router_probs)
+        CK(cudaMemcpyAsync(router_probs, c->probs.p, (size_t)T * w->E * 4, cudaMemcpyDeviceToHost, s));
+    if (expert_ids)
+        CK(cudaMemcpyAsync(expert_ids, c->ids.p, (size_t)T * w->k * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return check_status(c);
+}
+
+extern "C" int moe_b200_block_ffn(const moe_b200_weights *w, const float *rms_weight, float eps,
+                                  const float *router_bias, float *x, int T, float *x_norm,
+                                  float *router_probs, int *expert_ids,
+                                  const moe_b200_opts *opts) {
+    int rc = block_args_check(w, rms_weight, x, T);
+    if (rc || T == 0) return rc;
+    Ctx *c;
+    if ((rc = get_ctx(w->device, &c))) return rc;
+    const size_t xb = (size_t)T * w->d * 4;
+    if ((rc = grow(c->io_x, xb))) return rc;
+    if ((rc = grow(c->xn, xb))) return rc;
+    if ((rc = grow(c->io_rms, (size_t)w->d * 4))) return rc;
+    if ((rc = grow(c->io_bias, (size_t)w->E * 4))) return rc;
+    if ((rc = ensure_workspace(c, w, T))) return rc;
+    cudaStream_t s = c->stream;
+    CK(cudaMemcpyAsync(c->io_x.p, x, xb, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(c->io_rms.p, rms_weight, (size_t)w->d * 4, cudaMemcpyHostToDevice, s));
+    const float *d_bias = nullptr;
+    if (router_bias) {
+        CK(cudaMemcpyAsync(c->io_bias.p, router_bias, (size_t)w->E * 4, cudaMemcpyHostToDevice, s));
+        d_bias = (const float *)c->io_bias.p;
+    }
+    const BlockNorm bn{(const float *)c->io_rms.p, eps, (float *)c->xn.p};
+    rc = forward_on(c, w, d_bias, (const float *)c->io_x.p, T, (float *)c->io_x.p,
+                    (float *)c->probs.p, (int *)c->ids.p, opts, s, &bn);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(x, c->io_x.p, xb, cudaMemcpyDeviceToHost, s));
+    if (x_norm) CK(cudaMemcpyAsync(x_norm, c->xn.p, xb, cudaMemcpyDeviceToHost, s));
     if (router_probs)
         CK(cudaMemcpyAsync(router_probs, c->probs.p, (size_t)T * w->E * 4, cudaMemcpyDeviceToHost, s));
     if (expert_ids)

@@ -106,6 +106,9 @@ extern "C" int moe_b200_forward_noalloc(const moe_b200_weights *w, const float *
     if (!w || !d_x || !d_out)
         return set_last_error(MOE_B200_E_INVALID, "moe_b200_forward_noalloc: null weights, x or out");
     if (T < 0) return set_last_error(MOE_B200_E_INVALID, "moe_b200_forward_noalloc: T < 0");
+    if (((uintptr_t)d_x | (uintptr_t)d_out) & 15)
+        return set_last_error(MOE_B200_E_INVALID,
+                              "moe_b200_forward_noalloc: x and out must be 16-byte aligned");
     if (T == 0) return MOE_B200_OK;
     Scratch sc;
     const size_t need = carve(w, T, nullptr, &sc);

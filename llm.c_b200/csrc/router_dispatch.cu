@@ -107,12 +107,14 @@ dispatch_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad,
 // K7  combine — out[t] = Σ_r w_{t,r} · y[pos(t,r)] for r = 0..k-1 in rank
 // order, starting from zero with one fused multiply-add per term, as the
 // reference accumulates (src/transformer.c:296,355-358).  No atomics: the
-// result is bit-stable run to run.
+// result is bit-stable run to run.  With `resid` (block_forward's residual,
+// src/transformer.c:767) the finished sum is added to it, as
+// mat_add_inplace does (src/matrix.c:491-500); resid may be out itself.
 // ---------------------------------------------------------------------
 __global__ void __launch_bounds__(256)
 combine_kernel(const float *__restrict__ y, int d, int d_pad, int T, int k,
                const int *__restrict__ pos_of, const float *__restrict__ wts,
-               float *__restrict__ out, const float *__restrict__ y2)
+               float *out, const float *__restrict__ y2, const float *resid)
 {
     // y2 (optional): the second K half of the down GEMM, added to y first
     const int t = blockIdx.x;
@@ -142,6 +144,11 @@ combine_kernel(const float *__restrict__ y, int d, int d_pad, int T, int k,
                     acc.w = __fmaf_rn(w[r], v.w, acc.w);
                 }
             }
+            if (resid) {
+                const float4 x = reinterpret_cast<const float4 *>(resid + (size_t)t * d)[c];
+                acc.x = __fadd_rn(x.x, acc.x); acc.y = __fadd_rn(x.y, acc.y);
+                acc.z = __fadd_rn(x.z, acc.z); acc.w = __fadd_rn(x.w, acc.w);
+            }
             reinterpret_cast<float4 *>(o)[c] = acc;
         }
     } else {
@@ -152,6 +159,7 @@ combine_kernel(const float *__restrict__ y, int d, int d_pad, int T, int k,
                 if (y2) v = __fadd_rn(v, __ldg(y2 + (size_t)pos[r] * d_pad + c));
                 acc = __fmaf_rn(w[r], v, acc);
             }
+            if (resid) acc = __fadd_rn(resid[(size_t)t * d + c], acc);
             o[c] = acc;
         }
     }
@@ -175,12 +183,12 @@ cudaError_t launch_dispatch(const float *x, int T, int d, int d_pad, int E, int 
 
 cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
                            const int *pos_of, const float *wts, float *out, cudaStream_t s,
-                           const float *y2)
+                           const float *y2, const float *resid)
 {
     int threads = 256;
     const int work = (d & 3) == 0 ? d / 4 : d;
     if (work < 256) threads = max(32, round_up(work, 32));
-    combine_kernel<<<T, threads, 0, s>>>(y, d, d_pad, T, k, pos_of, wts, out, y2);
+    combine_kernel<<<T, threads, 0, s>>>(y, d, d_pad, T, k, pos_of, wts, out, y2, resid);
     return cudaGetLastError();
 }
 

@@ -81,6 +81,10 @@ def lib() -> C.CDLL:
     L.moe_b200_profile_read.argtypes = [C.POINTER(C.c_double), _ip]
     L.moe_b200_synth_fill.argtypes = [_vp, C.c_size_t, C.c_uint64, C.c_uint64, C.c_uint64,
                                       C.c_float, _vp]
+    L.moe_b200_block_ffn.argtypes = [_vp, _fp, C.c_float, _fp, _fp, C.c_int, _fp, _fp, _ip,
+                                     C.POINTER(Opts)]
+    L.moe_b200_block_ffn_device.argtypes = [_vp, _vp, C.c_float, _vp, _vp, C.c_int, _vp, _vp,
+                                            _vp, C.POINTER(Opts), _vp]
     L.moe_b200_checkpoint_config.argtypes = [C.c_char_p, _vp]
     L.moe_b200_checkpoint_load_experts.argtypes = [C.c_char_p, C.c_int, C.POINTER(_vp)]
     L.moe_b200_decoder_create.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp)]
@@ -238,6 +242,50 @@ def moe_forward_device(w: MoEWeights, x_ptr: int, T: int, out_ptr: int,
     o = _opts(path, cta_pair)
     _check(lib().moe_b200_forward_device(w.handle, bias_ptr, x_ptr, T, out_ptr, probs_ptr,
                                          ids_ptr, C.byref(o), stream), "moe_b200_forward_device")
+
+
+def block_ffn(w: MoEWeights, x: np.ndarray, rms_weight: np.ndarray, eps: float = 1e-5,
+              bias: np.ndarray | None = None, path: int = PATH_AUTO, cta_pair: bool = False,
+              want_norm: bool = True):
+    """block_forward's FFN half (src/transformer.c:752-767) on host buffers:
+    returns (x + moe(rms_norm(x)) [T×d], rms_norm(x) [T×d] or None,
+    probs [T×E], ids [T×k]).  `x` itself is not modified."""
+    xo = np.array(x, np.float32, order="C", copy=True)
+    T = xo.shape[0]
+    xn = np.empty_like(xo) if want_norm else None
+    probs = np.empty((T, w.E), np.float32)
+    ids = np.empty((T, w.top_k), np.int32)
+    rw = np.ascontiguousarray(rms_weight, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    o = _opts(path, cta_pair)
+    _check(lib().moe_b200_block_ffn(w.handle, _f(rw), float(eps), _f(b), _f(xo), T, _f(xn),
+                                    _f(probs), _i(ids), C.byref(o)), "moe_b200_block_ffn")
+    return xo, xn, probs, ids
+
+
+def block_ffn_host_ptr(w: MoEWeights, rms_ptr: int, eps: float, x_ptr: int, T: int,
+                       x_norm_ptr: int | None = None, probs_ptr: int | None = None,
+                       ids_ptr: int | None = None, bias_ptr: int | None = None,
+                       path: int = PATH_AUTO, cta_pair: bool = False):
+    """Host-buffer block FFN from raw host pointers (e.g. pinned torch tensors);
+    x updated in place."""
+    o = _opts(path, cta_pair)
+    cf = lambda p: C.cast(p, _fp) if p else None  # noqa: E731
+    _check(lib().moe_b200_block_ffn(w.handle, cf(rms_ptr), float(eps), cf(bias_ptr), cf(x_ptr),
+                                    T, cf(x_norm_ptr), cf(probs_ptr),
+                                    C.cast(ids_ptr, _ip) if ids_ptr else None, C.byref(o)),
+           "moe_b200_block_ffn")
+
+
+def block_ffn_device(w: MoEWeights, rms_ptr: int, eps: float, x_ptr: int, T: int,
+                     x_norm_ptr: int | None = None, probs_ptr: int | None = None,
+                     ids_ptr: int | None = None, bias_ptr: int | None = None,
+                     path: int = PATH_AUTO, stream: int | None = None, cta_pair: bool = False):
+    """Device-buffer block FFN, x updated in place, asynchronous on `stream`."""
+    o = _opts(path, cta_pair)
+    _check(lib().moe_b200_block_ffn_device(w.handle, rms_ptr, float(eps), bias_ptr, x_ptr, T,
+                                           x_norm_ptr, probs_ptr, ids_ptr, C.byref(o), stream),
+           "moe_b200_block_ffn_device")
 
 
 def last_counts(w: MoEWeights) -> np.ndarray:

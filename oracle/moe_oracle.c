@@ -12,6 +12,9 @@
  *   ffn_forward                           src/transformer.c:157-165
  *   moe_forward                           src/transformer.c:287-366
  *   mat_mul_add (bias broadcast)          src/matrix.c:418-439
+ *   rms_norm                              src/matrix.c:666-713
+ *   hsum256                               include/simd.h:110-121
+ *   block_forward, FFN half               src/transformer.c:752-767
  */
 #include "oracle.h"
 
@@ -422,4 +425,52 @@ void oracle_moe_forward_synth(const float *x, int T, int d,
                        NULL, rows, n_rows, forced_ids, out, probs, ids,
                        threads);
     free(s.wg); free(s.wu); free(s.wd);
+}
+
+/* ========================================================================
+ * RMSNorm and the FFN half of block_forward
+ * ===================================================================== */
+
+/* hsum256 (include/simd.h:110-121): upper half added to lower half, then
+ * (s0 + s1) + (s2 + s3). */
+static float hsum8(const float *l) {
+    const float s0 = l[0] + l[4], s1 = l[1] + l[5], s2 = l[2] + l[6], s3 = l[3] + l[7];
+    return (s0 + s1) + (s2 + s3);
+}
+
+void oracle_rms_norm(const float *x, int rows, int cols, const float *weight, float eps,
+                     float *out) {
+    for (int i = 0; i < rows; i++) {
+        const float *xr = x + (size_t)i * cols;
+        float *yr = out + (size_t)i * cols;
+        float a[16] = {0};
+        int j = 0;
+        for (; j <= cols - 16; j += 16)
+            for (int l = 0; l < 16; l++) a[l] = fmaf(xr[j + l], xr[j + l], a[l]);
+        float b[8];
+        for (int l = 0; l < 8; l++) b[l] = a[l] + a[l + 8];
+        for (; j <= cols - 8; j += 8)
+            for (int l = 0; l < 8; l++) b[l] = fmaf(xr[j + l], xr[j + l], b[l]);
+        float ss = hsum8(b);
+        for (; j < cols; j++) ss += xr[j] * xr[j];
+        const float inv = 1.0f / sqrtf(ss / (float)cols + eps);
+        for (int c = 0; c < cols; c++) yr[c] = xr[c] * inv * weight[c];
+    }
+}
+
+void oracle_block_ffn(float *x, int T, int d, const float *rms_weight, float eps,
+                      const float *W_router, const float *bias, int E, int k, int F,
+                      const float *const *W_gate, const float *const *W_up,
+                      const float *const *W_down, float *xn, float *probs, int *ids,
+                      int threads) {
+    const size_t n = (size_t)T * d;
+    float *norm = xn ? xn : (float *)malloc(n * sizeof(float));
+    float *ffn = (float *)malloc(n * sizeof(float));
+    if (!norm || !ffn) { fprintf(stderr, "[oracle] OOM\n"); abort(); }
+    oracle_rms_norm(x, T, d, rms_weight, eps, norm);
+    oracle_moe_forward(norm, T, d, W_router, bias, E, k, W_gate, W_up, W_down, F, NULL, T, NULL,
+                       ffn, probs, ids, threads);
+    for (size_t i = 0; i < n; i++) x[i] = x[i] + ffn[i];
+    free(ffn);
+    if (!xn) free(norm);
 }

@@ -55,6 +55,24 @@ float oracle_exp_ref(float v);
  * the tail. In place on m[rows × cols]. */
 void oracle_softmax_rows(float *m, int rows, int cols);
 
+/* rms_norm restated (src/matrix.c:666-713, AVX2+FMA build), per row of
+ * x[rows × cols]: sum of squares in 16 fused-multiply-add lanes over
+ * 16-column chunks, lanes j and j+8 added, further 8-column chunks fused
+ * into those 8 lanes, hsum tree, scalar tail (multiply, then add);
+ * inv = 1 / sqrt(ss / cols + eps); out = (x * inv) * weight. */
+void oracle_rms_norm(const float *x, int rows, int cols, const float *weight, float eps,
+                     float *out);
+
+/* The FFN half of block_forward (src/transformer.c:752-767) for a MoE
+ * block: xn = rms_norm(x, rms_weight); x += moe_forward(xn), the add
+ * being mat_add_inplace's (src/matrix.c:491-500).  x is updated in place;
+ * xn (T×d, may be NULL), probs and ids as oracle_moe_forward. */
+void oracle_block_ffn(float *x, int T, int d, const float *rms_weight, float eps,
+                      const float *W_router, const float *bias, int E, int k, int F,
+                      const float *const *W_gate, const float *const *W_up,
+                      const float *const *W_down, float *xn, float *probs, int *ids,
+                      int threads);
+
 /* swiglu restated (src/matrix.c:618-655): h = silu(g) * u elementwise. */
 void oracle_swiglu(const float *g, const float *u, float *h, int n);
 

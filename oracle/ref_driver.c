@@ -133,3 +133,11 @@ int ref_inference_pos(void *s) { return ((InferenceState *)s)->seq_pos; }
 /* llm.c's own checkpoint format (model_save / model_load, src/transformer.c:573-697) */
 int ref_model_save(void *m, const char *path) { return model_save((const Model *)m, path); }
 void *ref_model_load(const char *path) { return model_load(path); }
+
+/* the reference's rms_norm (src/matrix.c:666-713) over plain arrays */
+void ref_rms_norm(const float *x, int rows, int cols, const float *weight, float eps,
+                  float *out) {
+    Matrix in = {(float *)x, NULL, rows, cols};
+    Matrix o = {out, NULL, rows, cols};
+    rms_norm(&in, weight, eps, &o);
+}

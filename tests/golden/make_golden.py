@@ -17,6 +17,18 @@ Special cases hand-built on top of the generator:
   ties_zero_row token rows 0..3 are all-zero, so all E logits tie
                 (ids must be 0, 1, ..., k-1)
 
+Block cases (block_*.npz): the FFN half of block_forward
+(src/transformer.c:752-767) — the reference's rms_norm, moe_forward and
+the residual add — on oracle_lib.BlockProblem inputs (x ~ N(0, 4), rms_ffn
+weights 1 + N(0, 0.1), eps 1e-5).  Stored per case:
+  ids, probs          as above
+  x_out [R×d] f32     x after the block for rows `rows`
+  x_norm [R×d] f32    the reference's rms_norm output for those rows (its
+                      1/sqrtf is a -ffast-math estimate, so these bits are
+                      this host's; tests compare them within 5e-7)
+  ffn_out [R×d] f32   the MoE output before the residual (cache->ffn_out)
+  x_out_sum           float64 sum of the full x after the block
+
 Run:  python tests/golden/make_golden.py   (needs the reference sources
 built into oracle/_ref; the committed .npz files are what tests read)
 """
@@ -41,6 +53,20 @@ CASES = [
     ("ties_zero_row", 32, 16, 8, 3, 32, 4, "zero"),
     ("c1", 2048, 256, 8, 2, 1024, 0, None),
 ]
+
+
+BLOCK_CASES = [
+    # name, T, d, E, k, F, seed  (d = 44: 16-lane chunks, one 8-lane chunk and a
+    # 4-column tail; d = 13: no 16-lane chunk, a 5-column tail, unaligned rows)
+    ("block_odd", 97, 44, 6, 3, 72, 5),
+    ("block_d13", 33, 13, 4, 2, 24, 8),
+    ("block_c1", 2048, 256, 8, 2, 1024, 0),
+]
+
+
+def moe_fixtures():
+    """The MoE-layer fixtures (the block_* files hold block cases)."""
+    return sorted(p for p in HERE.glob("*.npz") if not p.stem.startswith("block_"))
 
 
 def build_problem(T, d, E, k, F, seed, tweak):
@@ -70,6 +96,18 @@ def main():
                             tweak=str(tweak), w_std=np.float32(0.02),
                             ids=ids, probs=probs, rows=rows, out=out[rows],
                             out_sum=np.float64(out.astype(np.float64).sum()))
+        print(f"{name}: T={T} d={d} E={E} k={k} F={F} -> {HERE / (name + '.npz')}")
+    for name, T, d, E, k, F, seed in BLOCK_CASES:
+        p = O.BlockProblem(T, d, E, k, F, seed=seed)
+        x_out, x_norm, probs, ids, ffn_out = p.ref_block(threads=1)
+        rows = np.arange(T, dtype=np.int32)
+        if T > 256:
+            rows = np.sort(np.random.default_rng(seed).choice(T, 256, replace=False)).astype(np.int32)
+        np.savez_compressed(HERE / f"{name}.npz",
+                            T=T, d=d, E=E, k=k, F=F, seed=seed, x_std=np.float32(4.0),
+                            eps=np.float32(1e-5), ids=ids, probs=probs, rows=rows,
+                            x_out=x_out[rows], x_norm=x_norm[rows], ffn_out=ffn_out[rows],
+                            x_out_sum=np.float64(x_out.astype(np.float64).sum()))
         print(f"{name}: T={T} d={d} E={E} k={k} F={F} -> {HERE / (name + '.npz')}")
 
 

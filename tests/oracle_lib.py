@@ -66,6 +66,12 @@ def oracle():
         lib.oracle_moe_forward_synth.argtypes = [
             _fp, C.c_int, C.c_int, _fp, _fp, C.c_int, C.c_int, C.c_int,
             C.c_uint64, C.c_float, _ip, C.c_int, _ip, _fp, _fp, _ip, C.c_int]
+        lib.oracle_rms_norm.argtypes = [_fp, C.c_int, C.c_int, _fp, C.c_float, _fp]
+        lib.oracle_rms_norm.restype = None
+        lib.oracle_block_ffn.argtypes = [_fp, C.c_int, C.c_int, _fp, C.c_float, _fp, _fp,
+                                         C.c_int, C.c_int, C.c_int, C.POINTER(_fp),
+                                         C.POINTER(_fp), C.POINTER(_fp), _fp, _fp, _ip, C.c_int]
+        lib.oracle_block_ffn.restype = None
         lib.oracle_ffn_forward.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp,
                                            C.c_int, _fp]
         _oracle = lib
@@ -101,6 +107,8 @@ def ref():
         lib.ref_inference_logits.argtypes = [C.c_void_p]
         lib.ref_inference_pos.restype = C.c_int
         lib.ref_inference_pos.argtypes = [C.c_void_p]
+        lib.ref_rms_norm.argtypes = [_fp, C.c_int, C.c_int, _fp, C.c_float, _fp]
+        lib.ref_rms_norm.restype = None
         lib.ref_model_save.restype = C.c_int
         lib.ref_model_save.argtypes = [C.c_void_p, C.c_char_p]
         lib.ref_model_load.restype = C.c_void_p
@@ -219,6 +227,63 @@ class MoEProblem:
         return out, probs, ids
 
 
+def stream_rms():
+    """Synthetic stream of the RMSNorm weights (clear of the expert streams,
+    which start at 0x100)."""
+    return 4
+
+
+class BlockProblem(MoEProblem):
+    """The FFN half of llm.c's block_forward (src/transformer.c:752-767) on a
+    seeded synthetic MoE layer: x is the residual stream (N(0, x_std)), the
+    block's rms_ffn weights are 1 + N(0, 0.1), eps as llm.c's configs."""
+
+    def __init__(self, T, d, E, k, F, seed=0, x_std=4.0, eps=1e-5, **kw):
+        super().__init__(T, d, E, k, F, seed=seed, x_std=x_std, **kw)
+        self.eps = np.float32(eps)
+        self.rms_w = (np.float32(1.0) + synth(seed, stream_rms(), d, 0.1)).astype(np.float32)
+
+    def oracle_rms(self):
+        xn = np.empty_like(self.x)
+        oracle().oracle_rms_norm(_f(self.x), self.T, self.d, _f(self.rms_w), self.eps, _f(xn))
+        return xn
+
+    def ref_rms(self):
+        xn = np.empty_like(self.x)
+        ref().ref_rms_norm(_f(self.x), self.T, self.d, _f(self.rms_w), self.eps, _f(xn))
+        return xn
+
+    def moe_on(self, xn):
+        """This layer's MoE problem with x_norm as its input."""
+        moe = MoEProblem.__new__(MoEProblem)
+        moe.__dict__.update(self.__dict__)
+        moe.x = np.ascontiguousarray(xn, np.float32)
+        return moe
+
+    def oracle_block(self, threads=0):
+        """(x after the block, x_norm, probs, ids) from the CPU restatement."""
+        T, d, E, k, F = self.T, self.d, self.E, self.k, self.F
+        x = self.x.copy()
+        xn = np.empty_like(x)
+        probs = np.empty((T, E), np.float32)
+        ids = np.empty((T, k), np.int32)
+        g = _ptr_array([e[0] for e in self.experts])
+        u = _ptr_array([e[1] for e in self.experts])
+        dn = _ptr_array([e[2] for e in self.experts])
+        oracle().oracle_block_ffn(_f(x), T, d, _f(self.rms_w), self.eps, _f(self.W_router),
+                                  _f(self.bias), E, k, F, g, u, dn, _f(xn), _f(probs), _i(ids),
+                                  threads)
+        return x, xn, probs, ids
+
+    def ref_block(self, threads=0):
+        """The same through the reference's own rms_norm and moe_forward, plus
+        the FFN output (cache->ffn_out); the residual add is
+        mat_add_inplace's plain fp32 add."""
+        xn = self.ref_rms()
+        out, probs, ids = self.moe_on(xn).ref_forward(threads=threads)
+        return (self.x + out).astype(np.float32), xn, probs, ids, out
+
+
 def routing_mismatch_allowed(logits_row: np.ndarray, ids_a, ids_b, k: int,
                              gap: float = 1e-6) -> bool:
     """True when two top-k rankings of one token differ only where the
@@ -244,8 +309,9 @@ def release_ref_model(m_ptr):
     """Free a reference llm.c Model (from ref_model_init) after dropping the
     device copies the B200 library keeps for it: the expert sets uploaded by
     the drop-in moe_forward / inference_step (keyed by each block's
-    MoEWeights pointer) and inference_step's device decoder (keyed by the
-    Model pointer).  The library's residency cache is keyed by pointer, so
+    MoEWeights pointer, or for dense blocks run through the block FFN drop-in
+    by their FFNWeights pointer, the same union member) and inference_step's
+    device decoder (keyed by the Model pointer).  The library's residency cache is keyed by pointer, so
     a later model allocated at the same addresses would otherwise meet the
     stale copies (its contract: invalidate before changing or freeing)."""
     import moe_b200 as M
@@ -253,10 +319,8 @@ def release_ref_model(m_ptr):
     L = M.lib()
     L.moe_b200_invalidate.argtypes = [C.c_void_p]
     model = LM.Model.from_address(m_ptr)
-    moe_off = LM.BlockWeights.u.offset        # the MoEWeights member of the union
+    ffn_off = LM.BlockWeights.u.offset        # the FFNWeights / MoEWeights union
     for l in range(model.weights.n_layers):
-        blk = model.weights.blocks[l]
-        if blk.use_moe:
-            L.moe_b200_invalidate(C.addressof(blk) + moe_off)
+        L.moe_b200_invalidate(C.addressof(model.weights.blocks[l]) + ffn_off)
     L.moe_b200_invalidate(m_ptr)
     ref().ref_model_free(m_ptr)

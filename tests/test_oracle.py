@@ -7,7 +7,7 @@ import pytest
 import oracle_lib as O
 from golden import make_golden as G
 
-GOLDEN = sorted(p for p in G.HERE.glob("*.npz"))
+GOLDEN = G.moe_fixtures()
 
 
 def load_case(path):

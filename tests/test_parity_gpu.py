@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 TOL = {M.PATH_FP32: 1e-5, M.PATH_TF32: 2e-3, M.PATH_TF32X3: 1e-5}
 PATHS = [M.PATH_FP32, M.PATH_TF32, M.PATH_TF32X3]
 PATH_IDS = ["fp32", "tf32", "tf32x3"]
-GOLDEN = sorted(G.HERE.glob("*.npz"))
+GOLDEN = G.moe_fixtures()
 
 
 def load_case(path):

@@ -18,7 +18,7 @@ from golden import make_golden as G
 
 pytestmark = pytest.mark.gpu
 
-GOLDEN = sorted(G.HERE.glob("*.npz"))
+GOLDEN = G.moe_fixtures()
 
 
 def _upload(p):
