@@ -159,6 +159,39 @@ int moe_b200_block_ffn_device(const moe_b200_weights *w, const float *d_rms_weig
                               float *d_router_probs, int *d_expert_ids,
                               const moe_b200_opts *opts, void *stream);
 
+/* ---- backward (training) --------------------------------------------------
+ * llm.c has no MoE backward (model_backward, src/transformer.c:981-1013,
+ * stops at the norms and attention) and leaves the Switch load-balancing loss
+ * to the training loop (src/transformer.c:280-282).  This is the gradient of
+ * the forward above with the top-k choice held fixed, plus aux_coef · L_aux:
+ *   L_aux = n_experts · Σ_e f_e · P_e,  f_e = tokens routed to e / (T·top_k),
+ *   P_e = mean router probability of e.
+ * Gradients accumulate (+=) in a moe_b200_grads object, in llm.c's layouts:
+ * W_router [d×E], router bias [E], W_gate / W_up [d×F], W_down [F×d] per
+ * expert.  FP32 arithmetic (the forward is recomputed on the FP32 path), every
+ * sum in a fixed order: bit-stable run to run. */
+typedef struct moe_b200_grads moe_b200_grads;
+
+int moe_b200_grads_create(const moe_b200_weights *w, moe_b200_grads **g);   /* zeroed */
+int moe_b200_grads_zero(moe_b200_grads *g);
+/* Any pointer may be NULL (that part is skipped). */
+int moe_b200_grads_download(const moe_b200_grads *g, float *dW_router, float *d_bias,
+                            float *const *dW_gate, float *const *dW_up, float *const *dW_down);
+int moe_b200_grads_free(moe_b200_grads *g);
+
+/* Host buffers, synchronous.  x [T×d] the forward's input, dy [T×d] the
+ * gradient of the loss with respect to the forward's output; writes
+ * dx [T×d] and, when aux_loss is not NULL, L_aux of this batch (its gradient
+ * enters with weight aux_coef whether or not the value is requested). */
+int moe_b200_backward(const moe_b200_weights *w, const float *router_bias, const float *x,
+                      int T, const float *dy, float aux_coef, float *dx, moe_b200_grads *g,
+                      float *aux_loss);
+
+/* Same on device buffers (16-byte aligned), asynchronous on `stream`. */
+int moe_b200_backward_device(const moe_b200_weights *w, const float *d_bias, const float *d_x,
+                             int T, const float *d_dy, float aux_coef, float *d_dx,
+                             moe_b200_grads *g, float *d_aux_loss, void *stream);
+
 /* Size of the static device array behind moe_b200_forward_noalloc. */
 #define MOE_B200_NOALLOC_SCRATCH_BYTES (16u << 20)
 

@@ -54,8 +54,12 @@ __global__ void __launch_bounds__(256)
 ffma_grouped_kernel(const float *__restrict__ A, int K,
                     const float *__restrict__ B, int b_rows_per_expert,
                     float *__restrict__ C, int ldc, const int *__restrict__ plan, int E,
-                    float *const *__restrict__ out_ptrs, const int2 *__restrict__ ret)
+                    float *const *__restrict__ out_ptrs, const int2 *__restrict__ ret,
+                    float *__restrict__ gu_save)
 {
+    // gu_save (SWIGLU, optional): the gate and up pre-activations [rows × 2·ldc]
+    // in the weights' row order (per 128 columns: 128 gate, then 128 up), for
+    // the backward
     __shared__ __align__(16) float As[BK][BM + 4];
     __shared__ __align__(16) float Bs[BK][BN + 4];
     __shared__ __align__(16) float Us[BK][BN + 4];
@@ -120,6 +124,12 @@ ffma_grouped_kernel(const float *__restrict__ A, int K,
         } else {
             o = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
         }
+        if (SWIGLU && gu_save != nullptr) {
+            float *g = gu_save + (size_t)(row0 + r) * 2 * ldc + (n0 / 128) * 256 + (n0 % 128) + tx * 4;
+            *reinterpret_cast<float4 *>(g) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            *reinterpret_cast<float4 *>(g + 128) =
+                make_float4(accu[i][0], accu[i][1], accu[i][2], accu[i][3]);
+        }
         float *dst = C + (size_t)(row0 + r) * ldc;
         if (!SWIGLU && ret != nullptr) {          // expert-parallel return to the owner
             const int2 rr = ret[row0 + r];
@@ -133,11 +143,12 @@ ffma_grouped_kernel(const float *__restrict__ A, int K,
 static int mtile_bound(int rows_bound, int E, int bm) { return ceil_div(rows_bound, bm) + E; }
 
 cudaError_t launch_ffma_upgate(const float *x_perm, int d_pad, const float *w_ug, int F_pad,
-                               float *h, const int *plan, int E, int rows_bound, cudaStream_t s)
+                               float *h, const int *plan, int E, int rows_bound, cudaStream_t s,
+                               float *gu_save)
 {
     dim3 grid(mtile_bound(rows_bound, E, BM), F_pad / BN);
     ffma_grouped_kernel<true><<<grid, 256, 0, s>>>(x_perm, d_pad, w_ug, 2 * F_pad, h, F_pad, plan, E,
-                                                   nullptr, nullptr);
+                                                   nullptr, nullptr, gu_save);
     return cudaGetLastError();
 }
 
@@ -147,7 +158,7 @@ cudaError_t launch_ffma_down(const float *h, int F_pad, const float *w_d, int d_
 {
     dim3 grid(mtile_bound(rows_bound, E, BM), d_pad / BN);
     ffma_grouped_kernel<false><<<grid, 256, 0, s>>>(h, F_pad, w_d, d_pad, y, d_pad, plan, E,
-                                                    y_ptrs, ret);
+                                                    y_ptrs, ret, nullptr);
     return cudaGetLastError();
 }
 

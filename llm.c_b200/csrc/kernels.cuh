@@ -32,6 +32,22 @@ cudaError_t launch_dispatch_scan(const int *tile_cnt, int T, int E, int *tile_pr
 cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
                            const int *pos_of, const float *wts, float *out, cudaStream_t s,
                            const float *y2 = nullptr, const float *resid = nullptr);
+// MoE backward (moe_backward.cu); rows are the expert-sorted (token, rank)
+// slots of the forward's plan.
+struct BwdArgs {
+    int T, d, E, k, F, d_pad, F_pad, rows_bound;
+    const int *plan, *pos_of, *ids;
+    const float *x, *x_perm, *gu, *h, *y, *probs, *wts;   // forward state
+    const float *router, *ug, *dn;                          // device weights
+    const float *dy;                                        // [T × d]
+    float aux_coef;
+    float *dw, *dO, *dgu, *dxp, *dlogit, *pmean;            // workspace (dxp may be y)
+    float *dx;                                              // [T × d]
+    float *g_router, *g_bias, *g_gate, *g_up, *g_down;      // accumulated gradients
+    float *aux_loss;                                        // device scalar or null
+};
+cudaError_t launch_moe_backward(const BwdArgs &a, cudaStream_t s, int *launches);
+
 // block_forward's pre-FFN RMSNorm over rows of x[T × d] (block_ffn.cu)
 cudaError_t launch_rmsnorm(const float *x, int T, int d, const float *weight, float eps,
                            float *out, cudaStream_t s);
@@ -41,7 +57,8 @@ int rmsnorm_max_d();
 //   upgate: H[rows×F_pad] = swiglu(X_perm·Wg^T, X_perm·Wu^T)
 //   down:   Y[rows×d_pad] = H·Wd^T
 cudaError_t launch_ffma_upgate(const float *x_perm, int d_pad, const float *w_ug, int F_pad,
-                               float *h, const int *plan, int E, int rows_bound, cudaStream_t s);
+                               float *h, const int *plan, int E, int rows_bound, cudaStream_t s,
+                               float *gu_save = nullptr);
 cudaError_t launch_ffma_down(const float *h, int F_pad, const float *w_d, int d_pad,
                              float *y, const int *plan, int E, int rows_bound, cudaStream_t s,
                              float *const *y_ptrs = nullptr, const int2 *ret = nullptr);

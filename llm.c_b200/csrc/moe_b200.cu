@@ -116,6 +116,8 @@ struct Ctx {
     Buf rpart;                           // split-K router partial logits (small T)
     Buf io_x, io_out, io_bias;
     Buf xn, io_rms;                      // block FFN: RMSNorm output, host-call norm weights
+    Buf gu, dO, dgu, dw, dlogit, pmean;  // backward: saved pre-activations and gradients
+    Buf io_dy, io_dx, io_aux;
     int last_E = 0;
     int last_launches = 0;
     int last_path = 0;
@@ -216,7 +218,8 @@ extern "C" void moe_b200_shutdown(void) {
         Buf *bufs[] = {&c->probs, &c->ids, &c->wts, &c->loc, &c->tile_cnt, &c->tile_pref,
                        &c->plan, &c->pos_of, &c->x_perm, &c->h, &c->y, &c->xs, &c->hs,
                        &c->rpart, &c->y2, &c->io_x, &c->io_out, &c->io_bias,
-                       &c->xn, &c->io_rms};
+                       &c->xn, &c->io_rms, &c->gu, &c->dO, &c->dgu, &c->dw, &c->dlogit,
+                       &c->pmean, &c->io_dy, &c->io_dx, &c->io_aux};
         for (Buf *b : bufs) free_buf(*b);
         cudaFree(c->status);
         cudaStreamDestroy(c->stream);
@@ -720,6 +723,186 @@ extern "C" int moe_b200_block_ffn(const moe_b200_weights *w, const float *rms_we
         CK(cudaMemcpyAsync(router_probs, c->probs.p, (size_t)T * w->E * 4, cudaMemcpyDeviceToHost, s));
     if (expert_ids)
         CK(cudaMemcpyAsync(expert_ids, c->ids.p, (size_t)T * w->k * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    return check_status(c);
+}
+
+// ---------------------------------------------------------------------
+// backward (moe_backward.cu): gradient buffers in llm.c's layouts
+// ---------------------------------------------------------------------
+struct moe_b200_grads {
+    int device = -1;
+    int d = 0, F = 0, E = 0;
+    float *router = nullptr, *bias = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+};
+
+static void grads_release(moe_b200_grads *g) {
+    for (float *p : {g->router, g->bias, g->gate, g->up, g->down})
+        if (p) cudaFree(p);
+    delete g;
+}
+
+extern "C" int moe_b200_grads_create(const moe_b200_weights *w, moe_b200_grads **out) {
+    if (!w || !out) return fail(MOE_B200_E_INVALID, "null argument");
+    *out = nullptr;
+    Ctx *c;
+    int rc = get_ctx(w->device, &c);
+    if (rc) return rc;
+    auto *g = new moe_b200_grads();
+    g->device = w->device;
+    g->d = w->d; g->F = w->F; g->E = w->E;
+    const size_t dE = (size_t)w->d * w->E, dFE = (size_t)w->d * w->F * w->E;
+    const struct { float **p; size_t n; } parts[] = {
+        {&g->router, dE}, {&g->bias, (size_t)w->E}, {&g->gate, dFE}, {&g->up, dFE}, {&g->down, dFE}};
+    for (const auto &pt : parts) {
+        if (cudaMalloc(pt.p, pt.n * 4) != cudaSuccess || cudaMemset(*pt.p, 0, pt.n * 4) != cudaSuccess) {
+            cudaGetLastError();
+            grads_release(g);
+            return fail(MOE_B200_E_NOMEM, "gradient buffers");
+        }
+    }
+    *out = g;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_grads_zero(moe_b200_grads *g) {
+    if (!g) return fail(MOE_B200_E_INVALID, "null gradients");
+    const size_t dE = (size_t)g->d * g->E, dFE = (size_t)g->d * g->F * g->E;
+    CK(cudaMemset(g->router, 0, dE * 4));
+    CK(cudaMemset(g->bias, 0, (size_t)g->E * 4));
+    CK(cudaMemset(g->gate, 0, dFE * 4));
+    CK(cudaMemset(g->up, 0, dFE * 4));
+    CK(cudaMemset(g->down, 0, dFE * 4));
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_grads_download(const moe_b200_grads *g, float *dW_router, float *d_bias,
+                                       float *const *dW_gate, float *const *dW_up,
+                                       float *const *dW_down) {
+    if (!g) return fail(MOE_B200_E_INVALID, "null gradients");
+    CK(cudaDeviceSynchronize());
+    const size_t dF = (size_t)g->d * g->F;
+    if (dW_router) CK(cudaMemcpy(dW_router, g->router, (size_t)g->d * g->E * 4, cudaMemcpyDeviceToHost));
+    if (d_bias) CK(cudaMemcpy(d_bias, g->bias, (size_t)g->E * 4, cudaMemcpyDeviceToHost));
+    for (int e = 0; e < g->E; e++) {
+        if (dW_gate && dW_gate[e])
+            CK(cudaMemcpy(dW_gate[e], g->gate + e * dF, dF * 4, cudaMemcpyDeviceToHost));
+        if (dW_up && dW_up[e])
+            CK(cudaMemcpy(dW_up[e], g->up + e * dF, dF * 4, cudaMemcpyDeviceToHost));
+        if (dW_down && dW_down[e])
+            CK(cudaMemcpy(dW_down[e], g->down + e * dF, dF * 4, cudaMemcpyDeviceToHost));
+    }
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_grads_free(moe_b200_grads *g) {
+    if (!g) return MOE_B200_OK;
+    cudaDeviceSynchronize();
+    grads_release(g);
+    return MOE_B200_OK;
+}
+
+// The FP32 forward again (saving the gate/up pre-activations), then the
+// backward kernels, all on stream s.
+static int backward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, const float *d_x,
+                       int T, const float *d_dy, float aux_coef, float *d_dx, moe_b200_grads *g,
+                       float *d_aux, cudaStream_t s) {
+    int rc = ensure_workspace(c, w, T);
+    if (rc) return rc;
+    const int E = w->E, k = w->k, d = w->d;
+    const size_t rows = (size_t)T * k;
+    if ((rc = grow(c->gu, rows * 2 * w->F_pad * 4)) || (rc = grow(c->dO, rows * w->d_pad * 4)) ||
+        (rc = grow(c->dgu, rows * 2 * w->F_pad * 4)) || (rc = grow(c->dw, rows * 4)) ||
+        (rc = grow(c->dlogit, (size_t)T * E * 4)) || (rc = grow(c->pmean, (size_t)E * 4)))
+        return rc;
+    float *probs = (float *)c->probs.p, *wts = (float *)c->wts.p;
+    int *ids = (int *)c->ids.p, *plan = (int *)c->plan.p, *pos_of = (int *)c->pos_of.p;
+    float *x_perm = (float *)c->x_perm.p, *h = (float *)c->h.p, *y = (float *)c->y.p;
+    const int nsplit = router_splits(T, d);
+    if (nsplit > 1 && (rc = grow(c->rpart, (size_t)nsplit * T * E * 4))) return rc;
+    CK(launch_router(d_x, T, d, w->router, d_bias, E, k, probs, ids, wts, (int *)c->loc.p,
+                     (int *)c->tile_cnt.p, s, (float *)c->rpart.p, nsplit));
+    CK(launch_dispatch(d_x, T, d, w->d_pad, E, k, ids, (int *)c->loc.p, (int *)c->tile_cnt.p,
+                       (int *)c->tile_pref.p, plan, pos_of, x_perm, 0, c->status, s));
+    CK(launch_ffma_upgate(x_perm, w->d_pad, w->ug, w->F_pad, h, plan, E, (int)rows, s,
+                          (float *)c->gu.p));
+    CK(launch_ffma_down(h, w->F_pad, w->dn, w->d_pad, y, plan, E, (int)rows, s));
+    BwdArgs a{};
+    a.T = T; a.d = d; a.E = E; a.k = k; a.F = w->F; a.d_pad = w->d_pad; a.F_pad = w->F_pad;
+    a.rows_bound = (int)rows;
+    a.plan = plan; a.pos_of = pos_of; a.ids = ids;
+    a.x = d_x; a.x_perm = x_perm; a.gu = (const float *)c->gu.p; a.h = h; a.y = y;
+    a.probs = probs; a.wts = wts;
+    a.router = w->router; a.ug = w->ug; a.dn = w->dn;
+    a.dy = d_dy; a.aux_coef = aux_coef;
+    a.dw = (float *)c->dw.p; a.dO = (float *)c->dO.p; a.dgu = (float *)c->dgu.p;
+    a.dxp = y;                                // y is last read by the combine backward
+    a.dlogit = (float *)c->dlogit.p; a.pmean = (float *)c->pmean.p;
+    a.dx = d_dx;
+    a.g_router = g->router; a.g_bias = g->bias; a.g_gate = g->gate; a.g_up = g->up;
+    a.g_down = g->down;
+    a.aux_loss = d_aux;
+    int n = 0;
+    CK(launch_moe_backward(a, s, &n));
+    c->last_E = E;
+    c->last_launches = (nsplit > 1 ? 2 : 1) + 2 + 2 + n;
+    c->last_path = MOE_B200_PATH_FP32;
+    return MOE_B200_OK;
+}
+
+static int backward_args_check(const moe_b200_weights *w, const moe_b200_grads *g, int T) {
+    if (!w || !g) return fail(MOE_B200_E_INVALID, "null weights or gradients");
+    if (g->d != w->d || g->F != w->F || g->E != w->E || g->device != w->device)
+        return fail(MOE_B200_E_INVALID, "gradients were made for another expert set");
+    if (T < 0) return fail(MOE_B200_E_INVALID, "T=%d", T);
+    if ((int64_t)T * w->k > (int64_t)1 << 30) return fail(MOE_B200_E_INVALID, "T too large");
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_backward_device(const moe_b200_weights *w, const float *d_bias,
+                                        const float *d_x, int T, const float *d_dy,
+                                        float aux_coef, float *d_dx, moe_b200_grads *g,
+                                        float *d_aux_loss, void *stream) {
+    int rc = backward_args_check(w, g, T);
+    if (rc || T == 0) return rc;
+    if (!d_x || !d_dy || !d_dx) return fail(MOE_B200_E_INVALID, "null x, dy or dx");
+    if (!aligned16(d_x) || !aligned16(d_dy) || !aligned16(d_dx))
+        return fail(MOE_B200_E_INVALID, "device x, dy and dx must be 16-byte aligned");
+    Ctx *c;
+    if ((rc = get_ctx(w->device, &c))) return rc;
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    return backward_on(c, w, d_bias, d_x, T, d_dy, aux_coef, d_dx, g, d_aux_loss, s);
+}
+
+extern "C" int moe_b200_backward(const moe_b200_weights *w, const float *router_bias,
+                                 const float *x, int T, const float *dy, float aux_coef, float *dx,
+                                 moe_b200_grads *g, float *aux_loss) {
+    int rc = backward_args_check(w, g, T);
+    if (rc) return rc;
+    if (T == 0) {
+        if (aux_loss) *aux_loss = 0.0f;
+        return MOE_B200_OK;
+    }
+    if (!x || !dy || !dx) return fail(MOE_B200_E_INVALID, "null x, dy or dx");
+    Ctx *c;
+    if ((rc = get_ctx(w->device, &c))) return rc;
+    const size_t xb = (size_t)T * w->d * 4;
+    if ((rc = grow(c->io_x, xb)) || (rc = grow(c->io_dy, xb)) || (rc = grow(c->io_dx, xb)) ||
+        (rc = grow(c->io_bias, (size_t)w->E * 4)) || (rc = grow(c->io_aux, 4)))
+        return rc;
+    cudaStream_t s = c->stream;
+    CK(cudaMemcpyAsync(c->io_x.p, x, xb, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(c->io_dy.p, dy, xb, cudaMemcpyHostToDevice, s));
+    const float *d_bias = nullptr;
+    if (router_bias) {
+        CK(cudaMemcpyAsync(c->io_bias.p, router_bias, (size_t)w->E * 4, cudaMemcpyHostToDevice, s));
+        d_bias = (const float *)c->io_bias.p;
+    }
+    rc = backward_on(c, w, d_bias, (const float *)c->io_x.p, T, (const float *)c->io_dy.p,
+                     aux_coef, (float *)c->io_dx.p, g, aux_loss ? (float *)c->io_aux.p : nullptr, s);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(dx, c->io_dx.p, xb, cudaMemcpyDeviceToHost, s));
+    if (aux_loss) CK(cudaMemcpyAsync(aux_loss, c->io_aux.p, 4, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
     return check_status(c);
 }

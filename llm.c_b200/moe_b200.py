@@ -85,6 +85,14 @@ def lib() -> C.CDLL:
                                      C.POINTER(Opts)]
     L.moe_b200_block_ffn_device.argtypes = [_vp, _vp, C.c_float, _vp, _vp, C.c_int, _vp, _vp,
                                             _vp, C.POINTER(Opts), _vp]
+    L.moe_b200_grads_create.argtypes = [_vp, C.POINTER(_vp)]
+    L.moe_b200_grads_zero.argtypes = [_vp]
+    L.moe_b200_grads_download.argtypes = [_vp, _fp, _fp, C.POINTER(_fp), C.POINTER(_fp),
+                                          C.POINTER(_fp)]
+    L.moe_b200_grads_free.argtypes = [_vp]
+    L.moe_b200_backward.argtypes = [_vp, _fp, _fp, C.c_int, _fp, C.c_float, _fp, _vp, _fp]
+    L.moe_b200_backward_device.argtypes = [_vp, _vp, _vp, C.c_int, _vp, C.c_float, _vp, _vp,
+                                           _vp, _vp]
     L.moe_b200_checkpoint_config.argtypes = [C.c_char_p, _vp]
     L.moe_b200_checkpoint_load_experts.argtypes = [C.c_char_p, C.c_int, C.POINTER(_vp)]
     L.moe_b200_decoder_create.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp)]
@@ -286,6 +294,70 @@ def block_ffn_device(w: MoEWeights, rms_ptr: int, eps: float, x_ptr: int, T: int
     _check(lib().moe_b200_block_ffn_device(w.handle, rms_ptr, float(eps), bias_ptr, x_ptr, T,
                                            x_norm_ptr, probs_ptr, ids_ptr, C.byref(o), stream),
            "moe_b200_block_ffn_device")
+
+
+class MoEGrads:
+    """Accumulated gradients of an expert set (moe_b200_grads), in llm.c's
+    layouts: W_router [d×E], bias [E], W_gate / W_up [d×F], W_down [F×d]."""
+
+    def __init__(self, w: MoEWeights):
+        h = _vp()
+        _check(lib().moe_b200_grads_create(w.handle, C.byref(h)), "moe_b200_grads_create")
+        self.handle = h.value
+        self.d, self.F, self.E = w.d, w.F, w.E
+
+    def zero(self):
+        _check(lib().moe_b200_grads_zero(self.handle), "moe_b200_grads_zero")
+
+    def download(self):
+        """(dW_router, d_bias, [dW_gate], [dW_up], [dW_down])."""
+        d, F, E = self.d, self.F, self.E
+        wr = np.empty((d, E), np.float32)
+        b = np.empty(E, np.float32)
+        g = [np.empty((d, F), np.float32) for _ in range(E)]
+        u = [np.empty((d, F), np.float32) for _ in range(E)]
+        dn = [np.empty((F, d), np.float32) for _ in range(E)]
+        _check(lib().moe_b200_grads_download(self.handle, _f(wr), _f(b),
+                                              (_fp * E)(*[_f(a) for a in g]),
+                                              (_fp * E)(*[_f(a) for a in u]),
+                                              (_fp * E)(*[_f(a) for a in dn])),
+               "moe_b200_grads_download")
+        return wr, b, g, u, dn
+
+    def free(self):
+        if self.handle:
+            lib().moe_b200_grads_free(self.handle)
+            self.handle = 0
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def moe_backward(w: MoEWeights, x: np.ndarray, dy: np.ndarray, grads: MoEGrads,
+                 bias: np.ndarray | None = None, aux_coef: float = 0.0):
+    """Backward of moe_forward at x given dy (host buffers): returns
+    (dx [T×d], L_aux); weight gradients accumulate into `grads`."""
+    x = np.ascontiguousarray(x, np.float32)
+    dy = np.ascontiguousarray(dy, np.float32)
+    T = x.shape[0]
+    dx = np.empty_like(x)
+    aux = np.zeros(1, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    _check(lib().moe_b200_backward(w.handle, _f(b), _f(x), T, _f(dy), float(aux_coef), _f(dx),
+                                   grads.handle, _f(aux)), "moe_b200_backward")
+    return dx, float(aux[0])
+
+
+def moe_backward_device(w: MoEWeights, x_ptr: int, T: int, dy_ptr: int, dx_ptr: int,
+                        grads: MoEGrads, bias_ptr: int | None = None, aux_coef: float = 0.0,
+                        aux_ptr: int | None = None, stream: int | None = None):
+    """Device-buffer backward, asynchronous on `stream`."""
+    _check(lib().moe_b200_backward_device(w.handle, bias_ptr, x_ptr, T, dy_ptr, float(aux_coef),
+                                          dx_ptr, grads.handle, aux_ptr, stream),
+           "moe_b200_backward_device")
 
 
 def last_counts(w: MoEWeights) -> np.ndarray:

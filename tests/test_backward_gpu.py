@@ -1,0 +1,148 @@
+"""MoE backward on the B200 (moe_b200_backward*) against float64 torch
+autograd of the same forward with the GPU's routing held fixed
+(tests/torch_ref.py).
+
+Tolerance: max|Δ| / max|ref| <= 1e-5 for dx and every weight gradient
+(FP32 arithmetic against a float64 reference), and the aux loss within
+1e-5 relative.  Also: bit-stable repeats, accumulation across calls, the
+device entry point equal to the host one, edge shapes (T = 1, k = 1,
+E = 1, d not a multiple of 4) and rejected arguments."""
+import numpy as np
+import pytest
+import torch
+
+import moe_b200 as M
+import oracle_lib as O
+import torch_ref
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def upload(p):
+    return M.MoEWeights.upload(p.W_router, [e[0] for e in p.experts], [e[1] for e in p.experts],
+                               [e[2] for e in p.experts], p.k)
+
+
+def _dy(p, seed):
+    return (np.random.default_rng(seed).standard_normal((p.T, p.d)) * 0.1).astype(np.float32)
+
+
+def _check(p, w, dy, aux_coef):
+    g = M.MoEGrads(w)
+    dx, aux = M.moe_backward(w, p.x, dy, g, bias=p.bias, aux_coef=aux_coef)
+    got = g.download()
+    _, _, ids = M.moe_forward(w, p.x, bias=p.bias, path=M.PATH_FP32)
+    ref = torch_ref.moe_grads(p.x, p.W_router, p.bias, p.experts, ids, dy, aux_coef)
+    assert O.rel_err(dx, ref[0]) < TOL
+    assert O.rel_err(got[0], ref[1]) < TOL                   # W_router
+    if p.bias is not None:
+        assert O.rel_err(got[1], ref[2]) < TOL               # bias
+    for name, a, b in (("gate", got[2], ref[3]), ("up", got[3], ref[4]), ("down", got[4], ref[5])):
+        for e in range(p.E):
+            if np.any(ids == e):
+                assert O.rel_err(a[e], b[e]) < TOL, f"{name}[{e}]"
+            else:
+                assert not np.any(a[e]), f"{name}[{e}] of an unused expert"
+    assert abs(aux - ref[6]) <= 1e-5 * abs(ref[6])
+    g.free()
+    return dx, got
+
+
+@pytest.mark.parametrize("shape,bias,aux", [
+    ((97, 44, 6, 3, 72), "normal", 0.01),
+    ((512, 256, 8, 2, 512), None, 0.0),
+    ((300, 128, 16, 4, 256), "normal", 0.1),
+    ((33, 13, 4, 2, 24), "normal", 0.05),       # d not a multiple of 4
+    ((1, 64, 8, 2, 128), None, 0.01),           # one token
+    ((64, 64, 8, 1, 96), None, 0.01),           # top-1
+], ids=["odd", "mid", "k4", "d13", "T1", "k1"])
+def test_backward_matches_autograd(moe, shape, bias, aux):
+    T, d, E, k, F = shape
+    p = O.MoEProblem(T, d, E, k, F, seed=T + d + E, bias=bias)
+    w = upload(p)
+    _check(p, w, _dy(p, T), aux)
+    w.free()
+
+
+def test_backward_single_expert(moe):
+    """E = 1: softmax over one logit is 1, so the router gets no gradient."""
+    p = O.MoEProblem(50, 64, 1, 1, 96, seed=4)
+    w = upload(p)
+    dx, got = _check(p, w, _dy(p, 1), 0.5)
+    assert not np.any(got[0])
+    w.free()
+
+
+def test_backward_bit_stable_and_accumulates(moe):
+    p = O.MoEProblem(256, 128, 8, 2, 256, seed=9, bias="normal")
+    w = upload(p)
+    dy = _dy(p, 2)
+    g1, g2 = M.MoEGrads(w), M.MoEGrads(w)
+    dx1, a1 = M.moe_backward(w, p.x, dy, g1, bias=p.bias, aux_coef=0.02)
+    dx2, a2 = M.moe_backward(w, p.x, dy, g2, bias=p.bias, aux_coef=0.02)
+    assert np.array_equal(dx1, dx2) and a1 == a2
+    one = g1.download()
+    for a, b in zip(one, g2.download()):
+        for u, v in zip(a if isinstance(a, list) else [a], b if isinstance(b, list) else [b]):
+            assert np.array_equal(u, v)
+    M.moe_backward(w, p.x, dy, g1, bias=p.bias, aux_coef=0.02)     # accumulates: g1 = 2·one
+    two = g1.download()
+    for a, b in zip(two, one):
+        for u, v in zip(a if isinstance(a, list) else [a], b if isinstance(b, list) else [b]):
+            assert np.array_equal(u, 2 * v)
+    g1.zero()
+    assert not np.any(g1.download()[4][0])
+    g1.free()
+    g2.free()
+    w.free()
+
+
+def test_backward_device_equals_host(moe):
+    p = O.MoEProblem(200, 256, 8, 2, 384, seed=5, bias="normal")
+    w = upload(p)
+    dy = _dy(p, 3)
+    gh = M.MoEGrads(w)
+    dx_h, aux_h = M.moe_backward(w, p.x, dy, gh, bias=p.bias, aux_coef=0.01)
+    dev = torch.device("cuda", 0)
+    x = torch.from_numpy(p.x).to(dev)
+    tdy = torch.from_numpy(dy).to(dev)
+    b = torch.from_numpy(p.bias).to(dev)
+    dx = torch.empty_like(x)
+    aux = torch.empty(1, device=dev)
+    gd = M.MoEGrads(w)
+    M.moe_backward_device(w, x.data_ptr(), p.T, tdy.data_ptr(), dx.data_ptr(), gd,
+                          bias_ptr=b.data_ptr(), aux_coef=0.01, aux_ptr=aux.data_ptr(),
+                          stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(dx.cpu().numpy(), dx_h)
+    assert float(aux.item()) == aux_h
+    for a, b2 in zip(gh.download(), gd.download()):
+        for u, v in zip(a if isinstance(a, list) else [a], b2 if isinstance(b2, list) else [b2]):
+            assert np.array_equal(u, v)
+    gh.free()
+    gd.free()
+    w.free()
+
+
+def test_backward_rejects_bad_arguments(moe):
+    p = O.MoEProblem(16, 64, 4, 2, 64, seed=1)
+    q = O.MoEProblem(16, 64, 8, 2, 64, seed=1)
+    w, wq = upload(p), upload(q)
+    g = M.MoEGrads(wq)
+    with pytest.raises(M.MoEError) as e:               # gradients of another expert set
+        M.moe_backward(w, p.x, _dy(p, 1), g)
+    assert e.value.status == M.E_INVALID
+    g.free()
+    g = M.MoEGrads(w)
+    dev = torch.device("cuda", 0)
+    flat = torch.zeros(p.T * p.d + 1, device=dev)
+    with pytest.raises(M.MoEError) as e:               # misaligned device buffer
+        M.moe_backward_device(w, flat.data_ptr() + 4, p.T, flat.data_ptr(), flat.data_ptr(), g)
+    assert e.value.status == M.E_INVALID
+    dx, aux = M.moe_backward(w, p.x[:0], _dy(p, 1)[:0], g)   # T = 0: nothing to do
+    assert dx.shape == (0, p.d) and aux == 0.0
+    g.free()
+    w.free()
+    wq.free()
