@@ -405,6 +405,75 @@ def run_decode(args):
 # ----------------------------------------------------------------------------
 # GPU
 # ----------------------------------------------------------------------------
+def run_backward(args, c):
+    """The MoE backward (FP32 FFMA kernels; the forward recomputed inside) on one
+    GPU: tokens/s and FLOP rate against the FP32 FFMA peak."""
+    import torch
+    import moe_b200 as M
+    M.init(0)
+    T, d, E, k, F, seed = c["T"], c["d"], c["E"], c["k"], c["F"], c["seed"]
+    w = M.MoEWeights.synth(seed, W_STD, d, F, E, k)
+    g = M.MoEGrads(w)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    x = torch.empty((T, d), device="cuda")
+    M.synth_fill(x.data_ptr(), T * d, seed, M.STREAM_X, 1.0, cuda_stream=stream.cuda_stream)
+    dy = torch.empty((T, d), device="cuda")
+    M.synth_fill(dy.data_ptr(), T * d, seed + 1, M.STREAM_X, 0.1, cuda_stream=stream.cuda_stream)
+    dx = torch.empty_like(x)
+    aux = torch.empty(1, device="cuda")
+    bias = None
+    if c["bias"] == "zipf":
+        bias = torch.from_numpy(zipf_bias(E)).cuda()
+    elif c["bias"] == "normal":
+        bias = torch.empty(E, device="cuda")
+        M.synth_fill(bias.data_ptr(), E, seed, M.STREAM_BIAS, 1.0, cuda_stream=stream.cuda_stream)
+    bptr = bias.data_ptr() if bias is not None else None
+
+    def step():
+        M.moe_backward_device(w, x.data_ptr(), T, dy.data_ptr(), dx.data_ptr(), g, bias_ptr=bptr,
+                              aux_coef=0.01, aux_ptr=aux.data_ptr(), stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches = M.last_launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    rows = T * k
+    flops = 18.0 * rows * d * F + 6.0 * T * d * E      # forward recompute + backward
+    props = torch.cuda.get_device_properties(0)
+    clocks = clk.summary()
+    mhz = clocks.get("sm_max_mhz") or 1965.0
+    fp32_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+    achieved = flops / (ms / 1000.0) / 1e12
+    line = {
+        "metric": "moe_backward_tokens_per_s", "value": T / (ms / 1000.0), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": args.config + "-backward", "T": T, "d_model": d, "n_experts": E,
+                   "top_k": k, "d_ff": F, "router_bias": c["bias"], "aux_coef": 0.01,
+                   "path": "fp32 (FFMA)"},
+        "roofline": {"bound": "fp32 FFMA", "achieved": achieved, "peak": fp32_peak,
+                     "unit": "TFLOP/s", "frac": achieved / fp32_peak,
+                     "peak_src": "nominal: SMs x 128 FP32 lanes x 2 x max SM clock",
+                     "flops_per_step": flops},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    g.free()
+    w.free()
+
+
 def block_ffn_measure(args, M, w, x, bptr, host_bias_ptr, path, stream, stage_ms_moe, n_moe,
                       moe_ms, T, d, E, k):
     """Device and end-to-end timing of moe_b200_block_ffn (RMSNorm + MoE +
@@ -484,6 +553,8 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=6.0,
                     help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--backward", action="store_true",
+                    help="time the MoE backward (moe_b200_backward_device) instead of the forward")
     ap.add_argument("--cta-pair", action="store_true",
                     help="TF32 path on the CTA-pair (cta_group::2) GEMM kernels")
     ap.add_argument("--tokens", type=int, default=None,
@@ -501,6 +572,9 @@ def main():
 
     if args.config == "c2":
         run_decode(args)
+        return
+    if args.backward:
+        run_backward(args, c)
         return
     if args.impl == "reference":
         run_reference_arm(args, c)
