@@ -406,8 +406,10 @@ def run_decode(args):
 # GPU
 # ----------------------------------------------------------------------------
 def run_backward(args, c):
-    """The MoE backward (FP32 FFMA kernels; the forward recomputed inside) on one
-    GPU: tokens/s and FLOP rate against the FP32 FFMA peak."""
+    """The MoE backward (the forward recomputed inside) on one GPU: tokens/s
+    and FLOP rate against the peak of the arithmetic the path runs on (TF32
+    tensor cores: the measured bf16 rate / 2; FP32 FFMA: the nominal FFMA
+    peak)."""
     import torch
     import moe_b200 as M
     M.init(0)
@@ -430,14 +432,18 @@ def run_backward(args, c):
         M.synth_fill(bias.data_ptr(), E, seed, M.STREAM_BIAS, 1.0, cuda_stream=stream.cuda_stream)
     bptr = bias.data_ptr() if bias is not None else None
 
+    path = {"auto": M.PATH_AUTO, "tf32": M.PATH_TF32, "fp32": M.PATH_FP32}[args.path]
+
     def step():
         M.moe_backward_device(w, x.data_ptr(), T, dy.data_ptr(), dx.data_ptr(), g, bias_ptr=bptr,
-                              aux_coef=0.01, aux_ptr=aux.data_ptr(), stream=stream.cuda_stream)
+                              aux_coef=0.01, aux_ptr=aux.data_ptr(), stream=stream.cuda_stream,
+                              path=path)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     launches = M.last_launches()
+    path_used = M.last_path()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clk:
         torch.cuda.synchronize()
@@ -451,9 +457,15 @@ def run_backward(args, c):
     flops = 18.0 * rows * d * F + 6.0 * T * d * E      # forward recompute + backward
     props = torch.cuda.get_device_properties(0)
     clocks = clk.summary()
-    mhz = clocks.get("sm_max_mhz") or 1965.0
-    fp32_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
     achieved = flops / (ms / 1000.0) / 1e12
+    if path_used == M.PATH_TF32:
+        peaks = measured_peaks()
+        peak = peaks["bf16_sustained"] / 2.0
+        bound, peak_src = "tensor (TF32)", peaks["src"] + " bf16 sustained / 2 (TF32 rate)"
+    else:
+        mhz = clocks.get("sm_max_mhz") or 1965.0
+        peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+        bound, peak_src = "fp32 FFMA", "nominal: SMs x 128 FP32 lanes x 2 x max SM clock"
     line = {
         "metric": "moe_backward_tokens_per_s", "value": T / (ms / 1000.0), "unit": "tokens/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -461,10 +473,10 @@ def run_backward(args, c):
         "data": "synthetic",
         "config": {"workload": args.config + "-backward", "T": T, "d_model": d, "n_experts": E,
                    "top_k": k, "d_ff": F, "router_bias": c["bias"], "aux_coef": 0.01,
-                   "path": "fp32 (FFMA)"},
-        "roofline": {"bound": "fp32 FFMA", "achieved": achieved, "peak": fp32_peak,
-                     "unit": "TFLOP/s", "frac": achieved / fp32_peak,
-                     "peak_src": "nominal: SMs x 128 FP32 lanes x 2 x max SM clock",
+                   "path": args.path,
+                   "path_run": "tf32 (tcgen05)" if path_used == M.PATH_TF32 else "fp32 (FFMA)"},
+        "roofline": {"bound": bound, "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "peak_src": peak_src,
                      "flops_per_step": flops},
         "gpu_launches": launches * args.steps,
         "clocks": clocks,

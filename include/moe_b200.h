@@ -168,8 +168,11 @@ int moe_b200_block_ffn_device(const moe_b200_weights *w, const float *d_rms_weig
  *   P_e = mean router probability of e.
  * Gradients accumulate (+=) in a moe_b200_grads object, in llm.c's layouts:
  * W_router [d×E], router bias [E], W_gate / W_up [d×F], W_down [F×d] per
- * expert.  FP32 arithmetic (the forward is recomputed on the FP32 path), every
- * sum in a fixed order: bit-stable run to run. */
+ * expert.  The forward is recomputed inside the call.  Arithmetic by
+ * opts->path: MOE_B200_PATH_FP32 (or TF32X3) FP32 FFMA, tolerance 1e-5;
+ * MOE_B200_PATH_TF32 tcgen05 tensor cores, tolerance 2e-3; AUTO picks TF32
+ * when the average expert group fills half a 128-row tile (the forward's
+ * rule).  Every sum runs in a fixed order: bit-stable run to run. */
 typedef struct moe_b200_grads moe_b200_grads;
 
 int moe_b200_grads_create(const moe_b200_weights *w, moe_b200_grads **g);   /* zeroed */
@@ -185,12 +188,13 @@ int moe_b200_grads_free(moe_b200_grads *g);
  * enters with weight aux_coef whether or not the value is requested). */
 int moe_b200_backward(const moe_b200_weights *w, const float *router_bias, const float *x,
                       int T, const float *dy, float aux_coef, float *dx, moe_b200_grads *g,
-                      float *aux_loss);
+                      float *aux_loss, const moe_b200_opts *opts);
 
 /* Same on device buffers (16-byte aligned), asynchronous on `stream`. */
 int moe_b200_backward_device(const moe_b200_weights *w, const float *d_bias, const float *d_x,
                              int T, const float *d_dy, float aux_coef, float *d_dx,
-                             moe_b200_grads *g, float *d_aux_loss, void *stream);
+                             moe_b200_grads *g, float *d_aux_loss, const moe_b200_opts *opts,
+                             void *stream);
 
 /* Size of the static device array behind moe_b200_forward_noalloc. */
 #define MOE_B200_NOALLOC_SCRATCH_BYTES (16u << 20)

@@ -65,8 +65,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const int *__restrict__ plan, int E, int num_kb, int b_rows_per_expert,
                 int NT, float *__restrict__ out, int ldo, DeviceStatus *status,
-                float *const *__restrict__ out_ptrs, const int2 *__restrict__ ret)
+                float *const *__restrict__ out_ptrs, const int2 *__restrict__ ret,
+                float *__restrict__ gu_save)
 {
+    // gu_save (SWIGLU, optional): the gate and up pre-activations [rows × 2·ldo]
+    // in the weights' row order (per 128 columns: 128 gate, then 128 up), for
+    // the backward
     constexpr int B_BYTES = BN * BK * 4;
     constexpr uint32_t TMEM_COLS = 2 * BN;        // two accumulator buffers
     constexpr uint32_t IDESC = idesc_tf32(BM, BN);
@@ -208,10 +212,14 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             float *stage = sEpi + q * EPI_FLOATS;
             const int sub = lane >> 3, c4 = (lane & 7) * 4;
             float *rowdst[8];
+            float *gudst[8];
 #pragma unroll
             for (int pass = 0; pass < 8; pass++) {
                 const int r = pass * 4 + sub;
                 rowdst[pass] = nullptr;
+                gudst[pass] = nullptr;
+                if (SWIGLU && gu_save != nullptr && q * 32 + r < nvalid)
+                    gudst[pass] = gu_save + (size_t)(row0 + r) * 2 * ldo + (size_t)c.ni * 256;
                 if (q * 32 + r < nvalid) {
                     const size_t grow = (size_t)(row0 + r);
                     if (!SWIGLU && ret != nullptr) {
@@ -231,6 +239,24 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     float u[32];
                     tmem_ld32(taddr + col, v);
                     tmem_ld32(taddr + BN / 2 + col, u);
+                    if (gu_save != nullptr) {
+#pragma unroll
+                        for (int half = 0; half < 2; half++) {
+#pragma unroll
+                            for (int j = 0; j < 32; j++) stage[lane * 33 + j] = half ? u[j] : v[j];
+                            __syncwarp();
+#pragma unroll
+                            for (int pass = 0; pass < 8; pass++) {
+                                const int r = pass * 4 + sub;
+                                if (gudst[pass] != nullptr) {
+                                    const float *sr = stage + r * 33 + c4;
+                                    *reinterpret_cast<float4 *>(gudst[pass] + half * 128 + col + c4) =
+                                        make_float4(sr[0], sr[1], sr[2], sr[3]);
+                                }
+                            }
+                            __syncwarp();
+                        }
+                    }
 #pragma unroll
                     for (int j = 0; j < 32; j++)   // h feeds the TF32 down GEMM: rounded
                         v[j] = round_tf32(swiglu_ref(v[j], u[j]));
@@ -297,13 +323,14 @@ static int tile_bound(int rows_bound, int E) { return ceil_div(rows_bound, tc::B
 
 cudaError_t launch_tc_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, const int *plan,
                              int E, int rows_bound, int num_sms, DeviceStatus *status,
-                             cudaStream_t s)
+                             cudaStream_t s, float *gu_save)
 {
     const int NT = F_pad / 128;               // 256 weight rows (128 gate + 128 up) per tile
     const int bound = tile_bound(rows_bound, E) * NT;
     const int grid = max(1, min(num_sms, bound));
     tc::tc_grouped_gemm<256, true><<<grid, tc::kThreads, tc::smem_bytes<256>(), s>>>(
-        g.tmA, g.tmB, plan, E, d_pad / tc::BK, 2 * F_pad, NT, h, F_pad, status, nullptr, nullptr);
+        g.tmA, g.tmB, plan, E, d_pad / tc::BK, 2 * F_pad, NT, h, F_pad, status, nullptr, nullptr,
+        gu_save);
     return cudaGetLastError();
 }
 
@@ -317,10 +344,12 @@ cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float 
     const int grid = max(1, min(num_sms, bound));
     if (bn == 256)
         tc::tc_grouped_gemm<256, false><<<grid, tc::kThreads, tc::smem_bytes<256>(), s>>>(
-            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status, y_ptrs, ret);
+            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status, y_ptrs, ret,
+            nullptr);
     else
         tc::tc_grouped_gemm<128, false><<<grid, tc::kThreads, tc::smem_bytes<128>(), s>>>(
-            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status, y_ptrs, ret);
+            g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status, y_ptrs, ret,
+            nullptr);
     return cudaGetLastError();
 }
 

@@ -23,7 +23,10 @@ int router_splits(int T, int d);
 cudaError_t launch_dispatch(const float *x, int T, int d, int d_pad, int E, int k,
                             const int *ids, const int *loc, const int *tile_cnt,
                             int *tile_pref, int *plan, int *pos_of, float *x_perm,
-                            int round_to_tf32, DeviceStatus *status, cudaStream_t s);
+                            int round_to_tf32, DeviceStatus *status, cudaStream_t s,
+                            int align = 1);
+// zero rows [off[e] + cnt[e], off[e + 1]) of every expert segment of buf [rows × ld]
+cudaError_t launch_zero_pad_rows(float *buf, int ld, const int *plan, int E, cudaStream_t s);
 
 // scan only (the expert-parallel path does its own gather)
 cudaError_t launch_dispatch_scan(const int *tile_cnt, int T, int E, int *tile_pref, int *plan,
@@ -42,11 +45,43 @@ struct BwdArgs {
     const float *dy;                                        // [T × d]
     float aux_coef;
     float *dw, *dO, *dgu, *dxp, *dlogit, *pmean;            // workspace (dxp may be y)
+    float *wr_part;                                         // [router_wgrad_splits × d × E]
     float *dx;                                              // [T × d]
     float *g_router, *g_bias, *g_gate, *g_up, *g_down;      // accumulated gradients
     float *aux_loss;                                        // device scalar or null
+    int round_tf32;                                         // dO feeds TF32 GEMMs
 };
+// the whole backward on FP32 FFMA, or its three parts (the tensor-core
+// backward replaces the middle one)
+constexpr int kRouterWgradSplits = 64;
+int router_wgrad_splits(int T, int d, int E);
 cudaError_t launch_moe_backward(const BwdArgs &a, cudaStream_t s, int *launches);
+cudaError_t launch_bwd_head(const BwdArgs &a, cudaStream_t s, int *n);
+cudaError_t launch_bwd_ffma_gemms(const BwdArgs &a, cudaStream_t s, int *n);
+cudaError_t launch_bwd_tail(const BwdArgs &a, cudaStream_t s, int *n);
+
+// tcgen05 TF32 backward GEMMs (expert_tc_bwd.cu): dH + SwiGLU backward,
+// dW_down, dW_gate / dW_up, dX_perm.  Expert segments of the plan start at
+// multiples of 32 rows with zeroed alignment rows in h, dO and x_perm.  The
+// *_mn maps use the 128-byte swizzle with 32-byte atoms, the *_k maps the
+// plain 128-byte swizzle.
+struct TcBwd {
+    CUtensorMap tm_dO_k;    // dO    [rows × d_pad], box 128 rows (K-major A)
+    CUtensorMap tm_dn_mn;   // dn    [E·d_pad × F_pad], box 32 rows (MN-major B)
+    CUtensorMap tm_h_mn;    // h     [rows × F_pad], box 32 rows
+    CUtensorMap tm_dO_mn;   // dO    [rows × d_pad], box 32 rows
+    CUtensorMap tm_x_mn;    // x_perm [rows × d_pad], box 32 rows
+    CUtensorMap tm_dgu_mn;  // dGU   [rows × 2·F_pad], box 32 rows
+    CUtensorMap tm_dgu_k;   // dGU   [rows × 2·F_pad], box 128 rows (K-major A)
+    CUtensorMap tm_ug_mn;   // ug    [E·2·F_pad × d_pad], box 32 rows
+    const int *plan;
+    int E, d, F, d_pad, F_pad, rows_bound, num_sms;
+    const float *gu;        // saved gate / up pre-activations
+    float *dgu, *dxp;
+    float *g_down, *g_gate, *g_up;
+    DeviceStatus *status;
+};
+cudaError_t launch_tc_bwd(const TcBwd &g, cudaStream_t s);
 
 // block_forward's pre-FFN RMSNorm over rows of x[T × d] (block_ffn.cu)
 cudaError_t launch_rmsnorm(const float *x, int T, int d, const float *weight, float eps,
@@ -69,7 +104,8 @@ struct TcGemm {
     CUtensorMap tmB;   // weights [E*NB × K_pad], box {32, BN}, SW128
 };
 cudaError_t launch_tc_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, const int *plan,
-                             int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s);
+                             int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s,
+                             float *gu_save = nullptr);
 // y_ptrs/ret (expert parallel): output row i goes to y_ptrs[ret[i].x] + ret[i].y * d_pad
 cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float *y, const int *plan,
                            int E, int rows_bound, int num_sms, DeviceStatus *status, cudaStream_t s,

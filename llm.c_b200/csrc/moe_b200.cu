@@ -65,7 +65,10 @@ static EncodeTiledFn get_encode() {
 }
 
 // 2-D fp32 row-major [rows × cols] tensor, box {32, box_rows}, 128B swizzle.
-static int make_tmap(CUtensorMap *m, const float *ptr, int64_t rows, int64_t cols, int box_rows) {
+static int make_tmap(CUtensorMap *m, const float *ptr, int64_t rows, int64_t cols, int box_rows,
+                     bool mn_major = false) {
+    // mn_major: operand read MN-major by tcgen05 kind::tf32, which takes only
+    // the 128-byte swizzle with 32-byte atoms
     EncodeTiledFn enc = get_encode();
     if (!enc) return fail(MOE_B200_E_CUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -73,7 +76,8 @@ static int make_tmap(CUtensorMap *m, const float *ptr, int64_t rows, int64_t col
     cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(ptr), dims, strides,
-                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MOE_B200_E_CUDA, "cuTensorMapEncodeTiled error %d", (int)r);
     return MOE_B200_OK;
@@ -117,7 +121,7 @@ struct Ctx {
     Buf io_x, io_out, io_bias;
     Buf xn, io_rms;                      // block FFN: RMSNorm output, host-call norm weights
     Buf gu, dO, dgu, dw, dlogit, pmean;  // backward: saved pre-activations and gradients
-    Buf io_dy, io_dx, io_aux;
+    Buf io_dy, io_dx, io_aux, wr_part;
     int last_E = 0;
     int last_launches = 0;
     int last_path = 0;
@@ -219,7 +223,7 @@ extern "C" void moe_b200_shutdown(void) {
                        &c->plan, &c->pos_of, &c->x_perm, &c->h, &c->y, &c->xs, &c->hs,
                        &c->rpart, &c->y2, &c->io_x, &c->io_out, &c->io_bias,
                        &c->xn, &c->io_rms, &c->gu, &c->dO, &c->dgu, &c->dw, &c->dlogit,
-                       &c->pmean, &c->io_dy, &c->io_dx, &c->io_aux};
+                       &c->pmean, &c->io_dy, &c->io_dx, &c->io_aux, &c->wr_part};
         for (Buf *b : bufs) free_buf(*b);
         cudaFree(c->status);
         cudaStreamDestroy(c->stream);
@@ -802,31 +806,58 @@ extern "C" int moe_b200_grads_free(moe_b200_grads *g) {
     return MOE_B200_OK;
 }
 
-// The FP32 forward again (saving the gate/up pre-activations), then the
-// backward kernels, all on stream s.
+// The forward again (saving the gate/up pre-activations), then the backward
+// kernels, all on stream s.  FP32: FFMA GEMMs, every expert segment packed.
+// TF32: tcgen05 GEMMs; expert segments start at multiples of 32 rows with
+// zeroed alignment rows, because the weight-gradient GEMMs run K over them.
 static int backward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, const float *d_x,
                        int T, const float *d_dy, float aux_coef, float *d_dx, moe_b200_grads *g,
-                       float *d_aux, cudaStream_t s) {
+                       float *d_aux, const moe_b200_opts *opts, cudaStream_t s) {
     int rc = ensure_workspace(c, w, T);
     if (rc) return rc;
     const int E = w->E, k = w->k, d = w->d;
+    int path = pick_path(w, T, opts);
+    if (path != MOE_B200_PATH_TF32) path = MOE_B200_PATH_FP32;
+    const bool tc = path == MOE_B200_PATH_TF32;
     const size_t rows = (size_t)T * k;
-    if ((rc = grow(c->gu, rows * 2 * w->F_pad * 4)) || (rc = grow(c->dO, rows * w->d_pad * 4)) ||
-        (rc = grow(c->dgu, rows * 2 * w->F_pad * 4)) || (rc = grow(c->dw, rows * 4)) ||
-        (rc = grow(c->dlogit, (size_t)T * E * 4)) || (rc = grow(c->pmean, (size_t)E * 4)))
+    const size_t rows_buf = tc ? rows + (size_t)31 * E : rows;      // with alignment rows
+    if ((rc = grow(c->x_perm, rows_buf * w->d_pad * 4)) || (rc = grow(c->h, rows_buf * w->F_pad * 4)) ||
+        (rc = grow(c->y, rows_buf * w->d_pad * 4)) || (rc = grow(c->gu, rows_buf * 2 * w->F_pad * 4)) ||
+        (rc = grow(c->dO, rows_buf * w->d_pad * 4)) || (rc = grow(c->dgu, rows_buf * 2 * w->F_pad * 4)) ||
+        (rc = grow(c->dw, rows * 4)) || (rc = grow(c->dlogit, (size_t)T * E * 4)) ||
+        (rc = grow(c->pmean, (size_t)E * 4)) ||
+        (rc = grow(c->wr_part, (size_t)router_wgrad_splits(T, d, E) * d * E * 4)))
         return rc;
     float *probs = (float *)c->probs.p, *wts = (float *)c->wts.p;
     int *ids = (int *)c->ids.p, *plan = (int *)c->plan.p, *pos_of = (int *)c->pos_of.p;
     float *x_perm = (float *)c->x_perm.p, *h = (float *)c->h.p, *y = (float *)c->y.p;
+    float *gu = (float *)c->gu.p, *dO = (float *)c->dO.p, *dgu = (float *)c->dgu.p;
     const int nsplit = router_splits(T, d);
     if (nsplit > 1 && (rc = grow(c->rpart, (size_t)nsplit * T * E * 4))) return rc;
     CK(launch_router(d_x, T, d, w->router, d_bias, E, k, probs, ids, wts, (int *)c->loc.p,
                      (int *)c->tile_cnt.p, s, (float *)c->rpart.p, nsplit));
     CK(launch_dispatch(d_x, T, d, w->d_pad, E, k, ids, (int *)c->loc.p, (int *)c->tile_cnt.p,
-                       (int *)c->tile_pref.p, plan, pos_of, x_perm, 0, c->status, s));
-    CK(launch_ffma_upgate(x_perm, w->d_pad, w->ug, w->F_pad, h, plan, E, (int)rows, s,
-                          (float *)c->gu.p));
-    CK(launch_ffma_down(h, w->F_pad, w->dn, w->d_pad, y, plan, E, (int)rows, s));
+                       (int *)c->tile_pref.p, plan, pos_of, x_perm, tc ? 1 : 0, c->status, s,
+                       tc ? 32 : 1));
+    int fwd_launches = (nsplit > 1 ? 2 : 1) + 2;
+    if (tc) {
+        CK(launch_zero_pad_rows(x_perm, w->d_pad, plan, E, s));
+        TcGemm up, dn;
+        if ((rc = make_tmap(&up.tmA, x_perm, (int64_t)rows_buf, w->d_pad, 128))) return rc;
+        if ((rc = make_tmap(&dn.tmA, h, (int64_t)rows_buf, w->F_pad, 128))) return rc;
+        up.tmB = w->tm_ug;
+        dn.tmB = w->tm_dn;
+        CK(launch_tc_upgate(up, w->d_pad, w->F_pad, h, plan, E, (int)rows, c->num_sms, c->status,
+                            s, gu));
+        CK(launch_zero_pad_rows(h, w->F_pad, plan, E, s));
+        CK(launch_tc_down(dn, w->F_pad, w->d_pad, w->down_bn, y, plan, E, (int)rows, c->num_sms,
+                          c->status, s, nullptr, nullptr));
+        fwd_launches += 4;
+    } else {
+        CK(launch_ffma_upgate(x_perm, w->d_pad, w->ug, w->F_pad, h, plan, E, (int)rows, s, gu));
+        CK(launch_ffma_down(h, w->F_pad, w->dn, w->d_pad, y, plan, E, (int)rows, s));
+        fwd_launches += 2;
+    }
     BwdArgs a{};
     a.T = T; a.d = d; a.E = E; a.k = k; a.F = w->F; a.d_pad = w->d_pad; a.F_pad = w->F_pad;
     a.rows_bound = (int)rows;
@@ -838,15 +869,42 @@ static int backward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, c
     a.dw = (float *)c->dw.p; a.dO = (float *)c->dO.p; a.dgu = (float *)c->dgu.p;
     a.dxp = y;                                // y is last read by the combine backward
     a.dlogit = (float *)c->dlogit.p; a.pmean = (float *)c->pmean.p;
+    a.wr_part = (float *)c->wr_part.p;
     a.dx = d_dx;
     a.g_router = g->router; a.g_bias = g->bias; a.g_gate = g->gate; a.g_up = g->up;
     a.g_down = g->down;
     a.aux_loss = d_aux;
+    a.round_tf32 = tc ? 1 : 0;
     int n = 0;
-    CK(launch_moe_backward(a, s, &n));
+    if (!tc) {
+        CK(launch_moe_backward(a, s, &n));
+    } else {
+        CK(launch_bwd_head(a, s, &n));
+        CK(launch_zero_pad_rows(dO, w->d_pad, plan, E, s));
+        TcBwd b{};
+        const int64_t rb = (int64_t)rows_buf;
+        if ((rc = make_tmap(&b.tm_dO_k, dO, rb, w->d_pad, 128)) ||
+            (rc = make_tmap(&b.tm_dn_mn, w->dn, (int64_t)E * w->d_pad, w->F_pad, 32, true)) ||
+            (rc = make_tmap(&b.tm_h_mn, h, rb, w->F_pad, 32, true)) ||
+            (rc = make_tmap(&b.tm_dO_mn, dO, rb, w->d_pad, 32, true)) ||
+            (rc = make_tmap(&b.tm_x_mn, x_perm, rb, w->d_pad, 32, true)) ||
+            (rc = make_tmap(&b.tm_dgu_mn, dgu, rb, 2 * w->F_pad, 32, true)) ||
+            (rc = make_tmap(&b.tm_dgu_k, dgu, rb, 2 * w->F_pad, 128)) ||
+            (rc = make_tmap(&b.tm_ug_mn, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 32, true)))
+            return rc;
+        b.plan = plan;
+        b.E = E; b.d = d; b.F = w->F; b.d_pad = w->d_pad; b.F_pad = w->F_pad;
+        b.rows_bound = (int)rows; b.num_sms = c->num_sms;
+        b.gu = gu; b.dgu = dgu; b.dxp = y;
+        b.g_down = g->down; b.g_gate = g->gate; b.g_up = g->up;
+        b.status = c->status;
+        CK(launch_tc_bwd(b, s));
+        CK(launch_bwd_tail(a, s, &n));
+        n += 1 + 5;         // dO alignment rows; dH, dGU alignment rows, dWd, dWgu, dX
+    }
     c->last_E = E;
-    c->last_launches = (nsplit > 1 ? 2 : 1) + 2 + 2 + n;
-    c->last_path = MOE_B200_PATH_FP32;
+    c->last_launches = fwd_launches + n;
+    c->last_path = path;
     return MOE_B200_OK;
 }
 
@@ -862,7 +920,8 @@ static int backward_args_check(const moe_b200_weights *w, const moe_b200_grads *
 extern "C" int moe_b200_backward_device(const moe_b200_weights *w, const float *d_bias,
                                         const float *d_x, int T, const float *d_dy,
                                         float aux_coef, float *d_dx, moe_b200_grads *g,
-                                        float *d_aux_loss, void *stream) {
+                                        float *d_aux_loss, const moe_b200_opts *opts,
+                                        void *stream) {
     int rc = backward_args_check(w, g, T);
     if (rc || T == 0) return rc;
     if (!d_x || !d_dy || !d_dx) return fail(MOE_B200_E_INVALID, "null x, dy or dx");
@@ -871,12 +930,12 @@ extern "C" int moe_b200_backward_device(const moe_b200_weights *w, const float *
     Ctx *c;
     if ((rc = get_ctx(w->device, &c))) return rc;
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
-    return backward_on(c, w, d_bias, d_x, T, d_dy, aux_coef, d_dx, g, d_aux_loss, s);
+    return backward_on(c, w, d_bias, d_x, T, d_dy, aux_coef, d_dx, g, d_aux_loss, opts, s);
 }
 
 extern "C" int moe_b200_backward(const moe_b200_weights *w, const float *router_bias,
                                  const float *x, int T, const float *dy, float aux_coef, float *dx,
-                                 moe_b200_grads *g, float *aux_loss) {
+                                 moe_b200_grads *g, float *aux_loss, const moe_b200_opts *opts) {
     int rc = backward_args_check(w, g, T);
     if (rc) return rc;
     if (T == 0) {
@@ -899,7 +958,8 @@ extern "C" int moe_b200_backward(const moe_b200_weights *w, const float *router_
         d_bias = (const float *)c->io_bias.p;
     }
     rc = backward_on(c, w, d_bias, (const float *)c->io_x.p, T, (const float *)c->io_dy.p,
-                     aux_coef, (float *)c->io_dx.p, g, aux_loss ? (float *)c->io_aux.p : nullptr, s);
+                     aux_coef, (float *)c->io_dx.p, g, aux_loss ? (float *)c->io_aux.p : nullptr,
+                     opts, s);
     if (rc) return rc;
     CK(cudaMemcpyAsync(dx, c->io_dx.p, xb, cudaMemcpyDeviceToHost, s));
     if (aux_loss) CK(cudaMemcpyAsync(aux_loss, c->io_aux.p, 4, cudaMemcpyDeviceToHost, s));

@@ -135,7 +135,8 @@ __device__ __forceinline__ int gate_col(int f) { return (f >> 7) * 256 + (f & 12
 __global__ void __launch_bounds__(256)
 bwd_combine_kernel(const float *__restrict__ dy, const float *__restrict__ y,
                    const int *__restrict__ pos_of, const float *__restrict__ wts, int d, int d_pad,
-                   int k, float *__restrict__ dw, float *__restrict__ dO) {
+                   int k, float *__restrict__ dw, float *__restrict__ dO, int round) {
+    // round: dO feeds TF32 tensor-core GEMMs, so it is rounded to nearest TF32
     __shared__ float red[8];
     const int t = blockIdx.x;
     const float *g = dy + (size_t)t * d;
@@ -148,7 +149,8 @@ bwd_combine_kernel(const float *__restrict__ dy, const float *__restrict__ y,
         for (int j = threadIdx.x; j < d_pad; j += 256) {
             const float gj = j < d ? __ldg(g + j) : 0.f;
             if (j < d) part = __fmaf_rn(gj, __ldg(yr + j), part);
-            o[j] = __fmul_rn(w, gj);
+            const float v = __fmul_rn(w, gj);
+            o[j] = round ? round_tf32(v) : v;
         }
         part = warp_sum(part);
         if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = part;
@@ -360,14 +362,19 @@ bwd_router_dx_kernel(const float *__restrict__ dlogit, const float *__restrict__
     }
 }
 
-// ---- W_r gradient: g_router[j][e] += Σ_t x[t][j] · dlogit[t][e]
+// ---- W_r gradient: g_router[j][e] += Σ_t x[t][j] · dlogit[t][e].  The
+// token range is split over blockIdx.z (fixed split points); each split
+// writes its partial sums, and bwd_router_wgrad_reduce adds them in split
+// order.
 __global__ void __launch_bounds__(256)
 bwd_router_wgrad_kernel(const float *__restrict__ x, const float *__restrict__ dlogit, int T, int d,
-                        int E, int xvec, int evec, float *__restrict__ g_router) {
+                        int E, int xvec, int evec, int chunk, float *__restrict__ part) {
     const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+    const int t0 = blockIdx.z * chunk, t1 = min(T, t0 + chunk);
     float acc[4][4];
-    gemm_tile<false, false>(x, d, m0, d, xvec, dlogit, E, n0, E, evec, 0, T, acc);
+    gemm_tile<false, false>(x, d, m0, d, xvec, dlogit, E, n0, E, evec, t0, t1, acc);
     const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+    float *p = part + (size_t)blockIdx.z * d * E;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         const int j = m0 + ty * 4 + i;
@@ -375,9 +382,29 @@ bwd_router_wgrad_kernel(const float *__restrict__ x, const float *__restrict__ d
 #pragma unroll
         for (int c = 0; c < 4; c++) {
             const int e = n0 + tx * 4 + c;
-            if (e < E) g_router[(size_t)j * E + e] = __fadd_rn(g_router[(size_t)j * E + e], acc[i][c]);
+            if (e < E) p[(size_t)j * E + e] = acc[i][c];
         }
     }
+}
+
+__global__ void __launch_bounds__(256)
+bwd_router_wgrad_reduce(const float *__restrict__ part, int splits, size_t n,
+                        float *__restrict__ g_router) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        float s = part[i];
+        for (int z = 1; z < splits; z++) s = __fadd_rn(s, part[(size_t)z * n + i]);
+        g_router[i] = __fadd_rn(g_router[i], s);
+    }
+}
+
+// splits of the router weight gradient's token range (at most kRouterSplits)
+int router_wgrad_splits(int T, int d, int E) {
+    const int tiles = ceil_div(d, BM) * ceil_div(E, BN);
+    int s = ceil_div(2 * 148, tiles);
+    s = min(s, kRouterWgradSplits);
+    s = min(s, max(1, T / 256));
+    return max(1, s);
 }
 
 // ---- dx[t] = (Σ_r dX_perm[pos(t, r)], rank order) + the router part already in dx
@@ -401,54 +428,74 @@ bwd_dx_gather_kernel(const float *__restrict__ dxp, const int *__restrict__ pos_
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
-cudaError_t launch_moe_backward(const BwdArgs &a, cudaStream_t s, int *launches) {
+// combine, renormalisation / aux / softmax backward, column sums, L_aux
+cudaError_t launch_bwd_head(const BwdArgs &a, cudaStream_t s, int *n) {
     const int T = a.T, E = a.E, k = a.k;
-    int n = 0;
-    if (T <= 0) {
-        if (launches) *launches = 0;
-        return cudaSuccess;
-    }
-    bwd_combine_kernel<<<T, 256, 0, s>>>(a.dy, a.y, a.pos_of, a.wts, a.d, a.d_pad, k, a.dw, a.dO);
-    n++;
+    bwd_combine_kernel<<<T, 256, 0, s>>>(a.dy, a.y, a.pos_of, a.wts, a.d, a.d_pad, k, a.dw, a.dO,
+                                         a.round_tf32);
     const float aux_scale = a.aux_coef * (float)E / ((float)T * (float)T * (float)k);
     const int *cnt = a.plan;
     bwd_router_kernel<<<ceil_div(T, 8), 256, 0, s>>>(a.probs, a.ids, a.wts, a.dw, cnt, T, E, k,
                                                      aux_scale, a.dlogit);
-    n++;
     bwd_colsum_kernel<<<E, 256, 0, s>>>(a.probs, a.dlogit, T, E, a.pmean, a.g_bias);
-    n++;
+    *n += 3;
     if (a.aux_loss) {
         bwd_aux_kernel<<<1, 32, 0, s>>>(a.pmean, cnt, T, E, k, a.aux_loss);
-        n++;
+        *n += 1;
     }
+    return cudaGetLastError();
+}
+
+// the expert GEMMs on FP32 FFMA: dH + SwiGLU backward, dWd, dWg / dWu, dX_perm
+cudaError_t launch_bwd_ffma_gemms(const BwdArgs &a, cudaStream_t s, int *n) {
+    const int E = a.E;
     const int mt = ceil_div(a.rows_bound, BM) + E;
     bwd_dh_kernel<<<dim3(mt, a.F_pad / BN), 256, 0, s>>>(a.dO, a.d_pad, a.dn, a.F_pad, a.gu, a.dgu,
                                                          a.plan, E);
-    n++;
     bwd_wgrad_down_kernel<<<dim3(a.F_pad / BM, a.d_pad / BN, E), 256, 0, s>>>(
         a.h, a.F_pad, a.dO, a.d_pad, a.F, a.d, a.plan, E, a.g_down);
-    n++;
     bwd_wgrad_upgate_kernel<<<dim3(a.d_pad / BM, 2 * a.F_pad / BN, E), 256, 0, s>>>(
         a.x_perm, a.d_pad, a.dgu, a.F_pad, a.d, a.F, a.plan, E, a.g_gate, a.g_up);
-    n++;
     bwd_dxp_kernel<<<dim3(mt, a.d_pad / BN), 256, 0, s>>>(a.dgu, a.F_pad, a.ug, a.d_pad, a.dxp,
                                                           a.plan, E);
-    n++;
+    *n += 4;
+    return cudaGetLastError();
+}
+
+// the router's dx and dW_router, then dx gathered over the ranks
+cudaError_t launch_bwd_tail(const BwdArgs &a, cudaStream_t s, int *n) {
+    const int T = a.T, E = a.E, k = a.k;
     const int evec = (E % 4 == 0) && aligned16(a.dlogit) && aligned16(a.router);
     bwd_router_dx_kernel<<<dim3(ceil_div(T, BM), ceil_div(a.d, BN)), 256, 0, s>>>(
         a.dlogit, a.router, T, a.d, E, evec, a.dx);
-    n++;
     const int xvec = (a.d % 4 == 0) && aligned16(a.x);
     const int dvec = (E % 4 == 0) && aligned16(a.dlogit);
-    bwd_router_wgrad_kernel<<<dim3(ceil_div(a.d, BM), ceil_div(E, BN)), 256, 0, s>>>(
-        a.x, a.dlogit, T, a.d, E, xvec, dvec, a.g_router);
-    n++;
+    const int splits = router_wgrad_splits(T, a.d, E);
+    const int chunk = round_up(ceil_div(T, splits), BK);
+    const int zs = ceil_div(T, chunk);
+    bwd_router_wgrad_kernel<<<dim3(ceil_div(a.d, BM), ceil_div(E, BN), zs), 256, 0, s>>>(
+        a.x, a.dlogit, T, a.d, E, xvec, dvec, chunk, a.wr_part);
+    const size_t nre = (size_t)a.d * E;
+    const int rblocks = (int)((nre + 255) / 256 < 1024 ? (nre + 255) / 256 : 1024);
+    bwd_router_wgrad_reduce<<<rblocks, 256, 0, s>>>(a.wr_part, zs, nre, a.g_router);
+    *n += 1;
     int threads = 256;
     if (a.d < 256) threads = max(32, round_up(a.d, 32));
     bwd_dx_gather_kernel<<<T, threads, 0, s>>>(a.dxp, a.pos_of, a.d, a.d_pad, k, a.dx);
-    n++;
-    if (launches) *launches = n;
+    *n += 3;
     return cudaGetLastError();
+}
+
+cudaError_t launch_moe_backward(const BwdArgs &a, cudaStream_t s, int *launches) {
+    int n = 0;
+    cudaError_t e = cudaSuccess;
+    if (a.T > 0) {
+        e = launch_bwd_head(a, s, &n);
+        if (e == cudaSuccess) e = launch_bwd_ffma_gemms(a, s, &n);
+        if (e == cudaSuccess) e = launch_bwd_tail(a, s, &n);
+    }
+    if (launches) *launches = n;
+    return e;
 }
 
 }  // namespace moe

@@ -12,10 +12,12 @@ namespace moe {
 // the tile histograms (tile_pref), total count, expert row offset in the
 // permuted buffer, and the m-tile prefixes the grouped GEMMs schedule on.
 // Plan layout (ints): cnt[E] | off[E+1] | mt128[E+1] | mt64[E+1] | mt256[E+1]
+// With align > 1 every expert's rows start at a multiple of align (the
+// backward's weight-gradient GEMMs run K over an expert's rows with TMA).
 // ---------------------------------------------------------------------
 __global__ void __launch_bounds__(1024)
 dispatch_scan_kernel(const int *__restrict__ tile_cnt, int n_tiles, int E,
-                     int *__restrict__ tile_pref, int *__restrict__ plan)
+                     int *__restrict__ tile_pref, int *__restrict__ plan, int align)
 {
     __shared__ int cnt_s[kMaxExperts];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -44,7 +46,7 @@ dispatch_scan_kernel(const int *__restrict__ tile_cnt, int n_tiles, int E,
         for (int e = 0; e < E; e++) {
             cnt[e] = cnt_s[e];
             off[e] = o; mt128[e] = m1; mt64[e] = m2; mt256[e] = m3;
-            o += cnt_s[e];
+            o += (cnt_s[e] + align - 1) / align * align;
             m1 += (cnt_s[e] + 127) / 128;
             m2 += (cnt_s[e] + 63) / 64;
             m3 += (cnt_s[e] + 255) / 256;
@@ -171,10 +173,10 @@ combine_kernel(const float *__restrict__ y, int d, int d_pad, int T, int k,
 cudaError_t launch_dispatch(const float *x, int T, int d, int d_pad, int E, int k,
                             const int *ids, const int *loc, const int *tile_cnt,
                             int *tile_pref, int *plan, int *pos_of, float *x_perm,
-                            int round_to_tf32, DeviceStatus *status, cudaStream_t s)
+                            int round_to_tf32, DeviceStatus *status, cudaStream_t s, int align)
 {
     const int tiles = ceil_div(T, kRouterTile);
-    dispatch_scan_kernel<<<1, 1024, 0, s>>>(tile_cnt, tiles, E, tile_pref, plan);
+    dispatch_scan_kernel<<<1, 1024, 0, s>>>(tile_cnt, tiles, E, tile_pref, plan, align);
     const int warps = T * k;
     dispatch_gather_kernel<<<ceil_div(warps, 8), 256, 0, s>>>(x, T, d, d_pad, k, E, ids, loc,
                                                                tile_pref, plan, pos_of, x_perm, round_to_tf32, status);
@@ -198,7 +200,26 @@ namespace moe {
 cudaError_t launch_dispatch_scan(const int *tile_cnt, int T, int E, int *tile_pref, int *plan,
                                  cudaStream_t s)
 {
-    dispatch_scan_kernel<<<1, 1024, 0, s>>>(tile_cnt, ceil_div(T, kRouterTile), E, tile_pref, plan);
+    dispatch_scan_kernel<<<1, 1024, 0, s>>>(tile_cnt, ceil_div(T, kRouterTile), E, tile_pref, plan, 1);
+    return cudaGetLastError();
+}
+}  // namespace moe
+
+namespace moe {
+// Zero the alignment rows of every expert segment, [off[e] + cnt[e],
+// off[e + 1]), of a [rows × ld] expert-sorted buffer.
+__global__ void __launch_bounds__(256)
+zero_pad_rows_kernel(float *__restrict__ buf, int ld, const int *__restrict__ plan, int E)
+{
+    const int e = blockIdx.x;
+    const int *cnt = plan, *off = plan + E;
+    const size_t r0 = (size_t)off[e] + cnt[e], r1 = (size_t)off[e + 1];
+    for (size_t i = r0 * ld + threadIdx.x; i < r1 * ld; i += blockDim.x) buf[i] = 0.0f;
+}
+
+cudaError_t launch_zero_pad_rows(float *buf, int ld, const int *plan, int E, cudaStream_t s)
+{
+    zero_pad_rows_kernel<<<E, 256, 0, s>>>(buf, ld, plan, E);
     return cudaGetLastError();
 }
 }  // namespace moe

@@ -90,9 +90,10 @@ def lib() -> C.CDLL:
     L.moe_b200_grads_download.argtypes = [_vp, _fp, _fp, C.POINTER(_fp), C.POINTER(_fp),
                                           C.POINTER(_fp)]
     L.moe_b200_grads_free.argtypes = [_vp]
-    L.moe_b200_backward.argtypes = [_vp, _fp, _fp, C.c_int, _fp, C.c_float, _fp, _vp, _fp]
+    L.moe_b200_backward.argtypes = [_vp, _fp, _fp, C.c_int, _fp, C.c_float, _fp, _vp, _fp,
+                                    C.POINTER(Opts)]
     L.moe_b200_backward_device.argtypes = [_vp, _vp, _vp, C.c_int, _vp, C.c_float, _vp, _vp,
-                                           _vp, _vp]
+                                           _vp, C.POINTER(Opts), _vp]
     L.moe_b200_checkpoint_config.argtypes = [C.c_char_p, _vp]
     L.moe_b200_checkpoint_load_experts.argtypes = [C.c_char_p, C.c_int, C.POINTER(_vp)]
     L.moe_b200_decoder_create.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(_vp)]
@@ -337,26 +338,30 @@ class MoEGrads:
 
 
 def moe_backward(w: MoEWeights, x: np.ndarray, dy: np.ndarray, grads: MoEGrads,
-                 bias: np.ndarray | None = None, aux_coef: float = 0.0):
+                 bias: np.ndarray | None = None, aux_coef: float = 0.0, path: int = PATH_FP32):
     """Backward of moe_forward at x given dy (host buffers): returns
-    (dx [T×d], L_aux); weight gradients accumulate into `grads`."""
+    (dx [T×d], L_aux); weight gradients accumulate into `grads`.  path:
+    PATH_FP32 (FFMA, 1e-5), PATH_TF32 (tensor cores, 2e-3) or PATH_AUTO."""
     x = np.ascontiguousarray(x, np.float32)
     dy = np.ascontiguousarray(dy, np.float32)
     T = x.shape[0]
     dx = np.empty_like(x)
     aux = np.zeros(1, np.float32)
     b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    o = _opts(path)
     _check(lib().moe_b200_backward(w.handle, _f(b), _f(x), T, _f(dy), float(aux_coef), _f(dx),
-                                   grads.handle, _f(aux)), "moe_b200_backward")
+                                   grads.handle, _f(aux), C.byref(o)), "moe_b200_backward")
     return dx, float(aux[0])
 
 
 def moe_backward_device(w: MoEWeights, x_ptr: int, T: int, dy_ptr: int, dx_ptr: int,
                         grads: MoEGrads, bias_ptr: int | None = None, aux_coef: float = 0.0,
-                        aux_ptr: int | None = None, stream: int | None = None):
+                        aux_ptr: int | None = None, stream: int | None = None,
+                        path: int = PATH_FP32):
     """Device-buffer backward, asynchronous on `stream`."""
+    o = _opts(path)
     _check(lib().moe_b200_backward_device(w.handle, bias_ptr, x_ptr, T, dy_ptr, float(aux_coef),
-                                          dx_ptr, grads.handle, aux_ptr, stream),
+                                          dx_ptr, grads.handle, aux_ptr, C.byref(o), stream),
            "moe_b200_backward_device")
 
 
