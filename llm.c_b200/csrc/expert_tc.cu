@@ -212,14 +212,10 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             float *stage = sEpi + q * EPI_FLOATS;
             const int sub = lane >> 3, c4 = (lane & 7) * 4;
             float *rowdst[8];
-            float *gudst[8];
 #pragma unroll
             for (int pass = 0; pass < 8; pass++) {
                 const int r = pass * 4 + sub;
                 rowdst[pass] = nullptr;
-                gudst[pass] = nullptr;
-                if (SWIGLU && gu_save != nullptr && q * 32 + r < nvalid)
-                    gudst[pass] = gu_save + (size_t)(row0 + r) * 2 * ldo + (size_t)c.ni * 256;
                 if (q * 32 + r < nvalid) {
                     const size_t grow = (size_t)(row0 + r);
                     if (!SWIGLU && ret != nullptr) {
@@ -239,22 +235,15 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                     float u[32];
                     tmem_ld32(taddr + col, v);
                     tmem_ld32(taddr + BN / 2 + col, u);
-                    if (gu_save != nullptr) {
+                    if (gu_save != nullptr && q * 32 + lane < nvalid) {
+                        // this lane's row, 32 consecutive gate then up columns,
+                        // stored straight from registers
+                        float *gp = gu_save + (size_t)(row0 + lane) * 2 * ldo + (size_t)c.ni * 256 + col;
 #pragma unroll
-                        for (int half = 0; half < 2; half++) {
-#pragma unroll
-                            for (int j = 0; j < 32; j++) stage[lane * 33 + j] = half ? u[j] : v[j];
-                            __syncwarp();
-#pragma unroll
-                            for (int pass = 0; pass < 8; pass++) {
-                                const int r = pass * 4 + sub;
-                                if (gudst[pass] != nullptr) {
-                                    const float *sr = stage + r * 33 + c4;
-                                    *reinterpret_cast<float4 *>(gudst[pass] + half * 128 + col + c4) =
-                                        make_float4(sr[0], sr[1], sr[2], sr[3]);
-                                }
-                            }
-                            __syncwarp();
+                        for (int j = 0; j < 32; j += 4) {
+                            *reinterpret_cast<float4 *>(gp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                            *reinterpret_cast<float4 *>(gp + 128 + j) =
+                                make_float4(u[j], u[j + 1], u[j + 2], u[j + 3]);
                         }
                     }
 #pragma unroll

@@ -24,7 +24,9 @@
 // the K-major operands, read as MN-major, leaves the accumulator at zero.)
 //
 // Same warp roles, ring, double-buffered TMEM accumulators and bounded waits
-// as the forward kernel (expert_tc.cu).  The weight-gradient epilogue adds
+// as the forward kernel (expert_tc.cu), with eight epilogue warps instead of
+// four: the backward epilogues (SwiGLU backward, gradient read-modify-write)
+// are heavier than the forward's and would otherwise bound the short-K tiles.  The weight-gradient epilogue adds
 // into the gradient buffers; each element belongs to one tile, so there are
 // no atomics.
 #include "tc_common.cuh"
@@ -38,7 +40,7 @@ constexpr int BM = 128;
 constexpr int BK = 32;
 constexpr int STAGES = 4;
 constexpr int GM = 8;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;   // producer, MMA issuer, 8 epilogue warps
 constexpr int A_BYTES = BM * BK * 4;
 constexpr int CHUNK_BYTES = 32 * BK * 4;        // one 32-float MN chunk of 32 K rows
 constexpr int EPI_FLOATS = 32 * 33;
@@ -140,7 +142,7 @@ tc_bwd_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BYTES;
     float *sEpi = reinterpret_cast<float *>(sB + STAGES * B_BYTES);
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + 4 * EPI_FLOATS);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + 8 * EPI_FLOATS);
     uint64_t *full = bars;
     uint64_t *empty = bars + STAGES;
     uint64_t *tfull = bars + 2 * STAGES;
@@ -159,7 +161,7 @@ tc_bwd_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], 128);
+            mbar_init(&tempty[b], 256);
         }
         mbar_init(fin, 1);
         *abort_flag = 0;
@@ -259,10 +261,14 @@ tc_bwd_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
+        // two warps per TMEM lane quarter (a warp reaches lanes 32·(warp % 4)
+        // and up), each taking half of the tile's columns
+        const int ew = warp - 2;
         const int q = warp & 3;
+        const int col_lo = (ew >> 2) * (BN / 2);
         int acc = 0;
         uint32_t acc_phase = 0;
-        float *stage = sEpi + q * EPI_FLOATS;
+        float *stage = sEpi + ew * EPI_FLOATS;
         const int sub = lane >> 3, c4 = (lane & 7) * 4;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
             const Tile t = decode<MODE>(tile, a);
@@ -275,7 +281,7 @@ tc_bwd_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
             const int mrow0 = q * 32;                 // this warp's first tile row
 #pragma unroll 1
-            for (int col = 0; col < BN; col += 32) {
+            for (int col = col_lo; col < col_lo + BN / 2; col += 32) {
                 float v[32];
                 tmem_ld32(taddr + col, v);
 #pragma unroll
@@ -320,41 +326,64 @@ tc_bwd_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                         *reinterpret_cast<float4 *>(a.out + base[pass] + 128) =
                             make_float4(du[0], du[1], du[2], du[3]);
                     }
-                } else {
+                } else if constexpr (MODE == DX) {
 #pragma unroll
-                for (int pass = 0; pass < 8; pass++) {
-                    const int r = pass * 4 + sub;           // row within this warp's 32
-                    const float *sr = stage + r * 33 + c4;
-                    const float x0 = sr[0], x1 = sr[1], x2 = sr[2], x3 = sr[3];
-                    const int n = t.ni * BN + col + c4;     // first of 4 output columns
-                    if (MODE == DX) {
+                    for (int pass = 0; pass < 8; pass++) {
+                        const int r = pass * 4 + sub;       // row within this warp's 32
                         if (mrow0 + r >= t.nvalid) continue;
+                        const float *sr = stage + r * 33 + c4;
                         const size_t row = (size_t)(t.a_row + mrow0 + r);
-                        *reinterpret_cast<float4 *>(a.out + row * a.ldo + n) =
-                            make_float4(x0, x1, x2, x3);
-                    } else {
-                        const int m = t.mi * BM + mrow0 + r;   // gradient row
-                        const float xs[4] = {x0, x1, x2, x3};
-                        if (MODE == WG_DOWN) {
-                            // dW_down[e][f = m][j = n]
-                            if (m >= a.F) continue;
-                            float *g = a.g0 + ((size_t)t.e * a.F + m) * a.d;
+                        *reinterpret_cast<float4 *>(a.out + row * a.ldo + t.ni * BN + col + c4) =
+                            make_float4(sr[0], sr[1], sr[2], sr[3]);
+                    }
+                } else {
+                    // weight gradients: read-modify-write of 4 consecutive elements
+                    // per lane and pass; all reads of the chunk are issued first
+                    //   WG_DOWN    dW_down[e][f = m][j = n]          rows of d
+                    //   WG_UPGATE  dW_gate / dW_up[e][j = m][f]      rows of F, n in the
+                    //              weights' gate/up column order
+                    const int rowlen = MODE == WG_DOWN ? a.d : a.F;
+                    const int mlim = MODE == WG_DOWN ? a.F : a.d;
+                    const int n = t.ni * BN + col + c4;
+                    const int within = n & 255;
+                    float *gbase = (MODE == WG_UPGATE && within >= 128) ? a.g1 : a.g0;
+                    const int c0 = MODE == WG_DOWN ? n : (n >> 8) * 128 + (within & 127);
+                    const int nv = max(0, min(4, rowlen - c0));        // valid columns
+                    const bool vec = nv == 4 && (rowlen & 3) == 0;
+                    float *dst[8];
+                    float cur[8][4];
 #pragma unroll
-                            for (int j = 0; j < 4; j++)
-                                if (n + j < a.d) g[n + j] = __fadd_rn(g[n + j], xs[j]);
-                        } else {
-                            // dW_gate / dW_up[e][j = m][f], column n in the gate/up order
-                            if (m >= a.d) continue;
-                            const int within = n & 255;
-                            float *g = (within >= 128 ? a.g1 : a.g0) +
-                                       ((size_t)t.e * a.d + m) * a.F;
-                            const int f = (n >> 8) * 128 + (within & 127);
+                    for (int pass = 0; pass < 8; pass++) {
+                        const int m = t.mi * BM + mrow0 + pass * 4 + sub;   // gradient row
+                        dst[pass] = (m < mlim && nv > 0)
+                                        ? gbase + ((size_t)t.e * mlim + m) * rowlen + c0
+                                        : nullptr;
+                        if (dst[pass] != nullptr) {
+                            if (vec) {
+                                const float4 v = *reinterpret_cast<const float4 *>(dst[pass]);
+                                cur[pass][0] = v.x; cur[pass][1] = v.y;
+                                cur[pass][2] = v.z; cur[pass][3] = v.w;
+                            } else {
 #pragma unroll
-                            for (int j = 0; j < 4; j++)
-                                if (f + j < a.F) g[f + j] = __fadd_rn(g[f + j], xs[j]);
+                                for (int j = 0; j < 4; j++) cur[pass][j] = j < nv ? dst[pass][j] : 0.f;
+                            }
                         }
                     }
-                }
+#pragma unroll
+                    for (int pass = 0; pass < 8; pass++) {
+                        if (dst[pass] == nullptr) continue;
+                        const float *sr = stage + (pass * 4 + sub) * 33 + c4;
+                        float o[4];
+#pragma unroll
+                        for (int j = 0; j < 4; j++) o[j] = __fadd_rn(cur[pass][j], sr[j]);
+                        if (vec) {
+                            *reinterpret_cast<float4 *>(dst[pass]) = make_float4(o[0], o[1], o[2], o[3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 4; j++)
+                                if (j < nv) dst[pass][j] = o[j];
+                        }
+                    }
                 }
                 __syncwarp();
             }
@@ -378,8 +407,9 @@ tc_bwd_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
 template <int BN>
 constexpr int smem_bytes() {
-    return STAGES * (A_BYTES + BN * BK * 4) + 4 * EPI_FLOATS * 4 + 1024 + 256;
+    return STAGES * (A_BYTES + BN * BK * 4) + 8 * EPI_FLOATS * 4 + 1024 + 256;
 }
+static_assert(smem_bytes<256>() <= 227 * 1024, "stage ring + epilogue staging exceed 227 KB");
 
 template <int BN, int MODE>
 static cudaError_t launch(const CUtensorMap &tmA, const CUtensorMap &tmB, const Args &a, int tiles,
