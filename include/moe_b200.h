@@ -52,7 +52,13 @@ typedef struct {
                             fastest measured), 1 = CTA-pair kernels (tcgen05
                             cta_group::2, M=256 over two SMs; down only when
                             d is padded to a multiple of 256)               */
-    int reserved[6];     /* zero                                              */
+    int host_chunks;     /* moe_b200_forward (host buffers): token chunks whose
+                            copies overlap the compute of the others; 0 = auto,
+                            1 = none.  Applied on the TF32 / FP32 paths to
+                            inputs of 64 MB and up, with chunks of at least
+                            4352 tokens, so results equal the one-chunk call
+                            bit for bit                                     */
+    int reserved[5];     /* zero                                              */
 } moe_b200_opts;
 
 /* Opaque device-resident expert set (router + E SwiGLU experts). */

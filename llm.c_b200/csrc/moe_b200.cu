@@ -11,6 +11,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -111,6 +112,11 @@ struct Ctx {
     int dec_pairs = 0;                   // co-resident CTA pairs of the 2-SM decode kernel
     int cc_major = 0, cc_minor = 0;
     cudaStream_t stream = nullptr;
+    // host-buffer forward pipeline: copies in and out on their own streams,
+    // ordered against the compute on `stream` by per-chunk events
+    static constexpr int kMaxChunks = 4;
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    cudaEvent_t ev_in[kMaxChunks] = {}, ev_done[kMaxChunks] = {};
     DeviceStatus *status = nullptr;      // device
     bool attrs_set = false;
     // workspace
@@ -226,6 +232,12 @@ extern "C" void moe_b200_shutdown(void) {
                        &c->pmean, &c->io_dy, &c->io_dx, &c->io_aux, &c->wr_part};
         for (Buf *b : bufs) free_buf(*b);
         cudaFree(c->status);
+        if (c->s_in) cudaStreamSynchronize(c->s_in), cudaStreamDestroy(c->s_in);
+        if (c->s_out) cudaStreamSynchronize(c->s_out), cudaStreamDestroy(c->s_out);
+        for (int k = 0; k < Ctx::kMaxChunks; k++) {
+            if (c->ev_in[k]) cudaEventDestroy(c->ev_in[k]);
+            if (c->ev_done[k]) cudaEventDestroy(c->ev_done[k]);
+        }
         cudaStreamDestroy(c->stream);
         delete c;
         g_ctx[i] = nullptr;
@@ -660,6 +672,109 @@ static int check_status(Ctx *c) {
     return MOE_B200_OK;
 }
 
+// Chunks of the host-buffer forward.  Copies overlap compute only when a
+// chunk's rows give the same bits as the whole call: the TF32 and FP32
+// expert paths compute every row independently of the others, and the
+// router sums its logits in one pass once a call has 64 router tiles (4033
+// tokens).  Chunks are rounded up to whole router tiles, which can shorten
+// the last one by up to 64 tokens per chunk, hence the 4096 + 64·kMaxChunks
+// floor.  1 = no pipeline.
+// The automatic count weighs the copies against the compute each extra chunk
+// adds: smaller expert groups fill tensor-core tiles less well, which costs
+// most when the expert weights dwarf the activations.  Measured end to end
+// (pinned buffers): configuration 3 (weights 13x the activations) 4.07 ms
+// in one chunk, 2.99 / 2.80 / 2.81 ms in 2 / 3 / 4; configuration 5 (45x)
+// 112.9 ms in one, 100.6 / 103.0 / 104.6 ms in 2 / 3 / 4.
+static int forward_chunks(const moe_b200_weights *w, int path, int T, size_t x_bytes, int want) {
+    if (path != MOE_B200_PATH_TF32 && path != MOE_B200_PATH_FP32) return 1;
+    if (x_bytes < ((size_t)64 << 20) || want == 1) return 1;
+    const int most = std::min(Ctx::kMaxChunks, T / (4096 + 64 * Ctx::kMaxChunks));
+    if (want <= 0) {
+        const double weight_bytes = 3.0 * w->d * w->F * w->E * 4.0;
+        want = weight_bytes > 24.0 * (double)x_bytes ? 2 : 3;
+    }
+    return std::max(1, std::min(want, most));
+}
+
+static int ensure_pipeline(Ctx *c) {
+    if (c->s_in) return MOE_B200_OK;
+    CK(cudaStreamCreateWithFlags(&c->s_in, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking));
+    for (int k = 0; k < Ctx::kMaxChunks; k++) {
+        CK(cudaEventCreateWithFlags(&c->ev_in[k], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&c->ev_done[k], cudaEventDisableTiming));
+    }
+    return MOE_B200_OK;
+}
+
+// The pipelined host-buffer forward: every chunk's H2D on s_in, its forward
+// on the library stream once its rows have landed, its D2H on s_out once
+// its forward is done.  With pinned host buffers the copies of one chunk
+// overlap the compute of the others.
+// block (optional): block_forward's FFN half; the result is x itself, updated
+// in place in io_x, and x_norm (host, optional) receives the RMSNorm rows
+// from the workspace xn.
+struct HostBlock {
+    const float *d_rms;
+    float eps;
+    float *x_norm;
+};
+
+static int forward_pipelined(Ctx *c, const moe_b200_weights *w, const float *d_bias,
+                             const float *x, int T, float *out, float *router_probs,
+                             int *expert_ids, const moe_b200_opts *opts, int chunks,
+                             const HostBlock *block = nullptr) {
+    int rc = ensure_pipeline(c);
+    if (rc) return rc;
+    const int d = w->d, E = w->E, k = w->k;
+    const int Tc = round_up(ceil_div(T, chunks), kRouterTile);
+    float *io_x = (float *)c->io_x.p;
+    float *io_out = block ? io_x : (float *)c->io_out.p;
+    float *xn = block ? (float *)c->xn.p : nullptr;
+    float *probs = (float *)c->probs.p;
+    int *ids = (int *)c->ids.p;
+    cudaStream_t s = c->stream;
+    int n = 0;
+    for (int t0 = 0; t0 < T; t0 += Tc, n++) {
+        const size_t tn = (size_t)std::min(Tc, T - t0);
+        // the previous call's D2H of this chunk must be done before its rows are reused
+        CK(cudaStreamWaitEvent(c->s_in, c->ev_done[n], 0));
+        CK(cudaMemcpyAsync(io_x + (size_t)t0 * d, x + (size_t)t0 * d, tn * d * 4,
+                           cudaMemcpyHostToDevice, c->s_in));
+        CK(cudaEventRecord(c->ev_in[n], c->s_in));
+    }
+    int launches = 0;
+    n = 0;
+    for (int t0 = 0; t0 < T; t0 += Tc, n++) {
+        const int tn = std::min(Tc, T - t0);
+        CK(cudaStreamWaitEvent(s, c->ev_in[n], 0));
+        BlockNorm bn{};
+        if (block) bn = BlockNorm{block->d_rms, block->eps, xn + (size_t)t0 * d};
+        rc = forward_on(c, w, d_bias, io_x + (size_t)t0 * d, tn, io_out + (size_t)t0 * d,
+                        probs + (size_t)t0 * E, ids + (size_t)t0 * k, opts, s,
+                        block ? &bn : nullptr);
+        if (rc) return rc;
+        launches += c->last_launches;
+        CK(cudaEventRecord(c->ev_done[n], s));
+        CK(cudaStreamWaitEvent(c->s_out, c->ev_done[n], 0));
+        CK(cudaMemcpyAsync(out + (size_t)t0 * d, io_out + (size_t)t0 * d, (size_t)tn * d * 4,
+                           cudaMemcpyDeviceToHost, c->s_out));
+        if (block && block->x_norm)
+            CK(cudaMemcpyAsync(block->x_norm + (size_t)t0 * d, xn + (size_t)t0 * d,
+                               (size_t)tn * d * 4, cudaMemcpyDeviceToHost, c->s_out));
+        if (router_probs)
+            CK(cudaMemcpyAsync(router_probs + (size_t)t0 * E, probs + (size_t)t0 * E,
+                               (size_t)tn * E * 4, cudaMemcpyDeviceToHost, c->s_out));
+        if (expert_ids)
+            CK(cudaMemcpyAsync(expert_ids + (size_t)t0 * k, ids + (size_t)t0 * k,
+                               (size_t)tn * k * 4, cudaMemcpyDeviceToHost, c->s_out));
+    }
+    c->last_launches = launches;
+    CK(cudaStreamSynchronize(c->s_out));
+    CK(cudaStreamSynchronize(s));
+    return check_status(c);
+}
+
 extern "C" int moe_b200_forward(const moe_b200_weights *w, const float *router_bias,
                                 const float *x, int T, float *out, float *router_probs,
                                 int *expert_ids, const moe_b200_opts *opts) {
@@ -677,14 +792,22 @@ extern "C" int moe_b200_forward(const moe_b200_weights *w, const float *router_b
     if ((rc = grow(c->io_bias, (size_t)w->E * 4))) return rc;
     if ((rc = ensure_workspace(c, w, T))) return rc;
     cudaStream_t s = c->stream;
-    CK(cudaMemcpyAsync(c->io_x.p, x, xb, cudaMemcpyHostToDevice, s));
     const float *d_bias = nullptr;
     if (router_bias) {
         CK(cudaMemcpyAsync(c->io_bias.p, router_bias, (size_t)w->E * 4, cudaMemcpyHostToDevice, s));
         d_bias = (const float *)c->io_bias.p;
     }
+    // the path is resolved once for the whole call, so every chunk runs the same one
+    moe_b200_opts o;
+    std::memset(&o, 0, sizeof o);
+    if (opts) o = *opts;
+    o.path = pick_path(w, T, opts);
+    const int chunks = forward_chunks(w, o.path, T, xb, o.host_chunks);
+    if (chunks > 1)
+        return forward_pipelined(c, w, d_bias, x, T, out, router_probs, expert_ids, &o, chunks);
+    CK(cudaMemcpyAsync(c->io_x.p, x, xb, cudaMemcpyHostToDevice, s));
     rc = forward_on(c, w, d_bias, (const float *)c->io_x.p, T, (float *)c->io_out.p,
-                    (float *)c->probs.p, (int *)c->ids.p, opts, s);
+                    (float *)c->probs.p, (int *)c->ids.p, &o, s);
     if (rc) return rc;
     CK(cudaMemcpyAsync(out, c->io_out.p, xb, cudaMemcpyDeviceToHost, s));
     if (router_probs)
@@ -710,16 +833,25 @@ extern "C" int moe_b200_block_ffn(const moe_b200_weights *w, const float *rms_we
     if ((rc = grow(c->io_bias, (size_t)w->E * 4))) return rc;
     if ((rc = ensure_workspace(c, w, T))) return rc;
     cudaStream_t s = c->stream;
-    CK(cudaMemcpyAsync(c->io_x.p, x, xb, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(c->io_rms.p, rms_weight, (size_t)w->d * 4, cudaMemcpyHostToDevice, s));
     const float *d_bias = nullptr;
     if (router_bias) {
         CK(cudaMemcpyAsync(c->io_bias.p, router_bias, (size_t)w->E * 4, cudaMemcpyHostToDevice, s));
         d_bias = (const float *)c->io_bias.p;
     }
+    moe_b200_opts o;
+    std::memset(&o, 0, sizeof o);
+    if (opts) o = *opts;
+    o.path = pick_path(w, T, opts);
+    const int chunks = forward_chunks(w, o.path, T, xb, o.host_chunks);
+    if (chunks > 1) {
+        const HostBlock hb{(const float *)c->io_rms.p, eps, x_norm};
+        return forward_pipelined(c, w, d_bias, x, T, x, router_probs, expert_ids, &o, chunks, &hb);
+    }
+    CK(cudaMemcpyAsync(c->io_x.p, x, xb, cudaMemcpyHostToDevice, s));
     const BlockNorm bn{(const float *)c->io_rms.p, eps, (float *)c->xn.p};
     rc = forward_on(c, w, d_bias, (const float *)c->io_x.p, T, (float *)c->io_x.p,
-                    (float *)c->probs.p, (int *)c->ids.p, opts, s, &bn);
+                    (float *)c->probs.p, (int *)c->ids.p, &o, s, &bn);
     if (rc) return rc;
     CK(cudaMemcpyAsync(x, c->io_x.p, xb, cudaMemcpyDeviceToHost, s));
     if (x_norm) CK(cudaMemcpyAsync(x_norm, c->xn.p, xb, cudaMemcpyDeviceToHost, s));

@@ -42,7 +42,8 @@ _vp = C.c_void_p
 
 
 class Opts(C.Structure):
-    _fields_ = [("path", C.c_int), ("cta_pair", C.c_int), ("reserved", C.c_int * 6)]
+    _fields_ = [("path", C.c_int), ("cta_pair", C.c_int), ("host_chunks", C.c_int),
+                ("reserved", C.c_int * 5)]
 
 
 _lib = None
@@ -130,10 +131,11 @@ def _i(a):
     return a.ctypes.data_as(_ip)
 
 
-def _opts(path: int, cta_pair: bool = False) -> Opts:
+def _opts(path: int, cta_pair: bool = False, host_chunks: int = 0) -> Opts:
     o = Opts()
     o.path = path
     o.cta_pair = int(bool(cta_pair))
+    o.host_chunks = int(host_chunks)
     return o
 
 
@@ -233,9 +235,10 @@ def moe_forward(w: MoEWeights, x: np.ndarray, bias: np.ndarray | None = None,
 
 def moe_forward_host_ptr(w: MoEWeights, x_ptr: int, T: int, out_ptr: int, probs_ptr: int | None,
                          ids_ptr: int | None, bias_ptr: int | None = None,
-                         path: int = PATH_AUTO, cta_pair: bool = False):
-    """Host-buffer forward from raw host pointers (e.g. pinned torch tensors)."""
-    o = _opts(path, cta_pair)
+                         path: int = PATH_AUTO, cta_pair: bool = False, host_chunks: int = 0):
+    """Host-buffer forward from raw host pointers (e.g. pinned torch tensors);
+    host_chunks: copy/compute pipeline chunks (0 auto, 1 none)."""
+    o = _opts(path, cta_pair, host_chunks)
     _check(lib().moe_b200_forward(w.handle, C.cast(bias_ptr, _fp) if bias_ptr else None,
                                   C.cast(x_ptr, _fp), T, C.cast(out_ptr, _fp),
                                   C.cast(probs_ptr, _fp) if probs_ptr else None,
