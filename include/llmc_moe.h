@@ -184,6 +184,21 @@ void moe_forward(const llmc_Matrix *x, const llmc_MoEWeights *w,
 void moe_b200_llmc_block_ffn(llmc_Matrix *x, const llmc_BlockWeights *bw,
                              llmc_ForwardCache *cache, const llmc_ModelConfig *cfg);
 
+/*
+ * moe_backward — the MoE block's backward, which llm.c's model_backward
+ * (src/transformer.c:981-1013) lacks, with ffn_backward's conventions
+ * (src/transformer.c:181-264): given the block input x and d_out = dL/d(out),
+ * the weight gradients are ADDED into w->W_router.grad and each expert's
+ * W_gate / W_up / W_down .grad (NULL ones are skipped) and d_x is
+ * overwritten.  The top-k choice is held fixed; with MOE_B200_AUX_COEF = c
+ * (default 0) the Switch load-balancing loss c · E · Σ_e f_e · P_e is
+ * included.  The forward is recomputed (MOE_B200_PATH as for moe_forward:
+ * tf32 tensor cores, fp32 FFMA, auto picks by group size).  Aborts on
+ * failure.
+ */
+void moe_backward(const llmc_Matrix *x, const llmc_MoEWeights *w, const llmc_ModelConfig *cfg,
+                  const llmc_ForwardCache *cache, const llmc_Matrix *d_out, llmc_Matrix *d_x);
+
 /* Drop the device copy of an expert set uploaded by moe_forward, given its
  * MoEWeights pointer, or the device decoder of inference_step's device mode,
  * given its Model pointer (no-op if none).  Returns MOE_B200_OK or a

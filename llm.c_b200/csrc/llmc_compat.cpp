@@ -4,6 +4,8 @@
 //                                                 with the MoE branch filled in
 //   moe_b200_llmc_block_ffn (src/transformer.c:752-767)  block_forward's
 //                                                 RMSNorm + FFN + residual
+//   moe_backward    the MoE counterpart of ffn_backward (src/transformer.c:
+//                   181-264), which llm.c's model_backward lacks
 //
 // Residency cache: one device expert set per MoEWeights pointer (and, for
 // dense blocks run through moe_b200_llmc_block_ffn, one single-expert set
@@ -30,6 +32,7 @@ struct Resident {
 std::mutex g_cache_mu;
 std::unordered_map<const void *, Resident> g_cache;
 std::unordered_map<const void *, Resident> g_dense;   // keyed by FFNWeights pointer
+std::unordered_map<const void *, moe_b200_grads *> g_grads;   // moe_backward's, per MoEWeights
 
 std::vector<const float *> host_sources(const llmc_MoEWeights *mw) {
     std::vector<const float *> v;
@@ -149,6 +152,66 @@ extern "C" void moe_b200_llmc_block_ffn(llmc_Matrix *x, const llmc_BlockWeights 
     if (rc) die(where, "block FFN", rc);
 }
 
+float env_aux_coef() {
+    const char *p = std::getenv("MOE_B200_AUX_COEF");
+    return p && *p ? std::strtof(p, nullptr) : 0.0f;
+}
+
+// The MoE block's backward with ffn_backward's conventions: the weight
+// gradients are added into the host .grad matrices (those that exist),
+// d_x is overwritten.  The device gradient buffers of each MoEWeights are
+// kept between calls (zeroed per call).
+extern "C" void moe_backward(const llmc_Matrix *x, const llmc_MoEWeights *mw,
+                             const llmc_ModelConfig *cfg, const llmc_ForwardCache *cache,
+                             const llmc_Matrix *d_out, llmc_Matrix *d_x) {
+    (void)cache;
+    const char *where = "moe_backward";
+    const int T = x->rows, d = x->cols, E = mw->n_experts, F = cfg->ffn_hidden;
+    if (d_out->rows != T || d_out->cols != d || d_x->rows != T || d_x->cols != d)
+        die(where, "shape mismatch", MOE_B200_E_INVALID);
+    moe_b200_weights *w = resident(mw, d, F, where);
+    moe_b200_grads *g = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_cache_mu);
+        auto it = g_grads.find(mw);
+        if (it != g_grads.end()) {
+            g = it->second;
+        } else {
+            const int rc = moe_b200_grads_create(w, &g);
+            if (rc) die(where, "gradient buffers", rc);
+            g_grads[mw] = g;
+        }
+    }
+    int rc = moe_b200_grads_zero(g);
+    if (rc) die(where, "gradient buffers", rc);
+    moe_b200_opts opts;
+    std::memset(&opts, 0, sizeof opts);
+    opts.path = env_path();
+    rc = moe_b200_backward(w, nullptr, x->data, T, d_out->data, env_aux_coef(), d_x->data, g,
+                           nullptr, &opts);
+    if (rc) die(where, "backward", rc);
+    const size_t dF = (size_t)d * F;
+    std::vector<float> wr((size_t)d * E), buf(3 * dF * (size_t)E);
+    std::vector<float *> gp(E), up(E), dp(E);
+    for (int e = 0; e < E; e++) {
+        gp[e] = buf.data() + (3 * (size_t)e + 0) * dF;
+        up[e] = buf.data() + (3 * (size_t)e + 1) * dF;
+        dp[e] = buf.data() + (3 * (size_t)e + 2) * dF;
+    }
+    rc = moe_b200_grads_download(g, wr.data(), nullptr, gp.data(), up.data(), dp.data());
+    if (rc) die(where, "gradient download", rc);
+    auto add = [](float *dst, const float *src, size_t n) {
+        if (dst)
+            for (size_t i = 0; i < n; i++) dst[i] += src[i];
+    };
+    add(mw->W_router.grad, wr.data(), wr.size());
+    for (int e = 0; e < E; e++) {
+        add(mw->experts[e].W_gate.grad, gp[e], dF);
+        add(mw->experts[e].W_up.grad, up[e], dF);
+        add(mw->experts[e].W_down.grad, dp[e], dF);
+    }
+}
+
 extern "C" void moe_forward(const llmc_Matrix *x, const llmc_MoEWeights *mw,
                             const llmc_ModelConfig *cfg, llmc_ForwardCache *cache,
                             llmc_Matrix *out) {
@@ -173,6 +236,11 @@ extern "C" int moe_b200_invalidate(const void *ptr) {
                 if (!rc) rc = r;
                 map->erase(it);
             }
+        }
+        auto gi = g_grads.find(ptr);
+        if (gi != g_grads.end()) {
+            moe_b200_grads_free(gi->second);
+            g_grads.erase(gi);
         }
     }
     std::lock_guard<std::mutex> lk(g_dec_mu);

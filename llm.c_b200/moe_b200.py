@@ -426,14 +426,38 @@ class LlmcMoE:
     exported drop-in `moe_forward` exactly as block_forward does
     (src/transformer.c:761-764)."""
 
-    def __init__(self, W_router, W_gate, W_up, W_down, top_k: int):
+    def __init__(self, W_router, W_gate, W_up, W_down, top_k: int, grads: bool = False):
         self._keep = [np.ascontiguousarray(a, np.float32) for a in (W_router, *W_gate, *W_up, *W_down)]
         E = len(W_gate)
         wr, g, u, dn = self._keep[0], self._keep[1:1 + E], self._keep[1 + E:1 + 2 * E], self._keep[1 + 2 * E:]
-        self.experts = (LlmcFFNWeights * E)(*[LlmcFFNWeights(_mat(g[e]), _mat(u[e]), _mat(dn[e]))
+        # llm.c's .grad buffers (zeroed) when asked: [W_router, gate.., up.., down..]
+        self.grads = [np.zeros_like(a) for a in self._keep] if grads else None
+
+        def mat(i):
+            a = self._keep[i]
+            gr = _f(self.grads[i]) if grads else None
+            return LlmcMatrix(_f(a), gr, a.shape[0], a.shape[1])
+
+        self.experts = (LlmcFFNWeights * E)(*[LlmcFFNWeights(mat(1 + e), mat(1 + E + e), mat(1 + 2 * E + e))
                                              for e in range(E)])
-        self.moe = LlmcMoEWeights(self.experts, _mat(wr), E, top_k)
+        self.moe = LlmcMoEWeights(self.experts, mat(0), E, top_k)
         self.d, self.E, self.k, self.F = wr.shape[0], E, top_k, g[0].shape[1]
+
+    def backward(self, x: np.ndarray, d_out: np.ndarray) -> np.ndarray:
+        """llm.c-style moe_backward: adds into self.grads, returns d_x."""
+        L = lib()
+        L.moe_backward.argtypes = [C.POINTER(LlmcMatrix), C.POINTER(LlmcMoEWeights),
+                                   C.POINTER(LlmcModelConfig), C.c_void_p,
+                                   C.POINTER(LlmcMatrix), C.POINTER(LlmcMatrix)]
+        L.moe_backward.restype = None
+        x = np.ascontiguousarray(x, np.float32)
+        d_out = np.ascontiguousarray(d_out, np.float32)
+        d_x = np.empty_like(x)
+        cfg = LlmcModelConfig()
+        cfg.d_model, cfg.ffn_hidden, cfg.n_experts, cfg.top_k_experts = self.d, self.F, self.E, self.k
+        L.moe_backward(C.byref(_mat(x)), C.byref(self.moe), C.byref(cfg), None,
+                       C.byref(_mat(d_out)), C.byref(_mat(d_x)))
+        return d_x
 
     def forward(self, x: np.ndarray):
         L = lib()

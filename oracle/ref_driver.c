@@ -10,6 +10,7 @@
  *   ref_softmax_rows  -> softmax_rows     (src/matrix.c:529-586)
  *   ref_swiglu        -> swiglu           (src/matrix.c:618-655)
  *   ref_ffn_forward   -> ffn_forward      (src/transformer.c:157-165)
+ *   ref_ffn_backward  -> ffn_backward     (src/transformer.c:181-264)
  *   ref_model_*       -> model_init / model_forward / model_free
  *                        (src/transformer.c:475-802), with srand(seed)
  *   ref_inference_*   -> inference_init / inference_step (src/inference.c)
@@ -73,6 +74,30 @@ void ref_swiglu(const float *g, const float *u, float *h, int n) {
     Matrix um = { (float *)u, NULL, 1, n };
     Matrix hm = { h, NULL, 1, n };
     swiglu(&gm, &um, &hm);
+}
+
+/* the reference's dense SwiGLU backward (ffn_backward, src/transformer.c:
+ * 181-264) at x: the saved gate/up pre-activations and h are made with the
+ * reference's own mat_mul and swiglu; weight gradients accumulate into dWg,
+ * dWu, dWd (llm.c's convention), d_x is overwritten */
+void ref_ffn_backward(const float *x, int n, int d, const float *Wg, const float *Wu,
+                      const float *Wd, int F, const float *d_out, float *dWg, float *dWu,
+                      float *dWd, float *d_x) {
+    FFNWeights w;
+    w.W_gate = (Matrix){ (float *)Wg, dWg, d, F };
+    w.W_up   = (Matrix){ (float *)Wu, dWu, d, F };
+    w.W_down = (Matrix){ (float *)Wd, dWd, F, d };
+    Matrix xm = { (float *)x, NULL, n, d };
+    Matrix gp = mat_alloc(n, F, 0), up = mat_alloc(n, F, 0), h = mat_alloc(n, F, 0);
+    mat_mul(&xm, &w.W_gate, &gp);
+    mat_mul(&xm, &w.W_up, &up);
+    swiglu(&gp, &up, &h);
+    Matrix dom = { (float *)d_out, NULL, n, d };
+    Matrix dxm = { d_x, NULL, n, d };
+    ffn_backward(&xm, &w, &gp, &up, &h, &dom, &dxm);
+    mat_free(&gp);
+    mat_free(&up);
+    mat_free(&h);
 }
 
 void ref_ffn_forward(const float *x, int n, int d, const float *Wg,

@@ -107,6 +107,9 @@ def ref():
         lib.ref_inference_logits.argtypes = [C.c_void_p]
         lib.ref_inference_pos.restype = C.c_int
         lib.ref_inference_pos.argtypes = [C.c_void_p]
+        lib.ref_ffn_backward.argtypes = [_fp, C.c_int, C.c_int, _fp, _fp, _fp, C.c_int, _fp,
+                                         _fp, _fp, _fp, _fp]
+        lib.ref_ffn_backward.restype = None
         lib.ref_rms_norm.argtypes = [_fp, C.c_int, C.c_int, _fp, C.c_float, _fp]
         lib.ref_rms_norm.restype = None
         lib.ref_model_save.restype = C.c_int

@@ -8,6 +8,8 @@ on the TF32 tensor-core path (TF32 operands through two chained GEMMs);
 the aux loss within 1e-5 relative on both.  Also: bit-stable repeats, accumulation across calls, the
 device entry point equal to the host one, edge shapes (T = 1, k = 1,
 E = 1, d not a multiple of 4) and rejected arguments."""
+import ctypes as C
+
 import numpy as np
 import pytest
 import torch
@@ -180,3 +182,58 @@ def test_backward_rejects_bad_arguments(moe):
     g.free()
     w.free()
     wq.free()
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference build absent")
+def test_dense_backward_matches_reference_ffn_backward(moe):
+    """One expert with a zero router is llm.c's dense FFN: the library's
+    backward equals the reference's own ffn_backward (src/transformer.c:
+    181-264) within the FP32 tolerance."""
+    T, d, F = 300, 256, 384
+    p = O.MoEProblem(T, d, 1, 1, F, seed=8)
+    p.W_router[:] = 0.0
+    w = upload(p)
+    dy = _dy(p, 4)
+    g = M.MoEGrads(w)
+    dx, _ = M.moe_backward(w, p.x, dy, g, path=M.PATH_FP32)
+    got = g.download()
+    Wg, Wu, Wd = p.experts[0]
+    dWg, dWu, dWd = np.zeros_like(Wg), np.zeros_like(Wu), np.zeros_like(Wd)
+    rdx = np.empty_like(dx)
+    O.ref().ref_ffn_backward(O._f(p.x), T, d, O._f(Wg), O._f(Wu), O._f(Wd), F, O._f(dy),
+                             O._f(dWg), O._f(dWu), O._f(dWd), O._f(rdx))
+    assert O.rel_err(dx, rdx) < TOL[M.PATH_FP32]
+    for a, b in ((got[2][0], dWg), (got[3][0], dWu), (got[4][0], dWd)):
+        assert O.rel_err(a, b) < TOL[M.PATH_FP32]
+    assert not np.any(got[0])
+    g.free()
+    w.free()
+
+
+def test_llmc_moe_backward_symbol(moe, monkeypatch):
+    """llm.c-struct moe_backward: adds into the .grad matrices (existing
+    contents kept), overwrites d_x, and equals the C-ABI backward."""
+    monkeypatch.setenv("MOE_B200_AUX_COEF", "0.02")
+    p = O.MoEProblem(200, 128, 8, 2, 192, seed=10)
+    llmc = M.LlmcMoE(p.W_router, [e[0] for e in p.experts], [e[1] for e in p.experts],
+                     [e[2] for e in p.experts], p.k, grads=True)
+    for a in llmc.grads:
+        a[:] = 1.0                                    # gradients already accumulated
+    dy = _dy(p, 6)
+    dx = llmc.backward(p.x, dy)
+    w = upload(p)
+    g = M.MoEGrads(w)
+    want_dx, _ = M.moe_backward(w, p.x, dy, g, aux_coef=0.02, path=M.PATH_AUTO)
+    wr, _, gg, gu, gd = g.download()
+    assert np.array_equal(dx, want_dx)
+    E = p.E
+    assert np.array_equal(llmc.grads[0], (1.0 + wr).astype(np.float32))
+    for e in range(E):
+        assert np.array_equal(llmc.grads[1 + e], 1.0 + gg[e])
+        assert np.array_equal(llmc.grads[1 + E + e], 1.0 + gu[e])
+        assert np.array_equal(llmc.grads[1 + 2 * E + e], 1.0 + gd[e])
+    L = M.lib()
+    L.moe_b200_invalidate.argtypes = [C.c_void_p]
+    assert L.moe_b200_invalidate(C.addressof(llmc.moe)) == 0
+    g.free()
+    w.free()

@@ -1,8 +1,11 @@
 """Pins of the float64 torch reference used for the backward tests
 (tests/torch_ref.py): its forward equals the oracle's restatement of
-llm.c's moe_forward (same routing), its aux loss is 1 for perfectly
-balanced routing, and its gradients pass a finite-difference check."""
+llm.c's moe_forward (same routing), its expert gradients equal llm.c's own
+dense ffn_backward (src/transformer.c:181-264) for a one-expert layer, its
+aux loss is 1 for perfectly balanced routing, and its gradients pass a
+finite-difference check."""
 import numpy as np
+import pytest
 import torch
 
 import oracle_lib as O
@@ -39,3 +42,23 @@ def test_reference_gradients_finite_difference():
         return (y * torch.tensor(dy)).sum() + 0.3 * aux
 
     assert torch.autograd.gradcheck(f, tuple(flat), eps=1e-6, atol=1e-7)
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference build absent")
+def test_reference_ffn_backward_matches_autograd():
+    """A one-expert MoE (zero router: p = 1, w = 1) is llm.c's dense FFN, so
+    the autograd expert gradients must equal the reference's ffn_backward."""
+    T, d, F = 40, 48, 72
+    p = O.MoEProblem(T, d, 1, 1, F, seed=6)
+    p.W_router[:] = 0.0
+    dy = np.random.default_rng(1).standard_normal((T, d)).astype(np.float32)
+    g, u, dn = p.experts[0]
+    dWg, dWu, dWd = np.zeros_like(g), np.zeros_like(u), np.zeros_like(dn)
+    dx = np.empty((T, d), np.float32)
+    O.ref().ref_ffn_backward(O._f(p.x), T, d, O._f(g), O._f(u), O._f(dn), F, O._f(dy),
+                             O._f(dWg), O._f(dWu), O._f(dWd), O._f(dx))
+    ref = torch_ref.moe_grads(p.x, p.W_router, None, p.experts, np.zeros((T, 1), np.int32), dy, 0.0)
+    assert O.rel_err(dx, ref[0]) < 1e-5
+    for got, want in ((dWg, ref[3][0]), (dWu, ref[4][0]), (dWd, ref[5][0])):
+        assert O.rel_err(got, want) < 1e-5
+    assert not np.any(ref[1])                  # one expert: no router gradient
