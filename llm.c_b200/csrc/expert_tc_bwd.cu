@@ -107,11 +107,20 @@ __device__ __forceinline__ Tile decode(int tile, const Args &a) {
         t.nvalid = __ldg(cnt + t.e) - t.mi * BM;
         t.nkb = a.num_kb;
     } else {
+        // inside an expert the index of the smaller operand runs fastest, so
+        // the CTAs running together share the tiles of the larger one:
+        // WG_UPGATE's A (X_perm, d columns) is smaller than its B (dGU, 2F),
+        // WG_DOWN's B (dO, d columns) smaller than its A (H, F)
         const int per = a.MT * a.NT;
         t.e = tile / per;
         const int rem = tile - t.e * per;
-        t.mi = rem / a.NT;
-        t.ni = rem - t.mi * a.NT;
+        if (MODE == WG_UPGATE) {
+            t.ni = rem / a.MT;
+            t.mi = rem - t.ni * a.MT;
+        } else {
+            t.mi = rem / a.NT;
+            t.ni = rem - t.mi * a.NT;
+        }
         t.a_row = __ldg(off + t.e);
         t.nkb = (__ldg(cnt + t.e) + BK - 1) / BK;
         t.nvalid = 0;
