@@ -26,9 +26,9 @@
 // Same warp roles, ring, double-buffered TMEM accumulators and bounded waits
 // as the forward kernel (expert_tc.cu), with eight epilogue warps instead of
 // four: the backward epilogues (SwiGLU backward, gradient read-modify-write)
-// are heavier than the forward's and would otherwise bound the short-K tiles.  The weight-gradient epilogue adds
-// into the gradient buffers; each element belongs to one tile, so there are
-// no atomics.
+// are heavier than the forward's and would otherwise bound the short-K tiles.
+// The weight-gradient epilogue adds into the gradient buffers; each element
+// belongs to one tile, so there are no atomics.
 #include "tc_common.cuh"
 
 namespace moe {

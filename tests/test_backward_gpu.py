@@ -5,9 +5,10 @@ autograd of the same forward with the GPU's routing held fixed
 Tolerance: max|Δ| / max|ref| for dx and every weight gradient, 1e-5 on
 the FP32 FFMA path (FP32 arithmetic against a float64 reference) and 4e-3
 on the TF32 tensor-core path (TF32 operands through two chained GEMMs);
-the aux loss within 1e-5 relative on both.  Also: bit-stable repeats, accumulation across calls, the
-device entry point equal to the host one, edge shapes (T = 1, k = 1,
-E = 1, d not a multiple of 4) and rejected arguments."""
+the aux loss within 1e-5 relative on both.  Also: bit-stable repeats,
+accumulation across calls, the device entry point equal to the host one,
+edge shapes (T = 1, k = 1, E = 1, d not a multiple of 4) and rejected
+arguments."""
 import ctypes as C
 
 import numpy as np
