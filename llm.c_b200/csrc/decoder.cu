@@ -130,15 +130,41 @@ __device__ __forceinline__ void rmsnorm_to_smem(const float *x, const float *__r
 // 32 output columns of v[0..n_in)·W[n_in × ld] (row-major, the reference's
 // matvec layout, src/inference.c:174-182): lane = column, warps split the
 // rows, partial sums added in warp order.  The value is valid in warp 0.
+// The first kPreRows rows of a thread's column do not depend on the input
+// vector, so a stage loads them (matvec32_preload) before the vector is
+// ready (RMSNorm, attention combine) and matvec32 starts from them; the sum
+// still runs over the rows in order, so the result is the same.
+constexpr int kPreRows = 48;
+struct MatvecPre {
+    float w[kPreRows];
+};
+
+__device__ __forceinline__ void matvec32_preload(const float *__restrict__ W, int n_in, int ld,
+                                                 int col, bool valid, MatvecPre &P) {
+    const int warp = threadIdx.x >> 5;
+    const int rows = (n_in + 7) / 8, r0 = warp * rows, r1 = min(n_in, r0 + rows);
+#pragma unroll
+    for (int u = 0; u < kPreRows; u++)
+        P.w[u] = (valid && r0 + u < r1) ? __ldg(W + (size_t)(r0 + u) * ld + col) : 0.0f;
+}
+
 __device__ __forceinline__ float matvec32(const float *v, const float *__restrict__ W, int n_in,
-                                          int ld, int col, bool valid, Smem &S) {
+                                          int ld, int col, bool valid, Smem &S,
+                                          const MatvecPre *P = nullptr) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rows = (n_in + 7) / 8, r0 = warp * rows, r1 = min(n_in, r0 + rows);
     float acc = 0.0f;
     if (valid) {
+        int first = r0;
+        if (P) {
+#pragma unroll
+            for (int u = 0; u < kPreRows; u++)
+                if (r0 + u < r1) acc = __fmaf_rn(v[r0 + u], P->w[u], acc);
+            first = r0 + kPreRows;
+        }
         // 24 rows' loads in flight before their FMAs (a decode step is
         // memory-latency bound); the sum still runs in row order
-        for (int i0 = r0; i0 < r1; i0 += 24) {
+        for (int i0 = first; i0 < r1; i0 += 24) {
             float wv[24];
 #pragma unroll
             for (int u = 0; u < 24; u++)
@@ -168,21 +194,27 @@ __device__ void qkv_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int 
                          int item, Smem &S) {
     const Dims &D = A.D;
     const float *src = layer == 0 ? A.embed + (size_t)token * D.d : A.x;
+    const int lane = threadIdx.x & 31, col = item * 32 + lane;
+    // weights and RoPE factors first: neither depends on the residual stream
+    MatvecPre P;
+    matvec32_preload(Lp.w_qkv, D.d, D.qkv, col, col < D.qkv, P);
+    const int c = col < D.nq ? col : col - D.nq;
+    const int half = D.hd / 2, pi = (c % D.hd) >> 1;
+    float cr = 0.0f, sr = 0.0f;
+    if (threadIdx.x < 32 && col < D.nq + D.kvd) {
+        cr = __ldg(A.rope_cos + (size_t)pos * half + pi);
+        sr = __ldg(A.rope_sin + (size_t)pos * half + pi);
+    }
     if (layer == 0 && item == 0)
         for (int i = threadIdx.x; i < D.d; i += kThreads) A.x[i] = __ldg(src + i);
     rmsnorm_to_smem(src, Lp.rms_attn, D, S);
-    const int lane = threadIdx.x & 31, col = item * 32 + lane;
-    const float v = matvec32(S.xn, Lp.w_qkv, D.d, D.qkv, col, col < D.qkv, S);
+    const float v = matvec32(S.xn, Lp.w_qkv, D.d, D.qkv, col, col < D.qkv, S, &P);
     if (threadIdx.x < 32) {
         // RoPE pairs (2i, 2i+1) of a head sit in adjacent lanes
         const float other = __shfl_xor_sync(0xffffffffu, v, 1);
         float *kc = A.kc + (size_t)layer * D.max_seq * D.kvd;
         float *vc = A.vc + (size_t)layer * D.max_seq * D.kvd;
         if (col < D.nq + D.kvd) {
-            const int c = col < D.nq ? col : col - D.nq;
-            const int half = D.hd / 2, pi = (c % D.hd) >> 1;
-            const float cr = __ldg(A.rope_cos + (size_t)pos * half + pi);
-            const float sr = __ldg(A.rope_sin + (size_t)pos * half + pi);
             const bool even = (c & 1) == 0;
             const float v0 = even ? v : other, v1 = even ? other : v;
             const float r = even ? __fsub_rn(__fmul_rn(v0, cr), __fmul_rn(v1, sr))
@@ -266,6 +298,9 @@ __device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chun
 __device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int item, Smem &S) {
     const Dims &D = A.D;
     const int nch = (pos + 1 + CH - 1) / CH;
+    const int lane = threadIdx.x & 31, col = item * 32 + lane;
+    MatvecPre P;                       // W_O rows do not wait for the attention output
+    matvec32_preload(Lp.w_o, D.nq, D.d, col, col < D.d, P);
     for (int t = threadIdx.x; t < D.nq; t += kThreads) {
         const int h = t / D.hd, i = t % D.hd;
         const float *ph = A.part + (size_t)h * D.nchunk * (D.hd + 2);
@@ -294,8 +329,7 @@ __device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int 
         S.xn[t] = __fdiv_rn(O, L);
     }
     __syncthreads();
-    const int lane = threadIdx.x & 31, col = item * 32 + lane;
-    const float v = matvec32(S.xn, Lp.w_o, D.nq, D.d, col, col < D.d, S);
+    const float v = matvec32(S.xn, Lp.w_o, D.nq, D.d, col, col < D.d, S, &P);
     if (threadIdx.x < 32 && col < D.d) A.x[col] = __fadd_rn(ldcg(A.x + col), v);
 }
 
@@ -397,9 +431,11 @@ __device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int item) {
 // 7: final RMSNorm and 32 columns of the LM head (x_norm·lm_head, [d × vocab]).
 __device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S) {
     const Dims &D = A.D;
-    if (!normed) rmsnorm_to_smem(A.x, A.rms_final, D, S);
     const int lane = threadIdx.x & 31, col = item * 32 + lane;
-    const float v = matvec32(S.xn, A.lm_head, D.d, D.vocab, col, col < D.vocab, S);
+    MatvecPre P;
+    matvec32_preload(A.lm_head, D.d, D.vocab, col, col < D.vocab, P);
+    if (!normed) rmsnorm_to_smem(A.x, A.rms_final, D, S);
+    const float v = matvec32(S.xn, A.lm_head, D.d, D.vocab, col, col < D.vocab, S, &P);
     if (threadIdx.x < 32 && col < D.vocab) A.logits[col] = v;
 }
 
