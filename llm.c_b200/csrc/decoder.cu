@@ -339,8 +339,16 @@ __device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int 
 // the ids and weights for the down stage.
 __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, bool publish, Smem &S) {
     const Dims &D = A.D;
-    rmsnorm_to_smem(A.x, Lp.rms_ffn, D, S);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the first 16 router weights of this lane's first expert, before the
+    // residual-stream wait of the RMSNorm
+    float w0[16];
+#pragma unroll
+    for (int u = 0; u < 16; u++) {
+        const int i = lane + 32 * u;
+        w0[u] = (warp < Lp.E && i < D.d) ? __ldg(Lp.router + (size_t)i * Lp.E + warp) : 0.0f;
+    }
+    rmsnorm_to_smem(A.x, Lp.rms_ffn, D, S);
     for (int e = warp; e < Lp.E; e += kThreads / 32) {
         float p = 0.0f;
         for (int i0 = lane; i0 < D.d; i0 += 32 * 16) {   // 16 loads in flight per lane
@@ -348,7 +356,8 @@ __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, bool publish, 
 #pragma unroll
             for (int u = 0; u < 16; u++) {
                 const int i = i0 + 32 * u;
-                wv[u] = i < D.d ? __ldg(Lp.router + (size_t)i * Lp.E + e) : 0.0f;
+                wv[u] = (e == warp && i0 == lane) ? w0[u]
+                        : i < D.d ? __ldg(Lp.router + (size_t)i * Lp.E + e) : 0.0f;
             }
 #pragma unroll
             for (int u = 0; u < 16; u++) {
@@ -382,12 +391,25 @@ __device__ void upgate_item(const StepArgs &A, const LayerPtrs &Lp, int item, Sm
     const float4 *uw = reinterpret_cast<const float4 *>(Lp.ug + (grow + 128) * D.d_pad);
     const float4 *x4 = reinterpret_cast<const float4 *>(S.xn);
     float g = 0.0f, u = 0.0f;
-    for (int i = lane; i < D.d_pad / 4; i += 32) {
-        const float4 xv = x4[i], a = __ldg(gw + i), b = __ldg(uw + i);
-        g = __fmaf_rn(xv.x, a.x, g); g = __fmaf_rn(xv.y, a.y, g);
-        g = __fmaf_rn(xv.z, a.z, g); g = __fmaf_rn(xv.w, a.w, g);
-        u = __fmaf_rn(xv.x, b.x, u); u = __fmaf_rn(xv.y, b.y, u);
-        u = __fmaf_rn(xv.z, b.z, u); u = __fmaf_rn(xv.w, b.w, u);
+    const int n4 = D.d_pad / 4;
+    for (int i0 = lane; i0 < n4; i0 += 32 * 4) {        // 4 gate/up float4 pairs in flight
+        float4 a[4], b[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int i = i0 + 32 * q;
+            a[q] = i < n4 ? __ldg(gw + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            b[q] = i < n4 ? __ldg(uw + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int i = i0 + 32 * q;
+            if (i >= n4) break;
+            const float4 xv = x4[i];
+            g = __fmaf_rn(xv.x, a[q].x, g); g = __fmaf_rn(xv.y, a[q].y, g);
+            g = __fmaf_rn(xv.z, a[q].z, g); g = __fmaf_rn(xv.w, a[q].w, g);
+            u = __fmaf_rn(xv.x, b[q].x, u); u = __fmaf_rn(xv.y, b[q].y, u);
+            u = __fmaf_rn(xv.z, b[q].z, u); u = __fmaf_rn(xv.w, b[q].w, u);
+        }
     }
     g = warp_sum(g);
     u = warp_sum(u);
