@@ -416,19 +416,23 @@ __device__ void upgate_item(const StepArgs &A, const LayerPtrs &Lp, int item, Sm
     if (lane == 0) A.h[(size_t)r * Lp.F_pad + f] = swiglu_ref(g, u);
 }
 
-// 6: 8 output columns, one warp each: y_r = h_r·W_down[ids[r]] row j
-// (packed [d_pad × F_pad]); x[j] += w_0·y_0 + w_1·y_1 + ... in rank order
-// (src/transformer.c:355-358).
-__device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int item) {
+// 6: one warp per (output column, rank): y_r = h_r·W_down[ids[r]] row j
+// (packed [d_pad × F_pad]), then x[j] += w_0·y_0 + w_1·y_1 + ... in rank
+// order (src/transformer.c:355-358).  A CTA's 8 warps cover down_cols(k)
+// columns, so the k rows of a column load in parallel.
+__host__ __device__ inline int down_cols(int k) { return k >= kThreads / 32 ? 1 : (kThreads / 32) / k; }
+
+__device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int item, Smem &S) {
     const Dims &D = A.D;
-    const int j = item * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (j >= D.d) return;
-    float out = 0.0f;
-    for (int r = 0; r < Lp.k; r++) {
+    const int cols = down_cols(Lp.k);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cw = warp / Lp.k, r = warp - cw * Lp.k;
+    const int j = item * cols + cw;
+    float y = 0.0f;
+    if (cw < cols && j < D.d) {
         const int e = __ldcg(A.ids + r);
         const float4 *wr = reinterpret_cast<const float4 *>(Lp.dn + ((size_t)e * D.d_pad + j) * Lp.F_pad);
         const float4 *hr = reinterpret_cast<const float4 *>(A.h + (size_t)r * Lp.F_pad);
-        float y = 0.0f;
         for (int i0 = lane; i0 < Lp.F_pad / 4; i0 += 32 * 8) {   // 8 float4 pairs in flight
             float4 a[8], hb[8];
 #pragma unroll
@@ -445,9 +449,19 @@ __device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int item) {
             }
         }
         y = warp_sum(y);
-        out = __fmaf_rn(ldcg(A.wts + r), y, out);
     }
-    if (lane == 0) A.x[j] = __fadd_rn(ldcg(A.x + j), out);
+    if (lane == 0) S.red[warp] = y;
+    __syncthreads();
+    if (threadIdx.x < cols) {
+        const int jj = item * cols + threadIdx.x;
+        if (jj < D.d) {
+            float out = 0.0f;
+            for (int rr = 0; rr < Lp.k; rr++)
+                out = __fmaf_rn(ldcg(A.wts + rr), S.red[threadIdx.x * Lp.k + rr], out);
+            A.x[jj] = __fadd_rn(ldcg(A.x + jj), out);
+        }
+    }
+    __syncthreads();                   // S.red is reused by the next item
 }
 
 // 7: final RMSNorm and 32 columns of the LM head (x_norm·lm_head, [d × vocab]).
@@ -485,7 +499,8 @@ __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer)
     upgate_item(A, Lp, blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) down_kernel(StepArgs A, int layer) {
-    down_item(A, A.layers[layer], blockIdx.x);
+    __shared__ Smem S;
+    down_item(A, A.layers[layer], blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) lmhead_kernel(StepArgs A) {
     __shared__ Smem S;
@@ -525,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs A) {
     const int token = A.state[0], pos = A.state[1];
     const int G = gridDim.x, b = blockIdx.x;
     unsigned phase = 0;
-    const int n_qkv = (D.qkv + 31) / 32, n_col = (D.d + 31) / 32, n_down = (D.d + 7) / 8;
+    const int n_qkv = (D.qkv + 31) / 32, n_col = (D.d + 31) / 32;
     const int nch = (pos + 1 + CH - 1) / CH;
     for (int l = 0; l < A.L; l++) {
         const LayerPtrs Lp = A.layers[l];
@@ -541,7 +556,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs A) {
             for (int it = b; it < n_ug; it += G) upgate_item(A, Lp, it, S);
         }
         if (!grid_barrier(A, ++phase * G, S)) return;
-        for (int it = b; it < n_down; it += G) down_item(A, Lp, it);
+        const int n_down = (D.d + down_cols(Lp.k) - 1) / down_cols(Lp.k);
+        for (int it = b; it < n_down; it += G) down_item(A, Lp, it, S);
         if (!grid_barrier(A, ++phase * G, S)) return;
     }
     const int n_lm = (D.vocab + 31) / 32;
@@ -660,7 +676,7 @@ int enqueue_step(moe_b200_decoder *m) {
         attn_kernel<<<dim3(D.nh, D.nchunk), kThreads, 0, s>>>(A, l);
         oproj_kernel<<<ceil_div(D.d, 32), kThreads, 0, s>>>(A, l);
         upgate_kernel<<<w->k * ceil_div(w->F, 8), kThreads, 0, s>>>(A, l);
-        down_kernel<<<ceil_div(D.d, 8), kThreads, 0, s>>>(A, l);
+        down_kernel<<<ceil_div(D.d, down_cols(w->k)), kThreads, 0, s>>>(A, l);
         n += 5;
     }
     lmhead_kernel<<<ceil_div(D.vocab, 32), kThreads, 0, s>>>(A);
