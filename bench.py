@@ -319,8 +319,8 @@ def run_decode(args):
     e2e_ms = 1000.0 * (time.perf_counter() - t0) / args.steps
     launches = ddec.launches
     ddec.free()
-    # the same step as one kernel per stage (31 launches in one graph)
-    sdec = M.Decoder(C.addressof(dec.model), cfg.max_seq, M.Decoder.STAGE_KERNELS)
+    # the same step as one persistent cooperative kernel (one launch per step)
+    sdec = M.Decoder(C.addressof(dec.model), cfg.max_seq, M.Decoder.PERSISTENT)
     for t in prefill:
         sdec.step(int(t))
     for t in toks[:args.warmup]:
@@ -374,15 +374,17 @@ def run_decode(args):
                 "h2d_bytes_per_step": 4, "d2h_bytes_per_step": cfg.vocab * 4,
                 "timing": "host wall clock around synchronous decoder steps (token up, logits "
                           "down)"},
-        "roofline": {"bound": "hbm", "kernel": "decode_step_kernel (the whole step)",
+        "roofline": {"bound": "hbm",
+                     "kernel": "the decode step's stage kernels (31 launches in one CUDA graph)",
                      "achieved": step_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": step_gbs / peaks["hbm_gbs"], "traffic": None,
                      "peak_src": peaks["src"] + " HBM copy bandwidth",
                      "note": f"{step_bytes / 1e6:.1f} MB read per step; latency-bound: "
-                             f"31 dependent stages behind grid barriers"},
-        "stage_kernels": {"tokens_per_s": 1000.0 / sk_ms, "ms_per_step": sk_ms,
+                             f"31 dependent stages"},
+        "persistent_kernel": {"tokens_per_s": 1000.0 / sk_ms, "ms_per_step": sk_ms,
                           "launches_per_step": stage_launches,
-                          "what": "the same device step as one kernel per stage"},
+                          "what": "the same device step as one persistent cooperative kernel "
+                                  "(stages behind a bounded grid barrier)"},
         "host_dropin": {"tokens_per_s": 1000.0 / host_ms, "ms_per_step": host_ms,
                         "what": "llm.c's inference_step restated on the host with the MoE "
                                 "blocks on the B200 (the drop-in symbol)",

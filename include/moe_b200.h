@@ -265,11 +265,14 @@ int moe_b200_device_info(int device, int *num_sms, int *cta_pairs);
  * MOE_B200_E_TIMEOUT if a bounded device wait ran out.  No counterpart in
  * llm.c beyond inference_step itself. */
 typedef struct moe_b200_decoder moe_b200_decoder;
-/* flags: 0 = the whole step as ONE persistent cooperative kernel (one CTA
- * per SM, stages separated by a bounded grid-wide barrier);
- * MOE_B200_DECODER_STAGE_KERNELS = one kernel per stage (31 for six
- * layers), the same arithmetic. */
+/* flags: 0 or MOE_B200_DECODER_STAGE_KERNELS = one kernel per stage (31
+ * for six layers, the faster variant measured, the default);
+ * MOE_B200_DECODER_PERSISTENT = the whole step as ONE persistent cooperative
+ * kernel (one CTA per SM, stages separated by a bounded grid-wide barrier).
+ * Both run the same arithmetic and give the same bits; asking for both is
+ * rejected. */
 #define MOE_B200_DECODER_STAGE_KERNELS 1
+#define MOE_B200_DECODER_PERSISTENT 2
 int moe_b200_decoder_create(const void *model, int max_seq, int flags, moe_b200_decoder **dec);
 int moe_b200_decoder_step(moe_b200_decoder *dec, int token, float *logits);
 /* Rewind to position `pos` (<= the current one); later steps overwrite the

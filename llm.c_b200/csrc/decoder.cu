@@ -649,12 +649,16 @@ StepArgs step_args(const moe_b200_decoder *m) {
     return A;
 }
 
+// The persistent single-kernel step when asked for; otherwise (the default,
+// the faster one measured) one kernel per stage.
+static bool persistent(int flags) { return (flags & MOE_B200_DECODER_PERSISTENT) != 0; }
+
 // the step's device work, in order, on m->stream
 int enqueue_step(moe_b200_decoder *m) {
     const Dims &D = m->D;
     cudaStream_t s = m->stream;
     StepArgs A = step_args(m);
-    if (!(m->flags & MOE_B200_DECODER_STAGE_KERNELS)) {
+    if (persistent(m->flags)) {
         DCK(cudaMemsetAsync(m->bar, 0, sizeof(unsigned), s));
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
@@ -704,6 +708,11 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
         hd % 32 || nh * hd > kMaxD || c.vocab_size <= 0 || L <= 0) {
         drop_ffns();
         return dfail(MOE_B200_E_INVALID, "unsupported model shape for the device decoder");
+    }
+    if ((flags & ~(MOE_B200_DECODER_STAGE_KERNELS | MOE_B200_DECODER_PERSISTENT)) ||
+        ((flags & MOE_B200_DECODER_STAGE_KERNELS) && persistent(flags))) {
+        drop_ffns();
+        return dfail(MOE_B200_E_INVALID, "unknown or conflicting decoder flags");
     }
     if (max_seq <= 0 || max_seq > src.rope_len) {
         drop_ffns();
@@ -777,7 +786,7 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
         cudaMemset(m->kc, 0, cache * 4) != cudaSuccess || cudaMemset(m->vc, 0, cache * 4) != cudaSuccess ||
         cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
         return bail(dfail(MOE_B200_E_CUDA, "decoder set-up"));
-    if (!(flags & MOE_B200_DECODER_STAGE_KERNELS)) {
+    if (persistent(flags)) {
         // one CTA per SM, all co-resident (cooperative launch)
         int per_sm = 0, sms = moe::device_sms(m->device);
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_step_kernel, kThreads, 0) !=
@@ -864,7 +873,7 @@ extern "C" int moe_b200_decoder_step(moe_b200_decoder *m, int token, float *logi
                             m->stream));
     DCK(cudaStreamSynchronize(m->stream));
     int err = 0;
-    if (!(m->flags & MOE_B200_DECODER_STAGE_KERNELS)) {
+    if (persistent(m->flags)) {
         DCK(cudaMemcpy(&err, m->err, 4, cudaMemcpyDeviceToHost));
         if (err) return dfail(MOE_B200_E_TIMEOUT, "decode step: grid barrier wait ran out");
     }

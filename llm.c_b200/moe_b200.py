@@ -627,7 +627,8 @@ class Decoder:
     or address of an llmc_Model, e.g. from llmc_model.LlmcDecoder or the
     reference's model_init): llm.c's inference_step on the B200."""
 
-    STAGE_KERNELS = 1      # one kernel per stage instead of one persistent kernel
+    STAGE_KERNELS = 1      # one kernel per stage (the default)
+    PERSISTENT = 2         # the whole step as one persistent cooperative kernel
 
     def __init__(self, model_ptr, max_seq: int, flags: int = 0):
         L = lib()

@@ -12,8 +12,8 @@ reference built from its own sources.
     (src/inference.c:231-358) within 5e-5;
   * rewinding (set_pos) and replaying gives bit-identical logits;
   * a full KV cache and an out-of-range token are rejected.
-Both device variants are checked: the whole step as one persistent
-cooperative kernel (default) and one kernel per stage.  The device sums in a
+Both device variants are checked: one kernel per stage (the default) and
+the whole step as one persistent cooperative kernel.  The device sums in a
 different (fixed) order than the host, so agreement is to fp32 rounding,
 not bit-exact; the two device variants run the same arithmetic and agree
 bit for bit."""
@@ -47,7 +47,7 @@ def _logits(R, s):
     return np.ctypeslib.as_array(R.ref_inference_logits(s), shape=(V,)).copy()
 
 
-MODES = [0, M.Decoder.STAGE_KERNELS]
+MODES = [M.Decoder.PERSISTENT, M.Decoder.STAGE_KERNELS]
 MODE_IDS = ["persistent", "stage_kernels"]
 
 
@@ -70,7 +70,7 @@ def test_moe_device_decode_matches_reference(moe, flags):
     R.ref_model_forward_last(m, O._i(toks), n, O._f(want))
     assert O.rel_err(got, want) < 1e-4
     assert int(np.argmax(got)) == int(np.argmax(want))
-    assert dec.launches == (1 if flags == 0 else 6 * 5 + 1)
+    assert dec.launches == (1 if flags == M.Decoder.PERSISTENT else 6 * 5 + 1)
     dec.free()
     R.ref_inference_free(s)
     O.release_ref_model(m)
@@ -98,8 +98,9 @@ def test_device_decode_variants_agree_and_rewind_is_deterministic(moe):
     R = O.ref()
     n = 70                                   # crosses a 64-position attention chunk
     m = _model(8, 2, max_seq=n + 2, L=2)
-    dec = M.Decoder(m, n + 2)
-    stage = M.Decoder(m, n + 2, M.Decoder.STAGE_KERNELS)
+    dec = M.Decoder(m, n + 2, M.Decoder.PERSISTENT)
+    stage = M.Decoder(m, n + 2)                       # the default: one kernel per stage
+    assert stage.launches == 2 * 5 + 1 and dec.launches == 1
     toks = np.random.default_rng(7).integers(0, V, n).astype(np.int32)
     first = np.empty((n, V), np.float32)
     other = np.empty(V, np.float32)
@@ -158,4 +159,13 @@ def test_inference_step_device_mode(moe, monkeypatch):
     L.moe_b200_invalidate.argtypes = [C.c_void_p]
     assert L.moe_b200_invalidate(m) == 0          # drops the model's device decoder
     R.ref_inference_free(s)
+    O.release_ref_model(m)
+
+
+def test_device_decode_rejects_conflicting_flags(moe):
+    m = _model(8, 2, max_seq=8, L=1)
+    for flags in (M.Decoder.STAGE_KERNELS | M.Decoder.PERSISTENT, 4):
+        with pytest.raises(M.MoEError) as e:
+            M.Decoder(m, 4, flags)
+        assert e.value.status == M.E_INVALID
     O.release_ref_model(m)
