@@ -276,21 +276,33 @@ __device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chun
         if (lane == 0) { dst[0] = m; dst[1] = l; }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < D.hd; i += kThreads) {
+    // the exp-weighted V sum: the chunk's positions are split over groups of
+    // hd threads (every thread of the CTA busy, one round of loads for a
+    // 64-position chunk), the group partials added in group order
+    const int groups = kThreads / D.hd, gi = threadIdx.x / D.hd, i = threadIdx.x - gi * D.hd;
+    const int per = (n + groups - 1) / groups;
+    if (gi < groups) {
+        const int jlo = gi * per, jhi = min(n, jlo + per);
         const float *vcol = vc + (size_t)j0 * D.kvd + g * D.hd + i;
         float o = 0.0f;
-        for (int jb = 0; jb < n; jb += 16) {          // 16 value loads in flight
+        for (int jb = jlo; jb < jhi; jb += 16) {      // 16 value loads in flight
             float vv[16];
 #pragma unroll
             for (int u = 0; u < 16; u++)
-                vv[u] = jb + u < n ? ldcg(vcol + (size_t)(jb + u) * D.kvd) : 0.0f;
+                vv[u] = jb + u < jhi ? ldcg(vcol + (size_t)(jb + u) * D.kvd) : 0.0f;
 #pragma unroll
             for (int u = 0; u < 16; u++)
-                if (jb + u < n) o = __fmaf_rn(S.sc[jb + u], vv[u], o);
+                if (jb + u < jhi) o = __fmaf_rn(S.sc[jb + u], vv[u], o);
         }
-        dst[2 + i] = o;
+        S.red[gi * D.hd + i] = o;
     }
-    __syncthreads();                   // S.qs / S.sc are reused by the next item
+    __syncthreads();
+    if (threadIdx.x < D.hd) {
+        float o = S.red[threadIdx.x];
+        for (int q = 1; q < groups; q++) o = __fadd_rn(o, S.red[q * D.hd + threadIdx.x]);
+        dst[2 + threadIdx.x] = o;
+    }
+    __syncthreads();                   // S.qs / S.sc / S.red are reused by the next item
 }
 
 // 3: softmax-weighted head outputs from the chunks, then x += head_out·W_O
