@@ -97,12 +97,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ void rmsnorm_to_smem(const float *x, const float *__restrict__ w,
                                                 const Dims &D, Smem &S) {
     constexpr int KEEP = 8;            // values kept in registers (d <= 2048)
-    float xv[KEEP];
+    float xv[KEEP], wv[KEEP];
     float ss = 0.0f;
 #pragma unroll
-    for (int u = 0; u < KEEP; u++) {
+    for (int u = 0; u < KEEP; u++) {   // the weights load alongside x, not after the sum
         const int i = threadIdx.x + u * kThreads;
         xv[u] = i < D.d ? ldcg(x + i) : 0.0f;
+        wv[u] = i < D.d ? __ldg(w + i) : 0.0f;
     }
 #pragma unroll
     for (int u = 0; u < KEEP; u++) ss = __fmaf_rn(xv[u], xv[u], ss);
@@ -120,7 +121,7 @@ __device__ __forceinline__ void rmsnorm_to_smem(const float *x, const float *__r
 #pragma unroll
     for (int u = 0; u < KEEP; u++) {
         const int i = threadIdx.x + u * kThreads;
-        if (i < D.d_pad) S.xn[i] = i < D.d ? __fmul_rn(__fmul_rn(xv[u], inv), __ldg(w + i)) : 0.0f;
+        if (i < D.d_pad) S.xn[i] = i < D.d ? __fmul_rn(__fmul_rn(xv[u], inv), wv[u]) : 0.0f;
     }
     for (int i = threadIdx.x + KEEP * kThreads; i < D.d_pad; i += kThreads)
         S.xn[i] = i < D.d ? __fmul_rn(__fmul_rn(ldcg(x + i), inv), __ldg(w + i)) : 0.0f;
@@ -327,16 +328,22 @@ __device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int 
                 lc[u] = ok ? ldcg(pc + 1) : 0.0f;
                 oc[u] = ok ? ldcg(pc + 2 + i) : 0.0f;
             }
-            // running rescale, chunk by chunk in order
+            // the batch's maximum first, so its exponentials are independent
+            // of each other; the sums still run chunk by chunk in order
+            float Mn = M;
+#pragma unroll
+            for (int u = 0; u < 12; u++) Mn = fmaxf(Mn, mc[u]);
+            const float a = expf(__fsub_rn(M, Mn));
+            L = __fmul_rn(L, a);
+            O = __fmul_rn(O, a);
 #pragma unroll
             for (int u = 0; u < 12; u++) {
                 if (c0 + u >= nch) break;
-                const float Mn = fmaxf(M, mc[u]);
-                const float a = expf(__fsub_rn(M, Mn)), b = expf(__fsub_rn(mc[u], Mn));
-                L = __fmaf_rn(lc[u], b, __fmul_rn(L, a));
-                O = __fmaf_rn(oc[u], b, __fmul_rn(O, a));
-                M = Mn;
+                const float b = expf(__fsub_rn(mc[u], Mn));
+                L = __fmaf_rn(lc[u], b, L);
+                O = __fmaf_rn(oc[u], b, O);
             }
+            M = Mn;
         }
         S.xn[t] = __fdiv_rn(O, L);
     }
