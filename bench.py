@@ -270,7 +270,11 @@ def run_decode(args):
     if rank != 0:
         return
     M.init(0)
-    cfg = LM.DecodeConfig(max_seq=DECODE_PREFILL + args.warmup + args.steps + 8)
+    # positions the host decoder state takes: the prefill, warm-up and timed
+    # steps, the 5 steps of the MoE stage split, then the 5 steps of the
+    # reference's own inference_step (the CPU baseline), which writes its KV
+    # cache without a bounds check; plus spare
+    cfg = LM.DecodeConfig(max_seq=DECODE_PREFILL + args.warmup + args.steps + 5 + 5 + 8)
     dec = LM.LlmcDecoder(cfg, seed=0)
     rng = np.random.default_rng(1)
     if args.impl == "reference":
@@ -338,12 +342,15 @@ def run_decode(args):
         dec.step(int(t))
     for t in toks[:args.warmup]:
         dec.step(int(t))
-    M.profile_enable(True)
-    M.profile_read()
     t0 = time.perf_counter()
     for t in toks[args.warmup:]:
         dec.step(int(t))
     host_ms = 1000.0 * (time.perf_counter() - t0) / args.steps
+    # the MoE stage split of the same steps, in a separate pass
+    M.profile_enable(True)
+    M.profile_read()
+    for t in toks[args.warmup:args.warmup + min(args.steps, 5)]:
+        dec.step(int(t))
     M.profile_enable(False)
     stage_ms, n_fw = M.profile_read()
     stage_avg = {s: v / max(n_fw, 1) for s, v in stage_ms.items()}
@@ -510,17 +517,20 @@ def block_ffn_measure(args, M, w, x, bptr, host_bias_ptr, path, stream, stage_ms
         step()
     torch.cuda.synchronize()
     launches = M.last_launches()
-    M.profile_enable(True)
-    M.profile_read()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):
         step()
     ev1.record(stream)
     torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    M.profile_enable(True)                      # stage split: a separate pass
+    M.profile_read()
+    for _ in range(min(args.steps, 5)):
+        step()
+    torch.cuda.synchronize()
     M.profile_enable(False)
     st, n = M.profile_read()
-    ms = ev0.elapsed_time(ev1) / args.steps
     # the RMSNorm runs inside the router stage: its time is the router stage's growth
     norm_ms = st["router"] / max(n, 1) - stage_ms_moe["router"] / max(n_moe, 1)
     norm_bytes = 2.0 * 4 * T * d                 # read x, write x_norm
@@ -679,8 +689,6 @@ def main():
 
     # ---- device-resident timed region (CUDA events on the launch stream,
     # barrier + synchronize on both sides, max over ranks)
-    M.profile_enable(True)
-    M.profile_read()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()
@@ -689,9 +697,16 @@ def main():
             step()
         ev1.record(stream)
         barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
+    # the per-stage split comes from a separate pass: the stage events would
+    # otherwise sit inside the timed region (every rank runs the same steps)
+    M.profile_enable(True)
+    M.profile_read()
+    for _ in range(min(args.steps, 5)):
+        step()
+    barrier()
     M.profile_enable(False)
     stage_ms, n_fw = M.profile_read()
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
     value = T / (ms / 1000.0)
 
     # ---- end to end through the public host-buffer C-ABI (pinned buffers,
