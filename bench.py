@@ -761,23 +761,30 @@ def main():
     if tfile.exists() and world == 1:
         tj = json.loads(tfile.read_text())
         traffic = tj.get(args.config, {}).get("upgate_bytes_per_launch")
-    if path_used == M.PATH_TF32:
+    # gate and up weights of the experts this rank's rows touch (each read
+    # once); under expert parallelism a rank's slice covers about 1/world
+    w_bytes = 2.0 * d * F * 4 * touched / world
+    up_flops = 4.0 * slice_rows * d * F
+    # the TF32 grouped GEMM is tensor-bound when the expert groups are large
+    # and weight-streaming (HBM-bound) when they are decode-sized
+    tf32_tensor_bound = (up_flops / (tf32_peak * 1e12)) >= (w_bytes / (peaks["hbm_gbs"] * 1e9))
+    if path_used == M.PATH_TF32 and tf32_tensor_bound:
         # tensor-bound grouped GEMM: 2 GEMMs (gate, up) of this rank's rows
-        up_flops = 4.0 * slice_rows * d * F
         achieved = up_flops / (up_ms / 1000.0) / 1e12
         roof = {"bound": "tensor", "kernel": "tc_grouped_gemm<256,swiglu> (expert up/gate)",
                 "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
                 "frac": achieved / tf32_peak, "traffic": traffic,
                 "peak_src": f"{peaks['src']} bf16 sustained / 2 (TF32 rate)"}
     else:
-        # weight-streaming (3xTF32 / FP32 FFMA): HBM-bound on the gate and up
-        # weights of the experts this rank's rows touch (each read once);
-        # under expert parallelism a rank's slice covers about 1/world of them
-        w_bytes = 2.0 * d * F * 4 * touched / world
+        # weight-streaming (3xTF32, FP32 FFMA, or TF32 on decode-sized
+        # groups): HBM-bound on the gate and up weights
         achieved = w_bytes / (up_ms / 1000.0) / 1e9
         roof = {"bound": "hbm",
-                "kernel": ("dec_gemm<up/gate> (3xTF32 weight streaming)"
-                           if path_used == M.PATH_TF32X3 else "ffma_grouped<up/gate> (FP32)"),
+                "kernel": {M.PATH_TF32X3: "dec_gemm<up/gate> (3xTF32 weight streaming)",
+                           M.PATH_TF32: ("dec_gemm<up/gate, one-pass TF32> (weight streaming)"
+                                         if T * k / E < 64 else
+                                         "tc_grouped_gemm<256,swiglu> (expert up/gate)"),
+                           }.get(path_used, "ffma_grouped<up/gate> (FP32)"),
                 "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                 "peak_src": peaks["src"] + " HBM copy bandwidth"}

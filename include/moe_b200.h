@@ -41,7 +41,9 @@ extern "C" {
 #define MOE_B200_PATH_AUTO   0  /* TF32 for prefill-sized expert groups (on
                                     average >= 64 rows per expert), 3xTF32
                                     weight streaming for decode-sized ones  */
-#define MOE_B200_PATH_TF32   1  /* tcgen05 TF32 grouped GEMMs (tol 2e-3)    */
+#define MOE_B200_PATH_TF32   1  /* tcgen05 TF32 (tol 2e-3): grouped GEMMs
+                                    for prefill-sized groups, one-pass TF32
+                                    weight streaming for decode-sized ones  */
 #define MOE_B200_PATH_FP32   2  /* FP32 FFMA grouped GEMMs (tol 1e-5)       */
 #define MOE_B200_PATH_TF32X3 3  /* tcgen05 3xTF32 weight-streaming GEMMs,
                                     FP32 accuracy (tol 1e-5)                */

@@ -56,16 +56,21 @@ MOE_DEV float swiglu_ref(float g, float u) {
 // e ascending, chosen experts skipped) and renormalisation (:334-337,350).
 // Leaves the probabilities in row and writes sel[k] (rank order) and w[k].
 MOE_DEV void route_token(float *row, int E, int k, int *sel, float *w) {
+    // (every small array below is indexed with compile-time indices only, so
+    // it stays in registers; the arithmetic and its order are the reference's)
     const int nv = E - E % 8;
     float mx = -1e38f;
     for (int e = 0; e < E; e++) mx = fmaxf(mx, row[e]);
     float lane[8];
 #pragma unroll
     for (int l = 0; l < 8; l++) lane[l] = 0.0f;
-    for (int e = 0; e < nv; e++) {
-        const float ex = exp_ref(__fsub_rn(row[e], mx));
-        row[e] = ex;
-        lane[e & 7] = __fadd_rn(lane[e & 7], ex);
+    for (int e0 = 0; e0 < nv; e0 += 8) {
+#pragma unroll
+        for (int l = 0; l < 8; l++) {
+            const float ex = exp_ref(__fsub_rn(row[e0 + l], mx));
+            row[e0 + l] = ex;
+            lane[l] = __fadd_rn(lane[l], ex);
+        }
     }
     const float a0 = __fadd_rn(lane[0], lane[4]), a1 = __fadd_rn(lane[1], lane[5]);
     const float a2 = __fadd_rn(lane[2], lane[6]), a3 = __fadd_rn(lane[3], lane[7]);
@@ -77,20 +82,34 @@ MOE_DEV void route_token(float *row, int E, int k, int *sel, float *w) {
     const float inv = __fdiv_rn(1.0f, sum);
     for (int e = 0; e < nv; e++) row[e] = __fmul_rn(row[e], inv);
     for (int e = nv; e < E; e++) row[e] = __fdiv_rn(row[e], sum);
-    for (int r = 0; r < k; r++) {
+    int pick[kMaxTopK];
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; r++) pick[r] = -1;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; r++) {
+        if (r >= k) break;
         float best = -1.0f;
         int best_e = 0;
         for (int e = 0; e < E; e++) {
             bool taken = false;
-            for (int q = 0; q < r; q++) taken |= (sel[q] == e);
+#pragma unroll
+            for (int q = 0; q < kMaxTopK; q++) taken |= (pick[q] == e);
             if (!taken && row[e] > best) { best = row[e]; best_e = e; }
         }
-        sel[r] = best_e;
+        pick[r] = best_e;
     }
     float s = 0.0f;
-    for (int r = 0; r < k; r++) s = __fadd_rn(s, row[sel[r]]);
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; r++)
+        if (r < k) s = __fadd_rn(s, row[pick[r]]);
     const float winv = (s > 1e-9f) ? __fdiv_rn(1.0f, s) : 0.0f;
-    for (int r = 0; r < k; r++) w[r] = __fmul_rn(row[sel[r]], winv);
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; r++) {
+        if (r < k) {
+            sel[r] = pick[r];
+            w[r] = __fmul_rn(row[pick[r]], winv);
+        }
+    }
 }
 
 // Round an fp32 value to the nearest TF32 (10-bit mantissa, ties away

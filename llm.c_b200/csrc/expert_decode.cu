@@ -155,12 +155,21 @@ __device__ __forceinline__ bool wait_done(uint64_t *done, int m, volatile int *a
 // warps arrive on rank 0's ready barrier (cluster-scope release); rank 0's
 // single commit per step arrives on both CTAs' done rings (multicast
 // commit, not a load).
-template <bool UPGATE, bool PAIR>
+// ONEPASS: plain TF32 (tolerance 2e-3, the prefill tensor-core path's
+// numerics) instead of 3xTF32.  One N=64 MMA per 8-wide K slice (W·X with X
+// rounded to nearest TF32 by the dispatch), accumulated in TMEM over the
+// whole tile (two per-tile accumulators of 64 columns, alternating, so the
+// epilogue of one tile overlaps the MMAs of the next); no W_small, no
+// per-step partials.  The converter warps only gate the ring (weight tile,
+// token tile, free accumulator) and the epilogue waits once per tile on
+// accfull[tile % 2].  H is stored rounded to nearest TF32.
+template <bool UPGATE, bool PAIR, bool ONEPASS>
 __global__ void __launch_bounds__(kThreads, 1)
 dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
          const __grid_constant__ CUtensorMap tmXs, const __grid_constant__ CUtensorMap tmXb32,
          DecArgs a)
 {
+    static_assert(!(PAIR && ONEPASS), "ONEPASS runs on single CTAs");
     constexpr int MM = PAIR ? 2 * MW : MW;                  // MMA M (weight rows per block)
     constexpr uint32_t IDESC_N128 = idesc_tf32(MM, 2 * NTOK);
     constexpr uint32_t IDESC_N64 = idesc_tf32(MM, NTOK);
@@ -177,7 +186,8 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
     uint64_t *wfull = bars, *xfull = wfull + NW, *ready = xfull + NX, *done = ready + NS;
     uint64_t *pempty = done + R;
     uint64_t *ups_ready = pempty + NSLOT, *ups_free = ups_ready + 1, *fin = ups_free + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(fin + 1);
+    uint64_t *accfull = fin + 1;                         // ONEPASS: [NSLOT] tile accumulators
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accfull + NSLOT);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -190,6 +200,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
         for (int s = 0; s < NS; s++) mbar_init(&ready[s], PAIR ? 256 : 128);
         for (int s = 0; s < R; s++) mbar_init(&done[s], 1);
         for (int s = 0; s < NSLOT; s++) mbar_init(&pempty[s], 128);
+        for (int s = 0; s < NSLOT; s++) mbar_init(&accfull[s], 1);
         mbar_init(ups_ready, 64);
         mbar_init(ups_free, 64);
         mbar_init(fin, 1);
@@ -260,6 +271,10 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                         } else {
                             tma_load_2d(dst, &tmW, (kb0 + kb) * BK, wrow, &full[st]);
                         }
+                    } else if (ONEPASS) {
+                        uint8_t *dst = sX + st * XB;
+                        mbar_expect_tx(&full[st], B_BYTES);
+                        tma_load_2d(dst, &tmXb, (kb0 + kb) * BK, t.row0, &full[st]);
                     } else if (!PAIR) {
                         uint8_t *dst = sX + st * XB;
                         mbar_expect_tx(&full[st], XB);
@@ -292,6 +307,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
             const uint32_t ts0 = tmem_base + WS_COL0;
             bool ok = true;
             uint32_t ph = 0;                      // parity of ready[] in this round of R steps
+            int kb = 0, tl = 0;                   // ONEPASS: K step in the tile, tile count
             for (int n0 = 0; n0 < nsteps && ok; n0 += R, ph ^= 1) {
 #pragma unroll
                 for (int j = 0; j < R; j++) {
@@ -309,20 +325,34 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                     const uint64_t dx = dx0 + (uint64_t)((j % NX) * (XB >> 4));
                     const uint64_t dx2 = dx + (uint64_t)(XB2 >> 4);      // MMA2's B
                     const uint32_t ts = ts0 + (uint32_t)(j * BK);
+                    if constexpr (ONEPASS) {
+                        const uint32_t dacc = tmem_base + (uint32_t)((tl & 1) * NTOK);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 8; kk++) {
-                        // cols 0..63: W·X_big, cols 64..127: W·X_small (X_big|X_small as one 128-row B)
-                        // then cols 0..63 += W_small·X_big (A: 8 columns of W_small in TMEM)
-                        if (PAIR) {
-                            mma_tf32_pair(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
-                            mma_tf32_ts_pair(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
-                        } else {
-                            mma_tf32(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
-                            mma_tf32_ts(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
+                        for (int kk = 0; kk < BK / 8; kk++)
+                            mma_tf32(dacc, dw + 2 * kk, dx + 2 * kk, IDESC_N64, (kb | kk) ? 1u : 0u);
+                        mma_commit(&done[j]);
+                        if (++kb == a.num_kb) {           // the tile's accumulator is complete
+                            mma_commit(&accfull[tl & 1]);
+                            kb = 0;
+                            tl++;
                         }
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < BK / 8; kk++) {
+                            // cols 0..63: W·X_big, cols 64..127: W·X_small (X_big|X_small as one
+                            // 128-row B), then cols 0..63 += W_small·X_big (A: 8 columns of
+                            // W_small in TMEM)
+                            if (PAIR) {
+                                mma_tf32_pair(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
+                                mma_tf32_ts_pair(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
+                            } else {
+                                mma_tf32(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
+                                mma_tf32_ts(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
+                            }
+                        }
+                        if (PAIR) mma_commit_pair(&done[j]);
+                        else mma_commit(&done[j]);
                     }
-                    if (PAIR) mma_commit_pair(&done[j]);
-                    else mma_commit(&done[j]);
                 }
             }
             if (!ok) set_abort(12);
@@ -346,36 +376,55 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
         Ring<NSLOT> rp;
         Ring<R> rlag;                             // step n - NS of the done ring
         bool ok = true;
-        for (int n = 0; n < nsteps; n++) {
-            if (!mbar_wait(&wfull[rw.i], rw.ph, abort_flag) ||
-                (cw == 2 && !mbar_wait(&xfull[rx.i], rx.ph, abort_flag)) ||
-                (cw == 3 && !mbar_wait(&pempty[rp.i], rp.ph ^ 1, abort_flag))) {
-                ok = false;
-                break;
+        if constexpr (ONEPASS) {
+            // gate only: every warp waits for the weight tile (which bounds
+            // how far ahead of the MMAs it runs), warp 2 for the token tile,
+            // warp 3 at a tile's first step for its free accumulator
+            int kb = 0;
+            for (int n = 0; n < nsteps; n++) {
+                if (!mbar_wait(&wfull[rw.i], rw.ph, abort_flag) ||
+                    (cw == 2 && !mbar_wait(&xfull[rx.i], rx.ph, abort_flag)) ||
+                    (cw == 3 && kb == 0 && !mbar_wait(&pempty[rp.i], rp.ph ^ 1, abort_flag))) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive(&ready[rs.i]);
+                rw.next(); rs.next(); rx.next();
+                if (++kb == a.num_kb) { kb = 0; rp.next(); }
             }
-            if (n >= NS) {                        // the W_small slot's last reader finished
-                if (!mbar_wait(&done[rlag.i], rlag.ph, abort_flag)) { ok = false; break; }
-                rlag.next();
+            if (!ok) set_abort(13);
+        } else {
+            for (int n = 0; n < nsteps; n++) {
+                if (!mbar_wait(&wfull[rw.i], rw.ph, abort_flag) ||
+                    (cw == 2 && !mbar_wait(&xfull[rx.i], rx.ph, abort_flag)) ||
+                    (cw == 3 && !mbar_wait(&pempty[rp.i], rp.ph ^ 1, abort_flag))) {
+                    ok = false;
+                    break;
+                }
+                if (n >= NS) {                        // the W_small slot's last reader finished
+                    if (!mbar_wait(&done[rlag.i], rlag.ph, abort_flag)) { ok = false; break; }
+                    rlag.next();
+                }
+                // this thread's weight row: its 128 bytes, 16-byte chunks
+                // permuted by the 128-byte swizzle (chunk c sits at c ^ (row % 8))
+                const uint8_t *wrow = sW + rw.i * A_BYTES + crow * 128;
+                float ws[BK];
+    #pragma unroll
+                for (int c = 0; c < BK / 4; c++) {
+                    const float4 v = *reinterpret_cast<const float4 *>(wrow + ((c ^ (crow & 7)) << 4));
+                    ws[4 * c + 0] = tf32_residual(v.x);
+                    ws[4 * c + 1] = tf32_residual(v.y);
+                    ws[4 * c + 2] = tf32_residual(v.z);
+                    ws[4 * c + 3] = tf32_residual(v.w);
+                }
+                tmem_st32(ws_lane + WS_COL0 + (uint32_t)(rs.i * BK), ws);
+                tc_fence_before();
+                if (PAIR) mbar_arrive_cluster(mapa(smem_u32(&ready[rs.i]), 0));
+                else mbar_arrive(&ready[rs.i]);
+                rw.next(); rs.next(); rx.next(); rp.next();
             }
-            // this thread's weight row: its 128 bytes, 16-byte chunks
-            // permuted by the 128-byte swizzle (chunk c sits at c ^ (row % 8))
-            const uint8_t *wrow = sW + rw.i * A_BYTES + crow * 128;
-            float ws[BK];
-#pragma unroll
-            for (int c = 0; c < BK / 4; c++) {
-                const float4 v = *reinterpret_cast<const float4 *>(wrow + ((c ^ (crow & 7)) << 4));
-                ws[4 * c + 0] = tf32_residual(v.x);
-                ws[4 * c + 1] = tf32_residual(v.y);
-                ws[4 * c + 2] = tf32_residual(v.z);
-                ws[4 * c + 3] = tf32_residual(v.w);
-            }
-            tmem_st32(ws_lane + WS_COL0 + (uint32_t)(rs.i * BK), ws);
-            tc_fence_before();
-            if (PAIR) mbar_arrive_cluster(mapa(smem_u32(&ready[rs.i]), 0));
-            else mbar_arrive(&ready[rs.i]);
-            rw.next(); rs.next(); rx.next(); rp.next();
+            if (!ok) set_abort(13);
         }
-        if (!ok) set_abort(13);
     } else {
         // ---------------- epilogue (warps 6..9) ----------------
         const int q = warp & 3;                   // TMEM lane quarter
@@ -389,20 +438,33 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
             float v[NTOK];
 #pragma unroll
             for (int j = 0; j < NTOK; j++) v[j] = 0.0f;
-            for (int kb = 0; kb < a.num_kb; kb++, n++) {
-                if (!wait_done(done, n, abort_flag)) { set_abort(14); ok = false; break; }
-                tc_fence_after();
-                const uint32_t taddr = lane_base + (uint32_t)((n % NSLOT) * SLOT_COLS);
-#pragma unroll
-                for (int c = 0; c < NTOK; c += 32) {
-                    float pb[32], ps[32];
-                    // W·X_big + W_small·X_big, and W·X_small
-                    tmem_ld32x2(taddr + c, taddr + NTOK + c, pb, ps);
-#pragma unroll
-                    for (int j = 0; j < 32; j++) v[c + j] = __fadd_rn(v[c + j], __fadd_rn(pb[j], ps[j]));
+            if constexpr (ONEPASS) {
+                const int slot = n & 1;           // n counts this CTA's tiles here
+                if (!mbar_wait(&accfull[slot], (uint32_t)((n >> 1) & 1), abort_flag)) {
+                    set_abort(14);
+                    break;
                 }
+                tc_fence_after();
+                tmem_ld64(lane_base + (uint32_t)(slot * NTOK), v);
                 tc_fence_before();
-                mbar_arrive(&pempty[n % NSLOT]);
+                mbar_arrive(&pempty[slot]);
+                n++;
+            } else {
+                for (int kb = 0; kb < a.num_kb; kb++, n++) {
+                    if (!wait_done(done, n, abort_flag)) { set_abort(14); ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t taddr = lane_base + (uint32_t)((n % NSLOT) * SLOT_COLS);
+#pragma unroll
+                    for (int c = 0; c < NTOK; c += 32) {
+                        float pb[32], ps[32];
+                        // W·X_big + W_small·X_big, and W·X_small
+                        tmem_ld32x2(taddr + c, taddr + NTOK + c, pb, ps);
+#pragma unroll
+                        for (int j = 0; j < 32; j++) v[c + j] = __fadd_rn(v[c + j], __fadd_rn(pb[j], ps[j]));
+                    }
+                    tc_fence_before();
+                    mbar_arrive(&pempty[n % NSLOT]);
+                }
             }
             if (!ok) break;
             if (UPGATE) {
@@ -421,8 +483,12 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                         if (j >= t.ntok) break;
                         const float h = swiglu_ref(v[j], ups[f * UPS_LD + j]);
                         const size_t o = (size_t)(t.row0 + j) * a.ldh + col;
-                        a.h_big[o] = h;
-                        a.h_small[o] = tf32_residual(h);
+                        if (ONEPASS) {
+                            a.h_big[o] = round_tf32(h);
+                        } else {
+                            a.h_big[o] = h;
+                            a.h_small[o] = tf32_residual(h);
+                        }
                     }
                     mbar_arrive(ups_free);
                 }
@@ -474,8 +540,12 @@ __global__ void split_tf32_kernel(const float4 *__restrict__ big, float4 *__rest
 }  // namespace dec
 
 cudaError_t dec_set_attributes() {
-    const void *fns[4] = {(const void *)dec::dec_gemm<true, false>, (const void *)dec::dec_gemm<false, false>,
-                          (const void *)dec::dec_gemm<true, true>, (const void *)dec::dec_gemm<false, true>};
+    const void *fns[6] = {(const void *)dec::dec_gemm<true, false, false>,
+                          (const void *)dec::dec_gemm<false, false, false>,
+                          (const void *)dec::dec_gemm<true, true, false>,
+                          (const void *)dec::dec_gemm<false, true, false>,
+                          (const void *)dec::dec_gemm<true, false, true>,
+                          (const void *)dec::dec_gemm<false, false, true>};
     for (const void *f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              dec::SMEM_BYTES);
@@ -498,7 +568,7 @@ int dec_max_pairs(int num_sms) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, dec::dec_gemm<true, true>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, dec::dec_gemm<true, true, false>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
@@ -521,9 +591,14 @@ static int dec_units(int rows_bound, int E, int NB, int cap) {
 
 template <bool UPGATE>
 static cudaError_t dec_launch(const DecMaps &m, const dec::DecArgs &a, int units, bool pair,
-                              cudaStream_t s) {
+                              bool onepass, cudaStream_t s) {
+    if (onepass) {
+        dec::dec_gemm<UPGATE, false, true><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
+            m.tmW, m.tmXb, m.tmXb, m.tmXb, a);
+        return cudaGetLastError();
+    }
     if (!pair) {
-        dec::dec_gemm<UPGATE, false><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
+        dec::dec_gemm<UPGATE, false, false><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
             m.tmW, m.tmXb, m.tmXs, m.tmXb, a);
         return cudaGetLastError();
     }
@@ -539,19 +614,20 @@ static cudaError_t dec_launch(const DecMaps &m, const dec::DecArgs &a, int units
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, dec::dec_gemm<UPGATE, true>, m.tmW, m.tmXb, m.tmXs, m.tmXb32, a);
+    return cudaLaunchKernelEx(&cfg, dec::dec_gemm<UPGATE, true, false>, m.tmW, m.tmXb, m.tmXs, m.tmXb32, a);
 }
 
 cudaError_t launch_dec_upgate(const DecMaps &m, int d_pad, int F_pad, float *h_big, float *h_small,
                               const int *plan, int E, int rows_bound, int num_sms, int max_pairs,
-                              DeviceStatus *status, cudaStream_t s)
+                              DeviceStatus *status, cudaStream_t s, bool onepass)
 {
-    const bool pair = max_pairs > 0;
+    const bool pair = max_pairs > 0 && !onepass;
     dec::DecArgs a{};
     a.plan = plan; a.E = E; a.num_kb = d_pad / dec::BK; a.ksplit = 1; a.NB = F_pad / (pair ? 128 : 64);
     a.w_rows_per_expert = 2 * F_pad; a.h_big = h_big; a.h_small = h_small; a.ldh = F_pad;
     a.status = status;
-    return dec_launch<true>(m, a, dec_units(rows_bound, E, a.NB, pair ? max_pairs : num_sms), pair, s);
+    return dec_launch<true>(m, a, dec_units(rows_bound, E, a.NB, pair ? max_pairs : num_sms), pair,
+                            onepass, s);
 }
 
 // K halves for the down GEMM (1 or 2): halves when its weight blocks would
@@ -564,9 +640,10 @@ int dec_down_ksplit(int F_pad, int d_pad, int rows_bound, int E, int num_sms) {
 
 cudaError_t launch_dec_down(const DecMaps &m, int F_pad, int d_pad, float *y, const int *plan,
                             int E, int rows_bound, int num_sms, int max_pairs, DeviceStatus *status,
-                            cudaStream_t s, float *const *y_ptrs, const int2 *ret, float *y2)
+                            cudaStream_t s, float *const *y_ptrs, const int2 *ret, float *y2,
+                            bool onepass)
 {
-    const bool pair = max_pairs > 0 && d_pad % (2 * dec::MW) == 0;
+    const bool pair = max_pairs > 0 && d_pad % (2 * dec::MW) == 0 && !onepass;
     const int kb = F_pad / dec::BK;
     if (y2 != nullptr && (kb % 2 != 0 || ret != nullptr)) return cudaErrorInvalidValue;
     dec::DecArgs a{};
@@ -577,7 +654,7 @@ cudaError_t launch_dec_down(const DecMaps &m, int F_pad, int d_pad, float *y, co
     a.status = status;
     return dec_launch<false>(m, a,
                              dec_units(rows_bound, E, a.NB * a.ksplit, pair ? max_pairs : num_sms),
-                             pair, s);
+                             pair, onepass, s);
 }
 
 }  // namespace moe

@@ -138,11 +138,12 @@ int dec_max_pairs(int num_sms);
 cudaError_t launch_split_tf32(float *big, float *small, size_t n, cudaStream_t s);
 cudaError_t launch_dec_upgate(const DecMaps &m, int d_pad, int F_pad, float *h_big, float *h_small,
                               const int *plan, int E, int rows_bound, int num_sms, int max_pairs,
-                              DeviceStatus *status, cudaStream_t s);
+                              DeviceStatus *status, cudaStream_t s, bool onepass = false);
 cudaError_t launch_dec_down(const DecMaps &m, int F_pad, int d_pad, float *y, const int *plan,
                             int E, int rows_bound, int num_sms, int max_pairs, DeviceStatus *status,
                             cudaStream_t s, float *const *y_ptrs = nullptr,
-                            const int2 *ret = nullptr, float *y2 = nullptr);
+                            const int2 *ret = nullptr, float *y2 = nullptr,
+                            bool onepass = false);
 // 2 when the down GEMM should run in two K halves (into y and a second
 // buffer y2, summed by the combine), else 1
 int dec_down_ksplit(int F_pad, int d_pad, int rows_bound, int E, int num_sms);

@@ -441,14 +441,19 @@ extern "C" int moe_b200_weights_download(const moe_b200_weights *w, float *W_rou
 // ---------------------------------------------------------------------
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 
+// Decode-sized expert groups (average below half a 128-row tile): the
+// expert GEMMs stream weights (dec_gemm) rather than fill token tiles.
+static bool decode_sized(const moe_b200_weights *w, int T) {
+    return (double)T * w->k / w->E < 64.0;
+}
+
 static int pick_path(const moe_b200_weights *w, int T, const moe_b200_opts *opts) {
     int path = opts ? opts->path : MOE_B200_PATH_AUTO;
     if (path == MOE_B200_PATH_AUTO) {
         // tensor-core tiles are 128 rows: use them once the average expert
         // group fills half a tile; smaller (decode-sized) groups stream the
         // weights through FP32 FFMA.
-        const double avg = (double)T * w->k / w->E;
-        path = avg >= 64.0 ? MOE_B200_PATH_TF32 : MOE_B200_PATH_TF32X3;
+        path = decode_sized(w, T) ? MOE_B200_PATH_TF32X3 : MOE_B200_PATH_TF32;
     }
     return path;
 }
@@ -544,7 +549,10 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
                        x_perm, path == MOE_B200_PATH_TF32, c->status, s));
     launches += 2;
     MARK(2);
-    if (path == MOE_B200_PATH_TF32) {
+    // TF32 on decode-sized groups: the weight-streaming kernel in its
+    // one-pass TF32 mode (same tolerance as the grouped GEMM)
+    const bool onepass = path == MOE_B200_PATH_TF32 && decode_sized(w, T);
+    if (path == MOE_B200_PATH_TF32 && !onepass) {
         TcGemm up, dn;
         const bool pair = opts && opts->cta_pair && c->tc2_pairs > 0;
         if ((rc = make_tmap(&up.tmA, x_perm, rows, w->d_pad, 128))) return rc;
@@ -568,31 +576,42 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
             CK(launch_tc_down(dn, w->F_pad, w->d_pad, w->down_bn, y, plan, E, rows, c->num_sms,
                               c->status, s));
         }
-    } else if (path == MOE_B200_PATH_TF32X3) {
-        if ((rc = grow(c->xs, (size_t)rows * w->d_pad * 4))) return rc;
-        if ((rc = grow(c->hs, (size_t)rows * w->F_pad * 4))) return rc;
-        float *xs = (float *)c->xs.p, *hs = (float *)c->hs.p;
+    } else if (path == MOE_B200_PATH_TF32X3 || onepass) {
+        float *xs = nullptr, *hs = nullptr;
+        if (!onepass) {
+            if ((rc = grow(c->xs, (size_t)rows * w->d_pad * 4))) return rc;
+            if ((rc = grow(c->hs, (size_t)rows * w->F_pad * 4))) return rc;
+            xs = (float *)c->xs.p;
+            hs = (float *)c->hs.p;
+        }
         DecMaps up, dn;
         up.tmW = w->tm_ug64;
         if ((rc = make_tmap(&up.tmXb, x_perm, rows, w->d_pad, 64))) return rc;
-        if ((rc = make_tmap(&up.tmXs, xs, rows, w->d_pad, 64))) return rc;
-        if ((rc = make_tmap(&up.tmXb32, x_perm, rows, w->d_pad, 32))) return rc;
         dn.tmW = w->tm_dn128;
         if ((rc = make_tmap(&dn.tmXb, h, rows, w->F_pad, 64))) return rc;
-        if ((rc = make_tmap(&dn.tmXs, hs, rows, w->F_pad, 64))) return rc;
-        if ((rc = make_tmap(&dn.tmXb32, h, rows, w->F_pad, 32))) return rc;
-        const int dpairs = (opts && opts->cta_pair) ? c->dec_pairs : 0;
+        if (onepass) {
+            up.tmXs = up.tmXb32 = up.tmXb;
+            dn.tmXs = dn.tmXb32 = dn.tmXb;
+        } else {
+            if ((rc = make_tmap(&up.tmXs, xs, rows, w->d_pad, 64))) return rc;
+            if ((rc = make_tmap(&up.tmXb32, x_perm, rows, w->d_pad, 32))) return rc;
+            if ((rc = make_tmap(&dn.tmXs, hs, rows, w->F_pad, 64))) return rc;
+            if ((rc = make_tmap(&dn.tmXb32, h, rows, w->F_pad, 32))) return rc;
+        }
+        const int dpairs = (opts && opts->cta_pair && !onepass) ? c->dec_pairs : 0;
         if (!dpairs && dec_down_ksplit(w->F_pad, w->d_pad, rows, E, c->num_sms) == 2) {
             if ((rc = grow(c->y2, (size_t)rows * w->d_pad * 4))) return rc;
             y2 = (float *)c->y2.p;
         }
-        CK(launch_split_tf32(x_perm, xs, (size_t)rows * w->d_pad, s));
+        if (!onepass) {
+            CK(launch_split_tf32(x_perm, xs, (size_t)rows * w->d_pad, s));
+            launches += 1;
+        }
         CK(launch_dec_upgate(up, w->d_pad, w->F_pad, h, hs, plan, E, rows, c->num_sms, dpairs,
-                             c->status, s));
+                             c->status, s, onepass));
         MARK(3);
         CK(launch_dec_down(dn, w->F_pad, w->d_pad, y, plan, E, rows, c->num_sms, dpairs,
-                           c->status, s, nullptr, nullptr, y2));
-        launches += 1;   // the split
+                           c->status, s, nullptr, nullptr, y2, onepass));
     } else if (path == MOE_B200_PATH_FP32) {
         CK(launch_ffma_upgate(x_perm, w->d_pad, w->ug, w->F_pad, h, plan, E, rows, s));
         MARK(3);
@@ -685,6 +704,11 @@ static int check_status(Ctx *c) {
 // (pinned buffers): configuration 3 (weights 13x the activations) 4.07 ms
 // in one chunk, 2.99 / 2.80 / 2.81 ms in 2 / 3 / 4; configuration 5 (45x)
 // 112.9 ms in one, 100.6 / 103.0 / 104.6 ms in 2 / 3 / 4.
+// tokens per chunk of a pipelined host call (the last chunk takes the rest)
+static int chunk_tokens(int T, int chunks) {
+    return (int)round_up(ceil_div(T, chunks), kRouterTile);
+}
+
 static int forward_chunks(const moe_b200_weights *w, int path, int T, size_t x_bytes, int want) {
     if (path != MOE_B200_PATH_TF32 && path != MOE_B200_PATH_FP32) return 1;
     if (x_bytes < ((size_t)64 << 20) || want == 1) return 1;
@@ -693,7 +717,14 @@ static int forward_chunks(const moe_b200_weights *w, int path, int T, size_t x_b
         const double weight_bytes = 3.0 * w->d * w->F * w->E * 4.0;
         want = weight_bytes > 24.0 * (double)x_bytes ? 2 : 3;
     }
-    return std::max(1, std::min(want, most));
+    int n = std::max(1, std::min(want, most));
+    // TF32 runs a different kernel on decode-sized groups: every chunk (the
+    // last is the smallest) must fall on the same side as the whole call,
+    // so that the result is bit-identical to one device call
+    if (path == MOE_B200_PATH_TF32)
+        while (n > 1 && decode_sized(w, T - (n - 1) * chunk_tokens(T, n)) != decode_sized(w, T))
+            n--;
+    return n;
 }
 
 static int ensure_pipeline(Ctx *c) {
@@ -727,7 +758,7 @@ static int forward_pipelined(Ctx *c, const moe_b200_weights *w, const float *d_b
     int rc = ensure_pipeline(c);
     if (rc) return rc;
     const int d = w->d, E = w->E, k = w->k;
-    const int Tc = round_up(ceil_div(T, chunks), kRouterTile);
+    const int Tc = chunk_tokens(T, chunks);
     float *io_x = (float *)c->io_x.p;
     float *io_out = block ? io_x : (float *)c->io_out.p;
     float *xn = block ? (float *)c->xn.p : nullptr;

@@ -141,9 +141,12 @@ __device__ __forceinline__ void router_tail(float *lg, int T, int E, int k, int 
         int sel[kMaxTopK];
         float wsel[kMaxTopK];
         route_token(lg + tid * (EB + 1), E, k, sel, wsel);
-        for (int r = 0; r < k; r++) {
-            sid[tid][r] = sel[r];
-            swt[tid][r] = wsel[r];
+#pragma unroll
+        for (int r = 0; r < kMaxTopK; r++) {
+            if (r < k) {
+                sid[tid][r] = sel[r];
+                swt[tid][r] = wsel[r];
+            }
         }
     }
     __syncthreads();
@@ -159,13 +162,21 @@ __device__ __forceinline__ void router_tail(float *lg, int T, int E, int k, int 
         ids[(size_t)t0 * k + q] = sid[r][c];
         wts[(size_t)t0 * k + q] = swt[r][c];
     }
-    // per-expert tile histogram and stable local ranks (token order)
-    for (int e = tid; e < E; e += 256) {
+    // per-expert tile histogram and stable local ranks (slot order: token,
+    // then rank): a warp per expert, 32 slots per ballot, ranks by prefix
+    // popcount
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nslot = nt * k;
+    for (int e = warp; e < E; e += 8) {
         int c = 0;
-        for (int r = 0; r < nt; r++)
-            for (int q = 0; q < k; q++)
-                if (sid[r][q] == e) loc[(size_t)(t0 + r) * k + q] = c++;
-        tile_cnt[(size_t)tile * E + e] = c;
+        for (int s0 = 0; s0 < nslot; s0 += 32) {
+            const int sl = s0 + lane;
+            const bool hit = sl < nslot && sid[sl / k][sl % k] == e;
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (hit) loc[(size_t)t0 * k + sl] = c + __popc(m & ((1u << lane) - 1u));
+            c += __popc(m);
+        }
+        if (lane == 0) tile_cnt[(size_t)tile * E + e] = c;
     }
 }
 
