@@ -10,10 +10,14 @@
 //   warp 1      TMEM allocator and MMA issuer: tcgen05.mma kind::tf32,
 //               M=128, N=BN, K=8, four per stage, accumulating in TMEM;
 //               tcgen05.commit frees the smem stage / publishes the tile
-//   warps 2..5  epilogue: tcgen05.ld 32x32b rows out of TMEM (two
+//   warps 2..9  epilogue: tcgen05.ld 32x32b rows out of TMEM (two
 //               accumulator buffers, so the epilogue of tile i overlaps
 //               the main loop of tile i+1), fused SwiGLU for up/gate,
-//               row-masked stores.
+//               row-masked stores.  Two warps per TMEM lane quarter, each
+//               on half of the tile's columns: the SwiGLU's dependent
+//               chains (exponential, IEEE division) are latency-bound, and
+//               with K short (d = 256..1024) the epilogue, not the MMAs,
+//               sets the pace, so two warps per scheduler halve it.
 // Tile order inside an expert is grouped by GM m-tiles so that the CTAs
 // running together share a few weight tiles and a few activation row
 // blocks in L2.
@@ -31,7 +35,8 @@ constexpr int BM = 128;
 constexpr int BK = 32;          // fp32 elements per K step = 128 bytes
 constexpr int STAGES = 4;
 constexpr int GM = 8;           // m-tiles per raster group
-constexpr int kThreads = 192;
+constexpr int EPI_WARPS = 8;   // two per TMEM lane quarter, each on half the columns
+constexpr int kThreads = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * BK * 4;
 constexpr int EPI_FLOATS = 32 * 33;   // per epilogue warp: 32×32 chunk, padded rows
 
@@ -80,8 +85,8 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                                                 ~static_cast<uintptr_t>(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + STAGES * A_BYTES;
-    float *sEpi = reinterpret_cast<float *>(sB + STAGES * B_BYTES);   // [4 warps][32][33]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + 4 * EPI_FLOATS);
+    float *sEpi = reinterpret_cast<float *>(sB + STAGES * B_BYTES);   // [EPI_WARPS][32][33]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sEpi + EPI_WARPS * EPI_FLOATS);
     uint64_t *full = bars;
     uint64_t *empty = bars + STAGES;
     uint64_t *tfull = bars + 2 * STAGES;
@@ -100,7 +105,7 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], 32 * EPI_WARPS);
         }
         mbar_init(fin, 1);
         *abort_flag = 0;
@@ -189,8 +194,10 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             mbar_wait(fin, 0, nullptr);
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue (warps 2..9) ----------------
         const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int ew = warp - 2;                // epilogue warp 0..7
+        const int half = ew >> 2;               // which half of the columns
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -209,7 +216,7 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             // through shared memory so that 8 lanes write one row's 128
             // bytes and a warp instruction covers 4 whole row segments
             // (full sectors locally, full-size packets over NVLink).
-            float *stage = sEpi + q * EPI_FLOATS;
+            float *stage = sEpi + ew * EPI_FLOATS;
             const int sub = lane >> 3, c4 = (lane & 7) * 4;
             float *rowdst[8];
 #pragma unroll
@@ -229,7 +236,7 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 }
             }
 #pragma unroll 1
-            for (int col = 0; col < NCOLS; col += 32) {
+            for (int col = half * (NCOLS / 2); col < (half + 1) * (NCOLS / 2); col += 32) {
                 float v[32];
                 if (SWIGLU) {
                     float u[32];
@@ -289,9 +296,11 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
 
 template <int BN>
 constexpr int smem_bytes() {
-    return STAGES * (A_BYTES + BN * BK * 4) + 4 * EPI_FLOATS * 4 + 1024 /*align slack*/ +
+    return STAGES * (A_BYTES + BN * BK * 4) + EPI_WARPS * EPI_FLOATS * 4 + 1024 /*align slack*/ +
            256 /*barriers*/;
 }
+
+static_assert(smem_bytes<256>() <= 227 * 1024, "shared memory per CTA");
 
 }  // namespace tc
 
