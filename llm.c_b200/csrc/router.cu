@@ -269,23 +269,40 @@ router_reduce_topk_kernel(const float *__restrict__ part, int nsplit, int T,
     __shared__ int sid[TT][kMaxTopK];
     __shared__ float swt[TT][kMaxTopK];
     const int tile = blockIdx.x, t0 = tile * TT;
-    for (int q = threadIdx.x; q < TT * E; q += 256) {
-        const int r = q / E, e = q % E, t = t0 + r;
-        if (t >= T) continue;
-        // splits summed in ascending order; their loads issued 8 at a time
-        const float *pp = part + (size_t)t * E + e;
-        const size_t stride = (size_t)T * E;
-        float v = 0.0f;
-        int sp = 0;
-        for (; sp + 8 <= nsplit; sp += 8) {
-            float a[8];
+    // Each thread owns VPT logits (q = tid + 256 i) and sums their splits in
+    // ascending order.  The loads of SB splits of all VPT logits are issued
+    // together (about 64 in flight per thread), so the L2 round trips
+    // overlap instead of running one logit after another.
+    constexpr int VPT = (TT * EB + 255) / 256;
+    constexpr int SB = VPT >= 32 ? 2 : (VPT >= 16 ? 4 : 8);
+    const size_t stride = (size_t)T * E;
+    int off[VPT];                                // logit index t·E + e, -1 if none
+    float v[VPT];
 #pragma unroll
-            for (int i = 0; i < 8; i++) a[i] = __ldg(pp + (size_t)(sp + i) * stride);
+    for (int i = 0; i < VPT; i++) {
+        const int q = threadIdx.x + 256 * i, r = q / E, e = q % E;
+        off[i] = (q < TT * E && t0 + r < T) ? (t0 + r) * E + e : -1;
+        v[i] = 0.0f;
+    }
+    for (int sp = 0; sp < nsplit; sp += SB) {
+        float a[VPT][SB];
 #pragma unroll
-            for (int i = 0; i < 8; i++) v = __fadd_rn(v, a[i]);
-        }
-        for (; sp < nsplit; sp++) v = __fadd_rn(v, __ldg(pp + (size_t)sp * stride));
-        lg[r * (EB + 1) + e] = bias ? __fadd_rn(v, __ldg(bias + e)) : v;
+        for (int i = 0; i < VPT; i++)
+#pragma unroll
+            for (int j = 0; j < SB; j++)
+                a[i][j] = (off[i] >= 0 && sp + j < nsplit)
+                              ? __ldg(part + (size_t)(sp + j) * stride + off[i]) : 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; i++)
+#pragma unroll
+            for (int j = 0; j < SB; j++)
+                if (sp + j < nsplit) v[i] = __fadd_rn(v[i], a[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; i++) {
+        if (off[i] < 0) continue;
+        const int q = threadIdx.x + 256 * i, r = q / E, e = q % E;
+        lg[r * (EB + 1) + e] = bias ? __fadd_rn(v[i], __ldg(bias + e)) : v[i];
     }
     __syncthreads();
     router_tail<EB>(lg, T, E, k, tile, probs, ids, wts, loc, tile_cnt, sid, swt);
