@@ -118,6 +118,7 @@ struct Ctx {
     cudaStream_t s_in = nullptr, s_out = nullptr;
     cudaEvent_t ev_in[kMaxChunks] = {}, ev_done[kMaxChunks] = {};
     DeviceStatus *status = nullptr;      // device
+    DeviceStatus *h_status = nullptr;    // pinned host copy, read back with each host call's results
     bool attrs_set = false;
     // workspace
     Buf probs, ids, wts, loc, tile_cnt, tile_pref, plan, pos_of, x_perm, h, y;
@@ -173,6 +174,7 @@ static int get_ctx(int device, Ctx **out) {
         CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
         CK(cudaMalloc(&c->status, sizeof(DeviceStatus)));
         CK(cudaMemset(c->status, 0, sizeof(DeviceStatus)));
+        CK(cudaHostAlloc(&c->h_status, sizeof(DeviceStatus), cudaHostAllocDefault));
         CK(tc_set_attributes());
         CK(dec_set_attributes());
         CK(tc2_set_attributes());
@@ -232,6 +234,7 @@ extern "C" void moe_b200_shutdown(void) {
                        &c->pmean, &c->io_dy, &c->io_dx, &c->io_aux, &c->wr_part};
         for (Buf *b : bufs) free_buf(*b);
         cudaFree(c->status);
+        if (c->h_status) cudaFreeHost(c->h_status);
         if (c->s_in) cudaStreamSynchronize(c->s_in), cudaStreamDestroy(c->s_in);
         if (c->s_out) cudaStreamSynchronize(c->s_out), cudaStreamDestroy(c->s_out);
         for (int k = 0; k < Ctx::kMaxChunks; k++) {
@@ -679,9 +682,13 @@ extern "C" int moe_b200_block_ffn_device(const moe_b200_weights *w, const float 
     return forward_on(c, w, d_bias, d_x, T, d_x, d_router_probs, d_expert_ids, opts, s, &bn);
 }
 
-static int check_status(Ctx *c) {
-    DeviceStatus st;
-    CK(cudaMemcpy(&st, c->status, sizeof st, cudaMemcpyDeviceToHost));
+// End of a synchronous host call on stream s: the status word comes back
+// on the stream with the results (one pinned async copy), so one stream
+// synchronisation covers both.
+static int sync_and_check(Ctx *c, cudaStream_t s) {
+    CK(cudaMemcpyAsync(c->h_status, c->status, sizeof(DeviceStatus), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    const DeviceStatus st = *c->h_status;
     if (st.timeout || st.bad_index) {
         CK(cudaMemset(c->status, 0, sizeof st));
         if (st.timeout)
@@ -802,8 +809,7 @@ static int forward_pipelined(Ctx *c, const moe_b200_weights *w, const float *d_b
     }
     c->last_launches = launches;
     CK(cudaStreamSynchronize(c->s_out));
-    CK(cudaStreamSynchronize(s));
-    return check_status(c);
+    return sync_and_check(c, s);
 }
 
 extern "C" int moe_b200_forward(const moe_b200_weights *w, const float *router_bias,
@@ -845,8 +851,7 @@ extern "C" int moe_b200_forward(const moe_b200_weights *w, const float *router_b
         CK(cudaMemcpyAsync(router_probs, c->probs.p, (size_t)T * w->E * 4, cudaMemcpyDeviceToHost, s));
     if (expert_ids)
         CK(cudaMemcpyAsync(expert_ids, c->ids.p, (size_t)T * w->k * 4, cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
-    return check_status(c);
+    return sync_and_check(c, s);
 }
 
 extern "C" int moe_b200_block_ffn(const moe_b200_weights *w, const float *rms_weight, float eps,
@@ -890,8 +895,7 @@ extern "C" int moe_b200_block_ffn(const moe_b200_weights *w, const float *rms_we
         CK(cudaMemcpyAsync(router_probs, c->probs.p, (size_t)T * w->E * 4, cudaMemcpyDeviceToHost, s));
     if (expert_ids)
         CK(cudaMemcpyAsync(expert_ids, c->ids.p, (size_t)T * w->k * 4, cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
-    return check_status(c);
+    return sync_and_check(c, s);
 }
 
 // ---------------------------------------------------------------------
@@ -1126,8 +1130,7 @@ extern "C" int moe_b200_backward(const moe_b200_weights *w, const float *router_
     if (rc) return rc;
     CK(cudaMemcpyAsync(dx, c->io_dx.p, xb, cudaMemcpyDeviceToHost, s));
     if (aux_loss) CK(cudaMemcpyAsync(aux_loss, c->io_aux.p, 4, cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
-    return check_status(c);
+    return sync_and_check(c, s);
 }
 
 extern "C" int moe_b200_last_counts(const moe_b200_weights *w, int *counts) {
