@@ -450,6 +450,20 @@ static bool decode_sized(const moe_b200_weights *w, int T) {
     return (double)T * w->k / w->E < 64.0;
 }
 
+// Column width of the TF32 down GEMM's tiles: 256 where the tiles fill the
+// SMs, else 128 (twice the tiles, so that small layers spread over more
+// SMs).  Sets the weight tensor map to match.  The width does not change
+// any output element's arithmetic, only which CTA computes it.
+static int down_tile_width(const Ctx *c, const moe_b200_weights *w, int rows, TcGemm *dn) {
+    const int tiles256 = (int)((ceil_div(rows, 128) + w->E) * (w->d_pad / 256));
+    if (w->down_bn == 256 && tiles256 < c->num_sms) {
+        dn->tmB = w->tm_dn128;
+        return 128;
+    }
+    dn->tmB = w->tm_dn;
+    return w->down_bn;
+}
+
 static int pick_path(const moe_b200_weights *w, int T, const moe_b200_opts *opts) {
     int path = opts ? opts->path : MOE_B200_PATH_AUTO;
     if (path == MOE_B200_PATH_AUTO) {
@@ -575,8 +589,8 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
             CK(launch_tc2_down(dn, w->F_pad, w->d_pad, y, plan, E, rows, c->tc2_pairs, c->status,
                                s));
         } else {
-            dn.tmB = w->tm_dn;
-            CK(launch_tc_down(dn, w->F_pad, w->d_pad, w->down_bn, y, plan, E, rows, c->num_sms,
+            const int bn = down_tile_width(c, w, rows, &dn);
+            CK(launch_tc_down(dn, w->F_pad, w->d_pad, bn, y, plan, E, rows, c->num_sms,
                               c->status, s));
         }
     } else if (path == MOE_B200_PATH_TF32X3 || onepass) {
@@ -1013,11 +1027,11 @@ static int backward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, c
         if ((rc = make_tmap(&up.tmA, x_perm, (int64_t)rows_buf, w->d_pad, 128))) return rc;
         if ((rc = make_tmap(&dn.tmA, h, (int64_t)rows_buf, w->F_pad, 128))) return rc;
         up.tmB = w->tm_ug;
-        dn.tmB = w->tm_dn;
+        const int bn = down_tile_width(c, w, (int)rows, &dn);
         CK(launch_tc_upgate(up, w->d_pad, w->F_pad, h, plan, E, (int)rows, c->num_sms, c->status,
                             s, gu));
         CK(launch_zero_pad_rows(h, w->F_pad, plan, E, s));
-        CK(launch_tc_down(dn, w->F_pad, w->d_pad, w->down_bn, y, plan, E, (int)rows, c->num_sms,
+        CK(launch_tc_down(dn, w->F_pad, w->d_pad, bn, y, plan, E, (int)rows, c->num_sms,
                           c->status, s, nullptr, nullptr));
         fwd_launches += 4;
     } else {
