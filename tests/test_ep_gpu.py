@@ -1,8 +1,12 @@
 """Multi-GPU test of the expert-parallel forward: 2 (or more) ranks, one
 process per GPU, each forwarding its share of the tokens.  Every row's
 arithmetic is independent of which rank computes it, so each rank's output
-must equal a single-GPU forward of the same tokens, bit for bit, on both
-expert paths.  Skipped when fewer than 2 GPUs are visible."""
+must equal a single-GPU forward of the same tokens, bit for bit, on every
+expert path, with one exception: TF32 on decode-sized expert groups runs
+the weight-streaming kernel's one-pass mode, whose single-GPU down GEMM
+adds two K halves while the expert-parallel one (rows written straight to
+their owners) does not split K; there the two agree to the TF32 tolerance.
+Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -58,7 +62,9 @@ def _worker(rank, world, port, q):
                 for rep in range(2):
                     out, probs, ids = ep.forward(xs, p.bias, path=path)
                     r_out, r_probs, r_ids = M.moe_forward(w, xs, p.bias, path=path)
+                    onepass = path == M.PATH_TF32 and T * k / E < 64
                     results.append(dict(rank=rank, case=(T, d, E), path=path, rep=rep,
+                                        tol=2e-3 if onepass else 1e-6,
                                         ids_equal=bool(np.array_equal(ids, r_ids)),
                                         probs_equal=bool(np.array_equal(probs, r_probs)),
                                         out_equal=bool(np.array_equal(out, r_out)),
@@ -102,4 +108,4 @@ def test_ep_matches_single_gpu():
                 assert r["slice_rows"] <= per + per // 4 + 256
             else:
                 assert r["ids_equal"] and r["probs_equal"], r
-                assert r["out_equal"] or r["rel_err"] < 1e-6, r
+                assert r["out_equal"] or r["rel_err"] < r["tol"], r
