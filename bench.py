@@ -168,7 +168,10 @@ def reference_sample(c, budget_s, threads):
     up = O._ptr_array(u)
     dp = O._ptr_array(dn)
 
+    keep = (g, u, dn)          # gp/up/dp hold raw pointers into these arrays
+
     def run(rows):
+        assert keep                # run() outlives this function: keep the weights alive
         xs = np.ascontiguousarray(x[rows])
         n = len(rows)
         out = np.empty((n, d), np.float32)
