@@ -229,10 +229,12 @@ def run_reference_arm(args, c):
 # ----------------------------------------------------------------------------
 # c2: the single-token decode step of a 6-layer llm.c model with MoE FFNs
 # ----------------------------------------------------------------------------
-def reference_decode_ms(dec, steps, threads):
+def reference_decode_ms(dec, steps, threads, prefill=()):
     """The reference's own pieces for one decode step on the same model:
     llm.c's inference_step (which leaves the MoE FFN out, src/inference.c:
-    342-343) plus, per MoE layer, llm.c's moe_forward on one token."""
+    342-343) plus, per MoE layer, llm.c's moe_forward on one token.
+    prefill: tokens run through the reference's inference_step first, untimed
+    (they fill its KV cache)."""
     sys.path.insert(0, str(REPO / "tests"))
     import oracle_lib as O
     import ctypes as C
@@ -241,6 +243,8 @@ def reference_decode_ms(dec, steps, threads):
     R.ref_inference_step.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
     m_ptr, s_ptr = C.addressof(dec.model), C.addressof(dec.state)
     c = dec.c
+    for t in prefill:
+        R.ref_inference_step(m_ptr, s_ptr, int(t))
     t0 = time.perf_counter()
     for i in range(steps):
         R.ref_inference_step(m_ptr, s_ptr, i % c.vocab)
@@ -272,7 +276,6 @@ def run_decode(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    M.init(0)
     # positions the host decoder state takes: the prefill, warm-up and timed
     # steps, the 5 steps of the MoE stage split, then the 5 steps of the
     # reference's own inference_step (the CPU baseline), which writes its KV
@@ -281,10 +284,11 @@ def run_decode(args):
     dec = LM.LlmcDecoder(cfg, seed=0)
     rng = np.random.default_rng(1)
     if args.impl == "reference":
+        # the reference alone, on the host: its inference_step fills the KV
+        # cache (untimed), then the timed steps
         threads = len(os.sched_getaffinity(0))
-        for t in rng.integers(0, cfg.vocab, DECODE_PREFILL):
-            dec.step(int(t))          # fill the KV cache (B200 path; not timed)
-        step_ms, moe_ms = reference_decode_ms(dec, max(args.steps, 3), threads)
+        step_ms, moe_ms = reference_decode_ms(dec, max(args.steps, 3), threads,
+                                              prefill=rng.integers(0, cfg.vocab, DECODE_PREFILL))
         value = 1000.0 / (step_ms + moe_ms)
         line = {"metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
                 "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
@@ -301,6 +305,7 @@ def run_decode(args):
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
+    M.init(0)
     prefill = rng.integers(0, cfg.vocab, DECODE_PREFILL)
     toks = rng.integers(0, cfg.vocab, args.warmup + args.steps)
 
