@@ -199,6 +199,17 @@ void moe_b200_llmc_block_ffn(llmc_Matrix *x, const llmc_BlockWeights *bw,
 void moe_backward(const llmc_Matrix *x, const llmc_MoEWeights *w, const llmc_ModelConfig *cfg,
                   const llmc_ForwardCache *cache, const llmc_Matrix *d_out, llmc_Matrix *d_x);
 
+/* Debug trace of the host inference_step above (not its device mode):
+ * while enabled, every step records each layer's pre-FFN normalised vector
+ * x_norm [d_model] and its FFN/MoE output [d_model] before the residual
+ * add; moe_b200_llmc_trace_read returns those of `layer` from the last step
+ * (MOE_B200_E_STATE before any).  Enabling clears the record.  No
+ * counterpart in llm.c: it exists so that each layer's MoE can be checked
+ * against the reference's moe_forward (src/transformer.c:287-366) on the
+ * same x_norm. */
+int moe_b200_llmc_trace_enable(int enable);
+int moe_b200_llmc_trace_read(int layer, float *x_norm, float *ffn_out);
+
 /* Drop the device copy of an expert set uploaded by moe_forward, given its
  * MoEWeights pointer, or the device decoder of inference_step's device mode,
  * given its Model pointer (no-op if none).  Returns MOE_B200_OK or a

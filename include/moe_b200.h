@@ -283,6 +283,13 @@ int moe_b200_decoder_set_pos(moe_b200_decoder *dec, int pos);
 int moe_b200_decoder_pos(const moe_b200_decoder *dec);
 /* Kernels in one step (the graph's launches). */
 int moe_b200_decoder_launches(const moe_b200_decoder *dec);
+/* Debug read-back of the last step's FFN half of `layer`: the pre-FFN
+ * normalised vector x_norm [d] (what the router and the experts read,
+ * src/inference.c:311) and the FFN/MoE branch output [d] before the
+ * residual add; either pointer may be NULL.  Synchronises the decoder.  For
+ * per-layer parity against the reference's moe_forward with T=1 on the same
+ * x_norm (src/transformer.c:287-366). */
+int moe_b200_decoder_trace(moe_b200_decoder *dec, int layer, float *x_norm, float *ffn_out);
 int moe_b200_decoder_destroy(moe_b200_decoder *dec);
 
 /* ---- llm.c checkpoints straight to the device ----------------------------

@@ -67,6 +67,7 @@ struct StepArgs {
     int *state, *ids;                  // state = {token, pos}
     unsigned *bar;                     // grid barrier counter (zeroed before each step)
     int *err;                          // barrier timeout flag
+    float *trace;                      // [L][2][d]: pre-FFN x_norm and FFN output per layer
 };
 
 struct Smem {
@@ -355,8 +356,10 @@ __device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int 
 // 4 (once per CTA before its up/gate items): RMSNorm into S.xn, router
 // logits and the reference's routing of the token into S.sel / S.w
 // (src/inference.c:311; src/transformer.c:299-337).  `publish` also stores
-// the ids and weights for the down stage.
-__device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, bool publish, Smem &S) {
+// the ids and weights for the down stage, and the normalised vector into
+// the layer's trace row.
+__device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, int layer, bool publish,
+                          Smem &S) {
     const Dims &D = A.D;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // the first 16 router weights of this lane's first expert, before the
@@ -368,6 +371,8 @@ __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, bool publish, 
         w0[u] = (warp < Lp.E && i < D.d) ? __ldg(Lp.router + (size_t)i * Lp.E + warp) : 0.0f;
     }
     rmsnorm_to_smem(A.x, Lp.rms_ffn, D, S);
+    if (publish)
+        for (int i = threadIdx.x; i < D.d; i += kThreads) A.trace[(size_t)layer * 2 * D.d + i] = S.xn[i];
     for (int e = warp; e < Lp.E; e += kThreads / 32) {
         float p = 0.0f;
         for (int i0 = lane; i0 < D.d; i0 += 32 * 16) {   // 16 loads in flight per lane
@@ -441,7 +446,7 @@ __device__ void upgate_item(const StepArgs &A, const LayerPtrs &Lp, int item, Sm
 // columns, so the k rows of a column load in parallel.
 __host__ __device__ inline int down_cols(int k) { return k >= kThreads / 32 ? 1 : (kThreads / 32) / k; }
 
-__device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int item, Smem &S) {
+__device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int item, Smem &S) {
     const Dims &D = A.D;
     const int cols = down_cols(Lp.k);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -477,6 +482,7 @@ __device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int item, Smem
             float out = 0.0f;
             for (int rr = 0; rr < Lp.k; rr++)
                 out = __fmaf_rn(ldcg(A.wts + rr), S.red[threadIdx.x * Lp.k + rr], out);
+            A.trace[((size_t)layer * 2 + 1) * D.d + jj] = out;
             A.x[jj] = __fadd_rn(ldcg(A.x + jj), out);
         }
     }
@@ -514,12 +520,12 @@ __global__ void __launch_bounds__(kThreads) oproj_kernel(StepArgs A, int layer) 
 __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     const LayerPtrs Lp = A.layers[layer];
-    route_cta(A, Lp, blockIdx.x == 0, S);
+    route_cta(A, Lp, layer, blockIdx.x == 0, S);
     upgate_item(A, Lp, blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) down_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
-    down_item(A, A.layers[layer], blockIdx.x, S);
+    down_item(A, A.layers[layer], layer, blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) lmhead_kernel(StepArgs A) {
     __shared__ Smem S;
@@ -571,12 +577,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs A) {
         if (!grid_barrier(A, ++phase * G, S)) return;
         const int n_ug = Lp.k * ((Lp.F + 7) / 8);
         if (b < n_ug) {
-            route_cta(A, Lp, b == 0, S);
+            route_cta(A, Lp, l, b == 0, S);
             for (int it = b; it < n_ug; it += G) upgate_item(A, Lp, it, S);
         }
         if (!grid_barrier(A, ++phase * G, S)) return;
         const int n_down = (D.d + down_cols(Lp.k) - 1) / down_cols(Lp.k);
-        for (int it = b; it < n_down; it += G) down_item(A, Lp, it, S);
+        for (int it = b; it < n_down; it += G) down_item(A, Lp, l, it, S);
         if (!grid_barrier(A, ++phase * G, S)) return;
     }
     const int n_lm = (D.vocab + 31) / 32;
@@ -613,6 +619,7 @@ struct moe_b200_decoder {
     int *state = nullptr, *ids = nullptr;        // state = {token, pos}
     unsigned *bar = nullptr;
     int *err = nullptr;
+    float *trace = nullptr;                      // [L][2][d], see StepArgs::trace
     int *h_token = nullptr;                      // pinned
     int maxF_pad = 0;
     cudaStream_t stream = nullptr;
@@ -649,7 +656,7 @@ void free_all(moe_b200_decoder *m) {
     cudaFree(m->rope_cos); cudaFree(m->rope_sin); cudaFree(m->kc); cudaFree(m->vc);
     cudaFree(m->x); cudaFree(m->q); cudaFree(m->part); cudaFree(m->h);
     cudaFree(m->logits); cudaFree(m->wts); cudaFree(m->state); cudaFree(m->ids);
-    cudaFree(m->bar); cudaFree(m->err);
+    cudaFree(m->bar); cudaFree(m->err); cudaFree(m->trace);
     if (m->h_token) cudaFreeHost(m->h_token);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -665,6 +672,7 @@ StepArgs step_args(const moe_b200_decoder *m) {
     A.kc = m->kc; A.vc = m->vc;
     A.x = m->x; A.q = m->q; A.part = m->part; A.h = m->h; A.logits = m->logits; A.wts = m->wts;
     A.state = m->state; A.ids = m->ids; A.bar = m->bar; A.err = m->err;
+    A.trace = m->trace;
     return A;
 }
 
@@ -792,6 +800,7 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
         cudaMalloc(&m->ids, kMaxTopK * 4) != cudaSuccess ||
         cudaMalloc(&m->state, 2 * 4) != cudaSuccess ||
         cudaMalloc(&m->bar, 4) != cudaSuccess || cudaMalloc(&m->err, 4) != cudaSuccess ||
+        cudaMalloc(&m->trace, (size_t)m->L * 2 * d * 4) != cudaSuccess ||
         cudaMallocHost(&m->h_token, 4) != cudaSuccess) {
         cudaGetLastError();
         return bail(dfail(MOE_B200_E_NOMEM, "decoder buffers do not fit"));
@@ -913,6 +922,22 @@ extern "C" int moe_b200_decoder_set_pos(moe_b200_decoder *m, int pos) {
 extern "C" int moe_b200_decoder_pos(const moe_b200_decoder *m) { return m ? m->pos : -1; }
 
 extern "C" int moe_b200_decoder_launches(const moe_b200_decoder *m) { return m ? m->launches : 0; }
+
+extern "C" int moe_b200_decoder_trace(moe_b200_decoder *m, int layer, float *x_norm,
+                                      float *ffn_out) {
+    if (!m) return dfail(MOE_B200_E_INVALID, "null decoder");
+    if (layer < 0 || layer >= m->L) return dfail(MOE_B200_E_INVALID, "layer out of range");
+    if (m->pos == 0) return dfail(MOE_B200_E_STATE, "no step taken yet");
+    DCK(cudaSetDevice(m->device));
+    DCK(cudaStreamSynchronize(m->stream));
+    const size_t d = (size_t)m->D.d;
+    if (x_norm)
+        DCK(cudaMemcpy(x_norm, m->trace + (size_t)layer * 2 * d, d * 4, cudaMemcpyDeviceToHost));
+    if (ffn_out)
+        DCK(cudaMemcpy(ffn_out, m->trace + ((size_t)layer * 2 + 1) * d, d * 4,
+                       cudaMemcpyDeviceToHost));
+    return MOE_B200_OK;
+}
 
 extern "C" int moe_b200_decoder_destroy(moe_b200_decoder *m) {
     if (!m) return MOE_B200_OK;

@@ -325,6 +325,44 @@ void softmax_vec(float *v, int n) {
 // The device keeps its own KV cache: s->kv_cache is not written; logits and
 // seq_pos are.  A rewound seq_pos rewinds the device cache; a seq_pos ahead
 // of it (steps taken on the host meanwhile) cannot be reconstructed.
+// Per-layer trace of the host step's FFN half (moe_b200_llmc_trace_*): the
+// pre-FFN x_norm and the FFN/MoE output of every layer of the last step.
+std::mutex g_trace_mu;
+bool g_trace_on = false;
+std::vector<float> g_trace;      // [L][2][d]
+int g_trace_d = 0, g_trace_L = 0;
+
+static void trace_layer(int L, int l, int d, const float *x_norm, const float *ffn_out) {
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    if (!g_trace_on) return;
+    if (g_trace_d != d || g_trace_L != L) {
+        g_trace.assign((size_t)L * 2 * d, 0.0f);
+        g_trace_d = d;
+        g_trace_L = L;
+    }
+    std::memcpy(g_trace.data() + (size_t)l * 2 * d, x_norm, (size_t)d * sizeof(float));
+    std::memcpy(g_trace.data() + ((size_t)l * 2 + 1) * d, ffn_out, (size_t)d * sizeof(float));
+}
+
+extern "C" int moe_b200_llmc_trace_enable(int enable) {
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    g_trace_on = enable != 0;
+    g_trace.clear();
+    g_trace_d = g_trace_L = 0;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_llmc_trace_read(int layer, float *x_norm, float *ffn_out) {
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    if (!g_trace_on || g_trace_L == 0) return MOE_B200_E_STATE;
+    if (layer < 0 || layer >= g_trace_L) return MOE_B200_E_INVALID;
+    const size_t d = (size_t)g_trace_d;
+    if (x_norm) std::memcpy(x_norm, g_trace.data() + (size_t)layer * 2 * d, d * sizeof(float));
+    if (ffn_out)
+        std::memcpy(ffn_out, g_trace.data() + ((size_t)layer * 2 + 1) * d, d * sizeof(float));
+    return MOE_B200_OK;
+}
+
 static bool device_mode() {
     const char *p = std::getenv("MOE_B200_DECODE");
     return p && !std::strcmp(p, "device");
@@ -411,12 +449,14 @@ extern "C" void inference_step(const llmc_Model *m, llmc_InferenceState *s, int 
             matvec(bw->ffn.W_up.data, s->x_norm, up, d, F);
             for (int i = 0; i < F; i++) h[i] = (gate[i] / (1.0f + std::exp(-gate[i]))) * up[i];
             matvec(bw->ffn.W_down.data, h, ffn_out, F, d);
+            trace_layer(cfg->n_layers, l, d, s->x_norm, ffn_out);
             for (int i = 0; i < d; i++) s->x[i] += ffn_out[i];
         } else {
             // the MoE branch the reference leaves out (src/inference.c:342-343)
             ffn_scratch.resize((size_t)d);
             float *ffn_out = ffn_scratch.data();
             run_moe(&bw->moe, F, s->x_norm, 1, d, ffn_out, nullptr, nullptr, "inference_step");
+            trace_layer(cfg->n_layers, l, d, s->x_norm, ffn_out);
             for (int i = 0; i < d; i++) s->x[i] += ffn_out[i];
         }
     }

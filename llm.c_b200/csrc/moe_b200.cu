@@ -469,7 +469,7 @@ static int pick_path(const moe_b200_weights *w, int T, const moe_b200_opts *opts
     if (path == MOE_B200_PATH_AUTO) {
         // tensor-core tiles are 128 rows: use them once the average expert
         // group fills half a tile; smaller (decode-sized) groups stream the
-        // weights through FP32 FFMA.
+        // weights through the 3xTF32 tensor-core kernel (FP32 accuracy).
         path = decode_sized(w, T) ? MOE_B200_PATH_TF32X3 : MOE_B200_PATH_TF32;
     }
     return path;

@@ -30,13 +30,19 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[MOE_B200_NOALLO
 
 namespace {
 
+constexpr int kMaxDevices = 64;
 std::mutex g_na_mu;
-unsigned char *g_na_ptr[64] = {nullptr};   // device address of the array, per device
+unsigned char *g_na_ptr[kMaxDevices] = {nullptr};   // device address of the array, per device
 
 // Set-up, once per device, with that device current.  On the host the
 // array's name is only a stand-in for the device symbol, so its device
-// address has to be fetched before any kernel can be given it.
+// address has to be fetched before any kernel can be given it.  The cached
+// address belongs to the device's current context: it does not survive a
+// cudaDeviceReset of that device (the library has to be reloaded then).
 int na_setup(int dev, unsigned char **ptr) {
+    if (dev < 0 || dev >= kMaxDevices)
+        return set_last_error(MOE_B200_E_INVALID,
+                              "moe_b200_forward_noalloc: device ordinal beyond 63");
     std::lock_guard<std::mutex> lk(g_na_mu);
     if (!g_na_ptr[dev]) {
         void *p = nullptr;
@@ -154,10 +160,12 @@ extern "C" int moe_b200_forward_noalloc(const moe_b200_weights *w, const float *
     if ((rc = na_cuda(launch_combine(sc.y, w->d, w->d_pad, T, w->k, sc.pos_of, sc.wts, d_out, s),
                       "combine launch")))
         return rc;
-    if ((rc = na_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize"))) return rc;
+    // the status word comes back on the caller's stream, then one wait
     DeviceStatus st;
-    if ((rc = na_cuda(cudaMemcpy(&st, sc.status, sizeof st, cudaMemcpyDeviceToHost), "cudaMemcpy")))
+    if ((rc = na_cuda(cudaMemcpyAsync(&st, sc.status, sizeof st, cudaMemcpyDeviceToHost, s),
+                      "cudaMemcpyAsync")))
         return rc;
+    if ((rc = na_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize"))) return rc;
     if (st.bad_index)
         return set_last_error(MOE_B200_E_CUDA, "device bounds check rejected an index");
     if (st.timeout) return set_last_error(MOE_B200_E_TIMEOUT, "device wait timed out");

@@ -104,6 +104,9 @@ def lib() -> C.CDLL:
     L.moe_b200_decoder_pos.argtypes = [_vp]
     L.moe_b200_decoder_launches.argtypes = [_vp]
     L.moe_b200_decoder_destroy.argtypes = [_vp]
+    L.moe_b200_decoder_trace.argtypes = [_vp, C.c_int, _fp, _fp]
+    L.moe_b200_llmc_trace_enable.argtypes = [C.c_int]
+    L.moe_b200_llmc_trace_read.argtypes = [C.c_int, _fp, _fp]
     _lib = L
     return L
 
@@ -610,6 +613,18 @@ class EP:
             self.handle = 0
 
 
+def llmc_trace_enable(on: bool = True):
+    """Record each layer's (x_norm, ffn_out) in the host inference_step."""
+    _check(lib().moe_b200_llmc_trace_enable(1 if on else 0), "moe_b200_llmc_trace_enable")
+
+
+def llmc_trace_read(layer: int, d: int):
+    xn = np.empty(d, np.float32)
+    fo = np.empty(d, np.float32)
+    _check(lib().moe_b200_llmc_trace_read(int(layer), _f(xn), _f(fo)), "moe_b200_llmc_trace_read")
+    return xn, fo
+
+
 def _path(path) -> bytes:
     return str(path).encode()
 
@@ -665,6 +680,15 @@ class Decoder:
     @property
     def launches(self) -> int:
         return int(lib().moe_b200_decoder_launches(self.handle))
+
+    def trace(self, layer: int, d: int):
+        """(x_norm, ffn_out) of `layer` in the last step: the pre-FFN
+        normalised vector and the FFN/MoE output before the residual add."""
+        xn = np.empty(d, np.float32)
+        fo = np.empty(d, np.float32)
+        _check(lib().moe_b200_decoder_trace(self.handle, int(layer), _f(xn), _f(fo)),
+               "moe_b200_decoder_trace")
+        return xn, fo
 
     def free(self):
         if self.handle:

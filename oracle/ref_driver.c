@@ -166,3 +166,37 @@ void ref_rms_norm(const float *x, int rows, int cols, const float *weight, float
     Matrix o = {out, NULL, rows, cols};
     rms_norm(&in, weight, eps, &o);
 }
+
+/* logits of positions [first, n) of model_forward over tokens[0..n)
+ * (rows = n - first, row-major into `out`) */
+void ref_model_forward_rows(void *mp, const int *tokens, int n, int first, float *out) {
+    Model *m = (Model *)mp;
+    int V = m->cfg.vocab_size;
+    Matrix lg = mat_alloc(n, V, 0);
+    model_forward(m, tokens, n, &lg);
+    memcpy(out, lg.data + (size_t)first * V, (size_t)(n - first) * V * sizeof(float));
+    mat_free(&lg);
+}
+
+/* the reference's moe_forward with block `layer`'s own MoE weights of a
+ * Model (src/transformer.c:287-366) on x [T×d]; probs / ids may be NULL */
+int ref_model_moe_forward(void *mp, int layer, const float *x, int T, float *out, float *probs,
+                          int *ids) {
+    Model *m = (Model *)mp;
+    if (layer < 0 || layer >= m->cfg.n_layers || !m->weights.blocks[layer].use_moe) return -1;
+    const MoEWeights *mw = &m->weights.blocks[layer].moe;
+    const int d = m->cfg.d_model, E = mw->n_experts, k = mw->top_k;
+    float *pb = probs ? probs : (float *)malloc((size_t)T * E * sizeof(float));
+    int *ib = ids ? ids : (int *)malloc((size_t)T * k * sizeof(int));
+    if (!pb || !ib) return -1;
+    ForwardCache cache;
+    memset(&cache, 0, sizeof cache);
+    cache.router_probs = pb;
+    cache.expert_ids = ib;
+    Matrix xm = { (float *)x, NULL, T, d };
+    Matrix om = { out, NULL, T, d };
+    moe_forward(&xm, mw, &m->cfg, &cache, &om);
+    if (!probs) free(pb);
+    if (!ids) free(ib);
+    return 0;
+}

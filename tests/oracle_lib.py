@@ -99,6 +99,10 @@ def ref():
         lib.ref_model_init.argtypes = [C.c_int] * 11 + [C.c_float, C.c_float, C.c_uint]
         lib.ref_model_free.argtypes = [C.c_void_p]
         lib.ref_model_forward_last.argtypes = [C.c_void_p, _ip, C.c_int, _fp]
+        lib.ref_model_forward_rows.argtypes = [C.c_void_p, _ip, C.c_int, C.c_int, _fp]
+        lib.ref_model_forward_rows.restype = None
+        lib.ref_model_moe_forward.argtypes = [C.c_void_p, C.c_int, _fp, C.c_int, _fp, _fp, _ip]
+        lib.ref_model_moe_forward.restype = C.c_int
         lib.ref_inference_init.restype = C.c_void_p
         lib.ref_inference_init.argtypes = [C.c_void_p]
         lib.ref_inference_free.argtypes = [C.c_void_p]

@@ -72,6 +72,46 @@ def test_noalloc_matches_device_entry_point_two_calls(moe):
     w.free()
 
 
+_FRESH_PROCESS = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
+import moe_b200 as M, oracle_lib as O
+M.init(0)
+p = O.MoEProblem(8, 384, 8, 2, 1536, seed=5)
+w = M.MoEWeights.upload(p.W_router, [e[0] for e in p.experts], [e[1] for e in p.experts],
+                        [e[2] for e in p.experts], p.k)
+x = torch.randn(400, 384, device="cuda")
+out = torch.empty_like(x)
+probs = torch.empty(400, 8, device="cuda")
+ids = torch.empty(400, 2, dtype=torch.int32, device="cuda")
+M.moe_forward_noalloc(w, x.data_ptr(), 40, out.data_ptr(), probs.data_ptr(), ids.data_ptr())
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info()[0]
+M.moe_forward_noalloc(w, x.data_ptr(), 400, out.data_ptr(), probs.data_ptr(), ids.data_ptr())
+torch.cuda.synchronize()
+free1 = torch.cuda.mem_get_info()[0]
+assert torch.isfinite(out).all()
+print("FREE", free0, free1)
+"""
+
+
+def test_noalloc_allocates_nothing_in_a_fresh_process():
+    """In a new process the library has no workspace yet, so a call that fell
+    back on it would have to allocate: 400 tokens need about 8 MB of
+    intermediates, beyond the driver's 2 MB allocation granularity.  After a
+    40-token warm-up (which loads the kernels), the device's free memory must
+    not move across the 400-token call."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    repo = Path(__file__).resolve().parent.parent
+    r = subprocess.run([sys.executable, "-c", _FRESH_PROCESS, str(repo / "llm.c_b200"),
+                        str(repo / "tests")], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    free0, free1 = (int(v) for v in r.stdout.split("FREE")[1].split())
+    assert free0 == free1, f"free device memory moved by {free0 - free1} bytes"
+
+
 def test_noalloc_rejects_oversized_call(moe):
     import torch
     w = M.MoEWeights.synth(3, 0.02, 1024, 4096, 8, 2)
