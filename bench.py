@@ -6,12 +6,19 @@
 
 A step is one forward of the MoE layer over the config's T tokens.  With N
 GPUs (torchrun) the layer runs expert-parallel: tokens are split across
-ranks, the global expert-sorted rows are split into N equal slices (weights
-replicated), token rows reach their slice owner and results return by
-direct NVLink peer stores, and NCCL carries the counts and two barriers;
-`value` is the whole job's tokens/s (T fixed: strong scaling) and the timing
-is the max over ranks.  Inputs are seeded synthetic tensors with
-the config's shapes and distributions (no dataset is involved).
+ranks; the experts are sharded (E/N base experts per rank plus spare slots
+that a load-aware rebalance fills with replicas of hot experts, copied over
+NVLink, before the timed region); token rows reach a rank holding their
+expert and results return by direct NVLink peer stores, and NCCL carries
+the counts and two barriers; `value` is the whole job's tokens/s (T fixed:
+strong scaling) and the timing is the max over ranks.  Inputs are seeded
+synthetic tensors with the config's shapes and distributions (no dataset is
+involved).
+
+The default line (c5) also carries sub-records measured in the same run on
+one GPU: the FP32-accuracy path on c5 (`fp32_path`), the decode-sized
+configuration c4 on AUTO (3xTF32, FP32 accuracy) and on TF32 (`decode`), and
+the c2 single-token decode step (`decode_c2`).
 
 Printed: one JSON line on rank 0 (see the keys in `main`).
 """
@@ -44,6 +51,7 @@ CONFIGS = {
 }
 W_STD = 0.02
 ZIPF_S = 1.1
+EP_SPARE_SLOTS = 4          # spare expert slots per rank for hot-expert replicas
 
 
 def flops_per_step(c):
@@ -383,8 +391,9 @@ def run_decode(args):
                    "n_heads": cfg.n_heads, "n_kv_heads": cfg.n_kv_heads, "d_ff": cfg.ffn,
                    "n_experts": cfg.n_experts, "top_k": cfg.top_k,
                    "kv_cached_tokens": DECODE_PREFILL, "batch": 1,
-                   "parallelism": "single GPU; the whole decode step on the device as one "
-                                  "persistent cooperative kernel (moe_b200_decoder)"},
+                   "parallelism": "single GPU; the whole decode step on the device: 31 stage "
+                                  "kernels replayed as one CUDA graph (moe_b200_decoder, the "
+                                  "default variant)"},
         "e2e": {"value": 1000.0 / e2e_ms, "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": 4, "d2h_bytes_per_step": cfg.vocab * 4,
                 "timing": "host wall clock around synchronous decoder steps (token up, logits "
@@ -574,6 +583,144 @@ def block_ffn_measure(args, M, w, x, bptr, host_bias_ptr, path, stream, stage_ms
     }
 
 
+def rank_experts(split, placement, rank):
+    """Experts whose rows `rank` computes under a split (M.ep_split)."""
+    n = 0
+    for e in range(placement.shape[1]):
+        if placement[rank, e] < 0:
+            continue
+        holders = list(split["holders"][e, :split["n_holders"][e]])
+        i = holders.index(rank)
+        n += int(split["row_begin"][e, i + 1] > split["row_begin"][e, i])
+    return n
+
+
+def _timed(step, stream, steps, warmup):
+    """Mean device ms of `step` over `steps` launches after `warmup`, CUDA
+    events on `stream`, synchronised on both sides."""
+    import torch
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    return ev0.elapsed_time(ev1) / steps
+
+
+def fp32_path_record(M, w, x, bptr, stream, c):
+    """c5 on the FP32-accuracy expert path (FP32 FFMA grouped GEMMs, 1e-5),
+    beside the TF32 headline: tokens/s and the FFMA rate of the layer."""
+    import torch
+    T, d, E, k, F = c["T"], c["d"], c["E"], c["k"], c["F"]
+    out = torch.empty((T, d), device="cuda")
+
+    def step():
+        M.moe_forward_device(w, x.data_ptr(), T, out.data_ptr(), bias_ptr=bptr, path=M.PATH_FP32,
+                             stream=stream.cuda_stream)
+
+    with ClockSampler(0) as clk:
+        ms = _timed(step, stream, steps=2, warmup=1)
+    props = torch.cuda.get_device_properties(0)
+    clocks = clk.summary()
+    mhz = clocks.get("sm_mhz") or 1965.0
+    ffma_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+    tflops = flops_per_step(c) / (ms / 1000.0) / 1e12
+    return {"tokens_per_s": T / (ms / 1000.0), "ms_per_step": ms, "dtype": "f32",
+            "path_run": "fp32 (FFMA grouped GEMMs)", "tolerance": 1e-5,
+            "achieved_tflops": tflops, "ffma_peak_tflops": ffma_peak,
+            "frac_of_ffma_peak": tflops / ffma_peak,
+            "peak_src": "nominal: SMs x 128 FP32 lanes x 2 x median SM clock under load",
+            "clocks": clocks}
+
+
+def decode_c4_record(M, stream):
+    """Configuration 4 (256 tokens, d 2048, E 32, top-4, d_ff 5632): a
+    decode-sized layer, weight-streaming and HBM-bound.  AUTO runs the 3xTF32
+    kernel (FP32 accuracy, 1e-5); TF32 its one-pass mode (2e-3).  Roofline:
+    the touched experts' gate and up weight bytes over the up/gate kernel's
+    device time, against the measured HBM copy bandwidth."""
+    import torch
+    c = CONFIGS["c4"]
+    T, d, E, k, F, seed = c["T"], c["d"], c["E"], c["k"], c["F"], c["seed"]
+    w = M.MoEWeights.synth(seed, W_STD, d, F, E, k)
+    x = torch.empty((T, d), device="cuda")
+    M.synth_fill(x.data_ptr(), T * d, seed, M.STREAM_X, 1.0, cuda_stream=stream.cuda_stream)
+    out = torch.empty((T, d), device="cuda")
+    peaks = measured_peaks()
+    rec = {"workload": "c4", "T": T, "d_model": d, "n_experts": E, "top_k": k, "d_ff": F}
+    for name, path, tol in (("auto", M.PATH_AUTO, 1e-5), ("tf32", M.PATH_TF32, 2e-3)):
+        def step():
+            M.moe_forward_device(w, x.data_ptr(), T, out.data_ptr(), path=path,
+                                 stream=stream.cuda_stream)
+        with ClockSampler(0) as clk:
+            ms = _timed(step, stream, steps=20, warmup=3)
+        path_run = M.last_path()
+        counts = M.last_counts(w)
+        M.profile_enable(True)
+        M.profile_read()
+        for _ in range(5):
+            step()
+        torch.cuda.synchronize()
+        M.profile_enable(False)
+        st, n = M.profile_read()
+        up_ms = st["upgate"] / max(n, 1)
+        touched = int(np.count_nonzero(counts))
+        gbs = 2.0 * d * F * 4 * touched / (up_ms / 1000.0) / 1e9
+        rec[name] = {"tokens_per_s": T / (ms / 1000.0), "ms_per_step": ms,
+                     "path_run": {M.PATH_TF32: "tf32 (one-pass weight streaming)",
+                                  M.PATH_TF32X3: "tf32x3 (FP32 accuracy)"}.get(path_run, "?"),
+                     "tolerance": tol,
+                     "roofline": {"bound": "hbm", "kernel": "dec_gemm<up/gate>",
+                                  "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                  "frac": gbs / peaks["hbm_gbs"],
+                                  "peak_src": peaks["src"] + " HBM copy bandwidth"},
+                     "stages_ms": {s_: v / max(n, 1) for s_, v in st.items()},
+                     "clocks": clk.summary()}
+    w.free()
+    return rec
+
+
+def decode_c2_record(M):
+    """Configuration 2: one token through the 6-layer MoE model with a
+    512-token KV cache, the whole step on the device (31 stage kernels in
+    one CUDA graph)."""
+    import llmc_model as LM
+    steps = 40
+    cfg = LM.DecodeConfig(max_seq=DECODE_PREFILL + steps + 8)
+    dec = LM.LlmcDecoder(cfg, seed=0)
+    rng = np.random.default_rng(1)
+    ddec = M.Decoder(C.addressof(dec.model), cfg.max_seq)
+    for t in rng.integers(0, cfg.vocab, DECODE_PREFILL):
+        ddec.step(int(t))
+    toks = rng.integers(0, cfg.vocab, steps)
+    with ClockSampler(0) as clk:
+        t0 = time.perf_counter()
+        for t in toks:
+            ddec.step(int(t))
+        ms = 1000.0 * (time.perf_counter() - t0) / steps
+    launches = ddec.launches
+    ddec.free()
+    nq, kv = cfg.n_heads * cfg.head_dim, cfg.n_kv_heads * cfg.head_dim
+    P = DECODE_PREFILL + steps / 2.0
+    step_bytes = 4.0 * (cfg.n_layers * (cfg.d * (nq + 2 * kv) + nq * cfg.d + 2 * cfg.d
+                                        + cfg.top_k * 3 * cfg.d * cfg.ffn
+                                        + cfg.d * cfg.n_experts + 2 * P * kv)
+                        + cfg.d * cfg.vocab + 2 * cfg.d)
+    peaks = measured_peaks()
+    gbs = step_bytes / (ms / 1000.0) / 1e9
+    return {"workload": "c2", "tokens_per_s": 1000.0 / ms, "ms_per_step": ms,
+            "kv_cached_tokens": DECODE_PREFILL, "launches_per_step": launches,
+            "timing": "host wall clock around synchronous decoder steps (token up)",
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": gbs / peaks["hbm_gbs"],
+                         "bytes_per_step": step_bytes},
+            "clocks": clk.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -585,6 +732,10 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=6.0,
                     help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="skip the fp32_path / decode / decode_c2 sub-records of the c5 line")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="override n_experts (small profiling cases of the expert GEMMs)")
     ap.add_argument("--backward", action="store_true",
                     help="time the MoE backward (moe_b200_backward_device) instead of the forward")
     ap.add_argument("--cta-pair", action="store_true",
@@ -601,6 +752,8 @@ def main():
         c["T"] = args.tokens
     if args.d_ff:
         c["F"] = args.d_ff
+    if args.experts:
+        c["E"] = args.experts
 
     if args.config == "c2":
         run_decode(args)
@@ -635,7 +788,15 @@ def main():
     if T % world:
         raise SystemExit(f"T={T} is not divisible by {world} ranks")
     Tl = T // world                      # this rank's tokens (strong scaling: T fixed)
-    w = M.MoEWeights.synth(seed, W_STD, d, F, E, k)   # every rank holds all experts
+    n_slots = E
+    if world > 1:
+        # this rank's shard: its E/world base experts plus spare slots for
+        # the replicas of hot experts that the rebalance places
+        mine = M.ep_shard_experts(E, world, rank)
+        n_slots = min(E, len(mine) + EP_SPARE_SLOTS)
+        w = M.MoEWeights.synth_shard(seed, W_STD, d, F, E, k, mine, n_slots)
+    else:
+        w = M.MoEWeights.synth(seed, W_STD, d, F, E, k)
     # a dedicated stream: the legacy default stream's handle is 0, which the
     # library reads as "use the library stream"
     stream = torch.cuda.Stream()
@@ -683,6 +844,14 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    placement = None
+    if ep is not None:
+        # load-aware replicas from the first forward's counts (set-up, like
+        # the weight upload; not timed)
+        step()
+        barrier()
+        ep.rebalance()
+        barrier()
     for _ in range(args.warmup):
         step()
     barrier()
@@ -691,9 +860,12 @@ def main():
     if ep is None:
         counts = M.last_counts(w)
         slice_rows = Tl * k
+        my_experts = int(np.count_nonzero(counts))
     else:
         counts_all, slice_rows = ep.counts()
         counts = counts_all.sum(axis=0)
+        placement = ep.placement()
+        my_experts = rank_experts(M.ep_split(counts_all, placement, n_slots), placement, rank)
 
     # ---- device-resident timed region (CUDA events on the launch stream,
     # barrier + synchronize on both sides, max over ranks)
@@ -769,9 +941,9 @@ def main():
     if tfile.exists() and world == 1:
         tj = json.loads(tfile.read_text())
         traffic = tj.get(args.config, {}).get("upgate_bytes_per_launch")
-    # gate and up weights of the experts this rank's rows touch (each read
-    # once); under expert parallelism a rank's slice covers about 1/world
-    w_bytes = 2.0 * d * F * 4 * touched / world
+    # gate and up weights of the experts this rank computes rows of (each
+    # read once)
+    w_bytes = 2.0 * d * F * 4 * my_experts
     up_flops = 4.0 * slice_rows * d * F
     # the TF32 grouped GEMM is tensor-bound when the expert groups are large
     # and weight-streaming (HBM-bound) when they are decode-sized
@@ -803,18 +975,22 @@ def main():
         a2a = 4.0 * d * (T * k / world) * (world - 1) / world
         t_roof += a2a / 770e9
 
+    dtype = {M.PATH_TF32: "tf32", M.PATH_FP32: "f32", M.PATH_TF32X3: "tf32x3"}.get(path_used, "?")
     line = {
         "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic",
-        "config": {"workload": args.config + ("-profile" if (args.tokens or args.d_ff) else ""),
+        "config": {"workload": args.config + ("-profile" if (args.tokens or args.d_ff or
+                                                             args.experts) else ""),
                    "T": T, "d_model": d, "n_experts": E, "top_k": k,
                    "d_ff": F, "router_bias": c["bias"], "path": args.path,
                    "path_run": {M.PATH_TF32: "tf32", M.PATH_FP32: "fp32",
                                 M.PATH_TF32X3: "tf32x3"}.get(path_used, "?"),
-                   "parallelism": f"ep{world}" + (" (balanced slices, replicated weights)"
-                                                  if world > 1 else ""),
+                   "parallelism": f"ep{world}" + (
+                       f" (experts sharded {E // world} per rank + up to "
+                       f"{n_slots - E // world} hot-expert replicas, rows split by cost)"
+                       if world > 1 else ""),
                    "l2": "inputs larger than L2"
                    if 4 * T * d > 126e6 else "inputs smaller than L2 (no flush)"},
         "e2e": {"value": T / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_step": e2e_ms,
@@ -830,18 +1006,34 @@ def main():
     }
     if block is not None:
         line["block_ffn"] = block
+    if placement is not None:
+        held = (placement >= 0).sum(axis=1)
+        line["expert_parallel"] = {
+            "slots_per_rank": n_slots, "experts_held_per_rank": held.tolist(),
+            "weights_gb_per_rank_max": float(held.max() * 3 * d * F * 4 / 1e9),
+            "replicas": int((placement >= 0).sum() - E),
+            "recv_rows_by_rank": [r["slice_rows"] for r in stages_by_rank] if stages_by_rank else None}
+    subrecords = world == 1 and rank == 0 and args.config == "c5" and not (args.tokens or args.d_ff) \
+        and not args.no_sub
+    if subrecords:
+        line["fp32_path"] = fp32_path_record(M, w, x, bptr, stream, c)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = len(os.sched_getaffinity(0))
         tps, S, kind, desc, _, _ = reference_sample(c, budget_s=12.0, threads=threads)
         line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": kind,
                                 "sample": desc}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
     if ep is not None:
         ep.destroy()
         dist.barrier()
         dist.destroy_process_group()
     w.free()
+    if subrecords:
+        del x, out, probs, ids
+        torch.cuda.empty_cache()
+        line["decode"] = decode_c4_record(M, stream)
+        line["decode_c2"] = decode_c2_record(M)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 if __name__ == "__main__":
     main()

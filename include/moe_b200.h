@@ -106,6 +106,29 @@ int moe_b200_weights_upload(const float *W_router,
 int moe_b200_weights_synth(uint64_t seed, float w_std, int d, int F, int E,
                            int top_k, moe_b200_weights **out);
 
+/* Expert-parallel shards (no counterpart in llm.c, whose MoEWeights always
+ * hold every expert, include/transformer.h:53-58): a set with n_slots packed
+ * expert slots of which the first n_local hold the experts listed in
+ * experts[0..n_local) (global ids, distinct); the remaining slots are spares
+ * that moe_b200_ep_rebalance may fill with replicas of hot experts.  The
+ * router always covers all E experts (every rank routes its own tokens).
+ * Only the moe_b200_ep_* calls run a shard; the single-GPU entry points
+ * reject it with MOE_B200_E_INVALID.
+ *   _synth_shard: the experts from the seeded generator (the same values
+ *                 moe_b200_weights_synth gives those experts);
+ *   _upload_shard: W_gate[i], W_up[i], W_down[i] are local expert i's host
+ *                 matrices (llm.c's layouts), i < n_local. */
+int moe_b200_weights_synth_shard(uint64_t seed, float w_std, int d, int F, int E, int top_k,
+                                 int n_local, const int *experts, int n_slots,
+                                 moe_b200_weights **out);
+int moe_b200_weights_upload_shard(const float *W_router, const float *const *W_gate,
+                                  const float *const *W_up, const float *const *W_down,
+                                  int d, int F, int E, int top_k, int n_local,
+                                  const int *experts, int n_slots, moe_b200_weights **out);
+/* Slot count of a set and the global expert id in each slot (-1 = empty
+ * spare); slot_expert has room for n_slots ints (either may be NULL). */
+int moe_b200_weights_slots(const moe_b200_weights *w, int *n_slots, int *slot_expert);
+
 /* Free a weight set (synchronises the device). */
 int moe_b200_weights_free(moe_b200_weights *w);
 
@@ -311,14 +334,17 @@ int moe_b200_decoder_load(const char *path, int max_seq, int flags, moe_b200_dec
 /* llm.c has no multi-GPU path (README.md:379 lists it as a roadmap item);
  * these entry points extend moe_forward to G GPUs of one node.
  *
- * Every rank holds the full expert set (replicated weights) and routes its
- * own tokens.  The rows of all ranks, in global expert-sorted order, are
- * split into G equal contiguous slices and rank q computes the expert
- * products of slice q, so the load stays balanced however skewed expert
- * popularity is.  Token rows and result rows move by direct peer stores
- * over NVLink (CUDA IPC); NCCL carries only per-expert counts and two
- * barriers.  All calls except moe_b200_ep_unique_id are collective: every
- * rank makes them, in the same order. */
+ * Experts are sharded: each rank passes its shard (moe_b200_weights_*_shard:
+ * its base experts plus spare slots; a full set also works and then every
+ * rank holds every expert).  Every rank routes its own tokens.  The rows of
+ * an expert, over all source ranks, are split among the ranks that hold it
+ * so that the estimated GEMM cost per rank is as even as the placement
+ * allows; moe_b200_ep_rebalance adds replicas of hot experts in spare slots
+ * from the last forward's per-expert counts.  Token rows and result rows
+ * move by direct peer stores over NVLink (CUDA IPC); NCCL carries only
+ * per-expert counts and two barriers.  All calls except
+ * moe_b200_ep_unique_id, moe_b200_ep_split and moe_b200_ep_place are
+ * collective: every rank makes them, in the same order. */
 #define MOE_B200_EP_ID_BYTES 128
 typedef struct moe_b200_ep moe_b200_ep;
 
@@ -327,40 +353,76 @@ typedef struct moe_b200_ep moe_b200_ep;
 int moe_b200_ep_unique_id(void *id);
 
 /* Join the group: rank in [0, world), at most max_tokens_per_rank tokens per
- * forward on each rank (the same value on every rank), weights `w` (all E
- * experts) on this rank's device. */
+ * forward on each rank (the same value on every rank), this rank's expert
+ * set `w` (a shard or a full set; every rank the same slot count, and every
+ * expert held by some rank).  The group fills w's spare slots on rebalance.
+ * Receive buffers are sized for world·max_tokens_per_rank·top_k rows, so no
+ * routing can overflow them.  The environment variable
+ * MOE_B200_EP_TIMEOUT_MS sets the host watchdog (moe_b200_ep_set_timeout). */
 int moe_b200_ep_create(const void *id, int rank, int world, int max_tokens_per_rank,
-                       const moe_b200_weights *w, moe_b200_ep **out);
+                       moe_b200_weights *w, moe_b200_ep **out);
 
 /* Leave the group and free its buffers (collective). */
 int moe_b200_ep_destroy(moe_b200_ep *ep);
 
 /* Forward of this rank's T tokens (device buffers, asynchronous on
  * `stream`, NULL = the group's stream); same outputs as
- * moe_b200_forward_device for these tokens. */
+ * moe_b200_forward_device for these tokens.  AUTO resolves the arithmetic
+ * path from the group's capacity (max_tokens_per_rank · world), the same on
+ * every rank. */
 int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, const float *d_x, int T,
                                float *d_out, float *d_router_probs, int *d_expert_ids,
                                const moe_b200_opts *opts, void *stream);
 
-/* Same with host buffers, synchronous (H2D of x, D2H of the outputs). */
+/* Same with host buffers, synchronous (H2D of x, D2H of the outputs).  With
+ * a watchdog set, a step that does not finish in time (a rank that stopped
+ * joining the collectives) aborts the communicator and returns
+ * MOE_B200_E_TIMEOUT; the group must then be destroyed. */
 int moe_b200_ep_forward(moe_b200_ep *ep, const float *router_bias, const float *x, int T,
                         float *out, float *router_probs, int *expert_ids,
                         const moe_b200_opts *opts);
 
 /* Per-rank, per-expert counts of the last forward ([world × E]) and the
- * number of rows this rank's slice held; synchronises the device. */
-int moe_b200_ep_counts(moe_b200_ep *ep, int *counts_all, int *slice_rows);
+ * number of rows this rank received; synchronises the device. */
+int moe_b200_ep_counts(moe_b200_ep *ep, int *counts_all, int *recv_rows);
 
-/* The partition every rank derives from counts_all [world × E]: slices of
- * the global expert-sorted rows balanced on estimated GEMM cost (2 units per
- * 128-row tile of an expert in the slice, 1 per expert segment), cut at
- * 128-row tile boundaries; equal rows instead if a slice would exceed
- * `capacity` rows (0 = no limit).  Outputs: rows of expert e in `rank`'s
- * slice (cnt_rank[E]), global position of `rank`'s first row of each expert
- * (base_rank[E]), and the slice's start and size.  Host computation. */
-int moe_b200_ep_partition(const int *counts_all, int world, int E, int rank, long long capacity,
-                          int *cnt_rank, int *base_rank, long long *slice_start,
-                          long long *slice_rows);
+/* The current placement [world × E]: slot of expert e on rank q, or -1. */
+int moe_b200_ep_placement(const moe_b200_ep *ep, int *place);
+
+/* Collective: from the last forward's counts, every rank computes the same
+ * load-aware placement (moe_b200_ep_place from the base experts) and copies
+ * the weights of its new replicas from the expert's base holder over NVLink
+ * into its spare slots.  Call between forwards, not during one. */
+int moe_b200_ep_rebalance(moe_b200_ep *ep);
+
+/* Host watchdog of the host-buffer forward and of rebalance, in ms (0 = wait
+ * without limit, the default unless MOE_B200_EP_TIMEOUT_MS is set). */
+int moe_b200_ep_set_timeout(moe_b200_ep *ep, int timeout_ms);
+
+/* The split every rank derives each forward from counts_all [world × E] and
+ * place [world × E] (slot of e on rank q, -1 = not held; slots < n_slots):
+ * single-holder experts go whole to their holder; replicated experts, most
+ * rows first, are cut into 128-row tiles, each to the holder whose estimated
+ * cost after taking it is lowest (2 units per tile, 1 more for the first
+ * tile of a segment), and every holder takes its tiles as one contiguous
+ * range in ascending rank order.  Outputs: n_holders[E], holders[E × world]
+ * (ranks, ascending), row_begin[E × (world+1)] (holder i's first row in
+ * the expert's global order: source rank, then local order),
+ * recv_offset[E × world] (where holder i's range starts in its receive
+ * buffer, slots in slot order), and, if not NULL, recv_rows[world] and
+ * cost[world].  Host computation. */
+int moe_b200_ep_split(const int *counts_all, int world, int E, const int *place, int n_slots,
+                      int *n_holders, int *holders, int *row_begin, int *recv_offset,
+                      long long *recv_rows, long long *cost);
+
+/* The placement moe_b200_ep_rebalance adopts: from base_place (every rank's
+ * base experts), repeatedly take the rank with the highest estimated cost
+ * and its experts by the rows it carries, and place a replica on the least
+ * loaded rank with a free slot that does not hold that expert yet, keeping
+ * the first such move that lowers the highest cost; stop when none does.
+ * Host computation, deterministic. */
+int moe_b200_ep_place(const int *counts_all, int world, int E, const int *base_place,
+                      int n_slots, int *place);
 
 /* ---- stage timing ------------------------------------------------------ */
 
@@ -380,6 +442,25 @@ int moe_b200_profile_enable(int enable);
  * and the number of forwards timed since the last read; resets both.
  * Synchronises the timed streams. */
 int moe_b200_profile_read(double *stage_ms, int *n_forwards);
+
+/* ---- failure detection without a GPU fault ------------------------------
+ * Test hooks; no counterpart in llm.c, which aborts on any failure
+ * (src/transformer.c:28-32).  Neither faults, traps or hangs the GPU. */
+
+/* Make the n-th device allocation the library makes from now on (weights,
+ * workspace growth, expert-parallel buffers) fail as if the device were out
+ * of memory; the call reports MOE_B200_E_NOMEM and the library stays
+ * usable.  n = 0 turns the hook off. */
+int moe_b200_debug_fail_alloc(int n);
+
+/* One CTA waits on an mbarrier with the library's bounded-wait helper (the
+ * one every tensor-core kernel uses) for at most limit_us microseconds
+ * (<= 2 s), with nothing else in flight.  arrive = 1: the CTA arrives
+ * first, the wait succeeds, MOE_B200_OK.  arrive = 0: nobody arrives, the
+ * wait gives up, the kernel records its site in the status word and
+ * returns, and the call reports MOE_B200_E_TIMEOUT; the device stays
+ * usable. */
+int moe_b200_debug_wait_probe(int limit_us, int arrive);
 
 /* ---- synthetic inputs (benchmark plumbing) ----------------------------- */
 

@@ -1,28 +1,39 @@
 // ep.cu — expert-parallel MoE forward over NVLink (one process per GPU).
 //
-// Load balance by work, not by expert: every rank holds the full expert
-// set (replicated weights; c5's 45 GB fits a B200), routes its own tokens,
-// and all ranks derive the same partition of the GLOBAL expert-sorted row
-// order into G equal contiguous slices.  Rank q computes the expert GEMMs of
-// slice q.  The global order is expert-major, then source rank, then the
-// source's stable local order, so:
-//   * the rows a rank sends to one slice owner form one contiguous run of
-//     its local expert-sorted order;
-//   * the owner's slice is already grouped by expert, with the same plan
-//     format the single-GPU grouped GEMMs read.
+// Experts are sharded: each rank holds a shard of the expert set (for c5,
+// 8 of 64 experts per GPU at 8 GPUs) in n_slots packed slots, the first of
+// them its base experts, the rest spares.  Under skewed popularity (c5's
+// Zipf(1.1) sends ~30 % of all rows to one expert) no static sharding can
+// balance the work, so moe_b200_ep_rebalance places replicas of hot experts
+// in spare slots, load-aware, from the per-expert counts of the last forward
+// (every rank computes the same placement), and copies their weights from
+// the base holder's memory over NVLink.  Every forward then splits each
+// replicated expert's rows among its holders so the estimated GEMM cost per
+// rank is as even as the placement allows.  Every rank routes its own
+// tokens (the router covers all experts).
 //
-// Data movement is fused into the kernels and uses no NCCL data
-// collectives.  The dispatch gather stores each token row straight into
-// the slice owner's receive buffer (CUDA IPC peer mapping, NVLink stores),
-// with a return address (source rank, source row).  The down GEMM's
-// epilogue stores each result row straight back into the token owner's
-// output buffer.  NCCL carries only the per-expert counts (E ints per rank)
-// and two stream-ordered barriers, so a forward never waits on the host.
-// No TMA ever reads peer memory; every CTA loads only its own tiles.
+// Row order.  The rows of expert e, over all source ranks, are numbered in
+// the global order (source rank, then the source's stable local order).
+// Holder i of e (holders in ascending rank order) receives the contiguous
+// range [beg_e[i], beg_e[i+1]) of that order, so
+//   * the rows a source sends to one holder of e are one contiguous run of
+//     its local expert-sorted order;
+//   * a holder's receive buffer is grouped by slot with the same plan format
+//     (cnt | off | mt128 | mt64 | mt256 over slots) the single-GPU grouped
+//     GEMMs read, with the shard's packed slots as their weights.
+//
+// Data movement is fused into the kernels; NCCL carries no rows.  The
+// dispatch gather stores each token row straight into the holder's receive
+// buffer (CUDA IPC peer mapping, NVLink stores), with a return address
+// (source rank, source row).  The down GEMM's epilogue stores each result
+// row straight back into the token owner's output buffer.  NCCL carries the
+// per-expert counts (E ints per rank) and two stream-ordered barriers, so a
+// forward never waits on the host.  No TMA ever reads peer memory; the
+// replica copy of the rebalance is a plain-load kernel.
 //
 // Stream order per forward on rank r (every rank issues the same NCCL
 // calls in the same order):
-//   router -> scan -> allgather(counts) -> partition -> gather(peer stores)
+//   router -> scan -> allgather(counts) -> plan -> gather(peer stores)
 //   -> barrier -> up/gate -> down(peer stores) -> barrier -> combine
 #include "../../include/moe_b200.h"
 #include "kernels.cuh"
@@ -30,137 +41,288 @@
 
 #include "nccl_dyn.cuh"
 
+#include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 using namespace moe;
 
+namespace {
+constexpr int kMaxWorld = 64;
+constexpr int kTileRows = 128;
+
+// Estimated GEMM cost of an expert segment of n rows on one rank: 2 units
+// per 128-row m-tile, plus 1 for the segment (its partially filled last
+// tile and its own pass over the expert's weights).
+__host__ __device__ inline long long seg_cost(long long n) {
+    return n > 0 ? 2 * ((n + kTileRows - 1) / kTileRows) + 1 : 0;
+}
+}  // namespace
+
 // ---------------------------------------------------------------------
-// partition (host copy: tests and diagnostics; device copy: the forward)
+// The split of every expert's rows among its holders (host copy: tests,
+// placement; device copy: every forward).  Integer arithmetic only, so
+// every rank and the host derive the same result.
 //
-// Slices are balanced on estimated cost, not on rows: the grouped GEMMs
-// spend per 128-row m-tile, and each expert segment of a slice adds about
-// half an m-tile more (its partially filled last tile and its own pass over
-// the expert's weights).  So an expert with n rows costs 2·ceil(n/128) + 1
-// units, and slice boundaries fall on m-tile boundaries inside experts.  A
-// slice may then hold somewhat more rows than T·k/G; if any slice would
-// exceed the receive capacity, the partition falls back to equal rows.
-// Integer arithmetic throughout, so every rank (and the host copy) derives
-// the same boundaries.
+//   C[q*ldc + e]    rows of expert e on source rank q (all-gathered counts)
+//   place[q*E + e]  slot of expert e on rank q, or -1
+// Outputs (caller arrays):
+//   nh[e]                 number of holders of e
+//   hold[e*G + i]         rank of holder i (ascending)
+//   beg[e*(G+1) + i]      first row (in e's global order) of holder i;
+//                         beg[e*(G+1) + nh[e]] = rows of e
+//   dst[e*G + i]          offset of that range in holder i's receive buffer
+//   rows_q[q], load[q]    receive rows and estimated cost per rank (or null)
+// Single-holder experts go whole to their holder.  Replicated experts, the
+// most rows first, are cut into 128-row tiles, each given to the holder
+// whose cost after taking it is lowest (ties: lower rank), then every
+// holder takes its count of tiles as one contiguous range in holder order.
+// Returns 1 if an expert with rows has no holder, else 0.
 // ---------------------------------------------------------------------
-__host__ __device__ inline void ep_slices(const int *C, int G, int E, long long capacity,
-                                          long long *S /* G+1 */) {
-    long long M = 0, U = 0;
+__host__ __device__ inline int ep_split(const int *C, int ldc, int G, int E, const int *place,
+                                        int S, int *nh, int *hold, int *beg, int *dst,
+                                        long long *rows_q, long long *load_out) {
+    int tot[kMaxExperts];
+    long long load[kMaxWorld];
+    int tiles_of[kMaxWorld];
+    int bad = 0;
+    for (int q = 0; q < G; q++) load[q] = 0;
     for (int e = 0; e < E; e++) {
-        long long tot = 0;
-        for (int r = 0; r < G; r++) tot += C[r * E + e];
-        M += tot;
-        U += 2 * ((tot + 127) / 128) + (tot > 0 ? 1 : 0);
-    }
-    S[0] = 0;
-    int q = 1;
-    long long cum = 0, goff = 0;
-    for (int e = 0; e < E && q < G; e++) {
-        long long tot = 0;
-        for (int r = 0; r < G; r++) tot += C[r * E + e];
-        const long long tiles = (tot + 127) / 128;
-        const long long units = 2 * tiles + (tot > 0 ? 1 : 0);
-        // boundary q sits at cost q·U/G; place it inside this expert when the
-        // expert's cost range reaches it
-        while (q < G && (long long)q * U <= (long long)G * (cum + units)) {
-            const long long num = (long long)q * U - (long long)G * (cum + 1);   // 2t·G ≈ num
-            long long t = num <= 0 ? 0 : (num + G) / (2LL * G);
-            if (t > tiles) t = tiles;
-            const long long rows = 128 * t < tot ? 128 * t : tot;
-            S[q] = goff + rows;
-            q++;
+        int t = 0, n = 0;
+        for (int q = 0; q < G; q++) {
+            t += C[q * ldc + e];
+            if (place[q * E + e] >= 0) hold[e * G + n++] = q;
         }
-        cum += units;
-        goff += tot;
+        tot[e] = t;
+        nh[e] = n;
+        for (int i = 0; i <= G; i++) beg[e * (G + 1) + i] = t;
+        beg[e * (G + 1)] = 0;
+        if (n == 0 && t > 0) bad = 1;
+        if (n == 1) load[hold[e * G]] += seg_cost(t);
     }
-    for (; q < G; q++) S[q] = M;
-    S[G] = M;
-    bool fits = true;
-    for (q = 1; q <= G; q++) {
-        if (S[q] < S[q - 1]) S[q] = S[q - 1];
-        if (capacity > 0 && S[q] - S[q - 1] > capacity) fits = false;
+    // replicated experts, the most rows first (ties: lower expert id)
+    unsigned char done[kMaxExperts];
+    for (int e = 0; e < E; e++) done[e] = (unsigned char)(nh[e] <= 1);
+    while (true) {
+        int e = -1;
+        for (int c = 0; c < E; c++)
+            if (!done[c] && (e < 0 || tot[c] > tot[e])) e = c;
+        if (e < 0) break;
+        done[e] = 1;
+        const int n = nh[e];
+        for (int i = 0; i < n; i++) tiles_of[i] = 0;
+        const int tiles = (tot[e] + kTileRows - 1) / kTileRows;
+        for (int t = 0; t < tiles; t++) {
+            int best = 0;
+            long long best_c = 0;
+            for (int i = 0; i < n; i++) {
+                const long long c = load[hold[e * G + i]] + 2 + (tiles_of[i] == 0 ? 1 : 0);
+                if (i == 0 || c < best_c) { best = i; best_c = c; }
+            }
+            load[hold[e * G + best]] = best_c;
+            tiles_of[best]++;
+        }
+        int b = 0;
+        for (int i = 0; i < n; i++) {
+            beg[e * (G + 1) + i] = b;
+            const long long nb = (long long)b + (long long)kTileRows * tiles_of[i];
+            b = nb < tot[e] ? (int)nb : tot[e];
+        }
+        for (int i = n; i <= G; i++) beg[e * (G + 1) + i] = tot[e];
     }
-    if (!fits) {                               // equal rows always fit
-        const long long chunk = M > 0 ? (M + G - 1) / G : 1;
-        for (q = 0; q <= G; q++) S[q] = (long long)q * chunk < M ? (long long)q * chunk : M;
+    // receive layout of every rank: its slots in slot order
+    int slot_rows[kMaxExperts];
+    for (int q = 0; q < G; q++) {
+        for (int j = 0; j < S; j++) slot_rows[j] = 0;
+        for (int e = 0; e < E; e++) {
+            const int j = place[q * E + e];
+            if (j < 0) continue;
+            int i = 0;
+            while (hold[e * G + i] != q) i++;
+            slot_rows[j] = beg[e * (G + 1) + i + 1] - beg[e * (G + 1) + i];
+        }
+        long long off = 0;
+        for (int j = 0; j < S; j++) {
+            const long long r = slot_rows[j];
+            slot_rows[j] = (int)off;            // now the slot's offset
+            off += r;
+        }
+        if (rows_q) rows_q[q] = off;
+        for (int e = 0; e < E; e++) {
+            const int j = place[q * E + e];
+            if (j < 0) continue;
+            int i = 0;
+            while (hold[e * G + i] != q) i++;
+            dst[e * G + i] = slot_rows[j];
+        }
+    }
+    if (load_out)
+        for (int q = 0; q < G; q++) load_out[q] = load[q];
+    return bad;
+}
+
+// Load-aware placement (host): starting from every rank's base experts,
+// add replicas in spare slots while that lowers the highest estimated rank
+// cost under ep_split: take the most loaded rank, its experts by the rows it
+// carries of them, and place a replica on the least loaded rank with a free
+// slot that does not hold the expert yet; keep the first such move that
+// lowers the maximum.  Deterministic.
+static void ep_place_greedy(const int *C, int G, int E, int S, const int *base, int *place) {
+    std::memcpy(place, base, sizeof(int) * (size_t)G * E);
+    std::vector<int> nh(E), hold((size_t)E * G), beg((size_t)E * (G + 1)), dst((size_t)E * G);
+    std::vector<long long> load(G);
+    auto eval = [&]() -> long long {
+        ep_split(C, E, G, E, place, S, nh.data(), hold.data(), beg.data(), dst.data(), nullptr,
+                 load.data());
+        return *std::max_element(load.begin(), load.end());
+    };
+    auto free_slot = [&](int q) -> int {
+        std::vector<char> used(S, 0);
+        for (int e = 0; e < E; e++)
+            if (place[q * E + e] >= 0) used[place[q * E + e]] = 1;
+        for (int j = 0; j < S; j++)
+            if (!used[j]) return j;
+        return -1;
+    };
+    long long cur = eval();
+    for (int iter = 0; iter < G * S; iter++) {
+        const std::vector<long long> ld = load;
+        int hot = 0;
+        for (int q = 1; q < G; q++)
+            if (ld[q] > ld[hot]) hot = q;
+        // the hot rank's experts by the rows it carries of them
+        std::vector<std::pair<int, int>> cand;
+        for (int e = 0; e < E; e++) {
+            if (place[hot * E + e] < 0) continue;
+            int i = 0;
+            while (hold[(size_t)e * G + i] != hot) i++;
+            const int rows = beg[(size_t)e * (G + 1) + i + 1] - beg[(size_t)e * (G + 1) + i];
+            if (rows > 0) cand.push_back({-rows, e});
+        }
+        std::sort(cand.begin(), cand.end());
+        std::vector<int> targets(G);
+        for (int q = 0; q < G; q++) targets[q] = q;
+        std::stable_sort(targets.begin(), targets.end(),
+                         [&](int a, int b) { return ld[a] < ld[b]; });
+        bool moved = false;
+        for (const auto &ce : cand) {
+            const int e = ce.second;
+            for (int q : targets) {
+                if (q == hot || place[q * E + e] >= 0) continue;
+                const int j = free_slot(q);
+                if (j < 0) continue;
+                place[q * E + e] = j;
+                const long long m = eval();
+                if (m < cur) {
+                    cur = m;
+                    moved = true;
+                    break;
+                }
+                place[q * E + e] = -1;
+            }
+            if (moved) break;
+        }
+        if (!moved) break;
+        eval();                       // refresh hold/beg/load for the next pass
     }
 }
 
-__host__ __device__ inline void ep_partition(const int *C, int G, int E, int rank,
-                                             long long capacity, int *cnt_q, int *base_r,
-                                             long long *S /* G+1 */) {
-    ep_slices(C, G, E, capacity, S);
-    const long long lo = S[rank], hi = S[rank + 1];
-    long long goff = 0;
-    for (int e = 0; e < E; e++) {
-        long long tot = 0, before = 0;
-        for (int r = 0; r < G; r++) {
-            if (r < rank) before += C[r * E + e];
-            tot += C[r * E + e];
-        }
-        const long long a = goff > lo ? goff : lo;
-        const long long b = goff + tot < hi ? goff + tot : hi;
-        if (cnt_q) cnt_q[e] = b > a ? (int)(b - a) : 0;
-        if (base_r) base_r[e] = (int)(goff + before);
-        goff += tot;
-    }
-}
-
-// One thread: this rank's slice plan (cnt | off | mt128 | mt64 | mt256), the global
-// base of this rank's rows per expert, and the slice boundaries.
-__global__ void ep_plan_kernel(const int *__restrict__ counts_all, int G, int E, int rank,
-                               long long capacity, int *__restrict__ plan,
-                               int *__restrict__ base_r, int *__restrict__ slices)
+// One thread: the split, this rank's receive plan over its S slots
+// (cnt | off | mt128 | mt64 | mt256), and the global position of this rank's
+// first row of every expert.
+//
+// Every rank's all-gathered record is {generation, counts[E]}; each forward
+// advances this rank's generation (stamp[0]) once.  If any record carries
+// another generation than this rank's, the exchange did not happen (a rank
+// stopped joining and the communicator was aborted, leaving the previous
+// step's records): the kernel then flags it, marks the step `dead`, and
+// gives this rank an empty plan and empty splits, so that no kernel of the
+// step stores into another rank's memory.
+__global__ void ep_plan_kernel(const int *__restrict__ recs, int G, int E, int S, int rank,
+                               const int *__restrict__ place, int *__restrict__ stamp,
+                               int *__restrict__ plan, int *__restrict__ base_r,
+                               int *__restrict__ nh, int *__restrict__ hold,
+                               int *__restrict__ beg, int *__restrict__ dst,
+                               int *__restrict__ dead, DeviceStatus *status)
 {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    int *cnt = plan, *off = plan + E, *mt128 = off + E + 1, *mt64 = mt128 + E + 1;
-    int *mt256 = mt64 + E + 1;
-    long long S[65];
-    ep_partition(counts_all, G, E, rank, capacity, cnt, base_r, S);
-    int o = 0, m1 = 0, m2 = 0, m3 = 0;
-    for (int e = 0; e < E; e++) {
-        off[e] = o; mt128[e] = m1; mt64[e] = m2; mt256[e] = m3;
-        o += cnt[e];
-        m1 += (cnt[e] + 127) / 128;
-        m2 += (cnt[e] + 63) / 64;
-        m3 += (cnt[e] + 255) / 256;
+    const int gen = stamp[0];
+    bool ok = true;
+    for (int q = 0; q < G; q++) ok = ok && recs[q * (E + 1)] == gen;
+    stamp[0] = gen + 1;
+    *dead = ok ? 0 : 1;
+    if (!ok) atomicExch(&status->bad_index, 2);
+    if (!ok || ep_split(recs + 1, E + 1, G, E, place, S, nh, hold, beg, dst, nullptr, nullptr)) {
+        if (ok) atomicExch(&status->bad_index, 1);
+        *dead = 1;
+        for (int e = 0; e < E; e++) nh[e] = 0;
+        for (int i = 0; i < plan_ints(S); i++) plan[i] = 0;
+        return;
     }
-    off[E] = o; mt128[E] = m1; mt64[E] = m2; mt256[E] = m3;
-    for (int q = 0; q <= G; q++) slices[q] = (int)S[q];
+    int *cnt = plan, *off = plan + S, *mt128 = off + S + 1, *mt64 = mt128 + S + 1;
+    int *mt256 = mt64 + S + 1;
+    for (int j = 0; j < S; j++) cnt[j] = 0;
+    for (int e = 0; e < E; e++) {
+        const int j = place[rank * E + e];
+        if (j < 0 || j >= S) continue;
+        int i = 0;
+        while (hold[e * G + i] != rank) i++;
+        cnt[j] = beg[e * (G + 1) + i + 1] - beg[e * (G + 1) + i];
+    }
+    int o = 0, m1 = 0, m2 = 0, m3 = 0;
+    for (int j = 0; j < S; j++) {
+        off[j] = o; mt128[j] = m1; mt64[j] = m2; mt256[j] = m3;
+        o += cnt[j];
+        m1 += (cnt[j] + 127) / 128;
+        m2 += (cnt[j] + 63) / 64;
+        m3 += (cnt[j] + 255) / 256;
+    }
+    off[S] = o; mt128[S] = m1; mt64[S] = m2; mt256[S] = m3;
+    for (int e = 0; e < E; e++) {
+        int b = 0;
+        for (int r = 0; r < rank; r++) b += recs[r * (E + 1) + 1 + e];
+        base_r[e] = b;
+    }
 }
 
 // One warp per local (token, rank) entry: its local expert-sorted slot (for
-// the combine), its global slot, and a float4 copy of the token row into the
-// slice owner's receive buffer with the return address beside it.
+// the combine), its place in the expert's global row order, the holder whose
+// range contains it, and a float4 copy of the token row into that holder's
+// receive buffer with the return address beside it.
 __global__ void __launch_bounds__(256)
 ep_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad, int k, int E, int rank,
-                 int G, int max_rows, const int *__restrict__ ids, const int *__restrict__ loc,
+                 int G, int recv_rows, const int *__restrict__ ids, const int *__restrict__ loc,
                  const int *__restrict__ tile_pref, const int *__restrict__ plan_local,
-                 const int *__restrict__ base_r, const int *__restrict__ slices,
-                 float *const *__restrict__ recv_ptrs, int2 *const *__restrict__ ret_ptrs,
-                 int *__restrict__ pos_of, int round_to_tf32, DeviceStatus *status)
+                 const int *__restrict__ base_r, const int *__restrict__ nh,
+                 const int *__restrict__ hold, const int *__restrict__ beg,
+                 const int *__restrict__ dst, float *const *__restrict__ recv_ptrs,
+                 int2 *const *__restrict__ ret_ptrs, int *__restrict__ pos_of, int round_to_tf32,
+                 const int *__restrict__ dead, DeviceStatus *status)
 {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (warp < T * k) {
+    if (warp < T * k && !*dead) {
         const int t = warp / k;
         const int e = ids[warp];
-        const int lr = tile_pref[(size_t)(t / kRouterTile) * E + e] + loc[warp];
-        const int pos_local = plan_local[E + e] + lr;
-        const int gp = base_r[e] + lr;
-        int lo = 0, hi = G - 1;                 // slice q with slices[q] <= gp < slices[q+1]
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (slices[mid] <= gp) lo = mid; else hi = mid - 1;
+        bool ok = e >= 0 && e < E;
+        int q = -1, p = -1, pos_local = -1;
+        if (ok) {
+            const int lr = tile_pref[(size_t)(t / kRouterTile) * E + e] + loc[warp];
+            pos_local = plan_local[E + e] + lr;
+            const int gp = base_r[e] + lr;
+            const int n = nh[e];
+            int i = 0;
+            while (i + 1 < n && beg[e * (G + 1) + i + 1] <= gp) i++;
+            ok = n > 0 && gp >= beg[e * (G + 1) + i] && gp < beg[e * (G + 1) + i + 1];
+            if (ok) {
+                q = hold[e * G + i];
+                p = dst[e * G + i] + gp - beg[e * (G + 1) + i];
+            }
         }
-        const int q = lo, p = gp - slices[q];
-        if (e < 0 || e >= E || q < 0 || q >= G || p < 0 || p >= max_rows || pos_local < 0 ||
+        if (!ok || q < 0 || q >= G || p < 0 || p >= recv_rows || pos_local < 0 ||
             pos_local >= T * k) {
             if (lane == 0) atomicExch(&status->bad_index, 1);
         } else {
@@ -169,10 +331,10 @@ ep_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad, int k, in
                 ret_ptrs[q][p] = make_int2(rank, pos_local);
             }
             const float *src = x + (size_t)t * d;
-            float *dst = recv_ptrs[q] + (size_t)p * d_pad;
+            float *dstp = recv_ptrs[q] + (size_t)p * d_pad;
             if ((d & 3) == 0) {
                 const float4 *s4 = reinterpret_cast<const float4 *>(src);
-                float4 *d4 = reinterpret_cast<float4 *>(dst);
+                float4 *d4 = reinterpret_cast<float4 *>(dstp);
                 for (int c = lane; c < (d_pad >> 2); c += 32) {
                     float4 v = (c < (d >> 2)) ? __ldg(s4 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
                     if (round_to_tf32) {
@@ -184,7 +346,7 @@ ep_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad, int k, in
             } else {
                 for (int c = lane; c < d_pad; c += 32) {
                     const float v = (c < d) ? __ldg(src + c) : 0.0f;
-                    dst[c] = round_to_tf32 ? round_tf32(v) : v;
+                    dstp[c] = round_to_tf32 ? round_tf32(v) : v;
                 }
             }
         }
@@ -192,32 +354,50 @@ ep_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad, int k, in
     __threadfence_system();   // peer stores visible before the barrier that follows
 }
 
+// Plain-load copy of one packed expert slot from a peer's shard (IPC
+// mapping, NVLink loads) into a local slot.
+__global__ void __launch_bounds__(256)
+ep_slot_copy_kernel(const float4 *__restrict__ src, float4 *__restrict__ dst, size_t n4)
+{
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = src[i];
+}
+
 // ---------------------------------------------------------------------
 // state
 // ---------------------------------------------------------------------
 struct moe_b200_ep {
-    int rank = 0, world = 1, device = 0, max_T = 0, max_rows = 0, recv_rows = 0;
-    const moe_b200_weights *w = nullptr;
+    int rank = 0, world = 1, device = 0, max_T = 0, max_rows = 0, recv_rows = 0, S = 0, E = 0;
+    moe_b200_weights *w = nullptr;      // this rank's shard (spare slots filled by rebalance)
     ncclComm_t comm = nullptr;
     cudaStream_t stream = nullptr;      // library stream for the host-buffer entry
     DeviceStatus *status = nullptr;
+    // placement: slot of expert e on rank q (-1: not held); base = at creation
+    std::vector<int> place, base;
+    int *d_place = nullptr;
     // IPC-shared buffers (this rank's) and the peer tables
     float *recv_x = nullptr;            // [recv_rows × d_pad]
     int2 *ret = nullptr;                // [recv_rows]
-    float *y = nullptr;                 // [max_rows × d_pad] written by slice owners
+    float *y = nullptr;                 // [max_rows × d_pad] written by the holders
     float **d_recv_ptrs = nullptr, **d_y_ptrs = nullptr;
     int2 **d_ret_ptrs = nullptr;
+    std::vector<const float *> peer_ug, peer_dn;   // every rank's packed slots
     std::vector<void *> opened;         // peer mappings to close
     // local work buffers
     float *h = nullptr;                 // [recv_rows × F_pad]
-    float *xs = nullptr, *hs = nullptr; // 3xTF32 small parts of recv_x and h
+    float *xs = nullptr, *hs = nullptr; // 3xTF32 small parts of recv_x and h (on first use)
     float *rpart = nullptr;             // split-K router partial logits (small T)
     int rsplit = 1;
     float *probs = nullptr, *wts = nullptr;
     int *ids = nullptr, *loc = nullptr, *tile_cnt = nullptr, *tile_pref = nullptr;
-    int *plan_local = nullptr, *plan_q = nullptr, *pos_of = nullptr;
-    int *counts_all = nullptr, *base_r = nullptr, *slices = nullptr, *bar = nullptr;
+    // local record {generation, cnt[E] | off | ...}: the scan writes the plan
+    // at local + 1, the all-gather sends local[0 .. E] (generation, counts)
+    int *local = nullptr, *plan_local = nullptr, *plan_q = nullptr, *pos_of = nullptr;
+    int *recs = nullptr, *base_r = nullptr, *bar = nullptr, *dead = nullptr;
+    int *nh = nullptr, *hold = nullptr, *beg = nullptr, *dst = nullptr;
     float *io_x = nullptr, *io_out = nullptr, *io_bias = nullptr;
+    int timeout_ms = 0;                 // host watchdog on the group's barriers (0 = none)
     TcGemm up{}, dn{};
     DecMaps dup{}, ddn{};
 };
@@ -274,15 +454,116 @@ void ep_release(moe_b200_ep *ep) {
     cudaSetDevice(ep->device);
     cudaDeviceSynchronize();
     for (void *p : ep->opened) cudaIpcCloseMemHandle(p);
-    if (ep->comm) nccl().CommDestroy(ep->comm);
+    if (ep->comm) {
+        // the communicator is non-blocking: finalize, wait (bounded) until it
+        // is quiescent, then free it; abort if it does not settle
+        const ncclResult_t f = nccl().CommFinalize(ep->comm);   // usually ncclInProgress
+        bool settled = f == ncclSuccess || f == ncclInProgress;
+        const auto t0 = std::chrono::steady_clock::now();
+        const int limit_ms = ep->timeout_ms > 0 ? ep->timeout_ms : 30000;
+        while (settled) {
+            ncclResult_t a = ncclInProgress;
+            if (nccl().CommGetAsyncError(ep->comm, &a) != ncclSuccess ||
+                (a != ncclSuccess && a != ncclInProgress)) {
+                settled = false;
+                break;
+            }
+            if (a == ncclSuccess) break;
+            if (std::chrono::duration_cast<std::chrono::milliseconds>(
+                    std::chrono::steady_clock::now() - t0).count() > limit_ms) {
+                settled = false;
+                break;
+            }
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
+        if (settled) nccl().CommDestroy(ep->comm);
+        else nccl().CommAbort(ep->comm);
+    }
     void *bufs[] = {ep->recv_x, ep->ret, ep->y, ep->d_recv_ptrs, ep->d_y_ptrs, ep->d_ret_ptrs,
-                    ep->h, ep->xs, ep->hs, ep->rpart, ep->probs, ep->wts, ep->ids, ep->loc, ep->tile_cnt, ep->tile_pref,
-                    ep->plan_local, ep->plan_q, ep->pos_of, ep->counts_all, ep->base_r,
-                    ep->slices, ep->bar, ep->io_x, ep->io_out, ep->io_bias, ep->status};
+                    ep->h, ep->xs, ep->hs, ep->rpart, ep->probs, ep->wts, ep->ids, ep->loc,
+                    ep->tile_cnt, ep->tile_pref, ep->local, ep->plan_q, ep->pos_of,
+                    ep->recs, ep->base_r, ep->bar, ep->dead, ep->nh, ep->hold, ep->beg, ep->dst,
+                    ep->d_place, ep->io_x, ep->io_out, ep->io_bias, ep->status};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (ep->stream) cudaStreamDestroy(ep->stream);
     delete ep;
+}
+
+// Wait for `s` on the host, but for at most timeout_ms (0 = no limit).  A
+// rank that never reaches a collective leaves the others' NCCL kernels
+// spinning; past the limit the communicator is aborted, which ends those
+// kernels, and the call returns MOE_B200_E_TIMEOUT.  The group is unusable
+// afterwards (destroy it).
+int ep_wait(moe_b200_ep *ep, cudaStream_t s) {
+    if (ep->timeout_ms <= 0) {
+        EP_CK(cudaStreamSynchronize(s));
+        return MOE_B200_OK;
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        const cudaError_t q = cudaStreamQuery(s);
+        if (q == cudaSuccess) return MOE_B200_OK;
+        if (q != cudaErrorNotReady)
+            return ep_fail(MOE_B200_E_CUDA, "stream: %s%s", cudaGetErrorString(q));
+        ncclResult_t async_err = ncclSuccess;
+        if (ep->comm && nccl().CommGetAsyncError(ep->comm, &async_err) == ncclSuccess &&
+            async_err != ncclSuccess && async_err != ncclInProgress) {
+            nccl().CommAbort(ep->comm);
+            ep->comm = nullptr;
+            return ep_fail(MOE_B200_E_NCCL, "communicator error: %s%s",
+                           nccl().GetErrorString(async_err));
+        }
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+        if (ms > ep->timeout_ms) {
+            if (ep->comm) nccl().CommAbort(ep->comm);
+            ep->comm = nullptr;
+            return ep_fail(MOE_B200_E_TIMEOUT,
+                           "expert-parallel step did not finish within the watchdog limit; "
+                           "communicator aborted%s%s");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+// Settle an NCCL call on the group's non-blocking communicator: success,
+// or ncclInProgress waited out (bounded by the watchdog, after which the
+// communicator is aborted and MOE_B200_E_TIMEOUT returned).
+int ep_nccl(moe_b200_ep *ep, ncclResult_t r, const char *what) {
+    if (r == ncclSuccess) return MOE_B200_OK;
+    if (r != ncclInProgress || !ep->comm) {
+        if (ep->comm) nccl().CommAbort(ep->comm);
+        ep->comm = nullptr;
+        return ep_fail(MOE_B200_E_NCCL, "%s: %s", what, nccl().GetErrorString(r));
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        ncclResult_t a = ncclInProgress;
+        const ncclResult_t q = nccl().CommGetAsyncError(ep->comm, &a);
+        if (q == ncclSuccess && a == ncclSuccess) return MOE_B200_OK;
+        if (q != ncclSuccess || a != ncclInProgress) {
+            nccl().CommAbort(ep->comm);
+            ep->comm = nullptr;
+            return ep_fail(MOE_B200_E_NCCL, "%s: %s", what,
+                           nccl().GetErrorString(q != ncclSuccess ? q : a));
+        }
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+        if (ep->timeout_ms > 0 && ms > ep->timeout_ms) {
+            nccl().CommAbort(ep->comm);
+            ep->comm = nullptr;
+            return ep_fail(MOE_B200_E_TIMEOUT, "%s did not complete within the watchdog limit; "
+                                               "communicator aborted%s", what);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+int upload_place(moe_b200_ep *ep) {
+    EP_CK(cudaMemcpy(ep->d_place, ep->place.data(), ep->place.size() * sizeof(int),
+                     cudaMemcpyHostToDevice));
+    return MOE_B200_OK;
 }
 
 }  // namespace
@@ -301,25 +582,46 @@ extern "C" int moe_b200_ep_unique_id(void *id_out) {
     return MOE_B200_OK;
 }
 
-extern "C" int moe_b200_ep_partition(const int *counts_all, int world, int E, int rank,
-                                     long long capacity, int *cnt_rank, int *base_rank,
-                                     long long *slice_start, long long *slice_rows) {
-    if (!counts_all || world < 1 || world > 64 || E < 1 || rank < 0 || rank >= world)
-        return ep_fail(MOE_B200_E_INVALID, "bad partition arguments%s%s");
-    long long S[65];
-    ep_partition(counts_all, world, E, rank, capacity, cnt_rank, base_rank, S);
-    if (slice_start) *slice_start = S[rank];
-    if (slice_rows) *slice_rows = S[rank + 1] - S[rank];
+static int split_args_ok(const int *counts_all, int world, int E, const int *place, int n_slots) {
+    return counts_all && place && world >= 1 && world <= kMaxWorld && E >= 1 &&
+           E <= kMaxExperts && n_slots >= 1 && n_slots <= E;
+}
+
+extern "C" int moe_b200_ep_split(const int *counts_all, int world, int E, const int *place,
+                                 int n_slots, int *n_holders, int *holders, int *row_begin,
+                                 int *recv_offset, long long *recv_rows, long long *cost) {
+    if (!split_args_ok(counts_all, world, E, place, n_slots) || !n_holders || !holders ||
+        !row_begin || !recv_offset)
+        return ep_fail(MOE_B200_E_INVALID, "bad split arguments%s%s");
+    for (int i = 0; i < world * E; i++)
+        if (place[i] >= n_slots || place[i] < -1)
+            return ep_fail(MOE_B200_E_INVALID, "placement slot out of range%s%s");
+    if (ep_split(counts_all, E, world, E, place, n_slots, n_holders, holders, row_begin,
+                 recv_offset, recv_rows, cost))
+        return ep_fail(MOE_B200_E_INVALID, "an expert with rows has no holder%s%s");
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_ep_place(const int *counts_all, int world, int E, const int *base_place,
+                                 int n_slots, int *place) {
+    if (!split_args_ok(counts_all, world, E, base_place, n_slots) || !place)
+        return ep_fail(MOE_B200_E_INVALID, "bad placement arguments%s%s");
+    for (int e = 0; e < E; e++) {
+        int n = 0;
+        for (int q = 0; q < world; q++) n += base_place[q * E + e] >= 0;
+        if (n == 0) return ep_fail(MOE_B200_E_INVALID, "an expert has no base holder%s%s");
+    }
+    ep_place_greedy(counts_all, world, E, n_slots, base_place, place);
     return MOE_B200_OK;
 }
 
 extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
-                                  int max_tokens_per_rank, const moe_b200_weights *w,
+                                  int max_tokens_per_rank, moe_b200_weights *w,
                                   moe_b200_ep **out) {
-    if (!unique_id || !w || !out || world < 1 || world > 64 || rank < 0 || rank >= world ||
+    if (!unique_id || !w || !out || world < 1 || world > kMaxWorld || rank < 0 || rank >= world ||
         max_tokens_per_rank < 1)
         return ep_fail(MOE_B200_E_INVALID, "bad arguments to moe_b200_ep_create%s%s");
-    if ((int64_t)max_tokens_per_rank * w->k > (int64_t)1 << 30)
+    if ((int64_t)max_tokens_per_rank * w->k * world > (int64_t)1 << 30)
         return ep_fail(MOE_B200_E_INVALID, "max_tokens_per_rank too large%s%s");
     if (!nccl().ok) return ep_fail(MOE_B200_E_NCCL, "libnccl.so.2 not found%s%s");
     EP_CK(cudaSetDevice(w->device));
@@ -329,11 +631,13 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     ep->world = world;
     ep->device = w->device;
     ep->w = w;
+    ep->E = w->E;
+    ep->S = w->n_slots;
     ep->max_T = max_tokens_per_rank;
     ep->max_rows = max_tokens_per_rank * w->k;
-    // cost-balanced slices may hold more rows than T·k: 25% headroom, beyond
-    // which the partition falls back to equal rows
-    ep->recv_rows = ep->max_rows + ep->max_rows / 4 + 256;
+    // every token of every rank may route to experts this rank holds
+    ep->recv_rows = world * ep->max_rows;
+    if (const char *p = std::getenv("MOE_B200_EP_TIMEOUT_MS")) ep->timeout_ms = std::atoi(p);
     int rc = MOE_B200_OK;
 #define TRY(x)                      \
     do {                            \
@@ -343,21 +647,22 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
         }                           \
     } while (0)
     auto alloc = [&](void **p, size_t bytes) -> int {
-        cudaError_t e = cudaMalloc(p, bytes);
-        if (e != cudaSuccess)
+        cudaError_t e = dev_alloc(p, bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
             return ep_fail(MOE_B200_E_NOMEM, "expert-parallel buffers: %s%s", cudaGetErrorString(e));
+        }
         return MOE_B200_OK;
     };
     const size_t R = ep->max_rows, RR = ep->recv_rows, T = ep->max_T, E = w->E, G = world;
+    const size_t S = ep->S;
     const size_t tiles = ceil_div<size_t>(T, kRouterTile);
     TRY(alloc((void **)&ep->recv_x, RR * w->d_pad * 4));
     TRY(alloc((void **)&ep->ret, RR * sizeof(int2)));
     TRY(alloc((void **)&ep->y, R * w->d_pad * 4));
     TRY(alloc((void **)&ep->h, RR * w->F_pad * 4));
-    TRY(alloc((void **)&ep->xs, RR * w->d_pad * 4));
     ep->rsplit = router_splits((int)T, w->d);
     if (ep->rsplit > 1) TRY(alloc((void **)&ep->rpart, (size_t)ep->rsplit * T * E * 4));
-    TRY(alloc((void **)&ep->hs, RR * w->F_pad * 4));
     TRY(alloc((void **)&ep->probs, T * E * 4));
     TRY(alloc((void **)&ep->wts, R * 4));
     TRY(alloc((void **)&ep->ids, R * 4));
@@ -365,11 +670,17 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     TRY(alloc((void **)&ep->pos_of, R * 4));
     TRY(alloc((void **)&ep->tile_cnt, tiles * E * 4));
     TRY(alloc((void **)&ep->tile_pref, tiles * E * 4));
-    TRY(alloc((void **)&ep->plan_local, plan_ints(E) * 4));
-    TRY(alloc((void **)&ep->plan_q, plan_ints(E) * 4));
-    TRY(alloc((void **)&ep->counts_all, G * E * 4));
+    TRY(alloc((void **)&ep->local, (1 + plan_ints((int)E)) * 4));
+    ep->plan_local = ep->local + 1;
+    TRY(alloc((void **)&ep->plan_q, plan_ints((int)S) * 4));
+    TRY(alloc((void **)&ep->recs, G * (E + 1) * 4));
+    TRY(alloc((void **)&ep->dead, 4));
     TRY(alloc((void **)&ep->base_r, E * 4));
-    TRY(alloc((void **)&ep->slices, (G + 1) * 4));
+    TRY(alloc((void **)&ep->nh, E * 4));
+    TRY(alloc((void **)&ep->hold, E * G * 4));
+    TRY(alloc((void **)&ep->beg, E * (G + 1) * 4));
+    TRY(alloc((void **)&ep->dst, E * G * 4));
+    TRY(alloc((void **)&ep->d_place, G * E * 4));
     TRY(alloc((void **)&ep->bar, 4));
     TRY(alloc((void **)&ep->io_x, T * w->d * 4));
     TRY(alloc((void **)&ep->io_out, T * w->d * 4));
@@ -379,7 +690,9 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     TRY(alloc((void **)&ep->d_y_ptrs, G * sizeof(float *)));
     TRY(alloc((void **)&ep->d_ret_ptrs, G * sizeof(int2 *)));
     if (cudaMemset(ep->status, 0, sizeof(DeviceStatus)) != cudaSuccess ||
-        cudaMemset(ep->bar, 0, 4) != cudaSuccess ||
+        cudaMemset(ep->bar, 0, 4) != cudaSuccess || cudaMemset(ep->local, 0, 4) != cudaSuccess ||
+        cudaMemset(ep->recs, 0xff, G * (E + 1) * 4) != cudaSuccess ||
+        cudaMemset(ep->dead, 0, 4) != cudaSuccess ||
         cudaStreamCreateWithFlags(&ep->stream, cudaStreamNonBlocking) != cudaSuccess)
         TRY(ep_fail(MOE_B200_E_CUDA, "expert-parallel set-up failed%s%s"));
     TRY(ep_tmap(&ep->up.tmA, ep->recv_x, RR, w->d_pad, 128));
@@ -388,84 +701,102 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
     ep->dn.tmB = w->tm_dn;
     ep->dup.tmW = w->tm_ug64;
     TRY(ep_tmap(&ep->dup.tmXb, ep->recv_x, RR, w->d_pad, 64));
-    TRY(ep_tmap(&ep->dup.tmXs, ep->xs, RR, w->d_pad, 64));
     ep->dup.tmXb32 = ep->dup.tmXb;       // CTA-pair map, unused by the single-CTA kernels
     ep->ddn.tmW = w->tm_dn128;
     TRY(ep_tmap(&ep->ddn.tmXb, ep->h, RR, w->F_pad, 64));
-    TRY(ep_tmap(&ep->ddn.tmXs, ep->hs, RR, w->F_pad, 64));
     ep->ddn.tmXb32 = ep->ddn.tmXb;
 
-    // communicator
+    // communicator: non-blocking, so that a rank that never joins (or a bad
+    // id) ends in the watchdog's abort instead of a host thread blocked for
+    // good inside the bootstrap
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof id);
     {
-        ncclResult_t r = nccl().CommInitRank(&ep->comm, world, id, rank);
-        if (r != ncclSuccess) {
-            ep->comm = nullptr;
-            TRY(ep_fail(MOE_B200_E_NCCL, "ncclCommInitRank: %s%s", nccl().GetErrorString(r)));
-        }
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        ep->comm = nullptr;
+        const ncclResult_t r = nccl().CommInitRankConfig(&ep->comm, world, id, rank, &cfg);
+        TRY(ep_nccl(ep, r, "ncclCommInitRankConfig"));
     }
-    // exchange IPC handles of the three shared buffers (NCCL all-gather)
-    std::vector<float *> recv_ptrs(G), y_ptrs(G);
-    std::vector<int2 *> ret_ptrs(G);
-    recv_ptrs[rank] = ep->recv_x;
-    y_ptrs[rank] = ep->y;
-    ret_ptrs[rank] = ep->ret;
-    if (world > 1) {
-        // three IPC handles and this rank's max_tokens_per_rank (every rank
-        // must use the same capacity, or their partitions would differ)
-        constexpr size_t HB = 3 * sizeof(cudaIpcMemHandle_t) + 64;
-        struct {
-            cudaIpcMemHandle_t h[3];
-            long long max_t;
-            char pad[56];
-        } mine_blob;
-        static_assert(sizeof(mine_blob) == HB, "handle blob layout");
-        std::memset(&mine_blob, 0, sizeof mine_blob);
-        mine_blob.max_t = max_tokens_per_rank;
-        cudaIpcMemHandle_t *mine = mine_blob.h;
-        if (cudaIpcGetMemHandle(&mine[0], ep->recv_x) != cudaSuccess ||
-            cudaIpcGetMemHandle(&mine[1], ep->ret) != cudaSuccess ||
-            cudaIpcGetMemHandle(&mine[2], ep->y) != cudaSuccess)
-            TRY(ep_fail(MOE_B200_E_CUDA, "cudaIpcGetMemHandle failed%s%s"));
+    // exchange, over NCCL: IPC handles of the three shared buffers and of the
+    // shard's packed weights, the group's shape parameters (which must agree)
+    // and every rank's base experts
+    struct Blob {
+        cudaIpcMemHandle_t h[5];
+        long long max_t;
+        int n_slots, E, d, F;
+        int slot_expert[kMaxExperts];
+    };
+    Blob mine;
+    std::memset(&mine, 0, sizeof mine);
+    mine.max_t = max_tokens_per_rank;
+    mine.n_slots = w->n_slots;
+    mine.E = w->E; mine.d = w->d; mine.F = w->F;
+    for (int j = 0; j < w->n_slots; j++) mine.slot_expert[j] = w->slot_expert[j];
+    if (world > 1 && (cudaIpcGetMemHandle(&mine.h[0], ep->recv_x) != cudaSuccess ||
+                      cudaIpcGetMemHandle(&mine.h[1], ep->ret) != cudaSuccess ||
+                      cudaIpcGetMemHandle(&mine.h[2], ep->y) != cudaSuccess ||
+                      cudaIpcGetMemHandle(&mine.h[3], w->ug) != cudaSuccess ||
+                      cudaIpcGetMemHandle(&mine.h[4], w->dn) != cudaSuccess))
+        TRY(ep_fail(MOE_B200_E_CUDA, "cudaIpcGetMemHandle failed%s%s"));
+    const size_t HB = sizeof(Blob);
+    std::vector<Blob> all(G);
+    {
         unsigned char *dh = nullptr;
         TRY(alloc((void **)&dh, HB * G));
-        std::vector<unsigned char> all(HB * G);
         int step = MOE_B200_OK;
-        if (cudaMemcpy(dh + HB * rank, &mine_blob, HB, cudaMemcpyHostToDevice) != cudaSuccess)
+        if (cudaMemcpy(dh + HB * rank, &mine, HB, cudaMemcpyHostToDevice) != cudaSuccess)
             step = ep_fail(MOE_B200_E_CUDA, "handle upload failed%s%s");
-        if (!step) {
-            ncclResult_t r = nccl().AllGather(dh + HB * rank, dh, HB, ncclChar, ep->comm, ep->stream);
-            if (r != ncclSuccess)
-                step = ep_fail(MOE_B200_E_NCCL, "nccl().AllGather(handles): %s%s", nccl().GetErrorString(r));
-        }
-        if (!step && (cudaStreamSynchronize(ep->stream) != cudaSuccess ||
-                      cudaMemcpy(all.data(), dh, HB * G, cudaMemcpyDeviceToHost) != cudaSuccess))
+        if (!step)
+            step = ep_nccl(ep, nccl().AllGather(dh + HB * rank, dh, HB, ncclChar, ep->comm,
+                                                ep->stream), "ncclAllGather(handles)");
+        if (!step) step = ep_wait(ep, ep->stream);
+        if (!step && cudaMemcpy(all.data(), dh, HB * G, cudaMemcpyDeviceToHost) != cudaSuccess)
             step = ep_fail(MOE_B200_E_CUDA, "handle exchange failed%s%s");
         cudaFree(dh);
         TRY(step);
-        for (int q = 0; q < world; q++) {
-            long long their_t = 0;
-            std::memcpy(&their_t, all.data() + HB * q + 3 * sizeof(cudaIpcMemHandle_t), 8);
-            if (their_t != max_tokens_per_rank)
-                TRY(ep_fail(MOE_B200_E_INVALID,
-                            "max_tokens_per_rank differs between ranks%s%s"));
+    }
+    ep->place.assign(G * E, -1);
+    for (int q = 0; q < world; q++) {
+        const Blob &b = all[q];
+        if (b.max_t != max_tokens_per_rank || b.n_slots != w->n_slots || b.E != w->E ||
+            b.d != w->d || b.F != w->F)
+            TRY(ep_fail(MOE_B200_E_INVALID, "ranks disagree on max_tokens_per_rank, the expert "
+                                            "shape or the slot count%s%s"));
+        for (int j = 0; j < b.n_slots; j++)
+            if (b.slot_expert[j] >= 0) ep->place[(size_t)q * E + b.slot_expert[j]] = j;
+    }
+    for (size_t e = 0; e < E; e++) {
+        int n = 0;
+        for (size_t q = 0; q < G; q++) n += ep->place[q * E + e] >= 0;
+        if (n == 0) TRY(ep_fail(MOE_B200_E_INVALID, "an expert is held by no rank%s%s"));
+    }
+    ep->base = ep->place;
+    TRY(upload_place(ep));
+    // peer mappings
+    std::vector<float *> recv_ptrs(G), y_ptrs(G);
+    std::vector<int2 *> ret_ptrs(G);
+    ep->peer_ug.assign(G, nullptr);
+    ep->peer_dn.assign(G, nullptr);
+    recv_ptrs[rank] = ep->recv_x;
+    y_ptrs[rank] = ep->y;
+    ret_ptrs[rank] = ep->ret;
+    ep->peer_ug[rank] = w->ug;
+    ep->peer_dn[rank] = w->dn;
+    for (int q = 0; q < world; q++) {
+        if (q == rank) continue;
+        void *p[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+        for (int i = 0; i < 5; i++) {
+            cudaError_t e = cudaIpcOpenMemHandle(&p[i], all[q].h[i], cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess)
+                TRY(ep_fail(MOE_B200_E_CUDA, "cudaIpcOpenMemHandle: %s%s", cudaGetErrorString(e)));
+            ep->opened.push_back(p[i]);
         }
-        for (int q = 0; q < world; q++) {
-            if (q == rank) continue;
-            cudaIpcMemHandle_t hq[3];
-            std::memcpy(hq, all.data() + HB * q, 3 * sizeof(cudaIpcMemHandle_t));
-            void *p[3] = {nullptr, nullptr, nullptr};
-            for (int i = 0; i < 3; i++) {
-                cudaError_t e = cudaIpcOpenMemHandle(&p[i], hq[i], cudaIpcMemLazyEnablePeerAccess);
-                if (e != cudaSuccess)
-                    TRY(ep_fail(MOE_B200_E_CUDA, "cudaIpcOpenMemHandle: %s%s", cudaGetErrorString(e)));
-                ep->opened.push_back(p[i]);
-            }
-            recv_ptrs[q] = (float *)p[0];
-            ret_ptrs[q] = (int2 *)p[1];
-            y_ptrs[q] = (float *)p[2];
-        }
+        recv_ptrs[q] = (float *)p[0];
+        ret_ptrs[q] = (int2 *)p[1];
+        y_ptrs[q] = (float *)p[2];
+        ep->peer_ug[q] = (const float *)p[3];
+        ep->peer_dn[q] = (const float *)p[4];
     }
     if (cudaMemcpy(ep->d_recv_ptrs, recv_ptrs.data(), G * sizeof(float *), cudaMemcpyHostToDevice) ||
         cudaMemcpy(ep->d_y_ptrs, y_ptrs.data(), G * sizeof(float *), cudaMemcpyHostToDevice) ||
@@ -490,19 +821,32 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
         return ep_fail(MOE_B200_E_INVALID, "x and out must be 16-byte aligned%s%s");
     if (T < 0 || T > ep->max_T)
         return ep_fail(MOE_B200_E_INVALID, "T outside [0, max_tokens_per_rank]%s%s");
+    if (!ep->comm) return ep_fail(MOE_B200_E_STATE, "the group was aborted; destroy it%s%s");
     const moe_b200_weights *w = ep->w;
     EP_CK(cudaSetDevice(ep->device));
     ncclResult_t async_err = ncclSuccess;
     EP_NC(nccl().CommGetAsyncError(ep->comm, &async_err));
-    if (async_err != ncclSuccess)
+    if (async_err != ncclSuccess && async_err != ncclInProgress)
         return ep_fail(MOE_B200_E_NCCL, "communicator error: %s%s", nccl().GetErrorString(async_err));
     cudaStream_t s = stream ? (cudaStream_t)stream : ep->stream;
-    const int E = w->E, k = w->k, G = ep->world;
+    const int E = w->E, k = w->k, G = ep->world, S = ep->S;
     float *probs = d_router_probs ? d_router_probs : ep->probs;
     int *ids = d_expert_ids ? d_expert_ids : ep->ids;
+    // The path is decided from values every rank shares (the group's token
+    // capacity), never from this rank's own T: rows of one rank are computed
+    // on others, and all of them must run the same arithmetic.
+    const double avg_group = (double)ep->max_T * G * k / E;
     int path = opts ? opts->path : MOE_B200_PATH_AUTO;
     if (path == MOE_B200_PATH_AUTO)
-        path = ((double)T * G * k / E >= 64.0) ? MOE_B200_PATH_TF32 : MOE_B200_PATH_TF32X3;
+        path = avg_group >= 64.0 ? MOE_B200_PATH_TF32 : MOE_B200_PATH_TF32X3;
+    const bool onepass = path == MOE_B200_PATH_TF32 && avg_group < 64.0;
+    if (path == MOE_B200_PATH_TF32X3 && !ep->xs) {
+        EP_CK(cudaMalloc(&ep->xs, (size_t)ep->recv_rows * w->d_pad * 4));
+        EP_CK(cudaMalloc(&ep->hs, (size_t)ep->recv_rows * w->F_pad * 4));
+        int rc = ep_tmap(&ep->dup.tmXs, ep->xs, ep->recv_rows, w->d_pad, 64);
+        if (!rc) rc = ep_tmap(&ep->ddn.tmXs, ep->hs, ep->recv_rows, w->F_pad, 64);
+        if (rc) return rc;
+    }
     cudaEvent_t *ev = profile_events(ep->device);
 #define MARK(i) \
     if (ev) EP_CK(cudaEventRecord(ev[i], s))
@@ -519,50 +863,56 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
         EP_CK(cudaMemsetAsync(ep->plan_local, 0, E * sizeof(int), s));
     }
     MARK(1);
-    EP_NC(nccl().AllGather(ep->plan_local, ep->counts_all, E, ncclInt32, ep->comm, s));
-    ep_plan_kernel<<<1, 32, 0, s>>>(ep->counts_all, G, E, ep->rank, ep->recv_rows, ep->plan_q,
-                                    ep->base_r, ep->slices);
+    int rc = ep_nccl(ep, nccl().AllGather(ep->local, ep->recs, E + 1, ncclInt32, ep->comm, s),
+                     "ncclAllGather(counts)");
+    if (rc) return rc;
+    ep_plan_kernel<<<1, 32, 0, s>>>(ep->recs, G, E, S, ep->rank, ep->d_place, ep->local,
+                                    ep->plan_q, ep->base_r, ep->nh, ep->hold, ep->beg, ep->dst,
+                                    ep->dead, ep->status);
     EP_CK(cudaGetLastError());
     if (T > 0) {
         ep_gather_kernel<<<ceil_div(T * k, 8), 256, 0, s>>>(
             d_x, T, w->d, w->d_pad, k, E, ep->rank, G, ep->recv_rows, ids, ep->loc,
-            ep->tile_pref, ep->plan_local, ep->base_r, ep->slices, ep->d_recv_ptrs,
-            ep->d_ret_ptrs, ep->pos_of, path == MOE_B200_PATH_TF32, ep->status);
+            ep->tile_pref, ep->plan_local, ep->base_r, ep->nh, ep->hold, ep->beg, ep->dst,
+            ep->d_recv_ptrs, ep->d_ret_ptrs, ep->pos_of, path == MOE_B200_PATH_TF32, ep->dead,
+            ep->status);
         EP_CK(cudaGetLastError());
     }
-    EP_NC(nccl().AllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s));
+    if ((rc = ep_nccl(ep, nccl().AllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s),
+                      "ncclAllReduce(barrier)")))
+        return rc;
     MARK(2);
     const int rows = ep->recv_rows;
-    // TF32 on decode-sized groups (the single-GPU rule, on the whole job's
-    // rows per expert): the weight-streaming kernel's one-pass TF32 mode.
-    // The down GEMM does not split K here (its rows go straight to their
+    // TF32 on decode-sized groups runs the weight-streaming kernel's one-pass
+    // mode.  Its down GEMM does not split K here (rows go straight to their
     // owners), unlike the single-GPU call, so the two agree to the TF32
     // tolerance rather than bit for bit on this path.
-    const bool onepass = path == MOE_B200_PATH_TF32 && (double)T * G * k / E < 64.0;
     if (path == MOE_B200_PATH_TF32 && !onepass) {
         const int sms = device_sms(ep->device);
-        EP_CK(launch_tc_upgate(ep->up, w->d_pad, w->F_pad, ep->h, ep->plan_q, E, rows, sms,
+        EP_CK(launch_tc_upgate(ep->up, w->d_pad, w->F_pad, ep->h, ep->plan_q, S, rows, sms,
                                ep->status, s));
         MARK(3);
-        EP_CK(launch_tc_down(ep->dn, w->F_pad, w->d_pad, w->down_bn, ep->y, ep->plan_q, E, rows,
+        EP_CK(launch_tc_down(ep->dn, w->F_pad, w->d_pad, w->down_bn, ep->y, ep->plan_q, S, rows,
                              sms, ep->status, s, ep->d_y_ptrs, ep->ret));
     } else if (path == MOE_B200_PATH_TF32X3 || onepass) {
         const int sms = device_sms(ep->device);
         if (!onepass) EP_CK(launch_split_tf32(ep->recv_x, ep->xs, (size_t)rows * w->d_pad, s));
-        EP_CK(launch_dec_upgate(ep->dup, w->d_pad, w->F_pad, ep->h, ep->hs, ep->plan_q, E, rows,
+        EP_CK(launch_dec_upgate(ep->dup, w->d_pad, w->F_pad, ep->h, ep->hs, ep->plan_q, S, rows,
                                 sms, 0, ep->status, s, onepass));
         MARK(3);
-        EP_CK(launch_dec_down(ep->ddn, w->F_pad, w->d_pad, ep->y, ep->plan_q, E, rows, sms, 0,
+        EP_CK(launch_dec_down(ep->ddn, w->F_pad, w->d_pad, ep->y, ep->plan_q, S, rows, sms, 0,
                               ep->status, s, ep->d_y_ptrs, ep->ret, nullptr, onepass));
     } else {
-        EP_CK(launch_ffma_upgate(ep->recv_x, w->d_pad, w->ug, w->F_pad, ep->h, ep->plan_q, E, rows,
+        EP_CK(launch_ffma_upgate(ep->recv_x, w->d_pad, w->ug, w->F_pad, ep->h, ep->plan_q, S, rows,
                                  s));
         MARK(3);
-        EP_CK(launch_ffma_down(ep->h, w->F_pad, w->dn, w->d_pad, ep->y, ep->plan_q, E, rows, s,
+        EP_CK(launch_ffma_down(ep->h, w->F_pad, w->dn, w->d_pad, ep->y, ep->plan_q, S, rows, s,
                                ep->d_y_ptrs, ep->ret));
     }
     MARK(4);   // the wait for the other ranks counts under the combine stage
-    EP_NC(nccl().AllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s));
+    if ((rc = ep_nccl(ep, nccl().AllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm, s),
+                      "ncclAllReduce(barrier)")))
+        return rc;
     if (T > 0) EP_CK(launch_combine(ep->y, w->d, w->d_pad, T, k, ep->pos_of, ep->wts, d_out, s));
     MARK(5);
 #undef MARK
@@ -600,26 +950,94 @@ extern "C" int moe_b200_ep_forward(moe_b200_ep *ep, const float *router_bias, co
             EP_CK(cudaMemcpyAsync(expert_ids, ep->ids, (size_t)T * w->k * 4,
                                   cudaMemcpyDeviceToHost, s));
     }
-    EP_CK(cudaStreamSynchronize(s));
+    if ((rc = ep_wait(ep, s))) return rc;
     DeviceStatus st;
     EP_CK(cudaMemcpy(&st, ep->status, sizeof st, cudaMemcpyDeviceToHost));
     if (st.bad_index || st.timeout) {
         EP_CK(cudaMemset(ep->status, 0, sizeof st));
-        return st.timeout ? ep_fail(MOE_B200_E_TIMEOUT, "device wait timed out%s%s")
-                          : ep_fail(MOE_B200_E_CUDA, "device bounds check rejected an index%s%s");
+        if (st.timeout) return ep_fail(MOE_B200_E_TIMEOUT, "device wait timed out%s%s");
+        if (st.bad_index == 2)
+            return ep_fail(MOE_B200_E_NCCL, "a rank's count record is from another step: the "
+                                            "exchange did not happen%s%s");
+        return ep_fail(MOE_B200_E_CUDA, "device bounds check rejected an index%s%s");
     }
     return MOE_B200_OK;
 }
 
-extern "C" int moe_b200_ep_counts(moe_b200_ep *ep, int *counts_all, int *slice_rows) {
+extern "C" int moe_b200_ep_counts(moe_b200_ep *ep, int *counts_all, int *recv_rows) {
     if (!ep) return ep_fail(MOE_B200_E_INVALID, "null ep%s%s");
     EP_CK(cudaSetDevice(ep->device));
     EP_CK(cudaDeviceSynchronize());
-    if (counts_all)
-        EP_CK(cudaMemcpy(counts_all, ep->counts_all, (size_t)ep->world * ep->w->E * 4,
-                         cudaMemcpyDeviceToHost));
-    if (slice_rows)
-        EP_CK(cudaMemcpy(slice_rows, ep->plan_q + 2 * ep->w->E, sizeof(int),
-                         cudaMemcpyDeviceToHost));   // off[E] == rows of this slice
+    if (counts_all) {
+        std::vector<int> r((size_t)ep->world * (ep->E + 1));
+        EP_CK(cudaMemcpy(r.data(), ep->recs, r.size() * 4, cudaMemcpyDeviceToHost));
+        for (int q = 0; q < ep->world; q++)
+            std::memcpy(counts_all + (size_t)q * ep->E, r.data() + (size_t)q * (ep->E + 1) + 1,
+                        (size_t)ep->E * 4);
+    }
+    if (recv_rows)
+        EP_CK(cudaMemcpy(recv_rows, ep->plan_q + 2 * ep->S, sizeof(int),
+                         cudaMemcpyDeviceToHost));   // off[S] == rows this rank received
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_ep_placement(const moe_b200_ep *ep, int *place) {
+    if (!ep || !place) return ep_fail(MOE_B200_E_INVALID, "null argument%s%s");
+    std::memcpy(place, ep->place.data(), ep->place.size() * sizeof(int));
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_ep_rebalance(moe_b200_ep *ep) {
+    if (!ep) return ep_fail(MOE_B200_E_INVALID, "null ep%s%s");
+    if (!ep->comm) return ep_fail(MOE_B200_E_STATE, "the group was aborted; destroy it%s%s");
+    EP_CK(cudaSetDevice(ep->device));
+    EP_CK(cudaDeviceSynchronize());
+    const int G = ep->world, E = ep->E, S = ep->S;
+    std::vector<int> counts((size_t)G * E), place((size_t)G * E);
+    int rc = moe_b200_ep_counts(ep, counts.data(), nullptr);
+    if (rc) return rc;
+    ep_place_greedy(counts.data(), G, E, S, ep->base.data(), place.data());
+    // fill this rank's newly assigned slots from the expert's first base
+    // holder, over NVLink with plain loads; base slots never change, so the
+    // sources stay valid while the other ranks copy too
+    moe_b200_weights *w = ep->w;
+    const size_t ug_slot = (size_t)2 * w->F_pad * w->d_pad, dn_slot = (size_t)w->d_pad * w->F_pad;
+    const int sms = device_sms(ep->device);
+    for (int e = 0; e < E; e++) {
+        const int j = place[(size_t)ep->rank * E + e];
+        if (j < 0 || j == ep->place[(size_t)ep->rank * E + e]) continue;
+        int src = -1;
+        for (int q = 0; q < G && src < 0; q++)
+            if (ep->base[(size_t)q * E + e] >= 0) src = q;
+        const int sj = ep->base[(size_t)src * E + e];
+        ep_slot_copy_kernel<<<sms * 4, 256, 0, ep->stream>>>(
+            reinterpret_cast<const float4 *>(ep->peer_ug[src] + sj * ug_slot),
+            reinterpret_cast<float4 *>(w->ug + j * ug_slot), ug_slot / 4);
+        ep_slot_copy_kernel<<<sms * 4, 256, 0, ep->stream>>>(
+            reinterpret_cast<const float4 *>(ep->peer_dn[src] + sj * dn_slot),
+            reinterpret_cast<float4 *>(w->dn + j * dn_slot), dn_slot / 4);
+        EP_CK(cudaGetLastError());
+    }
+    // slots this rank gives up hold nothing from now on
+    for (int e = 0; e < E; e++) {
+        const int was = ep->place[(size_t)ep->rank * E + e];
+        if (was >= 0 && place[(size_t)ep->rank * E + e] != was) w->slot_expert[was] = -1;
+    }
+    for (int e = 0; e < E; e++) {
+        const int j = place[(size_t)ep->rank * E + e];
+        if (j >= 0) w->slot_expert[j] = e;
+    }
+    ep->place = place;
+    if ((rc = upload_place(ep))) return rc;
+    // every rank has its replicas before anyone forwards with the new placement
+    if ((rc = ep_nccl(ep, nccl().AllReduce(ep->bar, ep->bar, 1, ncclInt32, ncclSum, ep->comm,
+                                           ep->stream), "ncclAllReduce(barrier)")))
+        return rc;
+    return ep_wait(ep, ep->stream);
+}
+
+extern "C" int moe_b200_ep_set_timeout(moe_b200_ep *ep, int timeout_ms) {
+    if (!ep || timeout_ms < 0) return ep_fail(MOE_B200_E_INVALID, "bad arguments%s%s");
+    ep->timeout_ms = timeout_ms;
     return MOE_B200_OK;
 }

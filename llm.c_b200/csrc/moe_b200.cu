@@ -100,7 +100,7 @@ static int grow(Buf &b, size_t bytes) {
     b.p = nullptr;
     b.cap = 0;
     size_t want = bytes + bytes / 8 + 256;
-    CK(cudaMalloc(&b.p, want));
+    CK(dev_alloc(&b.p, want));
     b.cap = want;
     return MOE_B200_OK;
 }
@@ -261,17 +261,24 @@ static int check_shape(int d, int F, int E, int k) {
     return MOE_B200_OK;
 }
 
-static int weights_alloc(Ctx *c, int d, int F, int E, int k, moe_b200_weights **out) {
+// A set of n_slots packed expert slots (n_slots = E: a full set, slot e =
+// expert e) with a router over all E experts.
+static int weights_alloc(Ctx *c, int d, int F, int E, int k, moe_b200_weights **out,
+                         int n_slots = -1) {
     moe_b200_weights *w = new moe_b200_weights();
     w->device = c->device;
     w->d = d; w->F = F; w->E = E; w->k = k;
     w->d_pad = round_up(d, 128);
     w->F_pad = round_up(F, 128);
     w->down_bn = (w->d_pad % 256 == 0) ? 256 : 128;
-    const size_t ug = (size_t)E * 2 * w->F_pad * w->d_pad, dn = (size_t)E * w->d_pad * w->F_pad;
-    cudaError_t e1 = cudaMalloc(&w->router, (size_t)d * E * 4);
-    cudaError_t e2 = cudaMalloc(&w->ug, ug * 4);
-    cudaError_t e3 = cudaMalloc(&w->dn, dn * 4);
+    const int S = n_slots < 0 ? E : n_slots;
+    w->n_slots = S;
+    w->slot_expert.resize(S);
+    for (int j = 0; j < S; j++) w->slot_expert[j] = n_slots < 0 ? j : -1;
+    const size_t ug = (size_t)S * 2 * w->F_pad * w->d_pad, dn = (size_t)S * w->d_pad * w->F_pad;
+    cudaError_t e1 = dev_alloc((void **)&w->router, (size_t)d * E * 4);
+    cudaError_t e2 = e1 == cudaSuccess ? dev_alloc((void **)&w->ug, ug * 4) : e1;
+    cudaError_t e3 = e2 == cudaSuccess ? dev_alloc((void **)&w->dn, dn * 4) : e2;
     if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess) {
         cudaFree(w->router); cudaFree(w->ug); cudaFree(w->dn);
         delete w;
@@ -279,11 +286,11 @@ static int weights_alloc(Ctx *c, int d, int F, int E, int k, moe_b200_weights **
         return fail(MOE_B200_E_NOMEM, "weights (%.2f GB) do not fit on device %d",
                     (double)(ug + dn) * 4 / 1e9, c->device);
     }
-    int rc = make_tmap(&w->tm_ug, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 256);
-    if (rc == 0) rc = make_tmap(&w->tm_dn, w->dn, (int64_t)E * w->d_pad, w->F_pad, w->down_bn);
-    if (rc == 0) rc = make_tmap(&w->tm_ug64, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 64);
-    if (rc == 0) rc = make_tmap(&w->tm_dn128, w->dn, (int64_t)E * w->d_pad, w->F_pad, 128);
-    if (rc == 0) rc = make_tmap(&w->tm_ug128, w->ug, (int64_t)E * 2 * w->F_pad, w->d_pad, 128);
+    int rc = make_tmap(&w->tm_ug, w->ug, (int64_t)S * 2 * w->F_pad, w->d_pad, 256);
+    if (rc == 0) rc = make_tmap(&w->tm_dn, w->dn, (int64_t)S * w->d_pad, w->F_pad, w->down_bn);
+    if (rc == 0) rc = make_tmap(&w->tm_ug64, w->ug, (int64_t)S * 2 * w->F_pad, w->d_pad, 64);
+    if (rc == 0) rc = make_tmap(&w->tm_dn128, w->dn, (int64_t)S * w->d_pad, w->F_pad, 128);
+    if (rc == 0) rc = make_tmap(&w->tm_ug128, w->ug, (int64_t)S * 2 * w->F_pad, w->d_pad, 128);
     if (rc) {
         cudaFree(w->router); cudaFree(w->ug); cudaFree(w->dn);
         delete w;
@@ -390,6 +397,115 @@ extern "C" int moe_b200_weights_synth(uint64_t seed, float w_std, int d, int F, 
     return MOE_B200_OK;
 }
 
+// ---- expert-parallel shards ----
+static int check_shard(int E, int n_local, const int *experts, int n_slots) {
+    if (n_local < 0 || n_slots < 1 || n_local > n_slots || n_slots > E || (n_local > 0 && !experts))
+        return fail(MOE_B200_E_INVALID, "shard: need 0 <= n_local <= n_slots <= E (%d, %d, %d)",
+                    n_local, n_slots, E);
+    std::vector<char> seen(E, 0);
+    for (int i = 0; i < n_local; i++) {
+        if (experts[i] < 0 || experts[i] >= E || seen[experts[i]])
+            return fail(MOE_B200_E_INVALID, "shard: expert id %d out of range or repeated",
+                        experts[i]);
+        seen[experts[i]] = 1;
+    }
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_weights_synth_shard(uint64_t seed, float w_std, int d, int F, int E,
+                                            int top_k, int n_local, const int *experts,
+                                            int n_slots, moe_b200_weights **out) {
+    if (!out) return fail(MOE_B200_E_INVALID, "null argument");
+    int rc = check_shape(d, F, E, top_k);
+    if (!rc) rc = check_shard(E, n_local, experts, n_slots);
+    if (rc) return rc;
+    Ctx *c;
+    if ((rc = get_ctx(-1, &c))) return rc;
+    moe_b200_weights *w;
+    if ((rc = weights_alloc(c, d, F, E, top_k, &w, n_slots))) return rc;
+    w->shard = 1;
+    CK(launch_synth(w->router, (size_t)d * E, seed, MOE_B200_STREAM_ROUTER, 0, w_std, c->stream));
+    for (int j = 0; j < n_local; j++) {
+        const int ex = experts[j];
+        float *ug = w->ug + (size_t)j * 2 * w->F_pad * w->d_pad;
+        float *dn = w->dn + (size_t)j * w->d_pad * w->F_pad;
+        CK(launch_synth_pack_expert(ug, dn, d, F, w->d_pad, w->F_pad, seed,
+                                    MOE_B200_STREAM_EXPERT(ex, 0), MOE_B200_STREAM_EXPERT(ex, 1),
+                                    MOE_B200_STREAM_EXPERT(ex, 2), w_std, c->stream));
+        w->slot_expert[j] = ex;
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    *out = w;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_weights_upload_shard(const float *W_router, const float *const *W_gate,
+                                             const float *const *W_up, const float *const *W_down,
+                                             int d, int F, int E, int top_k, int n_local,
+                                             const int *experts, int n_slots,
+                                             moe_b200_weights **out) {
+    if (!out || !W_router || (n_local > 0 && (!W_gate || !W_up || !W_down)))
+        return fail(MOE_B200_E_INVALID, "null argument");
+    int rc = check_shape(d, F, E, top_k);
+    if (!rc) rc = check_shard(E, n_local, experts, n_slots);
+    if (rc) return rc;
+    Ctx *c;
+    if ((rc = get_ctx(-1, &c))) return rc;
+    moe_b200_weights *w;
+    if ((rc = weights_alloc(c, d, F, E, top_k, &w, n_slots))) return rc;
+    w->shard = 1;
+    float *stage = nullptr;
+    const size_t dF = (size_t)d * F;
+    if (n_local > 0 && cudaMalloc(&stage, 3 * dF * 4) != cudaSuccess) {
+        cudaGetLastError();
+        moe_b200_weights_free(w);
+        return fail(MOE_B200_E_NOMEM, "upload staging does not fit");
+    }
+    rc = MOE_B200_OK;
+    if (cudaMemcpy(w->router, W_router, (size_t)d * E * 4, cudaMemcpyHostToDevice))
+        rc = fail(MOE_B200_E_CUDA, "router upload failed");
+    for (int j = 0; j < n_local && !rc; j++) {
+        if (!W_gate[j] || !W_up[j] || !W_down[j]) {
+            rc = fail(MOE_B200_E_INVALID, "local expert %d has a null matrix", j);
+            break;
+        }
+        if (cudaMemcpyAsync(stage, W_gate[j], dF * 4, cudaMemcpyHostToDevice, c->stream) ||
+            cudaMemcpyAsync(stage + dF, W_up[j], dF * 4, cudaMemcpyHostToDevice, c->stream) ||
+            cudaMemcpyAsync(stage + 2 * dF, W_down[j], dF * 4, cudaMemcpyHostToDevice, c->stream)) {
+            rc = fail(MOE_B200_E_CUDA, "local expert %d upload failed", j);
+            break;
+        }
+        if ((rc = moe::weights_put_expert(w, j, stage, c->stream))) break;
+        if (cudaStreamSynchronize(c->stream)) {
+            rc = fail(MOE_B200_E_CUDA, "repack failed: %s", cudaGetErrorString(cudaGetLastError()));
+            break;
+        }
+        w->slot_expert[j] = experts[j];
+    }
+    if (stage) cudaFree(stage);
+    if (rc) {
+        moe_b200_weights_free(w);
+        return rc;
+    }
+    *out = w;
+    return MOE_B200_OK;
+}
+
+extern "C" int moe_b200_weights_slots(const moe_b200_weights *w, int *n_slots, int *slot_expert) {
+    if (!w) return fail(MOE_B200_E_INVALID, "null weights");
+    if (n_slots) *n_slots = w->n_slots;
+    if (slot_expert)
+        for (int j = 0; j < w->n_slots; j++) slot_expert[j] = w->slot_expert[j];
+    return MOE_B200_OK;
+}
+
+int moe::weights_full(const moe_b200_weights *w) {
+    if (w && w->shard)
+        return fail(MOE_B200_E_INVALID,
+                    "an expert-parallel shard holds only some experts: use moe_b200_ep_*");
+    return MOE_B200_OK;
+}
+
 extern "C" int moe_b200_weights_free(moe_b200_weights *w) {
     if (!w) return MOE_B200_OK;
     cudaSetDevice(w->device);
@@ -422,6 +538,7 @@ extern "C" int moe_b200_weights_download(const moe_b200_weights *w, float *W_rou
     const size_t dF = (size_t)d * F;
     if (W_router) CK(cudaMemcpy(W_router, w->router, (size_t)d * w->E * 4, cudaMemcpyDeviceToHost));
     if (!W_gate && !W_up && !W_down) return MOE_B200_OK;
+    if ((rc = weights_full(w))) return rc;
     float *stage = nullptr;
     CK(cudaMalloc(&stage, 3 * dF * 4));
     for (int ex = 0; ex < w->E; ex++) {
@@ -531,8 +648,9 @@ static int forward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, co
                       int T, float *d_out, float *d_probs, int *d_ids,
                       const moe_b200_opts *opts, cudaStream_t s,
                       const BlockNorm *bn = nullptr) {
-    int rc = ensure_workspace(c, w, T);
+    int rc = weights_full(w);
     if (rc) return rc;
+    if ((rc = ensure_workspace(c, w, T))) return rc;
     const int E = w->E, k = w->k, d = w->d;
     const int rows = T * k;
     float *probs = d_probs ? d_probs : (float *)c->probs.p;
@@ -931,8 +1049,9 @@ extern "C" int moe_b200_grads_create(const moe_b200_weights *w, moe_b200_grads *
     if (!w || !out) return fail(MOE_B200_E_INVALID, "null argument");
     *out = nullptr;
     Ctx *c;
-    int rc = get_ctx(w->device, &c);
+    int rc = weights_full(w);
     if (rc) return rc;
+    if ((rc = get_ctx(w->device, &c))) return rc;
     auto *g = new moe_b200_grads();
     g->device = w->device;
     g->d = w->d; g->F = w->F; g->E = w->E;
@@ -994,8 +1113,9 @@ extern "C" int moe_b200_grads_free(moe_b200_grads *g) {
 static int backward_on(Ctx *c, const moe_b200_weights *w, const float *d_bias, const float *d_x,
                        int T, const float *d_dy, float aux_coef, float *d_dx, moe_b200_grads *g,
                        float *d_aux, const moe_b200_opts *opts, cudaStream_t s) {
-    int rc = ensure_workspace(c, w, T);
+    int rc = weights_full(w);
     if (rc) return rc;
+    if ((rc = ensure_workspace(c, w, T))) return rc;
     const int E = w->E, k = w->k, d = w->d;
     int path = pick_path(w, T, opts);
     if (path != MOE_B200_PATH_TF32) path = MOE_B200_PATH_FP32;

@@ -17,6 +17,9 @@ namespace moe {
 struct NcclApi {
     decltype(&ncclGetUniqueId) GetUniqueId = nullptr;
     decltype(&ncclCommInitRank) CommInitRank = nullptr;
+    decltype(&ncclCommInitRankConfig) CommInitRankConfig = nullptr;
+    decltype(&ncclCommAbort) CommAbort = nullptr;
+    decltype(&ncclCommFinalize) CommFinalize = nullptr;
     decltype(&ncclCommDestroy) CommDestroy = nullptr;
     decltype(&ncclCommGetAsyncError) CommGetAsyncError = nullptr;
     decltype(&ncclAllGather) AllGather = nullptr;
@@ -35,13 +38,20 @@ inline const NcclApi &nccl() {
         api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
         api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
         api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        api.CommInitRankConfig = reinterpret_cast<decltype(api.CommInitRankConfig)>(
+            dlsym(h, "ncclCommInitRankConfig"));
+        api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(dlsym(h, "ncclCommAbort"));
+        api.CommFinalize =
+            reinterpret_cast<decltype(api.CommFinalize)>(dlsym(h, "ncclCommFinalize"));
         api.CommGetAsyncError =
             reinterpret_cast<decltype(api.CommGetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
         api.AllGather = reinterpret_cast<decltype(api.AllGather)>(dlsym(h, "ncclAllGather"));
         api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(h, "ncclAllReduce"));
         api.GetErrorString =
             reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
-        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.CommGetAsyncError &&
+        api.ok = api.GetUniqueId && api.CommInitRank && api.CommInitRankConfig && api.CommAbort &&
+                 api.CommFinalize &&
+                 api.CommDestroy && api.CommGetAsyncError &&
                  api.AllGather && api.AllReduce && api.GetErrorString;
     });
     return api;

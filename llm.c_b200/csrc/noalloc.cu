@@ -116,6 +116,7 @@ extern "C" int moe_b200_forward_noalloc(const moe_b200_weights *w, const float *
         return set_last_error(MOE_B200_E_INVALID,
                               "moe_b200_forward_noalloc: x and out must be 16-byte aligned");
     if (T == 0) return MOE_B200_OK;
+    if (int rcf = weights_full(w)) return rcf;
     Scratch sc;
     const size_t need = carve(w, T, nullptr, &sc);
     if ((int64_t)T * w->k > (int64_t)1 << 30 || need > (size_t)MOE_B200_NOALLOC_SCRATCH_BYTES) {

@@ -36,15 +36,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait.  Returns false on timeout or when another role aborted.
+// Bounded wait (limit_ns of %globaltimer, kWaitNs unless given).  Returns
+// false on timeout or when another role aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          volatile int *abort_flag) {
+                                          volatile int *abort_flag,
+                                          uint64_t limit_ns = kWaitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (abort_flag && *abort_flag) return false;
-        if (globaltimer_ns() - t0 > kWaitNs) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 

@@ -12,9 +12,16 @@
 struct moe_b200_weights {
     int device;
     int d, F, E, k, d_pad, F_pad;
+    // Packed expert slots.  A full set has n_slots == E with slot e holding
+    // expert e.  An expert-parallel shard (shard = 1) holds only some
+    // experts: slot_expert[j] is the global id in slot j, or -1 for a spare
+    // slot that a hot expert's replica may fill later.  The router always
+    // covers all E experts.
+    int n_slots = 0, shard = 0;
+    std::vector<int> slot_expert;
     float *router;   // [d × E] row-major (host layout)
-    float *ug;       // [E][2F_pad × d_pad]
-    float *dn;       // [E][d_pad × F_pad]
+    float *ug;       // [n_slots][2F_pad × d_pad]
+    float *dn;       // [n_slots][d_pad × F_pad]
     CUtensorMap tm_ug;        // box {32, 256}
     CUtensorMap tm_dn;        // box {32, 256 or 128}
     CUtensorMap tm_ug64;      // box {32, 64}: decode up/gate (64 gate + 64 up rows)
@@ -35,6 +42,11 @@ __attribute__((visibility("hidden"))) cudaEvent_t *profile_events(int device);
 __attribute__((visibility("hidden"))) void note_forward(int device, int E, int launches, int path);
 // Number of SMs of `device` (0 if the device is unusable).
 __attribute__((visibility("hidden"))) int device_sms(int device);
+// cudaMalloc through the fault-injection hook (moe_b200_debug_fail_alloc).
+__attribute__((visibility("hidden"))) cudaError_t dev_alloc(void **p, size_t bytes);
+// MOE_B200_OK for a full expert set; MOE_B200_E_INVALID (with a message)
+// for an expert-parallel shard, which only the moe_b200_ep_* calls run.
+__attribute__((visibility("hidden"))) int weights_full(const moe_b200_weights *w);
 
 // ---- building blocks shared by the upload, the checkpoint loader and the
 // device decoder ----

@@ -182,6 +182,56 @@ class MoEWeights:
         return cls(h.value, d, F, E, top_k)
 
     @classmethod
+    def synth_shard(cls, seed: int, w_std: float, d: int, F: int, E: int, top_k: int,
+                    experts, n_slots: int) -> "MoEWeights":
+        """An expert-parallel shard: the listed experts (global ids) from the
+        seeded generator in the first slots, the rest spare slots."""
+        ex = np.ascontiguousarray(experts, np.int32)
+        L = lib()
+        L.moe_b200_weights_synth_shard.argtypes = [C.c_uint64, C.c_float, C.c_int, C.c_int,
+                                                   C.c_int, C.c_int, C.c_int, _ip, C.c_int,
+                                                   C.POINTER(_vp)]
+        h = _vp()
+        _check(L.moe_b200_weights_synth_shard(seed, w_std, d, F, E, top_k, len(ex), _i(ex),
+                                              n_slots, C.byref(h)), "moe_b200_weights_synth_shard")
+        return cls(h.value, d, F, E, top_k)
+
+    @classmethod
+    def upload_shard(cls, W_router, W_gate, W_up, W_down, top_k: int, experts,
+                     n_slots: int) -> "MoEWeights":
+        """An expert-parallel shard from host matrices: W_gate[i] etc. are
+        those of global expert experts[i]."""
+        W_router = np.ascontiguousarray(W_router, np.float32)
+        d, E = W_router.shape
+        F = np.asarray(W_gate[0]).shape[1] if len(W_gate) else 1
+        ex = np.ascontiguousarray(experts, np.int32)
+        n = len(ex)
+        keep = [np.ascontiguousarray(a, np.float32) for a in (*W_gate, *W_up, *W_down)]
+        g = (_fp * max(n, 1))(*[_f(a) for a in keep[0:n]])
+        u = (_fp * max(n, 1))(*[_f(a) for a in keep[n:2 * n]])
+        dn = (_fp * max(n, 1))(*[_f(a) for a in keep[2 * n:3 * n]])
+        L = lib()
+        L.moe_b200_weights_upload_shard.argtypes = [_fp, C.POINTER(_fp), C.POINTER(_fp),
+                                                    C.POINTER(_fp), C.c_int, C.c_int, C.c_int,
+                                                    C.c_int, C.c_int, _ip, C.c_int,
+                                                    C.POINTER(_vp)]
+        h = _vp()
+        _check(L.moe_b200_weights_upload_shard(_f(W_router), g, u, dn, d, F, E, top_k, n, _i(ex),
+                                               n_slots, C.byref(h)),
+               "moe_b200_weights_upload_shard")
+        return cls(h.value, d, F, E, top_k)
+
+    def slots(self) -> np.ndarray:
+        """Global expert id in each packed slot (-1 = empty spare)."""
+        L = lib()
+        L.moe_b200_weights_slots.argtypes = [_vp, _ip, _ip]
+        n = C.c_int()
+        _check(L.moe_b200_weights_slots(self.handle, C.byref(n), None), "moe_b200_weights_slots")
+        out = np.empty(n.value, np.int32)
+        _check(L.moe_b200_weights_slots(self.handle, None, _i(out)), "moe_b200_weights_slots")
+        return out
+
+    @classmethod
     def from_checkpoint(cls, path, layer: int) -> "MoEWeights":
         """Block `layer`'s experts (or dense FFN, as one expert) of an llm.c
         checkpoint (model_save format), streamed straight to the device."""
@@ -537,21 +587,49 @@ def ep_unique_id() -> bytes:
     return buf.raw
 
 
-def ep_partition(counts_all: np.ndarray, rank: int, capacity: int = 0):
-    """The slice plan of `rank` from the per-rank expert counts [world × E]:
-    (rows per expert in the slice, global base of rank's rows per expert,
-    slice start, slice size); `capacity` caps the rows of any slice."""
+def ep_split(counts_all: np.ndarray, place: np.ndarray, n_slots: int):
+    """The per-forward split of every expert's rows among its holders, from
+    the per-rank expert counts [world × E] and the placement [world × E]
+    (slot of expert e on rank q, -1 = not held).  Returns a dict of numpy
+    arrays: n_holders [E], holders [E × world], row_begin [E × (world+1)],
+    recv_offset [E × world], recv_rows [world], cost [world]."""
     c = np.ascontiguousarray(counts_all, np.int32)
+    pl = np.ascontiguousarray(place, np.int32)
     G, E = c.shape
-    cnt = np.empty(E, np.int32)
-    base = np.empty(E, np.int32)
-    lo, rows = C.c_longlong(), C.c_longlong()
+    nh = np.empty(E, np.int32)
+    hold = np.empty((E, G), np.int32)
+    beg = np.empty((E, G + 1), np.int32)
+    dst = np.empty((E, G), np.int32)
+    rows = np.empty(G, np.int64)
+    cost = np.empty(G, np.int64)
     L = lib()
-    L.moe_b200_ep_partition.argtypes = [_ip, C.c_int, C.c_int, C.c_int, C.c_longlong, _ip, _ip,
-                                        C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]
-    _check(L.moe_b200_ep_partition(_i(c), G, E, rank, capacity, _i(cnt), _i(base),
-                                   C.byref(lo), C.byref(rows)), "moe_b200_ep_partition")
-    return cnt, base, int(lo.value), int(rows.value)
+    L.moe_b200_ep_split.argtypes = [_ip, C.c_int, C.c_int, _ip, C.c_int, _ip, _ip, _ip, _ip,
+                                    C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]
+    ll = C.POINTER(C.c_longlong)
+    _check(L.moe_b200_ep_split(_i(c), G, E, _i(pl), n_slots, _i(nh), _i(hold), _i(beg), _i(dst),
+                               rows.ctypes.data_as(ll), cost.ctypes.data_as(ll)),
+           "moe_b200_ep_split")
+    return dict(n_holders=nh, holders=hold, row_begin=beg, recv_offset=dst, recv_rows=rows,
+                cost=cost)
+
+
+def ep_place(counts_all: np.ndarray, base_place: np.ndarray, n_slots: int) -> np.ndarray:
+    """The load-aware placement moe_b200_ep_rebalance adopts for these
+    counts: the base placement plus replicas in spare slots."""
+    c = np.ascontiguousarray(counts_all, np.int32)
+    b = np.ascontiguousarray(base_place, np.int32)
+    G, E = c.shape
+    out = np.empty((G, E), np.int32)
+    L = lib()
+    L.moe_b200_ep_place.argtypes = [_ip, C.c_int, C.c_int, _ip, C.c_int, _ip]
+    _check(L.moe_b200_ep_place(_i(c), G, E, _i(b), n_slots, _i(out)), "moe_b200_ep_place")
+    return out
+
+
+def ep_shard_experts(E: int, world: int, rank: int) -> list:
+    """The contiguous base shard of `rank`: experts [rank·E/world, (rank+1)·E/world)."""
+    lo, hi = rank * E // world, (rank + 1) * E // world
+    return list(range(lo, hi))
 
 
 class EP:
@@ -567,6 +645,9 @@ class EP:
         L.moe_b200_ep_forward.argtypes = [_vp, _fp, _fp, C.c_int, _fp, _fp, _ip,
                                           C.POINTER(Opts)]
         L.moe_b200_ep_counts.argtypes = [_vp, _ip, _ip]
+        L.moe_b200_ep_placement.argtypes = [_vp, _ip]
+        L.moe_b200_ep_rebalance.argtypes = [_vp]
+        L.moe_b200_ep_set_timeout.argtypes = [_vp, C.c_int]
         h = _vp()
         _check(L.moe_b200_ep_create(uid, rank, world, max_tokens, w.handle, C.byref(h)),
                "moe_b200_ep_create")
@@ -607,10 +688,40 @@ class EP:
         _check(lib().moe_b200_ep_counts(self.handle, _i(c), C.byref(rows)), "moe_b200_ep_counts")
         return c, int(rows.value)
 
+    def placement(self) -> np.ndarray:
+        """[world × E]: slot of expert e on rank q, -1 = not held."""
+        out = np.empty((self.world, self.w.E), np.int32)
+        _check(lib().moe_b200_ep_placement(self.handle, _i(out)), "moe_b200_ep_placement")
+        return out
+
+    def rebalance(self):
+        """Collective: replicate hot experts into spare slots from the last
+        forward's counts."""
+        _check(lib().moe_b200_ep_rebalance(self.handle), "moe_b200_ep_rebalance")
+
+    def set_timeout(self, ms: int):
+        _check(lib().moe_b200_ep_set_timeout(self.handle, int(ms)), "moe_b200_ep_set_timeout")
+
     def destroy(self):
         if self.handle:
             lib().moe_b200_ep_destroy(self.handle)
             self.handle = 0
+
+
+def debug_fail_alloc(n: int):
+    """Fail the n-th device allocation the library makes from now on (0: off)."""
+    L = lib()
+    L.moe_b200_debug_fail_alloc.argtypes = [C.c_int]
+    _check(L.moe_b200_debug_fail_alloc(int(n)), "moe_b200_debug_fail_alloc")
+
+
+def debug_wait_probe(limit_us: int, arrive: bool):
+    """A bounded mbarrier wait on the device; raises MoEError(E_TIMEOUT) when
+    nobody arrives."""
+    L = lib()
+    L.moe_b200_debug_wait_probe.argtypes = [C.c_int, C.c_int]
+    _check(L.moe_b200_debug_wait_probe(int(limit_us), 1 if arrive else 0),
+           "moe_b200_debug_wait_probe")
 
 
 def llmc_trace_enable(on: bool = True):
