@@ -86,6 +86,19 @@ struct Smem {
 // L1 lines.  Weights, which no step writes, use the read-only path.
 __device__ __forceinline__ float ldcg(const float *p) { return __ldcg(p); }
 
+// Programmatic dependent launch.  The stage kernels are launched so that
+// the next kernel's CTAs may start while the current one runs: each calls
+// pdl_trigger() on entry, loads what does not depend on the previous stage
+// (weight rows, RoPE factors, cached keys of earlier positions), and calls
+// pdl_wait() before it reads anything the previous stage wrote or writes
+// anything.  pdl_wait() returns once the previous kernel has completed and
+// its writes are visible; in a kernel launched without the dependency (the
+// step's first kernel, the persistent variant) both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -207,6 +220,7 @@ __device__ void qkv_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int 
         cr = __ldg(A.rope_cos + (size_t)pos * half + pi);
         sr = __ldg(A.rope_sin + (size_t)pos * half + pi);
     }
+    pdl_wait();
     if (layer == 0 && item == 0)
         for (int i = threadIdx.x; i < D.d; i += kThreads) A.x[i] = __ldg(src + i);
     rmsnorm_to_smem(src, Lp.rms_attn, D, S);
@@ -240,19 +254,32 @@ __device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chun
     const float *vc = A.vc + (size_t)layer * D.max_seq * D.kvd;
     float *dst = A.part + ((size_t)h * D.nchunk + chunk) * (D.hd + 2);
     const int g = h / (D.nh / D.nkv);
-    for (int i = threadIdx.x; i < D.hd; i += kThreads) S.qs[i] = ldcg(A.q + h * D.hd + i);
-    __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int PW = CH / (kThreads / 32);          // positions per warp
     float kv[PW][4];                                  // hd <= 128: 4 values per lane
+    // every key load in flight first; keys of earlier steps' positions do not
+    // depend on this step, only position pos (this step's token) does
 #pragma unroll
-    for (int t = 0; t < PW; t++) {                    // every key load in flight first
+    for (int t = 0; t < PW; t++) {
         const int jj = warp + t * (kThreads / 32);
+        const float *kr = kc + (size_t)(j0 + jj) * D.kvd + g * D.hd;
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+            kv[t][c] = (jj < n && j0 + jj != pos && lane + 32 * c < D.hd) ? ldcg(kr + lane + 32 * c)
+                                                                          : 0.0f;
+    }
+    pdl_wait();
+#pragma unroll
+    for (int t = 0; t < PW; t++) {
+        const int jj = warp + t * (kThreads / 32);
+        if (j0 + jj != pos) continue;
         const float *kr = kc + (size_t)(j0 + jj) * D.kvd + g * D.hd;
 #pragma unroll
         for (int c = 0; c < 4; c++)
             kv[t][c] = (jj < n && lane + 32 * c < D.hd) ? ldcg(kr + lane + 32 * c) : 0.0f;
     }
+    for (int i = threadIdx.x; i < D.hd; i += kThreads) S.qs[i] = ldcg(A.q + h * D.hd + i);
+    __syncthreads();
 #pragma unroll
     for (int t = 0; t < PW; t++) {
         const int jj = warp + t * (kThreads / 32);
@@ -315,6 +342,7 @@ __device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int 
     const int lane = threadIdx.x & 31, col = item * 32 + lane;
     MatvecPre P;                       // W_O rows do not wait for the attention output
     matvec32_preload(Lp.w_o, D.nq, D.d, col, col < D.d, P);
+    pdl_wait();
     for (int t = threadIdx.x; t < D.nq; t += kThreads) {
         const int h = t / D.hd, i = t % D.hd;
         const float *ph = A.part + (size_t)h * D.nchunk * (D.hd + 2);
@@ -370,6 +398,7 @@ __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, int layer, boo
         const int i = lane + 32 * u;
         w0[u] = (warp < Lp.E && i < D.d) ? __ldg(Lp.router + (size_t)i * Lp.E + warp) : 0.0f;
     }
+    pdl_wait();
     rmsnorm_to_smem(A.x, Lp.rms_ffn, D, S);
     if (publish)
         for (int i = threadIdx.x; i < D.d; i += kThreads) A.trace[(size_t)layer * 2 * D.d + i] = S.xn[i];
@@ -453,6 +482,7 @@ __device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int
     const int cw = warp / Lp.k, r = warp - cw * Lp.k;
     const int j = item * cols + cw;
     float y = 0.0f;
+    pdl_wait();
     if (cw < cols && j < D.d) {
         const int e = __ldcg(A.ids + r);
         const float4 *wr = reinterpret_cast<const float4 *>(Lp.dn + ((size_t)e * D.d_pad + j) * Lp.F_pad);
@@ -495,6 +525,7 @@ __device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S) {
     const int lane = threadIdx.x & 31, col = item * 32 + lane;
     MatvecPre P;
     matvec32_preload(A.lm_head, D.d, D.vocab, col, col < D.vocab, P);
+    pdl_wait();
     if (!normed) rmsnorm_to_smem(A.x, A.rms_final, D, S);
     const float v = matvec32(S.xn, A.lm_head, D.d, D.vocab, col, col < D.vocab, S, &P);
     if (threadIdx.x < 32 && col < D.vocab) A.logits[col] = v;
@@ -504,31 +535,37 @@ __device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S) {
 
 __global__ void __launch_bounds__(kThreads) qkv_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
     qkv_item(A, Lp, layer, A.state[0], A.state[1], blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) attn_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    pdl_trigger();
     const int pos = A.state[1];
     if ((int)blockIdx.y * CH > pos) return;
     attn_item(A, layer, pos, blockIdx.x, blockIdx.y, S);
 }
 __global__ void __launch_bounds__(kThreads) oproj_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    pdl_trigger();
     oproj_item(A, A.layers[layer], A.state[1], blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
     route_cta(A, Lp, layer, blockIdx.x == 0, S);
     upgate_item(A, Lp, blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) down_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    pdl_trigger();
     down_item(A, A.layers[layer], layer, blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) lmhead_kernel(StepArgs A) {
     __shared__ Smem S;
+    pdl_trigger();
     lmhead_item(A, blockIdx.x, false, S);
     if (blockIdx.x == 0 && threadIdx.x == 0) A.state[1] += 1;
 }
@@ -626,6 +663,7 @@ struct moe_b200_decoder {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
+    bool pdl = true;                             // programmatic dependent launch of the stages
 };
 
 namespace {
@@ -700,18 +738,32 @@ int enqueue_step(moe_b200_decoder *m) {
         m->launches = 1;
         return MOE_B200_OK;
     }
+    // every kernel but the step's first may start while its predecessor
+    // runs (programmatic dependent launch; the kernels order their reads and
+    // writes with griddepcontrol, see pdl_wait)
     int n = 0;
+    auto launch = [&](auto kernel, dim3 grid, auto... args) -> cudaError_t {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = (m->pdl && n > 0) ? 1 : 0;
+        n++;
+        return cudaLaunchKernelEx(&cfg, kernel, args...);
+    };
     for (int l = 0; l < m->L; l++) {
         const moe_b200_weights *w = m->layers[l].ffn;
-        qkv_kernel<<<ceil_div(D.qkv, 32), kThreads, 0, s>>>(A, l);
-        attn_kernel<<<dim3(D.nh, D.nchunk), kThreads, 0, s>>>(A, l);
-        oproj_kernel<<<ceil_div(D.d, 32), kThreads, 0, s>>>(A, l);
-        upgate_kernel<<<w->k * ceil_div(w->F, 8), kThreads, 0, s>>>(A, l);
-        down_kernel<<<ceil_div(D.d, down_cols(w->k)), kThreads, 0, s>>>(A, l);
-        n += 5;
+        DCK(launch(qkv_kernel, dim3(ceil_div(D.qkv, 32)), A, l));
+        DCK(launch(attn_kernel, dim3(D.nh, D.nchunk), A, l));
+        DCK(launch(oproj_kernel, dim3(ceil_div(D.d, 32)), A, l));
+        DCK(launch(upgate_kernel, dim3(w->k * ceil_div(w->F, 8)), A, l));
+        DCK(launch(down_kernel, dim3(ceil_div(D.d, down_cols(w->k))), A, l));
     }
-    lmhead_kernel<<<ceil_div(D.vocab, 32), kThreads, 0, s>>>(A);
-    n += 1;
+    DCK(launch(lmhead_kernel, dim3(ceil_div(D.vocab, 32)), A));
     DCK(cudaGetLastError());
     m->launches = n;
     return MOE_B200_OK;
@@ -748,6 +800,7 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
     moe_b200_decoder *m = new moe_b200_decoder();
     cudaGetDevice(&m->device);
     m->flags = flags;
+    if (const char *p = std::getenv("MOE_B200_DECODER_PDL")) m->pdl = std::atoi(p) != 0;
     Dims &D = m->D;
     D.d = d; D.d_pad = round_up(d, 128); D.nh = nh; D.nkv = nkv; D.hd = hd; D.nq = nh * hd;
     D.kvd = nkv * hd; D.qkv = D.nq + 2 * D.kvd; D.vocab = c.vocab_size; D.max_seq = max_seq;
