@@ -68,6 +68,7 @@ struct StepArgs {
     unsigned *bar;                     // grid barrier counter (zeroed before each step)
     int *err;                          // barrier timeout flag
     float *trace;                      // [L][2][d]: pre-FFN x_norm and FFN output per layer
+    int pdl_early;                     // stage kernels: let the next kernel launch on entry
 };
 
 struct Smem {
@@ -87,11 +88,12 @@ struct Smem {
 __device__ __forceinline__ float ldcg(const float *p) { return __ldcg(p); }
 
 // Programmatic dependent launch.  The stage kernels are launched so that
-// the next kernel's CTAs may start while the current one runs: each calls
-// pdl_trigger() on entry, loads what does not depend on the previous stage
-// (weight rows, RoPE factors, cached keys of earlier positions), and calls
-// pdl_wait() before it reads anything the previous stage wrote or writes
-// anything.  pdl_wait() returns once the previous kernel has completed and
+// the next kernel's CTAs may start before the current one has finished (as
+// its CTAs exit, or, with pdl_early, as soon as they all started: each
+// calls pdl_trigger() on entry); a kernel loads what does not depend on the
+// previous stage (weight rows, RoPE factors, cached keys of earlier
+// positions) and calls pdl_wait() before it reads anything the previous
+// stage wrote or writes anything.  pdl_wait() returns once the previous kernel has completed and
 // its writes are visible; in a kernel launched without the dependency (the
 // step's first kernel, the persistent variant) both are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -535,37 +537,37 @@ __device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S) {
 
 __global__ void __launch_bounds__(kThreads) qkv_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
-    pdl_trigger();
+    if (A.pdl_early) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
     qkv_item(A, Lp, layer, A.state[0], A.state[1], blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) attn_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
-    pdl_trigger();
+    if (A.pdl_early) pdl_trigger();
     const int pos = A.state[1];
     if ((int)blockIdx.y * CH > pos) return;
     attn_item(A, layer, pos, blockIdx.x, blockIdx.y, S);
 }
 __global__ void __launch_bounds__(kThreads) oproj_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
-    pdl_trigger();
+    if (A.pdl_early) pdl_trigger();
     oproj_item(A, A.layers[layer], A.state[1], blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
-    pdl_trigger();
+    if (A.pdl_early) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
     route_cta(A, Lp, layer, blockIdx.x == 0, S);
     upgate_item(A, Lp, blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) down_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
-    pdl_trigger();
+    if (A.pdl_early) pdl_trigger();
     down_item(A, A.layers[layer], layer, blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) lmhead_kernel(StepArgs A) {
     __shared__ Smem S;
-    pdl_trigger();
+    if (A.pdl_early) pdl_trigger();
     lmhead_item(A, blockIdx.x, false, S);
     if (blockIdx.x == 0 && threadIdx.x == 0) A.state[1] += 1;
 }
@@ -663,7 +665,10 @@ struct moe_b200_decoder {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
-    bool pdl = true;                             // programmatic dependent launch of the stages
+    // programmatic dependent launch of the stage kernels: 0 off, 1 each kernel
+    // lets the next one launch on entry, 2 the next one launches as the
+    // current one's CTAs exit
+    int pdl = 2;
 };
 
 namespace {
@@ -711,6 +716,7 @@ StepArgs step_args(const moe_b200_decoder *m) {
     A.x = m->x; A.q = m->q; A.part = m->part; A.h = m->h; A.logits = m->logits; A.wts = m->wts;
     A.state = m->state; A.ids = m->ids; A.bar = m->bar; A.err = m->err;
     A.trace = m->trace;
+    A.pdl_early = m->pdl == 1;
     return A;
 }
 
@@ -751,7 +757,7 @@ int enqueue_step(moe_b200_decoder *m) {
         cfg.blockDim = dim3(kThreads, 1, 1);
         cfg.stream = s;
         cfg.attrs = attr;
-        cfg.numAttrs = (m->pdl && n > 0) ? 1 : 0;
+        cfg.numAttrs = (m->pdl != 0 && n > 0) ? 1 : 0;
         n++;
         return cudaLaunchKernelEx(&cfg, kernel, args...);
     };
@@ -800,7 +806,7 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
     moe_b200_decoder *m = new moe_b200_decoder();
     cudaGetDevice(&m->device);
     m->flags = flags;
-    if (const char *p = std::getenv("MOE_B200_DECODER_PDL")) m->pdl = std::atoi(p) != 0;
+    if (const char *p = std::getenv("MOE_B200_DECODER_PDL")) m->pdl = std::atoi(p);
     Dims &D = m->D;
     D.d = d; D.d_pad = round_up(d, 128); D.nh = nh; D.nkv = nkv; D.hd = hd; D.nq = nh * hd;
     D.kvd = nkv * hd; D.qkv = D.nq + 2 * D.kvd; D.vocab = c.vocab_size; D.max_seq = max_seq;

@@ -99,6 +99,7 @@ def _worker(rank, world, port, q):
                     results.append(dict(rank=rank, case=(T, d, E), placement=placement.tolist(),
                                         slots=shard.slots().tolist(), mine=mine,
                                         counts=counts_all.tolist(), n_slots=n_slots))
+            ep.forward(xs, p.bias)                # every rank's full share, then the counts
             counts_all, rows = ep.counts()
             results.append(dict(rank=rank, case=(T, d, E), counts_total=int(counts_all.sum()),
                                 want_total=T * k, recv_rows=rows))
