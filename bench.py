@@ -933,7 +933,8 @@ def main():
     stages_by_rank = None
     if dist is not None:
         stages_by_rank = [None] * world
-        dist.all_gather_object(stages_by_rank, {"stages": stage_avg, "slice_rows": slice_rows})
+        dist.all_gather_object(stages_by_rank, {"stages": stage_avg, "slice_rows": slice_rows,
+                                                "sm_mhz": clk.summary().get("sm_mhz")})
     up_ms = stage_avg["upgate"]
     touched = int(np.count_nonzero(counts))
     traffic = None
@@ -1004,6 +1005,16 @@ def main():
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    # time x median SM clock: compares runs at different power-capped clocks
+    mhz = [r["sm_mhz"] for r in stages_by_rank if r.get("sm_mhz")] if stages_by_rank else \
+        ([line["clocks"]["sm_mhz"]] if line["clocks"].get("sm_mhz") else [])
+    if mhz:
+        med = float(statistics.median(mhz))
+        line["clock_normalized"] = {"sm_mhz_median_over_ranks": med,
+                                    "ms_x_sm_ghz": ms * med / 1000.0,
+                                    "what": "ms per step x median SM clock (GHz) during the timed "
+                                            "region; equal work at equal efficiency gives equal "
+                                            "values at any clock"}
     if block is not None:
         line["block_ffn"] = block
     if placement is not None:

@@ -259,8 +259,9 @@ __device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chun
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int PW = CH / (kThreads / 32);          // positions per warp
     float kv[PW][4];                                  // hd <= 128: 4 values per lane
-    // every key load in flight first; keys of earlier steps' positions do not
-    // depend on this step, only position pos (this step's token) does
+    // every key and value load in flight first; the cache rows of earlier
+    // steps' positions do not depend on this step, only position pos (this
+    // step's token) does
 #pragma unroll
     for (int t = 0; t < PW; t++) {
         const int jj = warp + t * (kThreads / 32);
@@ -270,6 +271,18 @@ __device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chun
             kv[t][c] = (jj < n && j0 + jj != pos && lane + 32 * c < D.hd) ? ldcg(kr + lane + 32 * c)
                                                                           : 0.0f;
     }
+    // the value pass's positions for this thread: groups of hd threads split
+    // the chunk (at most CH / (kThreads / hd) = 32 positions each for hd <= 128)
+    constexpr int VMAX = 32;
+    const int groups = kThreads / D.hd, gi = threadIdx.x / D.hd, i = threadIdx.x - gi * D.hd;
+    const int per = (n + groups - 1) / groups;
+    const int jlo = gi * per, jhi = min(n, jlo + per);
+    const float *vcol = vc + (size_t)j0 * D.kvd + g * D.hd + i;
+    float vpre[VMAX];
+#pragma unroll
+    for (int u = 0; u < VMAX; u++)
+        vpre[u] = (gi < groups && jlo + u < jhi && j0 + jlo + u != pos)
+                      ? ldcg(vcol + (size_t)(jlo + u) * D.kvd) : 0.0f;
     pdl_wait();
 #pragma unroll
     for (int t = 0; t < PW; t++) {
@@ -308,22 +321,16 @@ __device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chun
     }
     __syncthreads();
     // the exp-weighted V sum: the chunk's positions are split over groups of
-    // hd threads (every thread of the CTA busy, one round of loads for a
-    // 64-position chunk), the group partials added in group order
-    const int groups = kThreads / D.hd, gi = threadIdx.x / D.hd, i = threadIdx.x - gi * D.hd;
-    const int per = (n + groups - 1) / groups;
+    // hd threads (every thread of the CTA busy; the values were loaded before
+    // the wait, only position pos's after it), the sum in position order, the
+    // group partials added in group order
     if (gi < groups) {
-        const int jlo = gi * per, jhi = min(n, jlo + per);
-        const float *vcol = vc + (size_t)j0 * D.kvd + g * D.hd + i;
         float o = 0.0f;
-        for (int jb = jlo; jb < jhi; jb += 16) {      // 16 value loads in flight
-            float vv[16];
 #pragma unroll
-            for (int u = 0; u < 16; u++)
-                vv[u] = jb + u < jhi ? ldcg(vcol + (size_t)(jb + u) * D.kvd) : 0.0f;
-#pragma unroll
-            for (int u = 0; u < 16; u++)
-                if (jb + u < jhi) o = __fmaf_rn(S.sc[jb + u], vv[u], o);
+        for (int u = 0; u < VMAX; u++) {
+            if (jlo + u >= jhi) break;
+            const float v = j0 + jlo + u == pos ? ldcg(vcol + (size_t)(jlo + u) * D.kvd) : vpre[u];
+            o = __fmaf_rn(S.sc[jlo + u], v, o);
         }
         S.red[gi * D.hd + i] = o;
     }
@@ -430,6 +437,19 @@ __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, int layer, boo
             for (int r = 0; r < Lp.k; r++) { A.ids[r] = S.sel[r]; A.wts[r] = S.w[r]; }
     }
     __syncthreads();
+}
+
+// After the routing (S.sel valid): the down rows of the selected experts
+// into L2, one 128-byte line per thread of the stage (thread t of nthreads),
+// so that the down stage's weight loads hit L2.
+__device__ __forceinline__ void prefetch_down(const StepArgs &A, const LayerPtrs &Lp, int t,
+                                              int nthreads, const Smem &S) {
+    const size_t lines = (size_t)A.D.d_pad * Lp.F_pad / 32;     // per expert
+    for (size_t l = t; l < lines * Lp.k; l += nthreads) {
+        const int r = (int)(l / lines);
+        const float *p = Lp.dn + (size_t)S.sel[r] * A.D.d_pad * Lp.F_pad + (l - r * lines) * 32;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    }
 }
 
 // 5: 8 hidden units of rank r: one warp per unit f, the gate and up rows of
@@ -558,6 +578,7 @@ __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer)
     if (A.pdl_early) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
     route_cta(A, Lp, layer, blockIdx.x == 0, S);
+    prefetch_down(A, Lp, blockIdx.x * kThreads + threadIdx.x, gridDim.x * kThreads, S);
     upgate_item(A, Lp, blockIdx.x, S);
 }
 __global__ void __launch_bounds__(kThreads) down_kernel(StepArgs A, int layer) {
@@ -617,6 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs A) {
         const int n_ug = Lp.k * ((Lp.F + 7) / 8);
         if (b < n_ug) {
             route_cta(A, Lp, l, b == 0, S);
+            prefetch_down(A, Lp, b * kThreads + threadIdx.x, min(G, n_ug) * kThreads, S);
             for (int it = b; it < n_ug; it += G) upgate_item(A, Lp, it, S);
         }
         if (!grid_barrier(A, ++phase * G, S)) return;

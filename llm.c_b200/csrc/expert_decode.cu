@@ -39,16 +39,6 @@
 //   * The converter warps wait for everything else the step needs — the
 //     weight tile, the token tile, a free TMEM partial slot, a free W_small
 //     slot — convert, and signal ready[step % NS] once.
-// Shared-memory traffic.  A K step moves ~88 KB through the SM's shared
-// memory when the MMA reads the weights from it: 32 KB of TMA writes
-// (weights, tokens), 16 KB read by the converter, 16 KB of A and 24 KB of B
-// operand reads; at 128 B/clk that is ~690 cycles, the ~700 measured per
-// step.  So in the single-CTA 3xTF32 kernel the converter writes the weight
-// tile itself into tensor memory beside W_small (one thread per row, the
-// values as loaded: the tensor core reads their TF32 bits, as it does from
-// shared memory), and both MMAs take A from tensor memory: 72 KB per step.
-// Tensor memory then holds 4 slots of [W | W_small] (64 columns each) after
-// the two 128-column partial slots.
 // Loads have long latencies under load (~2 us from HBM for the weights,
 // ~0.7 us from L2 for the token rows), so the shared-memory rings are as
 // deep as fits: weights W 8 × 16 KB (own producer warp, up to 8 steps
@@ -94,11 +84,6 @@ constexpr int SLOT_COLS = 2 * NTOK;
 constexpr uint32_t WS_COL0 = NSLOT * SLOT_COLS;
 constexpr uint32_t TMEM_COLS = 512;
 static_assert(WS_COL0 + NS * BK <= TMEM_COLS, "TMEM columns");
-// single-CTA 3xTF32: slots of [W | W_small] in tensor memory (A operands)
-constexpr int NSW = 4;
-constexpr int WSLOT_COLS = 2 * BK;
-static_assert(WS_COL0 + NSW * WSLOT_COLS <= TMEM_COLS, "TMEM columns (W slots)");
-static_assert(R % NSW == 0, "W slot ring");
 constexpr int UPS_LD = NTOK + 1;        // padded row of the up hand-off buffer
 constexpr int RING_BYTES = NW * A_BYTES + NX * X_BYTES;
 constexpr int SMEM_BYTES = RING_BYTES + 64 * UPS_LD * 4 + 1024 + 512;
@@ -185,7 +170,6 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
          DecArgs a)
 {
     static_assert(!(PAIR && ONEPASS), "ONEPASS runs on single CTAs");
-    constexpr bool TMEM_A = !PAIR && !ONEPASS;   // both A operands from tensor memory
     constexpr int MM = PAIR ? 2 * MW : MW;                  // MMA M (weight rows per block)
     constexpr uint32_t IDESC_N128 = idesc_tf32(MM, 2 * NTOK);
     constexpr uint32_t IDESC_N64 = idesc_tf32(MM, NTOK);
@@ -361,11 +345,6 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                             if (PAIR) {
                                 mma_tf32_pair(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
                                 mma_tf32_ts_pair(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
-                            } else if (TMEM_A) {
-                                // [W | W_small] slot j % NSW: 8 columns per K slice
-                                const uint32_t tw = ts0 + (uint32_t)((j % NSW) * WSLOT_COLS);
-                                mma_tf32_ts(d, tw + 8 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
-                                mma_tf32_ts(d, tw + BK + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
                             } else {
                                 mma_tf32(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
                                 mma_tf32_ts(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
@@ -415,8 +394,6 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
             }
             if (!ok) set_abort(13);
         } else {
-            constexpr int SLOTS = TMEM_A ? NSW : NS;      // TMEM operand slots
-            Ring<NSW> rt;                             // TMEM_A: [W | W_small] slot
             for (int n = 0; n < nsteps; n++) {
                 if (!mbar_wait(&wfull[rw.i], rw.ph, abort_flag) ||
                     (cw == 2 && !mbar_wait(&xfull[rx.i], rx.ph, abort_flag)) ||
@@ -424,31 +401,23 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                     ok = false;
                     break;
                 }
-                if (n >= SLOTS) {                     // the slot's last reader finished
+                if (n >= NS) {                        // the W_small slot's last reader finished
                     if (!mbar_wait(&done[rlag.i], rlag.ph, abort_flag)) { ok = false; break; }
                     rlag.next();
                 }
                 // this thread's weight row: its 128 bytes, 16-byte chunks
                 // permuted by the 128-byte swizzle (chunk c sits at c ^ (row % 8))
                 const uint8_t *wrow = sW + rw.i * A_BYTES + crow * 128;
-                float ws[BK], wv[BK];
+                float ws[BK];
     #pragma unroll
                 for (int c = 0; c < BK / 4; c++) {
                     const float4 v = *reinterpret_cast<const float4 *>(wrow + ((c ^ (crow & 7)) << 4));
-                    wv[4 * c + 0] = v.x; wv[4 * c + 1] = v.y;
-                    wv[4 * c + 2] = v.z; wv[4 * c + 3] = v.w;
                     ws[4 * c + 0] = tf32_residual(v.x);
                     ws[4 * c + 1] = tf32_residual(v.y);
                     ws[4 * c + 2] = tf32_residual(v.z);
                     ws[4 * c + 3] = tf32_residual(v.w);
                 }
-                if constexpr (TMEM_A) {
-                    const uint32_t tw = ws_lane + WS_COL0 + (uint32_t)(rt.i * WSLOT_COLS);
-                    tmem_st32x2(tw, wv, tw + BK, ws);
-                    rt.next();
-                } else {
-                    tmem_st32(ws_lane + WS_COL0 + (uint32_t)(rs.i * BK), ws);
-                }
+                tmem_st32(ws_lane + WS_COL0 + (uint32_t)(rs.i * BK), ws);
                 tc_fence_before();
                 if (PAIR) mbar_arrive_cluster(mapa(smem_u32(&ready[rs.i]), 0));
                 else mbar_arrive(&ready[rs.i]);

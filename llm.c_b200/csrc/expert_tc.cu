@@ -28,13 +28,22 @@
 // before it frees TMEM and exits.
 #include "tc_common.cuh"
 
+#include <cstdlib>
+
 namespace moe {
 namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 32;          // fp32 elements per K step = 128 bytes
 constexpr int STAGES = 4;
-constexpr int GM = 8;           // m-tiles per raster group
+// m-tiles per raster group (defaults; MOE_B200_TC_GROUP_M_UPGATE / _DOWN).
+// Up/gate (K = d): a group's activation rows are small (16 × 128 rows × d),
+// so 16 m-tiles halve the weight passes of the large experts against 8
+// (c5: 114 passes of the gate/up weights per launch instead of 175, ~35 %
+// less DRAM traffic, ~1 % faster, measured).  Down (K = F, rows 3.5× wider)
+// keeps 8, so a group's rows stay well inside L2.
+constexpr int GM = 8;
+constexpr int GM_UPGATE = 16;
 constexpr int EPI_WARPS = 8;   // two per TMEM lane quarter, each on half the columns
 constexpr int kThreads = 64 + 32 * EPI_WARPS;
 constexpr int A_BYTES = BM * BK * 4;
@@ -45,8 +54,10 @@ struct TileCoord {
 };
 
 // tile -> (expert, m-tile within expert, n-tile); tiles of expert e are
-// [mt128[e]*NT, mt128[e+1]*NT), grouped by GM m-tiles, n-tiles inside.
-__device__ __forceinline__ TileCoord decode_tile(int tile, const int *mt, int E, int NT) {
+// [mt128[e]*NT, mt128[e+1]*NT), grouped by gm m-tiles, n-tiles inside.
+// Each group reads all of the expert's weight tiles once, so an expert of
+// mt m-tiles streams its weights ceil(mt / gm) times.
+__device__ __forceinline__ TileCoord decode_tile(int tile, const int *mt, int E, int NT, int gm) {
     int lo = 0, hi = E;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -57,11 +68,11 @@ __device__ __forceinline__ TileCoord decode_tile(int tile, const int *mt, int E,
     const int m0 = __ldg(mt + lo);
     const int mcount = __ldg(mt + lo + 1) - m0;
     const int l = tile - m0 * NT;
-    const int g = l / (GM * NT);
-    const int rem = l - g * GM * NT;
-    const int gcount = min(GM, mcount - g * GM);
+    const int g = l / (gm * NT);
+    const int rem = l - g * gm * NT;
+    const int gcount = min(gm, mcount - g * gm);
     c.ni = rem / gcount;
-    c.ml = g * GM + (rem - c.ni * gcount);
+    c.ml = g * gm + (rem - c.ni * gcount);
     return c;
 }
 
@@ -71,7 +82,7 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 const int *__restrict__ plan, int E, int num_kb, int b_rows_per_expert,
                 int NT, float *__restrict__ out, int ldo, DeviceStatus *status,
                 float *const *__restrict__ out_ptrs, const int2 *__restrict__ ret,
-                float *__restrict__ gu_save)
+                float *__restrict__ gu_save, int gm)
 {
     // gu_save (SWIGLU, optional): the gate and up pre-activations [rows × 2·ldo]
     // in the weights' row order (per 128 columns: 128 gate, then 128 up), for
@@ -139,7 +150,7 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             uint32_t issued = 0, issued_phase = 0;    // bit s: stage s loaded / its phase
             bool ok = true;
             for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-                const TileCoord c = decode_tile(tile, mt, E, NT);
+                const TileCoord c = decode_tile(tile, mt, E, NT, gm);
                 const int a_row = __ldg(off + c.e) + c.ml * BM;
                 const int b_row = c.e * b_rows_per_expert + c.ni * BN;
                 for (int kb = 0; kb < num_kb; kb++) {
@@ -201,7 +212,7 @@ tc_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
-            const TileCoord c = decode_tile(tile, mt, E, NT);
+            const TileCoord c = decode_tile(tile, mt, E, NT, gm);
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
                 if (!*abort_flag) { *abort_flag = 1; atomicExch(&status->timeout, 3); }
                 break;
@@ -319,6 +330,22 @@ cudaError_t tc_set_attributes() {
 
 static int tile_bound(int rows_bound, int E) { return ceil_div(rows_bound, tc::BM) + E; }
 
+// m-tiles per raster group of the up/gate and of the down GEMM: the
+// environment variables MOE_B200_TC_GROUP_M_UPGATE / _DOWN (1..64) when set,
+// else tc::GM_UPGATE / tc::GM
+static int group_m(bool upgate) {
+    static const int gm[2] = {[] {
+        const char *p = std::getenv("MOE_B200_TC_GROUP_M_DOWN");
+        const int v = p ? std::atoi(p) : 0;
+        return v >= 1 && v <= 64 ? v : tc::GM;
+    }(), [] {
+        const char *p = std::getenv("MOE_B200_TC_GROUP_M_UPGATE");
+        const int v = p ? std::atoi(p) : 0;
+        return v >= 1 && v <= 64 ? v : tc::GM_UPGATE;
+    }()};
+    return gm[upgate ? 1 : 0];
+}
+
 cudaError_t launch_tc_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, const int *plan,
                              int E, int rows_bound, int num_sms, DeviceStatus *status,
                              cudaStream_t s, float *gu_save)
@@ -328,7 +355,7 @@ cudaError_t launch_tc_upgate(const TcGemm &g, int d_pad, int F_pad, float *h, co
     const int grid = max(1, min(num_sms, bound));
     tc::tc_grouped_gemm<256, true><<<grid, tc::kThreads, tc::smem_bytes<256>(), s>>>(
         g.tmA, g.tmB, plan, E, d_pad / tc::BK, 2 * F_pad, NT, h, F_pad, status, nullptr, nullptr,
-        gu_save);
+        gu_save, group_m(true));
     return cudaGetLastError();
 }
 
@@ -343,11 +370,11 @@ cudaError_t launch_tc_down(const TcGemm &g, int F_pad, int d_pad, int bn, float 
     if (bn == 256)
         tc::tc_grouped_gemm<256, false><<<grid, tc::kThreads, tc::smem_bytes<256>(), s>>>(
             g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status, y_ptrs, ret,
-            nullptr);
+            nullptr, group_m(false));
     else
         tc::tc_grouped_gemm<128, false><<<grid, tc::kThreads, tc::smem_bytes<128>(), s>>>(
             g.tmA, g.tmB, plan, E, F_pad / tc::BK, d_pad, NT, y, d_pad, status, y_ptrs, ret,
-            nullptr);
+            nullptr, group_m(false));
     return cudaGetLastError();
 }
 
