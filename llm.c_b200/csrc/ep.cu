@@ -54,11 +54,18 @@ namespace {
 constexpr int kMaxWorld = 64;
 constexpr int kTileRows = 128;
 
-// Estimated GEMM cost of an expert segment of n rows on one rank: 2 units
-// per 128-row m-tile, plus 1 for the segment (its partially filled last
-// tile and its own pass over the expert's weights).
+// Estimated GEMM cost of an expert segment of t 128-row m-tiles on one
+// rank, in half-m-tiles of tensor-core time: 2 per m-tile, but at least 2
+// m-tiles' worth, plus 2.  A segment streams the expert's weights at least
+// once, and on B200 that takes ~1.6 m-tiles of TF32 tensor time whatever
+// the shape (3·d·F·4 bytes at the HBM rate against 128 rows · 6·d·F flops
+// at the TF32 rate); a 2-GPU c5 run measured a segment of one partial tile
+// at ~3.3 m-tiles, so the floor is 2 m-tiles and the constant 2 more.
+__host__ __device__ inline long long seg_cost_tiles(long long t) {
+    return t > 0 ? 2 * (t > 2 ? t : 2) + 2 : 0;
+}
 __host__ __device__ inline long long seg_cost(long long n) {
-    return n > 0 ? 2 * ((n + kTileRows - 1) / kTileRows) + 1 : 0;
+    return seg_cost_tiles((n + kTileRows - 1) / kTileRows);
 }
 }  // namespace
 
@@ -78,8 +85,9 @@ __host__ __device__ inline long long seg_cost(long long n) {
 //   rows_q[q], load[q]    receive rows and estimated cost per rank (or null)
 // Single-holder experts go whole to their holder.  Replicated experts, the
 // most rows first, are cut into 128-row tiles, each given to the holder
-// whose cost after taking it is lowest (ties: lower rank), then every
-// holder takes its count of tiles as one contiguous range in holder order.
+// whose cost after taking it (seg_cost_tiles of its new tile count) is
+// lowest (ties: lower rank), then every holder takes its count of tiles as
+// one contiguous range in holder order.
 // Returns 1 if an expert with rows has no holder, else 0.
 // ---------------------------------------------------------------------
 __host__ __device__ inline int ep_split(const int *C, int ldc, int G, int E, const int *place,
@@ -119,7 +127,8 @@ __host__ __device__ inline int ep_split(const int *C, int ldc, int G, int E, con
             int best = 0;
             long long best_c = 0;
             for (int i = 0; i < n; i++) {
-                const long long c = load[hold[e * G + i]] + 2 + (tiles_of[i] == 0 ? 1 : 0);
+                const long long c = load[hold[e * G + i]] + seg_cost_tiles(tiles_of[i] + 1) -
+                                    seg_cost_tiles(tiles_of[i]);
                 if (i == 0 || c < best_c) { best = i; best_c = c; }
             }
             load[hold[e * G + best]] = best_c;

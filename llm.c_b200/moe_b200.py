@@ -627,9 +627,11 @@ def ep_place(counts_all: np.ndarray, base_place: np.ndarray, n_slots: int) -> np
 
 
 def ep_shard_experts(E: int, world: int, rank: int) -> list:
-    """The contiguous base shard of `rank`: experts [rank·E/world, (rank+1)·E/world)."""
-    lo, hi = rank * E // world, (rank + 1) * E // world
-    return list(range(lo, hi))
+    """The base shard of `rank`: experts rank, rank + world, rank + 2·world, ...
+    Strided, so that every rank gets a mix of popular and rare experts when
+    popularity falls with the expert index (the rare ones each cost a pass
+    over their weights for a handful of rows)."""
+    return list(range(rank, E, world))
 
 
 class EP:

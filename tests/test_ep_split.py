@@ -8,9 +8,9 @@ device runs every forward, and of the rebalance's placement):
     experts with one holder go whole to it;
   * ep_place: replicas go only to spare slots of ranks that do not hold the
     expert yet, never lower the balance, and under c5's Zipf(1.1) popularity
-    with 8 ranks (8 base experts and 4 spares each) bring the highest rank
-    cost close to the mean, where the plain 8-per-rank sharding leaves the
-    first rank with several times the mean;
+    with 8 ranks (8 base experts, strided, and 4 spares each) bring the
+    highest rank cost close to the mean, where the plain 8-per-rank sharding
+    leaves the first rank (which holds expert 0) with over twice the mean;
   * both are deterministic, and two gloo ranks that all-gather their counts
     derive the same placement and split."""
 import os
@@ -111,7 +111,7 @@ def test_place_zipf_c5_balance():
     cost0 = simulate(counts, base, S)["cost"]
     placed = M.ep_place(counts, base, S)
     cost1 = simulate(counts, placed, S)["cost"]
-    assert cost0.max() / cost0.mean() > 3.0        # plain sharding: rank 0 carries the hot experts
+    assert cost0.max() / cost0.mean() > 2.0        # plain sharding: rank 0 carries expert 0
     assert cost1.max() / cost1.mean() < 1.08
     assert cost1.max() <= cost0.max()
     # replicas only in spare slots, base experts kept in their slots
