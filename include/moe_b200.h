@@ -59,7 +59,10 @@ typedef struct {
                             1 = none.  Applied on the TF32 / FP32 paths to
                             inputs of 64 MB and up, with chunks of at least
                             4352 tokens, so results equal the one-chunk call
-                            bit for bit                                     */
+                            bit for bit.  moe_b200_ep_forward: the same, each
+                            chunk one collective forward (0 = 2 chunks when
+                            max_tokens_per_rank·d·4 >= 64 MB); every rank
+                            must pass the same value                        */
     int reserved[5];     /* zero                                              */
 } moe_b200_opts;
 
@@ -374,7 +377,9 @@ int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, const float
                                float *d_out, float *d_router_probs, int *d_expert_ids,
                                const moe_b200_opts *opts, void *stream);
 
-/* Same with host buffers, synchronous (H2D of x, D2H of the outputs).  With
+/* Same with host buffers, synchronous (H2D of x, D2H of the outputs, in
+ * token chunks whose copies overlap the other chunks' forwards, see
+ * moe_b200_opts.host_chunks; results do not depend on the chunking).  With
  * a watchdog set, a step that does not finish in time (a rank that stopped
  * joining the collectives) aborts the communicator and returns
  * MOE_B200_E_TIMEOUT; the group must then be destroyed. */
@@ -382,8 +387,9 @@ int moe_b200_ep_forward(moe_b200_ep *ep, const float *router_bias, const float *
                         float *out, float *router_probs, int *expert_ids,
                         const moe_b200_opts *opts);
 
-/* Per-rank, per-expert counts of the last forward ([world × E]) and the
- * number of rows this rank received; synchronises the device. */
+/* Per-rank, per-expert counts of the last collective forward ([world × E];
+ * after a chunked host-buffer call, its last chunk's) and the number of rows
+ * this rank received; synchronises the device. */
 int moe_b200_ep_counts(moe_b200_ep *ep, int *counts_all, int *recv_rows);
 
 /* The current placement [world × E]: slot of expert e on rank q, or -1. */

@@ -407,6 +407,10 @@ struct moe_b200_ep {
     int *nh = nullptr, *hold = nullptr, *beg = nullptr, *dst = nullptr;
     float *io_x = nullptr, *io_out = nullptr, *io_bias = nullptr;
     int timeout_ms = 0;                 // host watchdog on the group's barriers (0 = none)
+    // host-buffer forward: chunk copies in and out on their own streams
+    static constexpr int kMaxChunks = 4;
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    cudaEvent_t ev_in[kMaxChunks] = {}, ev_done[kMaxChunks] = {};
     TcGemm up{}, dn{};
     DecMaps dup{}, ddn{};
 };
@@ -496,6 +500,12 @@ void ep_release(moe_b200_ep *ep) {
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (ep->stream) cudaStreamDestroy(ep->stream);
+    if (ep->s_in) cudaStreamDestroy(ep->s_in);
+    if (ep->s_out) cudaStreamDestroy(ep->s_out);
+    for (int c = 0; c < moe_b200_ep::kMaxChunks; c++) {
+        if (ep->ev_in[c]) cudaEventDestroy(ep->ev_in[c]);
+        if (ep->ev_done[c]) cudaEventDestroy(ep->ev_done[c]);
+    }
     delete ep;
 }
 
@@ -702,8 +712,14 @@ extern "C" int moe_b200_ep_create(const void *unique_id, int rank, int world,
         cudaMemset(ep->bar, 0, 4) != cudaSuccess || cudaMemset(ep->local, 0, 4) != cudaSuccess ||
         cudaMemset(ep->recs, 0xff, G * (E + 1) * 4) != cudaSuccess ||
         cudaMemset(ep->dead, 0, 4) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&ep->stream, cudaStreamNonBlocking) != cudaSuccess)
+        cudaStreamCreateWithFlags(&ep->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ep->s_in, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&ep->s_out, cudaStreamNonBlocking) != cudaSuccess)
         TRY(ep_fail(MOE_B200_E_CUDA, "expert-parallel set-up failed%s%s"));
+    for (int c = 0; c < moe_b200_ep::kMaxChunks; c++)
+        if (cudaEventCreateWithFlags(&ep->ev_in[c], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ep->ev_done[c], cudaEventDisableTiming) != cudaSuccess)
+            TRY(ep_fail(MOE_B200_E_CUDA, "expert-parallel events%s%s"));
     TRY(ep_tmap(&ep->up.tmA, ep->recv_x, RR, w->d_pad, 128));
     ep->up.tmB = w->tm_ug;
     TRY(ep_tmap(&ep->dn.tmA, ep->h, RR, w->F_pad, 128));
@@ -931,6 +947,21 @@ extern "C" int moe_b200_ep_forward_device(moe_b200_ep *ep, const float *d_bias, 
     return MOE_B200_OK;
 }
 
+// Chunks of the host-buffer forward: opts->host_chunks when set, else 2 for
+// inputs of 64 MB and up (per rank, at the group's capacity) and 1 below.
+// Taken from values every rank shares, because every chunk is a collective
+// forward; rows are independent of the chunking, so results are not.
+static int ep_host_chunks(const moe_b200_ep *ep, const moe_b200_opts *opts) {
+    const moe_b200_weights *w = ep->w;
+    if (w->d % 4) return 1;                 // chunk starts must stay 16-byte aligned
+    int n = opts && opts->host_chunks > 0
+                ? opts->host_chunks
+                : ((size_t)ep->max_T * w->d * 4 >= ((size_t)64 << 20) ? 2 : 1);
+    if (n > moe_b200_ep::kMaxChunks) n = moe_b200_ep::kMaxChunks;
+    if (n > ep->max_T) n = ep->max_T;
+    return n < 1 ? 1 : n;
+}
+
 extern "C" int moe_b200_ep_forward(moe_b200_ep *ep, const float *router_bias, const float *x,
                                    int T, float *out, float *router_probs, int *expert_ids,
                                    const moe_b200_opts *opts) {
@@ -940,26 +971,46 @@ extern "C" int moe_b200_ep_forward(moe_b200_ep *ep, const float *router_bias, co
     const moe_b200_weights *w = ep->w;
     EP_CK(cudaSetDevice(ep->device));
     cudaStream_t s = ep->stream;
-    const size_t xb = (size_t)T * w->d * 4;
-    if (T > 0) EP_CK(cudaMemcpyAsync(ep->io_x, x, xb, cudaMemcpyHostToDevice, s));
+    const int d = w->d, E = w->E, k = w->k;
     const float *d_bias = nullptr;
     if (router_bias) {
-        EP_CK(cudaMemcpyAsync(ep->io_bias, router_bias, (size_t)w->E * 4, cudaMemcpyHostToDevice, s));
+        EP_CK(cudaMemcpyAsync(ep->io_bias, router_bias, (size_t)E * 4, cudaMemcpyHostToDevice, s));
         d_bias = ep->io_bias;
     }
-    int rc = moe_b200_ep_forward_device(ep, d_bias, ep->io_x, T, ep->io_out, ep->probs, ep->ids,
-                                        opts, s);
-    if (rc) return rc;
-    if (T > 0) {
-        EP_CK(cudaMemcpyAsync(out, ep->io_out, xb, cudaMemcpyDeviceToHost, s));
-        if (router_probs)
-            EP_CK(cudaMemcpyAsync(router_probs, ep->probs, (size_t)T * w->E * 4,
-                                  cudaMemcpyDeviceToHost, s));
-        if (expert_ids)
-            EP_CK(cudaMemcpyAsync(expert_ids, ep->ids, (size_t)T * w->k * 4,
-                                  cudaMemcpyDeviceToHost, s));
+    // chunk c's rows go up on s_in, its forward runs on s once they landed,
+    // its results come back on s_out once it finished: the copies of one
+    // chunk overlap the forwards of the others (pinned host buffers)
+    const int nch = ep_host_chunks(ep, opts);
+    const int chunk = (ep->max_T + nch - 1) / nch;
+    for (int c = 0; c < nch; c++) {
+        const int t0 = c * chunk;
+        const int tc = T - t0 < 0 ? 0 : (T - t0 < chunk ? T - t0 : chunk);
+        if (tc > 0)
+            EP_CK(cudaMemcpyAsync(ep->io_x + (size_t)t0 * d, x + (size_t)t0 * d,
+                                  (size_t)tc * d * 4, cudaMemcpyHostToDevice, ep->s_in));
+        EP_CK(cudaEventRecord(ep->ev_in[c], ep->s_in));
+        EP_CK(cudaStreamWaitEvent(s, ep->ev_in[c], 0));
+        int rc = moe_b200_ep_forward_device(ep, d_bias, ep->io_x + (size_t)t0 * d, tc,
+                                            ep->io_out + (size_t)t0 * d,
+                                            ep->probs + (size_t)t0 * E, ep->ids + (size_t)t0 * k,
+                                            opts, s);
+        if (rc) return rc;
+        EP_CK(cudaEventRecord(ep->ev_done[c], s));
+        EP_CK(cudaStreamWaitEvent(ep->s_out, ep->ev_done[c], 0));
+        if (tc > 0) {
+            EP_CK(cudaMemcpyAsync(out + (size_t)t0 * d, ep->io_out + (size_t)t0 * d,
+                                  (size_t)tc * d * 4, cudaMemcpyDeviceToHost, ep->s_out));
+            if (router_probs)
+                EP_CK(cudaMemcpyAsync(router_probs + (size_t)t0 * E, ep->probs + (size_t)t0 * E,
+                                      (size_t)tc * E * 4, cudaMemcpyDeviceToHost, ep->s_out));
+            if (expert_ids)
+                EP_CK(cudaMemcpyAsync(expert_ids + (size_t)t0 * k, ep->ids + (size_t)t0 * k,
+                                      (size_t)tc * k * 4, cudaMemcpyDeviceToHost, ep->s_out));
+        }
     }
-    if ((rc = ep_wait(ep, s))) return rc;
+    int rc = ep_wait(ep, s);
+    if (!rc) rc = ep_wait(ep, ep->s_out);
+    if (rc) return rc;
     DeviceStatus st;
     EP_CK(cudaMemcpy(&st, ep->status, sizeof st, cudaMemcpyDeviceToHost));
     if (st.bad_index || st.timeout) {

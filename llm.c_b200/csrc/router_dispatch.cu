@@ -105,6 +105,77 @@ dispatch_gather_kernel(const float *__restrict__ x, int T, int d, int d_pad,
     }
 }
 
+// K7, rows of 4-float multiples with k <= KT: the same arithmetic, with U
+// float4 columns per thread loaded together (U·KT row loads in flight, 8 or
+// 16 with the second K half) before any is used, so a thread's loads overlap
+// instead of waiting one round trip per column.
+template <int KT, int U>
+__global__ void __launch_bounds__(256)
+combine4_kernel(const float *__restrict__ y, int d, int d_pad, int T, int k,
+                const int *__restrict__ pos_of, const float *__restrict__ wts,
+                float *out, const float *__restrict__ y2, const float *resid)
+{
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const float4 *yr[KT], *y2r[KT];
+    float w[KT];
+#pragma unroll
+    for (int r = 0; r < KT; r++) {
+        const int p = r < k ? pos_of[(size_t)t * k + r] : 0;
+        w[r] = r < k ? wts[(size_t)t * k + r] : 0.0f;
+        yr[r] = reinterpret_cast<const float4 *>(y + (size_t)p * d_pad);
+        y2r[r] = y2 ? reinterpret_cast<const float4 *>(y2 + (size_t)p * d_pad) : nullptr;
+    }
+    const int n4 = d >> 2;
+    float4 *o = reinterpret_cast<float4 *>(out + (size_t)t * d);
+    const float4 *xr = resid ? reinterpret_cast<const float4 *>(resid + (size_t)t * d) : nullptr;
+    for (int c0 = threadIdx.x; c0 < n4; c0 += U * blockDim.x) {
+        float4 v[U][KT];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int c = c0 + u * blockDim.x;
+#pragma unroll
+            for (int r = 0; r < KT; r++)
+                v[u][r] = (r < k && c < n4) ? __ldg(yr[r] + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (y2) {
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int c = c0 + u * blockDim.x;
+#pragma unroll
+                for (int r = 0; r < KT; r++) {
+                    if (r < k && c < n4) {
+                        const float4 v2 = __ldg(y2r[r] + c);
+                        v[u][r].x = __fadd_rn(v[u][r].x, v2.x); v[u][r].y = __fadd_rn(v[u][r].y, v2.y);
+                        v[u][r].z = __fadd_rn(v[u][r].z, v2.z); v[u][r].w = __fadd_rn(v[u][r].w, v2.w);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int c = c0 + u * blockDim.x;
+            if (c >= n4) break;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int r = 0; r < KT; r++) {
+                if (r < k) {
+                    acc.x = __fmaf_rn(w[r], v[u][r].x, acc.x);
+                    acc.y = __fmaf_rn(w[r], v[u][r].y, acc.y);
+                    acc.z = __fmaf_rn(w[r], v[u][r].z, acc.z);
+                    acc.w = __fmaf_rn(w[r], v[u][r].w, acc.w);
+                }
+            }
+            if (xr) {
+                const float4 x = xr[c];
+                acc.x = __fadd_rn(x.x, acc.x); acc.y = __fadd_rn(x.y, acc.y);
+                acc.z = __fadd_rn(x.z, acc.z); acc.w = __fadd_rn(x.w, acc.w);
+            }
+            o[c] = acc;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------
 // K7  combine — out[t] = Σ_r w_{t,r} · y[pos(t,r)] for r = 0..k-1 in rank
 // order, starting from zero with one fused multiply-add per term, as the
@@ -190,7 +261,12 @@ cudaError_t launch_combine(const float *y, int d, int d_pad, int T, int k,
     int threads = 256;
     const int work = (d & 3) == 0 ? d / 4 : d;
     if (work < 256) threads = max(32, round_up(work, 32));
-    combine_kernel<<<T, threads, 0, s>>>(y, d, d_pad, T, k, pos_of, wts, out, y2, resid);
+    if ((d & 3) == 0 && k <= 2)
+        combine4_kernel<2, 4><<<T, threads, 0, s>>>(y, d, d_pad, T, k, pos_of, wts, out, y2, resid);
+    else if ((d & 3) == 0 && k <= 4)
+        combine4_kernel<4, 2><<<T, threads, 0, s>>>(y, d, d_pad, T, k, pos_of, wts, out, y2, resid);
+    else
+        combine_kernel<<<T, threads, 0, s>>>(y, d, d_pad, T, k, pos_of, wts, out, y2, resid);
     return cudaGetLastError();
 }
 
