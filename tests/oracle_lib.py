@@ -164,6 +164,8 @@ class MoEProblem:
         self.W_router = synth(seed, stream_router(), d * E, w_std).reshape(d, E)
         if bias is None:
             self.bias = None
+        elif not isinstance(bias, str):
+            self.bias = np.ascontiguousarray(bias, dtype=np.float32)
         elif bias == "normal":
             self.bias = synth(seed, stream_bias(), E, 1.0)
         elif bias == "zipf":

@@ -4,7 +4,8 @@ a program whose device memory belongs to another framework's allocator).
 All of its intermediates live in a static 16 MiB array inside the library.
 
 It is checked through the C-ABI against the regular device entry point on
-the same FP32 expert path, on two calls in a row with different inputs, so
+the same FP32 expert path, and against the CPU oracle (the restatement of
+the reference's moe_forward), on two calls in a row with different inputs, so
 that whatever the first call leaves in the shared array cannot leak into
 the second.  The tolerances are the parity tests' own: probabilities within
 2e-6 (the regular entry point may sum the router logits in another order),
@@ -69,6 +70,11 @@ def test_noalloc_matches_device_entry_point_two_calls(moe):
             assert O.routing_mismatch_allowed(logits[t], n_ids[t], r_ids[t], p.k)
         assert np.max(np.abs(n_probs - r_probs)) <= PROBS_TOL
         assert O.rel_err(n_out, r_out) < TOL
+        # and against the CPU restatement of the reference's moe_forward
+        q = O.MoEProblem(x.shape[0], 384, 8, 2, 1536, seed=11, bias=bias)
+        q.x = np.ascontiguousarray(x)
+        want, _, _ = q.oracle_forward(forced_ids=n_ids)
+        assert O.rel_err(n_out, want) < TOL
     w.free()
 
 
