@@ -67,6 +67,7 @@ struct StepArgs {
     int *state, *ids;                  // state = {token, pos}
     unsigned *bar;                     // grid barrier counter (zeroed before each step)
     int *err;                          // barrier timeout flag
+    int *err_host;                     // mapped pinned copy, written at the end of every step
     float *trace;                      // [L][2][d]: pre-FFN x_norm and FFN output per layer
     int pdl_early;                     // stage kernels: let the next kernel launch on entry
 };
@@ -590,7 +591,10 @@ __global__ void __launch_bounds__(kThreads) lmhead_kernel(StepArgs A) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
     lmhead_item(A, blockIdx.x, false, S);
-    if (blockIdx.x == 0 && threadIdx.x == 0) A.state[1] += 1;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        A.state[1] += 1;
+        *(volatile int *)A.err_host = *(volatile int *)A.err;   // read by the host after the step
+    }
 }
 
 // ---- the whole step as one persistent cooperative kernel ----
@@ -652,7 +656,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs A) {
         lmhead_item(A, it, normed, S);
         normed = true;                  // S.xn keeps the normalised vector across items
     }
-    if (b == 0 && threadIdx.x == 0) A.state[1] = pos + 1;
+    if (b == 0 && threadIdx.x == 0) {
+        A.state[1] = pos + 1;
+        *(volatile int *)A.err_host = *(volatile int *)A.err;
+    }
 }
 
 }  // namespace decs
@@ -680,6 +687,8 @@ struct moe_b200_decoder {
     int *state = nullptr, *ids = nullptr;        // state = {token, pos}
     unsigned *bar = nullptr;
     int *err = nullptr;
+    int *h_err = nullptr;                        // mapped pinned copy of err (StepArgs::err_host)
+    int *d_err_host = nullptr;                   // its device address
     float *trace = nullptr;                      // [L][2][d], see StepArgs::trace
     int *h_token = nullptr;                      // pinned
     int maxF_pad = 0;
@@ -723,6 +732,7 @@ void free_all(moe_b200_decoder *m) {
     cudaFree(m->logits); cudaFree(m->wts); cudaFree(m->state); cudaFree(m->ids);
     cudaFree(m->bar); cudaFree(m->err); cudaFree(m->trace);
     if (m->h_token) cudaFreeHost(m->h_token);
+    if (m->h_err) cudaFreeHost(m->h_err);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
 }
@@ -738,6 +748,7 @@ StepArgs step_args(const moe_b200_decoder *m) {
     A.x = m->x; A.q = m->q; A.part = m->part; A.h = m->h; A.logits = m->logits; A.wts = m->wts;
     A.state = m->state; A.ids = m->ids; A.bar = m->bar; A.err = m->err;
     A.trace = m->trace;
+    A.err_host = m->d_err_host;
     A.pdl_early = m->pdl == 1;
     return A;
 }
@@ -882,10 +893,13 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
         cudaMalloc(&m->state, 2 * 4) != cudaSuccess ||
         cudaMalloc(&m->bar, 4) != cudaSuccess || cudaMalloc(&m->err, 4) != cudaSuccess ||
         cudaMalloc(&m->trace, (size_t)m->L * 2 * d * 4) != cudaSuccess ||
-        cudaMallocHost(&m->h_token, 4) != cudaSuccess) {
+        cudaMallocHost(&m->h_token, 4) != cudaSuccess ||
+        cudaHostAlloc(&m->h_err, 4, cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer((void **)&m->d_err_host, m->h_err, 0) != cudaSuccess) {
         cudaGetLastError();
         return bail(dfail(MOE_B200_E_NOMEM, "decoder buffers do not fit"));
     }
+    *(volatile int *)m->h_err = 0;
     // h is zeroed once: the up/gate stage writes units [0, F), and the
     // padding units [F, F_pad) meet zero weight columns in the down stage
     if (cudaMemcpy(m->d_layers, lp.data(), lp.size() * sizeof(LayerPtrs),
@@ -981,11 +995,10 @@ extern "C" int moe_b200_decoder_step(moe_b200_decoder *m, int token, float *logi
         DCK(cudaMemcpyAsync(logits, m->logits, (size_t)m->D.vocab * 4, cudaMemcpyDeviceToHost,
                             m->stream));
     DCK(cudaStreamSynchronize(m->stream));
-    int err = 0;
-    if (persistent(m->flags)) {
-        DCK(cudaMemcpy(&err, m->err, 4, cudaMemcpyDeviceToHost));
-        if (err) return dfail(MOE_B200_E_TIMEOUT, "decode step: grid barrier wait ran out");
-    }
+    // the grid barrier's timeout flag comes back through mapped host memory,
+    // written by the step's last kernel (no copy, no second synchronisation)
+    if (*(volatile int *)m->h_err)
+        return dfail(MOE_B200_E_TIMEOUT, "decode step: grid barrier wait ran out");
     m->pos++;
     return MOE_B200_OK;
 }
