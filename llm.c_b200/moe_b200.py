@@ -662,7 +662,10 @@ class EP:
                                                 probs_ptr, ids_ptr, C.byref(o), stream),
                "moe_b200_ep_forward_device")
 
-    def forward(self, x: np.ndarray, bias: np.ndarray | None = None, path=PATH_AUTO):
+    def forward(self, x: np.ndarray, bias: np.ndarray | None = None, path=PATH_AUTO,
+                host_chunks: int = 0):
+        """Host-buffer forward (collective); host_chunks as moe_b200_opts, the
+        same on every rank."""
         x = np.ascontiguousarray(x, np.float32)
         T = x.shape[0]
         w = self.w
@@ -670,7 +673,7 @@ class EP:
         probs = np.empty((T, w.E), np.float32)
         ids = np.empty((T, w.top_k), np.int32)
         b = None if bias is None else np.ascontiguousarray(bias, np.float32)
-        o = _opts(path)
+        o = _opts(path, host_chunks=host_chunks)
         _check(lib().moe_b200_ep_forward(self.handle, _f(b), _f(x), T, _f(out), _f(probs),
                                          _i(ids), C.byref(o)), "moe_b200_ep_forward")
         return out, probs, ids

@@ -14,7 +14,8 @@ tolerance.
 Checked before and after moe_b200_ep_rebalance (which must place replicas
 of the hot experts of the Zipf case in spare slots, the same placement on
 every rank), with equal and with unequal token counts per rank (one rank
-with none), on AUTO and every explicit path.  Skipped when fewer than 2 GPUs
+with none), on AUTO and every explicit path; the host-buffer forward split into token
+chunks equals the unsplit one bit for bit.  Skipped when fewer than 2 GPUs
 are visible."""
 import os
 import socket
@@ -99,6 +100,12 @@ def _worker(rank, world, port, q):
                     results.append(dict(rank=rank, case=(T, d, E), placement=placement.tolist(),
                                         slots=shard.slots().tolist(), mine=mine,
                                         counts=counts_all.tolist(), n_slots=n_slots))
+            # the host-buffer forward in 3 token chunks (3 collective forwards)
+            # gives the 1-chunk results bit for bit
+            one = ep.forward(xs, p.bias, path=M.PATH_TF32, host_chunks=1)
+            three = ep.forward(xs, p.bias, path=M.PATH_TF32, host_chunks=3)
+            results.append(dict(rank=rank, case=(T, d, E), chunks_equal=all(
+                bool(np.array_equal(u, v)) for u, v in zip(one, three))))
             ep.forward(xs, p.bias)                # every rank's full share, then the counts
             counts_all, rows = ep.counts()
             results.append(dict(rank=rank, case=(T, d, E), counts_total=int(counts_all.sum()),
@@ -140,6 +147,8 @@ def test_ep_sharded_matches_single_gpu():
                 assert r["counts_total"] == r["want_total"]
             elif "placement" in r:
                 placements.setdefault(r["case"], []).append(r)
+            elif "chunks_equal" in r:
+                assert r["chunks_equal"], r
             else:
                 assert r["ids_equal"] and r["probs_equal"], r
                 assert r["out_equal"] or r["rel_err"] < r["tol"], r
