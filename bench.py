@@ -458,7 +458,8 @@ def run_backward(args, c):
         M.synth_fill(bias.data_ptr(), E, seed, M.STREAM_BIAS, 1.0, cuda_stream=stream.cuda_stream)
     bptr = bias.data_ptr() if bias is not None else None
 
-    path = {"auto": M.PATH_AUTO, "tf32": M.PATH_TF32, "fp32": M.PATH_FP32}[args.path]
+    path = {"auto": M.PATH_AUTO, "tf32": M.PATH_TF32, "fp32": M.PATH_FP32,
+            "tf32x3": M.PATH_TF32X3}[args.path]
 
     def step():
         M.moe_backward_device(w, x.data_ptr(), T, dy.data_ptr(), dx.data_ptr(), g, bias_ptr=bptr,
@@ -612,29 +613,45 @@ def _timed(step, stream, steps, warmup):
 
 
 def fp32_path_record(M, w, x, bptr, stream, c):
-    """c5 on the FP32-accuracy expert path (FP32 FFMA grouped GEMMs, 1e-5),
-    beside the TF32 headline: tokens/s and the FFMA rate of the layer."""
+    """c5 at FP32 accuracy (tolerance 1e-5), beside the TF32 headline, on
+    both expert paths that give it: the FP32 FFMA grouped GEMMs (tokens/s
+    and the FFMA rate of the layer) and the 3xTF32 tensor-core kernel
+    (`tf32x3`: tokens/s and its FLOP rate against the TF32 peak, of which
+    it issues three MMAs per product)."""
     import torch
     T, d, E, k, F = c["T"], c["d"], c["E"], c["k"], c["F"]
     out = torch.empty((T, d), device="cuda")
-
-    def step():
-        M.moe_forward_device(w, x.data_ptr(), T, out.data_ptr(), bias_ptr=bptr, path=M.PATH_FP32,
-                             stream=stream.cuda_stream)
-
-    with ClockSampler(0) as clk:
-        ms = _timed(step, stream, steps=2, warmup=1)
     props = torch.cuda.get_device_properties(0)
-    clocks = clk.summary()
-    mhz = clocks.get("sm_mhz") or 1965.0
-    ffma_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
-    tflops = flops_per_step(c) / (ms / 1000.0) / 1e12
-    return {"tokens_per_s": T / (ms / 1000.0), "ms_per_step": ms, "dtype": "f32",
-            "path_run": "fp32 (FFMA grouped GEMMs)", "tolerance": 1e-5,
-            "achieved_tflops": tflops, "ffma_peak_tflops": ffma_peak,
-            "frac_of_ffma_peak": tflops / ffma_peak,
-            "peak_src": "nominal: SMs x 128 FP32 lanes x 2 x median SM clock under load",
-            "clocks": clocks}
+    peaks = measured_peaks()
+    recs = {}
+    for path in (M.PATH_FP32, M.PATH_TF32X3):
+        def step():
+            M.moe_forward_device(w, x.data_ptr(), T, out.data_ptr(), bias_ptr=bptr, path=path,
+                                 stream=stream.cuda_stream)
+
+        with ClockSampler(0) as clk:
+            ms = _timed(step, stream, steps=2, warmup=1)
+        clocks = clk.summary()
+        tflops = flops_per_step(c) / (ms / 1000.0) / 1e12
+        rec = {"tokens_per_s": T / (ms / 1000.0), "ms_per_step": ms, "tolerance": 1e-5,
+               "achieved_tflops": tflops, "clocks": clocks}
+        if path == M.PATH_FP32:
+            mhz = clocks.get("sm_mhz") or 1965.0
+            ffma_peak = props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+            rec.update({"dtype": "f32", "path_run": "fp32 (FFMA grouped GEMMs)",
+                        "ffma_peak_tflops": ffma_peak, "frac_of_ffma_peak": tflops / ffma_peak,
+                        "peak_src": "nominal: SMs x 128 FP32 lanes x 2 x median SM clock under "
+                                    "load"})
+            recs.update(rec)
+        else:
+            tf32_peak = peaks["bf16_sustained"] / 2.0
+            rec.update({"dtype": "tf32x3", "path_run": "tf32x3 (3xTF32 weight-streaming kernel)",
+                        "tf32_peak_tflops": tf32_peak,
+                        "frac_of_tf32_peak_x3": 3.0 * tflops / tf32_peak,
+                        "peak_src": f"{peaks['src']} bf16 sustained / 2 (TF32 rate); three "
+                                    "MMAs per product"})
+            recs["tf32x3"] = rec
+    return recs
 
 
 def decode_c4_record(M, stream):
@@ -728,7 +745,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="c5", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--path", default="auto", choices=["auto", "tf32", "fp32"])
+    ap.add_argument("--path", default="auto", choices=["auto", "tf32", "fp32", "tf32x3"])
     ap.add_argument("--ref-budget", type=float, default=6.0,
                     help="seconds of CPU work per reference sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -783,7 +800,8 @@ def main():
                                 device_id=torch.device("cuda", local))
 
     M.init(local)
-    path = {"auto": M.PATH_AUTO, "tf32": M.PATH_TF32, "fp32": M.PATH_FP32}[args.path]
+    path = {"auto": M.PATH_AUTO, "tf32": M.PATH_TF32, "fp32": M.PATH_FP32,
+            "tf32x3": M.PATH_TF32X3}[args.path]
     T, d, E, k, F, seed = c["T"], c["d"], c["E"], c["k"], c["F"], c["seed"]
     if T % world:
         raise SystemExit(f"T={T} is not divisible by {world} ranks")

@@ -48,15 +48,17 @@
 // Warp roles (11 warps): 0 weight producer, 10 token producer, 1 TMEM
 // allocator + MMA issuer, 2-5 converter, 6-9 epilogue.  The tensor core's
 // own accumulation truncates, and over a long K that alone costs ~1e-5, so
-// each 32-wide K step is multiplied into a FRESH 128×128 TMEM partial (a
-// 2-slot ring) and the epilogue warps add the partials in registers with
-// IEEE round-to-nearest — the long sum over K is ordinary fp32 arithmetic,
-// as on the FFMA path.  Up/gate tiles hold 64 gate rows and the 64
+// every SPP K steps (SPP × 32 of K, 128 by default) are multiplied into a
+// FRESH 128×128 TMEM partial (a 2-slot ring) and the epilogue warps add the
+// partials in registers with IEEE round-to-nearest — the long sum over K is
+// ordinary fp32 arithmetic, as on the FFMA path.  Up/gate tiles hold 64 gate rows and the 64
 // matching up rows, so the SwiGLU runs in the epilogue: the warps holding
 // the up half hand their values to the gate-half warps through shared
 // memory, under an mbarrier pair.  Every wait is bounded; a timeout aborts
 // the CTA cleanly.
 #include "tc_common.cuh"
+
+#include <cstdlib>
 
 namespace moe {
 namespace dec {
@@ -163,13 +165,14 @@ __device__ __forceinline__ bool wait_done(uint64_t *done, int m, volatile int *a
 // per-step partials.  The converter warps only gate the ring (weight tile,
 // token tile, free accumulator) and the epilogue waits once per tile on
 // accfull[tile % 2].  H is stored rounded to nearest TF32.
-template <bool UPGATE, bool PAIR, bool ONEPASS>
+template <bool UPGATE, bool PAIR, bool ONEPASS, int SPP>
 __global__ void __launch_bounds__(kThreads, 1)
 dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
          const __grid_constant__ CUtensorMap tmXs, const __grid_constant__ CUtensorMap tmXb32,
          DecArgs a)
 {
     static_assert(!(PAIR && ONEPASS), "ONEPASS runs on single CTAs");
+    static_assert(R % (SPP * NSLOT) == 0, "a partial's steps sit in one unrolled ring period");
     constexpr int MM = PAIR ? 2 * MW : MW;                  // MMA M (weight rows per block)
     constexpr uint32_t IDESC_N128 = idesc_tf32(MM, 2 * NTOK);
     constexpr uint32_t IDESC_N64 = idesc_tf32(MM, NTOK);
@@ -320,7 +323,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = tmem_base + (uint32_t)((j % NSLOT) * SLOT_COLS);
+                    const uint32_t d = tmem_base + (uint32_t)(((j / SPP) % NSLOT) * SLOT_COLS);
                     const uint64_t dw = dw0 + (uint64_t)(j * (A_BYTES >> 4));
                     const uint64_t dx = dx0 + (uint64_t)((j % NX) * (XB >> 4));
                     const uint64_t dx2 = dx + (uint64_t)(XB2 >> 4);      // MMA2's B
@@ -342,11 +345,12 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                             // cols 0..63: W·X_big, cols 64..127: W·X_small (X_big|X_small as one
                             // 128-row B), then cols 0..63 += W_small·X_big (A: 8 columns of
                             // W_small in TMEM)
+                            const uint32_t acc = (kk || (j % SPP)) ? 1u : 0u;
                             if (PAIR) {
-                                mma_tf32_pair(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
+                                mma_tf32_pair(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, acc);
                                 mma_tf32_ts_pair(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
                             } else {
-                                mma_tf32(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, kk ? 1u : 0u);
+                                mma_tf32(d, dw + 2 * kk, dx + 2 * kk, IDESC_N128, acc);
                                 mma_tf32_ts(d, ts + 8 * kk, dx2 + 2 * kk, IDESC_N64, 1u);
                             }
                         }
@@ -397,7 +401,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
             for (int n = 0; n < nsteps; n++) {
                 if (!mbar_wait(&wfull[rw.i], rw.ph, abort_flag) ||
                     (cw == 2 && !mbar_wait(&xfull[rx.i], rx.ph, abort_flag)) ||
-                    (cw == 3 && !mbar_wait(&pempty[rp.i], rp.ph ^ 1, abort_flag))) {
+                    (cw == 3 && n % SPP == 0 && !mbar_wait(&pempty[rp.i], rp.ph ^ 1, abort_flag))) {
                     ok = false;
                     break;
                 }
@@ -421,7 +425,8 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                 tc_fence_before();
                 if (PAIR) mbar_arrive_cluster(mapa(smem_u32(&ready[rs.i]), 0));
                 else mbar_arrive(&ready[rs.i]);
-                rw.next(); rs.next(); rx.next(); rp.next();
+                rw.next(); rs.next(); rx.next();
+                if (n % SPP == SPP - 1) rp.next();
             }
             if (!ok) set_abort(13);
         }
@@ -450,10 +455,13 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                 mbar_arrive(&pempty[slot]);
                 n++;
             } else {
-                for (int kb = 0; kb < a.num_kb; kb++, n++) {
-                    if (!wait_done(done, n, abort_flag)) { set_abort(14); ok = false; break; }
+                for (int kb = 0; kb < a.num_kb; kb += SPP, n += SPP) {
+                    // the partial of steps n .. n+SPP-1 is complete once the
+                    // last of them has finished
+                    if (!wait_done(done, n + SPP - 1, abort_flag)) { set_abort(14); ok = false; break; }
                     tc_fence_after();
-                    const uint32_t taddr = lane_base + (uint32_t)((n % NSLOT) * SLOT_COLS);
+                    const uint32_t slot = (uint32_t)((n / SPP) % NSLOT);
+                    const uint32_t taddr = lane_base + slot * SLOT_COLS;
 #pragma unroll
                     for (int c = 0; c < NTOK; c += 32) {
                         float pb[32], ps[32];
@@ -463,7 +471,7 @@ dec_gemm(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtens
                         for (int j = 0; j < 32; j++) v[c + j] = __fadd_rn(v[c + j], __fadd_rn(pb[j], ps[j]));
                     }
                     tc_fence_before();
-                    mbar_arrive(&pempty[n % NSLOT]);
+                    mbar_arrive(&pempty[slot]);
                 }
             }
             if (!ok) break;
@@ -540,12 +548,20 @@ __global__ void split_tf32_kernel(const float4 *__restrict__ big, float4 *__rest
 }  // namespace dec
 
 cudaError_t dec_set_attributes() {
-    const void *fns[6] = {(const void *)dec::dec_gemm<true, false, false>,
-                          (const void *)dec::dec_gemm<false, false, false>,
-                          (const void *)dec::dec_gemm<true, true, false>,
-                          (const void *)dec::dec_gemm<false, true, false>,
-                          (const void *)dec::dec_gemm<true, false, true>,
-                          (const void *)dec::dec_gemm<false, false, true>};
+    const void *fns[14] = {(const void *)dec::dec_gemm<true, false, false, 1>,
+                           (const void *)dec::dec_gemm<false, false, false, 1>,
+                           (const void *)dec::dec_gemm<true, false, false, 2>,
+                           (const void *)dec::dec_gemm<false, false, false, 2>,
+                           (const void *)dec::dec_gemm<true, false, false, 4>,
+                           (const void *)dec::dec_gemm<false, false, false, 4>,
+                           (const void *)dec::dec_gemm<true, true, false, 1>,
+                           (const void *)dec::dec_gemm<false, true, false, 1>,
+                           (const void *)dec::dec_gemm<true, true, false, 2>,
+                           (const void *)dec::dec_gemm<false, true, false, 2>,
+                           (const void *)dec::dec_gemm<true, true, false, 4>,
+                           (const void *)dec::dec_gemm<false, true, false, 4>,
+                           (const void *)dec::dec_gemm<true, false, true, 1>,
+                           (const void *)dec::dec_gemm<false, false, true, 1>};
     for (const void *f : fns) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              dec::SMEM_BYTES);
@@ -568,7 +584,7 @@ int dec_max_pairs(int num_sms) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, dec::dec_gemm<true, true, false>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, dec::dec_gemm<true, true, false, 1>, &cfg) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
@@ -589,17 +605,46 @@ static int dec_units(int rows_bound, int E, int NB, int cap) {
     return bound < cap ? (bound > 0 ? bound : 1) : cap;
 }
 
+// K steps (of 32) per TMEM partial on the 3xTF32 path: 1, 2 or 4, the
+// largest that divides the tile's steps and does not exceed
+// MOE_B200_DEC_SPP (default 4).  Measured at c4 (one B200, 1965 MHz):
+// up/gate 0.732 / 0.695 / 0.680 ms for 1 / 2 / 4 steps per partial, layer
+// error against the oracle 1.4e-6 / 1.9e-6 / 2.7e-6 (3.1e-6 with d = 4096,
+// d_ff = 14336): fewer partials cut the epilogue's tensor-memory reads, and
+// each partial's in-tensor-core accumulation adds its truncation error.
+static int dec_spp(int num_kb) {
+    static const int want = [] {
+        const char *p = std::getenv("MOE_B200_DEC_SPP");
+        const int v = p ? std::atoi(p) : 4;
+        return v >= 4 ? 4 : (v >= 2 ? 2 : 1);
+    }();
+    int spp = want;
+    while (spp > 1 && num_kb % spp != 0) spp /= 2;
+    return spp;
+}
+
 template <bool UPGATE>
 static cudaError_t dec_launch(const DecMaps &m, const dec::DecArgs &a, int units, bool pair,
                               bool onepass, cudaStream_t s) {
     if (onepass) {
-        dec::dec_gemm<UPGATE, false, true><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
+        dec::dec_gemm<UPGATE, false, true, 1><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
             m.tmW, m.tmXb, m.tmXb, m.tmXb, a);
         return cudaGetLastError();
     }
     if (!pair) {
-        dec::dec_gemm<UPGATE, false, false><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
-            m.tmW, m.tmXb, m.tmXs, m.tmXb, a);
+        switch (dec_spp(a.num_kb)) {
+        case 4:
+            dec::dec_gemm<UPGATE, false, false, 4><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
+                m.tmW, m.tmXb, m.tmXs, m.tmXb, a);
+            break;
+        case 2:
+            dec::dec_gemm<UPGATE, false, false, 2><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
+                m.tmW, m.tmXb, m.tmXs, m.tmXb, a);
+            break;
+        default:
+            dec::dec_gemm<UPGATE, false, false, 1><<<units, dec::kThreads, dec::SMEM_BYTES, s>>>(
+                m.tmW, m.tmXb, m.tmXs, m.tmXb, a);
+        }
         return cudaGetLastError();
     }
     cudaLaunchConfig_t cfg = {};
@@ -614,7 +659,17 @@ static cudaError_t dec_launch(const DecMaps &m, const dec::DecArgs &a, int units
     cfg.stream = s;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, dec::dec_gemm<UPGATE, true, false>, m.tmW, m.tmXb, m.tmXs, m.tmXb32, a);
+    switch (dec_spp(a.num_kb)) {
+    case 4:
+        return cudaLaunchKernelEx(&cfg, dec::dec_gemm<UPGATE, true, false, 4>, m.tmW, m.tmXb,
+                                  m.tmXs, m.tmXb32, a);
+    case 2:
+        return cudaLaunchKernelEx(&cfg, dec::dec_gemm<UPGATE, true, false, 2>, m.tmW, m.tmXb,
+                                  m.tmXs, m.tmXb32, a);
+    default:
+        return cudaLaunchKernelEx(&cfg, dec::dec_gemm<UPGATE, true, false, 1>, m.tmW, m.tmXb,
+                                  m.tmXs, m.tmXb32, a);
+    }
 }
 
 cudaError_t launch_dec_upgate(const DecMaps &m, int d_pad, int F_pad, float *h_big, float *h_small,
