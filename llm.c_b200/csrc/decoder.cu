@@ -44,6 +44,8 @@ namespace decs {
 constexpr int kThreads = 256;           // 8 warps
 constexpr int CH = 64;                  // attention positions per chunk
 constexpr int kMaxD = 8192;             // d_model limit (normalised vector in smem)
+constexpr int kUnitsPerWarp = 2;        // up/gate stage: hidden units per warp
+constexpr int kUnitsPerCta = kUnitsPerWarp * kThreads / 32;
 
 struct Dims {
     int d, d_pad, nh, nkv, hd, nq, kvd, qkv, vocab, max_seq, nchunk;
@@ -70,6 +72,10 @@ struct StepArgs {
     int *err_host;                     // mapped pinned copy, written at the end of every step
     float *trace;                      // [L][2][d]: pre-FFN x_norm and FFN output per layer
     int pdl_early;                     // stage kernels: let the next kernel launch on entry
+    int flags;                         // stage kernels hand off through done[] (see stage_wait):
+                                       // 1 the next kernel may launch after a CTA's wait, 2 after its work
+    unsigned *done;                    // [6 L + 1] CTAs finished per stage, then per layer the
+                                       // up/gate stage's ids-published count (zeroed before each step)
 };
 
 struct Smem {
@@ -93,13 +99,87 @@ __device__ __forceinline__ float ldcg(const float *p) { return __ldcg(p); }
 // its CTAs exit, or, with pdl_early, as soon as they all started: each
 // calls pdl_trigger() on entry); a kernel loads what does not depend on the
 // previous stage (weight rows, RoPE factors, cached keys of earlier
-// positions) and calls pdl_wait() before it reads anything the previous
-// stage wrote or writes anything.  pdl_wait() returns once the previous kernel has completed and
-// its writes are visible; in a kernel launched without the dependency (the
-// step's first kernel, the persistent variant) both are no-ops.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// positions) and calls stage_wait() before it reads anything the previous
+// stage wrote or writes anything.  In the griddepcontrol modes stage_wait()
+// returns once the previous kernel has completed and its writes are visible
+// (in a kernel launched without the dependency, the step's first kernel,
+// it is a no-op).
+//
+// Flag mode (A.flags): griddepcontrol.wait returns only ~1-3 us after the
+// previous grid's last CTA exits (grid completion and memory flush), which
+// across 31 stages was a third of the step.  Instead every CTA of stage s
+// adds 1 to done[s] once its results are stored (stage_signal: CTA barrier,
+// then a device-scope fence and the add by one thread), and a CTA of stage
+// s + 1 waits until done[s] counts every CTA of stage s (acquire load,
+// bounded by kWaitNs; a timeout sets *A.err, which also releases every other
+// waiter).  Each CTA lets the next kernel launch only after its own wait
+// (griddepcontrol.launch_dependents), so that kernel's CTAs are placed only
+// once every CTA of this one is resident and past its wait: at most two
+// stages share the SMs, and the running one never waits on the waiting one.
+// Stage ids: 5 l + {0 qkv, 1 attn, 2 oproj, 3 upgate, 4 down}, 5 L the LM
+// head; -1 in the persistent kernel, whose grid barriers order the stages.
 __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__host__ __device__ inline int down_cols(int k);
+
+// CTAs launched for stage s (they match enqueue_step's grids)
+__device__ inline unsigned stage_ctas(const StepArgs &A, int s) {
+    const Dims &D = A.D;
+    if (s == 5 * A.L) return (unsigned)((D.vocab + 31) / 32);
+    const int l = s / 5;
+    switch (s % 5) {
+    case 0: return (unsigned)((D.qkv + 31) / 32);
+    case 1: return (unsigned)(D.nh * D.nchunk);
+    case 2: return (unsigned)((D.d + 31) / 32);
+    case 3: {
+        const LayerPtrs &Lp = A.layers[l];
+        return (unsigned)(Lp.k * ((Lp.F + kUnitsPerCta - 1) / kUnitsPerCta));
+    }
+    default: {
+        const int c = down_cols(A.layers[l].k);
+        return (unsigned)((D.d + c - 1) / c);
+    }
+    }
+}
+
+// Flag mode: wait (thread 0, then the CTA) until done[idx] reaches target.
+__device__ __forceinline__ void flag_wait(const StepArgs &A, int idx, unsigned target) {
+    if (threadIdx.x == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (true) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(A.done + idx)
+                         : "memory");
+            if (v >= target) break;
+            if (*(volatile int *)A.err) break;
+            if (globaltimer_ns() - t0 > kWaitNs) { atomicExch(A.err, 1); break; }
+            __nanosleep(32);
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ void stage_wait(const StepArgs &A, int st) {
+    if (st < 0) return;
+    if (!A.flags) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        return;
+    }
+    if (st > 0) flag_wait(A, st - 1, stage_ctas(A, st - 1));
+    if (A.flags == 1) pdl_trigger();
+}
+
+// Flag mode: this CTA's results of stage st are stored (every thread).
+__device__ __forceinline__ void stage_signal(const StepArgs &A, int st) {
+    if (!A.flags || st < 0) return;
+    if (A.flags == 2) pdl_trigger();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(A.done + st, 1u);
+    }
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -209,7 +289,7 @@ __device__ __forceinline__ float matvec32(const float *v, const float *__restric
 // starts from the token's embedding row; item 0 also stores it as the
 // residual stream.
 __device__ void qkv_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int token, int pos,
-                         int item, Smem &S) {
+                         int item, Smem &S, int st) {
     const Dims &D = A.D;
     const float *src = layer == 0 ? A.embed + (size_t)token * D.d : A.x;
     const int lane = threadIdx.x & 31, col = item * 32 + lane;
@@ -223,7 +303,7 @@ __device__ void qkv_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int 
         cr = __ldg(A.rope_cos + (size_t)pos * half + pi);
         sr = __ldg(A.rope_sin + (size_t)pos * half + pi);
     }
-    pdl_wait();
+    stage_wait(A, st);
     if (layer == 0 && item == 0)
         for (int i = threadIdx.x; i < D.d; i += kThreads) A.x[i] = __ldg(src + i);
     rmsnorm_to_smem(src, Lp.rms_attn, D, S);
@@ -250,7 +330,8 @@ __device__ void qkv_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int 
 // exp(s - m) and the exp-weighted V sum, written to part[h][chunk] =
 // {m, l, o[hd]} (scores q·k / sqrt(hd), GQA kvh = h / (nh / nkv),
 // src/inference.c:285-305).
-__device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chunk, Smem &S) {
+__device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chunk, Smem &S,
+                          int st) {
     const Dims &D = A.D;
     const int j0 = chunk * CH, n = min(CH, pos + 1 - j0);
     const float *kc = A.kc + (size_t)layer * D.max_seq * D.kvd;
@@ -284,7 +365,7 @@ __device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chun
     for (int u = 0; u < VMAX; u++)
         vpre[u] = (gi < groups && jlo + u < jhi && j0 + jlo + u != pos)
                       ? ldcg(vcol + (size_t)(jlo + u) * D.kvd) : 0.0f;
-    pdl_wait();
+    stage_wait(A, st);
 #pragma unroll
     for (int t = 0; t < PW; t++) {
         const int jj = warp + t * (kThreads / 32);
@@ -346,13 +427,24 @@ __device__ void attn_item(const StepArgs &A, int layer, int pos, int h, int chun
 
 // 3: softmax-weighted head outputs from the chunks, then x += head_out·W_O
 // for 32 columns (src/inference.c:307-309).
-__device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int item, Smem &S) {
+__device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int item, Smem &S,
+                           int st) {
     const Dims &D = A.D;
     const int nch = (pos + 1 + CH - 1) / CH;
     const int lane = threadIdx.x & 31, col = item * 32 + lane;
     MatvecPre P;                       // W_O rows do not wait for the attention output
     matvec32_preload(Lp.w_o, D.nq, D.d, col, col < D.d, P);
-    pdl_wait();
+    // Flag mode: the residual stream is final once this layer's Q/K/V stage
+    // is done (it waited for the previous layer's down stage, or wrote the
+    // embedding), which every attention CTA had seen before this kernel was
+    // launched; so this wait returns at once and the residual loads now.
+    const bool early_x = A.flags == 1 && st > 0;
+    float xres = 0.0f;
+    if (early_x) {
+        flag_wait(A, st - 2, stage_ctas(A, st - 2));
+        if (threadIdx.x < 32 && col < D.d) xres = ldcg(A.x + col);
+    }
+    stage_wait(A, st);
     for (int t = threadIdx.x; t < D.nq; t += kThreads) {
         const int h = t / D.hd, i = t % D.hd;
         const float *ph = A.part + (size_t)h * D.nchunk * (D.hd + 2);
@@ -388,7 +480,7 @@ __device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int 
     }
     __syncthreads();
     const float v = matvec32(S.xn, Lp.w_o, D.nq, D.d, col, col < D.d, S, &P);
-    if (threadIdx.x < 32 && col < D.d) A.x[col] = __fadd_rn(ldcg(A.x + col), v);
+    if (threadIdx.x < 32 && col < D.d) A.x[col] = __fadd_rn(early_x ? xres : ldcg(A.x + col), v);
 }
 
 // 4 (once per CTA before its up/gate items): RMSNorm into S.xn, router
@@ -397,7 +489,7 @@ __device__ void oproj_item(const StepArgs &A, const LayerPtrs &Lp, int pos, int 
 // the ids and weights for the down stage, and the normalised vector into
 // the layer's trace row.
 __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, int layer, bool publish,
-                          Smem &S) {
+                          Smem &S, int st) {
     const Dims &D = A.D;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // the first 16 router weights of this lane's first expert, before the
@@ -408,7 +500,7 @@ __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, int layer, boo
         const int i = lane + 32 * u;
         w0[u] = (warp < Lp.E && i < D.d) ? __ldg(Lp.router + (size_t)i * Lp.E + warp) : 0.0f;
     }
-    pdl_wait();
+    stage_wait(A, st);
     rmsnorm_to_smem(A.x, Lp.rms_ffn, D, S);
     if (publish)
         for (int i = threadIdx.x; i < D.d; i += kThreads) A.trace[(size_t)layer * 2 * D.d + i] = S.xn[i];
@@ -434,8 +526,13 @@ __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, int layer, boo
     __syncthreads();
     if (threadIdx.x == 0) {
         route_token(S.lg, Lp.E, Lp.k, S.sel, S.w);
-        if (publish)
+        if (publish) {
             for (int r = 0; r < Lp.k; r++) { A.ids[r] = S.sel[r]; A.wts[r] = S.w[r]; }
+            if (A.flags == 1) {                 // the down stage may load its rows now
+                __threadfence();
+                atomicAdd(A.done + 5 * A.L + 1 + layer, 1u);
+            }
+        }
     }
     __syncthreads();
 }
@@ -453,59 +550,79 @@ __device__ __forceinline__ void prefetch_down(const StepArgs &A, const LayerPtrs
     }
 }
 
-// 5: 8 hidden units of rank r: one warp per unit f, the gate and up rows of
-// expert S.sel[r] in the packed layout (128 gate rows, then the matching
-// 128 up rows), dot x_norm, the reference's silu(gate)·up into h[r][f].
+// 5: kUnitsPerCta hidden units of rank r, kUnitsPerWarp consecutive units
+// per warp (their loads in flight together): the gate and up rows of expert
+// S.sel[r] in the packed layout (128 gate rows, then the matching 128 up
+// rows), dot x_norm, the reference's silu(gate)·up into h[r][f].
 __device__ void upgate_item(const StepArgs &A, const LayerPtrs &Lp, int item, Smem &S) {
     const Dims &D = A.D;
-    const int nfb = (Lp.F + 7) / 8;
-    const int r = item / nfb, f = (item % nfb) * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (f >= Lp.F) return;
+    const int nfb = (Lp.F + kUnitsPerCta - 1) / kUnitsPerCta;
+    const int r = item / nfb, lane = threadIdx.x & 31;
+    const int f0 = (item % nfb) * kUnitsPerCta + (threadIdx.x >> 5) * kUnitsPerWarp;
+    if (f0 >= Lp.F) return;
     const int e = S.sel[r];
-    const size_t grow = (size_t)e * 2 * Lp.F_pad + (size_t)(f / 128) * 256 + (f % 128);
-    const float4 *gw = reinterpret_cast<const float4 *>(Lp.ug + grow * D.d_pad);
-    const float4 *uw = reinterpret_cast<const float4 *>(Lp.ug + (grow + 128) * D.d_pad);
-    const float4 *x4 = reinterpret_cast<const float4 *>(S.xn);
-    float g = 0.0f, u = 0.0f;
-    const int n4 = D.d_pad / 4;
-    for (int i0 = lane; i0 < n4; i0 += 32 * 4) {        // 4 gate/up float4 pairs in flight
-        float4 a[4], b[4];
+    const float4 *gw[kUnitsPerWarp], *uw[kUnitsPerWarp];
+    bool on[kUnitsPerWarp];
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int i = i0 + 32 * q;
-            a[q] = i < n4 ? __ldg(gw + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-            b[q] = i < n4 ? __ldg(uw + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int i = i0 + 32 * q;
-            if (i >= n4) break;
-            const float4 xv = x4[i];
-            g = __fmaf_rn(xv.x, a[q].x, g); g = __fmaf_rn(xv.y, a[q].y, g);
-            g = __fmaf_rn(xv.z, a[q].z, g); g = __fmaf_rn(xv.w, a[q].w, g);
-            u = __fmaf_rn(xv.x, b[q].x, u); u = __fmaf_rn(xv.y, b[q].y, u);
-            u = __fmaf_rn(xv.z, b[q].z, u); u = __fmaf_rn(xv.w, b[q].w, u);
-        }
+    for (int v = 0; v < kUnitsPerWarp; v++) {
+        const int f = f0 + v;
+        on[v] = f < Lp.F;
+        const size_t grow = (size_t)e * 2 * Lp.F_pad + (size_t)(f / 128) * 256 + (f % 128);
+        gw[v] = reinterpret_cast<const float4 *>(Lp.ug + grow * D.d_pad);
+        uw[v] = reinterpret_cast<const float4 *>(Lp.ug + (grow + 128) * D.d_pad);
     }
-    g = warp_sum(g);
-    u = warp_sum(u);
-    if (lane == 0) A.h[(size_t)r * Lp.F_pad + f] = swiglu_ref(g, u);
+    const float4 *x4 = reinterpret_cast<const float4 *>(S.xn);
+    float g[kUnitsPerWarp], u[kUnitsPerWarp];
+#pragma unroll
+    for (int v = 0; v < kUnitsPerWarp; v++) g[v] = u[v] = 0.0f;
+    const int n4 = D.d_pad / 4;
+    for (int i0 = lane; i0 < n4; i0 += 32 * 4) {        // 4 gate/up float4 pairs per unit in flight
+        float4 a[kUnitsPerWarp][4], b[kUnitsPerWarp][4];
+#pragma unroll
+        for (int v = 0; v < kUnitsPerWarp; v++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const int i = i0 + 32 * q;
+                const bool ok = on[v] && i < n4;
+                a[v][q] = ok ? __ldg(gw[v] + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                b[v][q] = ok ? __ldg(uw[v] + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+        for (int v = 0; v < kUnitsPerWarp; v++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const int i = i0 + 32 * q;
+                if (i >= n4) break;
+                const float4 xv = x4[i];
+                g[v] = __fmaf_rn(xv.x, a[v][q].x, g[v]); g[v] = __fmaf_rn(xv.y, a[v][q].y, g[v]);
+                g[v] = __fmaf_rn(xv.z, a[v][q].z, g[v]); g[v] = __fmaf_rn(xv.w, a[v][q].w, g[v]);
+                u[v] = __fmaf_rn(xv.x, b[v][q].x, u[v]); u[v] = __fmaf_rn(xv.y, b[v][q].y, u[v]);
+                u[v] = __fmaf_rn(xv.z, b[v][q].z, u[v]); u[v] = __fmaf_rn(xv.w, b[v][q].w, u[v]);
+            }
+    }
+#pragma unroll
+    for (int v = 0; v < kUnitsPerWarp; v++) {
+        const float gs = warp_sum(g[v]), us = warp_sum(u[v]);
+        if (lane == 0 && on[v]) A.h[(size_t)r * Lp.F_pad + f0 + v] = swiglu_ref(gs, us);
+    }
 }
 
 // 6: one warp per (output column, rank): y_r = h_r·W_down[ids[r]] row j
 // (packed [d_pad × F_pad]), then x[j] += w_0·y_0 + w_1·y_1 + ... in rank
 // order (src/transformer.c:355-358).  A CTA's 8 warps cover down_cols(k)
-// columns, so the k rows of a column load in parallel.
+// columns, so the k rows of a column load in parallel.  The sum runs over
+// the row in batches of 8 float4 per lane (padding lanes add 0·0).
 __host__ __device__ inline int down_cols(int k) { return k >= kThreads / 32 ? 1 : (kThreads / 32) / k; }
 
-__device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int item, Smem &S) {
+__device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int item, Smem &S,
+                          int st) {
     const Dims &D = A.D;
     const int cols = down_cols(Lp.k);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cw = warp / Lp.k, r = warp - cw * Lp.k;
     const int j = item * cols + cw;
     float y = 0.0f;
-    pdl_wait();
+    stage_wait(A, st);
     if (cw < cols && j < D.d) {
         const int e = __ldcg(A.ids + r);
         const float4 *wr = reinterpret_cast<const float4 *>(Lp.dn + ((size_t)e * D.d_pad + j) * Lp.F_pad);
@@ -542,13 +659,87 @@ __device__ void down_item(const StepArgs &A, const LayerPtrs &Lp, int layer, int
     __syncthreads();                   // S.red is reused by the next item
 }
 
+// Flag mode, the same arithmetic as down_item with the expert rows loaded
+// before the up/gate stage finishes: the up/gate stage's first CTA publishes
+// the layer's ids and weights right after it routes the token (done counter
+// ids_ready(layer)), so a CTA here waits for that, loads the first kDownPre
+// float4 of each lane's weight row (and the residual of its columns, final
+// since the W_O stage), and only then waits for h.  h (k × F_pad floats) is
+// staged in shared memory by the whole CTA.  Used when the rows fit
+// (F_pad ≤ 4 · 32 · kDownPre, k · F_pad ≤ kMaxD).
+constexpr int kDownPre = 16;            // two batches of 8
+__device__ __forceinline__ int ids_ready(const StepArgs &A, int layer) { return 5 * A.L + 1 + layer; }
+__device__ __forceinline__ bool down_flag_fits(const LayerPtrs &Lp) {
+    return Lp.F_pad / 4 <= 32 * kDownPre && Lp.k * Lp.F_pad <= kMaxD;
+}
+
+__device__ void down_item_flag(const StepArgs &A, const LayerPtrs &Lp, int layer, int item,
+                               Smem &S, int st) {
+    const Dims &D = A.D;
+    const int cols = down_cols(Lp.k);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cw = warp / Lp.k, r = warp - cw * Lp.k;
+    const int j = item * cols + cw;
+    const bool active = cw < cols && j < D.d;
+    const int n4 = Lp.F_pad / 4;
+    flag_wait(A, ids_ready(A, layer), 1u);
+    if (threadIdx.x < Lp.k) {
+        S.sel[threadIdx.x] = __ldcg(A.ids + threadIdx.x);
+        S.w[threadIdx.x] = ldcg(A.wts + threadIdx.x);
+    }
+    __syncthreads();
+    float4 wp[kDownPre];
+    if (active) {
+        const float4 *wr =
+            reinterpret_cast<const float4 *>(Lp.dn + ((size_t)S.sel[r] * D.d_pad + j) * Lp.F_pad);
+#pragma unroll
+        for (int u = 0; u < kDownPre; u++) {
+            const int i = lane + 32 * u;
+            wp[u] = i < n4 ? __ldg(wr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    const int jj = item * cols + threadIdx.x;
+    const float xres = (threadIdx.x < cols && jj < D.d) ? ldcg(A.x + jj) : 0.0f;
+    stage_wait(A, st);
+    {
+        const float4 *h4 = reinterpret_cast<const float4 *>(A.h);
+        float4 *s4 = reinterpret_cast<float4 *>(S.xn);
+        for (int i = threadIdx.x; i < Lp.k * n4; i += kThreads) s4[i] = __ldcg(h4 + i);
+    }
+    __syncthreads();
+    float y = 0.0f;
+    if (active) {
+        const float4 *hr = reinterpret_cast<const float4 *>(S.xn) + (size_t)r * n4;
+        // batches of 8 as in down_item, each run only where its loop would run it
+#pragma unroll
+        for (int u = 0; u < kDownPre; u++) {
+            if (lane + 32 * 8 * (u / 8) >= n4) break;
+            const int i = lane + 32 * u;
+            const float4 hb = i < n4 ? hr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            y = __fmaf_rn(hb.x, wp[u].x, y); y = __fmaf_rn(hb.y, wp[u].y, y);
+            y = __fmaf_rn(hb.z, wp[u].z, y); y = __fmaf_rn(hb.w, wp[u].w, y);
+        }
+        y = warp_sum(y);
+    }
+    if (lane == 0) S.red[warp] = y;
+    __syncthreads();
+    if (threadIdx.x < cols && jj < D.d) {
+        float out = 0.0f;
+        for (int rr = 0; rr < Lp.k; rr++)
+            out = __fmaf_rn(S.w[rr], S.red[threadIdx.x * Lp.k + rr], out);
+        A.trace[((size_t)layer * 2 + 1) * D.d + jj] = out;
+        A.x[jj] = __fadd_rn(xres, out);
+    }
+    __syncthreads();
+}
+
 // 7: final RMSNorm and 32 columns of the LM head (x_norm·lm_head, [d × vocab]).
-__device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S) {
+__device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S, int st) {
     const Dims &D = A.D;
     const int lane = threadIdx.x & 31, col = item * 32 + lane;
     MatvecPre P;
     matvec32_preload(A.lm_head, D.d, D.vocab, col, col < D.vocab, P);
-    pdl_wait();
+    stage_wait(A, st);
     if (!normed) rmsnorm_to_smem(A.x, A.rms_final, D, S);
     const float v = matvec32(S.xn, A.lm_head, D.d, D.vocab, col, col < D.vocab, S, &P);
     if (threadIdx.x < 32 && col < D.vocab) A.logits[col] = v;
@@ -560,37 +751,50 @@ __global__ void __launch_bounds__(kThreads) qkv_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
-    qkv_item(A, Lp, layer, A.state[0], A.state[1], blockIdx.x, S);
+    const int st = 5 * layer;
+    qkv_item(A, Lp, layer, A.state[0], A.state[1], blockIdx.x, S, st);
+    stage_signal(A, st);
 }
 __global__ void __launch_bounds__(kThreads) attn_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
-    const int pos = A.state[1];
-    if ((int)blockIdx.y * CH > pos) return;
-    attn_item(A, layer, pos, blockIdx.x, blockIdx.y, S);
+    const int pos = A.state[1], st = 5 * layer + 1;
+    // chunks past the step's position have no work (they still count as done)
+    if ((int)blockIdx.y * CH <= pos) attn_item(A, layer, pos, blockIdx.x, blockIdx.y, S, st);
+    stage_signal(A, st);
 }
-__global__ void __launch_bounds__(kThreads) oproj_kernel(StepArgs A, int layer) {
+__global__ void __launch_bounds__(kThreads, 1) oproj_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
-    oproj_item(A, A.layers[layer], A.state[1], blockIdx.x, S);
+    const int st = 5 * layer + 2;
+    oproj_item(A, A.layers[layer], A.state[1], blockIdx.x, S, st);
+    stage_signal(A, st);
 }
 __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
-    route_cta(A, Lp, layer, blockIdx.x == 0, S);
-    prefetch_down(A, Lp, blockIdx.x * kThreads + threadIdx.x, gridDim.x * kThreads, S);
+    const int st = 5 * layer + 3;
+    route_cta(A, Lp, layer, blockIdx.x == 0, S, st);
+    // in flag mode the down stage loads its rows itself once the ids are out
+    if (A.flags != 1 || !down_flag_fits(Lp))
+        prefetch_down(A, Lp, blockIdx.x * kThreads + threadIdx.x, gridDim.x * kThreads, S);
     upgate_item(A, Lp, blockIdx.x, S);
+    stage_signal(A, st);
 }
-__global__ void __launch_bounds__(kThreads) down_kernel(StepArgs A, int layer) {
+__global__ void __launch_bounds__(kThreads, 1) down_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
-    down_item(A, A.layers[layer], layer, blockIdx.x, S);
+    const int st = 5 * layer + 4;
+    const LayerPtrs Lp = A.layers[layer];
+    if (A.flags == 1 && down_flag_fits(Lp)) down_item_flag(A, Lp, layer, blockIdx.x, S, st);
+    else down_item(A, Lp, layer, blockIdx.x, S, st);
+    stage_signal(A, st);
 }
 __global__ void __launch_bounds__(kThreads) lmhead_kernel(StepArgs A) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
-    lmhead_item(A, blockIdx.x, false, S);
+    lmhead_item(A, blockIdx.x, false, S, 5 * A.L);
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         A.state[1] += 1;
         *(volatile int *)A.err_host = *(volatile int *)A.err;   // read by the host after the step
@@ -633,27 +837,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(StepArgs A) {
     const int nch = (pos + 1 + CH - 1) / CH;
     for (int l = 0; l < A.L; l++) {
         const LayerPtrs Lp = A.layers[l];
-        for (int it = b; it < n_qkv; it += G) qkv_item(A, Lp, l, token, pos, it, S);
+        for (int it = b; it < n_qkv; it += G) qkv_item(A, Lp, l, token, pos, it, S, -1);
         if (!grid_barrier(A, ++phase * G, S)) return;
-        for (int it = b; it < D.nh * nch; it += G) attn_item(A, l, pos, it / nch, it % nch, S);
+        for (int it = b; it < D.nh * nch; it += G) attn_item(A, l, pos, it / nch, it % nch, S, -1);
         if (!grid_barrier(A, ++phase * G, S)) return;
-        for (int it = b; it < n_col; it += G) oproj_item(A, Lp, pos, it, S);
+        for (int it = b; it < n_col; it += G) oproj_item(A, Lp, pos, it, S, -1);
         if (!grid_barrier(A, ++phase * G, S)) return;
-        const int n_ug = Lp.k * ((Lp.F + 7) / 8);
+        const int n_ug = Lp.k * ((Lp.F + kUnitsPerCta - 1) / kUnitsPerCta);
         if (b < n_ug) {
-            route_cta(A, Lp, l, b == 0, S);
+            route_cta(A, Lp, l, b == 0, S, -1);
             prefetch_down(A, Lp, b * kThreads + threadIdx.x, min(G, n_ug) * kThreads, S);
             for (int it = b; it < n_ug; it += G) upgate_item(A, Lp, it, S);
         }
         if (!grid_barrier(A, ++phase * G, S)) return;
         const int n_down = (D.d + down_cols(Lp.k) - 1) / down_cols(Lp.k);
-        for (int it = b; it < n_down; it += G) down_item(A, Lp, l, it, S);
+        for (int it = b; it < n_down; it += G) down_item(A, Lp, l, it, S, -1);
         if (!grid_barrier(A, ++phase * G, S)) return;
     }
     const int n_lm = (D.vocab + 31) / 32;
     bool normed = false;
     for (int it = b; it < n_lm; it += G) {
-        lmhead_item(A, it, normed, S);
+        lmhead_item(A, it, normed, S, -1);
         normed = true;                  // S.xn keeps the normalised vector across items
     }
     if (b == 0 && threadIdx.x == 0) {
@@ -686,6 +890,7 @@ struct moe_b200_decoder {
           *wts = nullptr;
     int *state = nullptr, *ids = nullptr;        // state = {token, pos}
     unsigned *bar = nullptr;
+    unsigned *done = nullptr;                    // [6 L + 1], StepArgs::done
     int *err = nullptr;
     int *h_err = nullptr;                        // mapped pinned copy of err (StepArgs::err_host)
     int *d_err_host = nullptr;                   // its device address
@@ -698,8 +903,8 @@ struct moe_b200_decoder {
     int launches = 0;
     // programmatic dependent launch of the stage kernels: 0 off, 1 each kernel
     // lets the next one launch on entry, 2 the next one launches as the
-    // current one's CTAs exit
-    int pdl = 2;
+    // current one's CTAs exit, 3 flag mode (see stage_wait)
+    int pdl = 3;
 };
 
 namespace {
@@ -730,7 +935,7 @@ void free_all(moe_b200_decoder *m) {
     cudaFree(m->rope_cos); cudaFree(m->rope_sin); cudaFree(m->kc); cudaFree(m->vc);
     cudaFree(m->x); cudaFree(m->q); cudaFree(m->part); cudaFree(m->h);
     cudaFree(m->logits); cudaFree(m->wts); cudaFree(m->state); cudaFree(m->ids);
-    cudaFree(m->bar); cudaFree(m->err); cudaFree(m->trace);
+    cudaFree(m->bar); cudaFree(m->done); cudaFree(m->err); cudaFree(m->trace);
     if (m->h_token) cudaFreeHost(m->h_token);
     if (m->h_err) cudaFreeHost(m->h_err);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -750,6 +955,8 @@ StepArgs step_args(const moe_b200_decoder *m) {
     A.trace = m->trace;
     A.err_host = m->d_err_host;
     A.pdl_early = m->pdl == 1;
+    A.flags = (m->flags & MOE_B200_DECODER_PERSISTENT) ? 0 : m->pdl == 3 ? 1 : m->pdl == 4 ? 2 : 0;
+    A.done = m->done;
     return A;
 }
 
@@ -779,7 +986,9 @@ int enqueue_step(moe_b200_decoder *m) {
     }
     // every kernel but the step's first may start while its predecessor
     // runs (programmatic dependent launch; the kernels order their reads and
-    // writes with griddepcontrol, see pdl_wait)
+    // writes with griddepcontrol or, in flag mode, the done[] counters,
+    // zeroed here: see stage_wait)
+    if (m->pdl >= 3) DCK(cudaMemsetAsync(m->done, 0, (size_t)(6 * m->L + 1) * sizeof(unsigned), s));
     int n = 0;
     auto launch = [&](auto kernel, dim3 grid, auto... args) -> cudaError_t {
         cudaLaunchConfig_t cfg = {};
@@ -799,7 +1008,7 @@ int enqueue_step(moe_b200_decoder *m) {
         DCK(launch(qkv_kernel, dim3(ceil_div(D.qkv, 32)), A, l));
         DCK(launch(attn_kernel, dim3(D.nh, D.nchunk), A, l));
         DCK(launch(oproj_kernel, dim3(ceil_div(D.d, 32)), A, l));
-        DCK(launch(upgate_kernel, dim3(w->k * ceil_div(w->F, 8)), A, l));
+        DCK(launch(upgate_kernel, dim3(w->k * ceil_div(w->F, kUnitsPerCta)), A, l));
         DCK(launch(down_kernel, dim3(ceil_div(D.d, down_cols(w->k))), A, l));
     }
     DCK(launch(lmhead_kernel, dim3(ceil_div(D.vocab, 32)), A));
@@ -892,6 +1101,7 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
         cudaMalloc(&m->ids, kMaxTopK * 4) != cudaSuccess ||
         cudaMalloc(&m->state, 2 * 4) != cudaSuccess ||
         cudaMalloc(&m->bar, 4) != cudaSuccess || cudaMalloc(&m->err, 4) != cudaSuccess ||
+        cudaMalloc(&m->done, (size_t)(6 * L + 1) * sizeof(unsigned)) != cudaSuccess ||
         cudaMalloc(&m->trace, (size_t)m->L * 2 * d * 4) != cudaSuccess ||
         cudaMallocHost(&m->h_token, 4) != cudaSuccess ||
         cudaHostAlloc(&m->h_err, 4, cudaHostAllocMapped) != cudaSuccess ||
