@@ -112,6 +112,86 @@ MOE_DEV void route_token(float *row, int E, int k, int *sel, float *w) {
     }
 }
 
+// route_token for E <= 8 with the row in registers: the same arithmetic in
+// the same order (E = 8: one 8-lane chunk, hsum tree; E < 8: the scalar
+// tail only), every array indexed by compile-time constants.  For a single
+// thread on the latency path (the device decode step), where route_token's
+// dependent shared-memory accesses cost microseconds.
+MOE_DEV void route_token8(float *row_io, int E, int k, int *sel, float *w) {
+    float row[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) row[e] = e < E ? row_io[e] : 0.0f;
+    float mx = -1e38f;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < E) mx = fmaxf(mx, row[e]);
+    if (E == 8) {
+        float lane[8];
+#pragma unroll
+        for (int l = 0; l < 8; l++) {
+            row[l] = exp_ref(__fsub_rn(row[l], mx));
+            lane[l] = __fadd_rn(0.0f, row[l]);
+        }
+        const float a0 = __fadd_rn(lane[0], lane[4]), a1 = __fadd_rn(lane[1], lane[5]);
+        const float a2 = __fadd_rn(lane[2], lane[6]), a3 = __fadd_rn(lane[3], lane[7]);
+        const float sum = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
+        const float inv = __fdiv_rn(1.0f, sum);
+#pragma unroll
+        for (int l = 0; l < 8; l++) row[l] = __fmul_rn(row[l], inv);
+    } else {
+        // no full 8-lane chunk: the zero lanes sum to 0, then the scalar tail
+        float sum = __fadd_rn(__fadd_rn(0.0f, 0.0f), __fadd_rn(0.0f, 0.0f));
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            if (e < E) {
+                row[e] = expf(__fsub_rn(row[e], mx));
+                sum = __fadd_rn(sum, row[e]);
+            }
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            if (e < E) row[e] = __fdiv_rn(row[e], sum);
+    }
+    int pick[kMaxTopK];
+    float pv[kMaxTopK];
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; r++) { pick[r] = -1; pv[r] = 0.0f; }
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; r++) {
+        if (r >= k) break;
+        float best = -1.0f;
+        int best_e = 0;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            if (e >= E) break;
+            bool taken = false;
+#pragma unroll
+            for (int q = 0; q < kMaxTopK; q++) taken |= (pick[q] == e);
+            if (!taken && row[e] > best) { best = row[e]; best_e = e; }
+        }
+        pick[r] = best_e;
+        float v = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            if (e == best_e) v = row[e];
+        pv[r] = v;
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; r++)
+        if (r < k) s = __fadd_rn(s, pv[r]);
+    const float winv = (s > 1e-9f) ? __fdiv_rn(1.0f, s) : 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; r++) {
+        if (r < k) {
+            sel[r] = pick[r];
+            w[r] = __fmul_rn(pv[r], winv);
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < E) row_io[e] = row[e];
+}
+
 // Round an fp32 value to the nearest TF32 (10-bit mantissa, ties away
 // from zero), returned as fp32 bits with the low 13 mantissa bits zero.
 // tcgen05 kind::tf32 reads only the TF32 bits of its fp32 operands, i.e.

@@ -144,6 +144,13 @@ __device__ inline unsigned stage_ctas(const StepArgs &A, int s) {
     }
 }
 
+// n floats from p into L2, one 128-byte line per thread of `nthreads`
+// (thread t of them); no registers held, nothing waits for it.
+__device__ __forceinline__ void prefetch_l2(const float *p, size_t n, int t, int nthreads) {
+    for (size_t l = t; l < (n + 31) / 32; l += nthreads)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p + l * 32));
+}
+
 // Flag mode: wait (thread 0, then the CTA) until done[idx] reaches target.
 __device__ __forceinline__ void flag_wait(const StepArgs &A, int idx, unsigned target) {
     if (threadIdx.x == 0) {
@@ -525,7 +532,8 @@ __device__ void route_cta(const StepArgs &A, const LayerPtrs &Lp, int layer, boo
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        route_token(S.lg, Lp.E, Lp.k, S.sel, S.w);
+        if (Lp.E <= 8) route_token8(S.lg, Lp.E, Lp.k, S.sel, S.w);
+        else route_token(S.lg, Lp.E, Lp.k, S.sel, S.w);
         if (publish) {
             for (int r = 0; r < Lp.k; r++) { A.ids[r] = S.sel[r]; A.wts[r] = S.w[r]; }
             if (A.flags == 1) {                 // the down stage may load its rows now
@@ -682,6 +690,13 @@ __device__ void down_item_flag(const StepArgs &A, const LayerPtrs &Lp, int layer
     const int j = item * cols + cw;
     const bool active = cw < cols && j < D.d;
     const int n4 = Lp.F_pad / 4;
+    // the next stage's weights into L2 while this layer's up/gate runs: its
+    // CTAs then preload them from L2 instead of HBM
+    {
+        const int t = blockIdx.x * kThreads + threadIdx.x, nt = gridDim.x * kThreads;
+        if (layer + 1 < A.L) prefetch_l2(A.layers[layer + 1].w_qkv, (size_t)D.d * D.qkv, t, nt);
+        else prefetch_l2(A.lm_head, (size_t)D.d * D.vocab, t, nt);
+    }
     flag_wait(A, ids_ready(A, layer), 1u);
     if (threadIdx.x < Lp.k) {
         S.sel[threadIdx.x] = __ldcg(A.ids + threadIdx.x);
