@@ -74,6 +74,8 @@ struct StepArgs {
     int pdl_early;                     // stage kernels: let the next kernel launch on entry
     int flags;                         // stage kernels hand off through done[] (see stage_wait):
                                        // 1 the next kernel may launch after a CTA's wait, 2 after its work
+    int early_mask;                    // flag mode: stage kinds (bit 0 qkv .. 4 down) whose CTAs
+                                       // let the next kernel launch on entry
     unsigned *done;                    // [6 L + 1] CTAs finished per stage, then per layer the
                                        // up/gate stage's ids-published count (zeroed before each step)
 };
@@ -765,6 +767,7 @@ __device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S, i
 __global__ void __launch_bounds__(kThreads) qkv_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
+    if (A.flags == 1 && (A.early_mask >> 0 & 1)) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
     const int st = 5 * layer;
     qkv_item(A, Lp, layer, A.state[0], A.state[1], blockIdx.x, S, st);
@@ -773,6 +776,7 @@ __global__ void __launch_bounds__(kThreads) qkv_kernel(StepArgs A, int layer) {
 __global__ void __launch_bounds__(kThreads) attn_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
+    if (A.flags == 1 && (A.early_mask >> 1 & 1)) pdl_trigger();
     const int pos = A.state[1], st = 5 * layer + 1;
     // chunks past the step's position have no work (they still count as done)
     if ((int)blockIdx.y * CH <= pos) attn_item(A, layer, pos, blockIdx.x, blockIdx.y, S, st);
@@ -781,6 +785,7 @@ __global__ void __launch_bounds__(kThreads) attn_kernel(StepArgs A, int layer) {
 __global__ void __launch_bounds__(kThreads, 1) oproj_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
+    if (A.flags == 1 && (A.early_mask >> 2 & 1)) pdl_trigger();
     const int st = 5 * layer + 2;
     oproj_item(A, A.layers[layer], A.state[1], blockIdx.x, S, st);
     stage_signal(A, st);
@@ -788,6 +793,7 @@ __global__ void __launch_bounds__(kThreads, 1) oproj_kernel(StepArgs A, int laye
 __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
+    if (A.flags == 1 && (A.early_mask >> 3 & 1)) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
     const int st = 5 * layer + 3;
     route_cta(A, Lp, layer, blockIdx.x == 0, S, st);
@@ -800,6 +806,7 @@ __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer)
 __global__ void __launch_bounds__(kThreads, 1) down_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
     if (A.pdl_early) pdl_trigger();
+    if (A.flags == 1 && (A.early_mask >> 4 & 1)) pdl_trigger();
     const int st = 5 * layer + 4;
     const LayerPtrs Lp = A.layers[layer];
     if (A.flags == 1 && down_flag_fits(Lp)) down_item_flag(A, Lp, layer, blockIdx.x, S, st);
@@ -920,6 +927,9 @@ struct moe_b200_decoder {
     // lets the next one launch on entry, 2 the next one launches as the
     // current one's CTAs exit, 3 flag mode (see stage_wait)
     int pdl = 3;
+    // flag mode: stage kinds whose CTAs trigger the next launch on entry;
+    // the down stage by default (c2 0.1466 -> 0.1461 ms; every stage: 0.168)
+    int early_mask = 16;
 };
 
 namespace {
@@ -972,6 +982,7 @@ StepArgs step_args(const moe_b200_decoder *m) {
     A.pdl_early = m->pdl == 1;
     A.flags = (m->flags & MOE_B200_DECODER_PERSISTENT) ? 0 : m->pdl == 3 ? 1 : m->pdl == 4 ? 2 : 0;
     A.done = m->done;
+    A.early_mask = m->early_mask;
     return A;
 }
 
@@ -1064,6 +1075,7 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
     cudaGetDevice(&m->device);
     m->flags = flags;
     if (const char *p = std::getenv("MOE_B200_DECODER_PDL")) m->pdl = std::atoi(p);
+    if (const char *p = std::getenv("MOE_B200_DECODER_EARLY")) m->early_mask = std::atoi(p);
     Dims &D = m->D;
     D.d = d; D.d_pad = round_up(d, 128); D.nh = nh; D.nkv = nkv; D.hd = hd; D.nq = nh * hd;
     D.kvd = nkv * hd; D.qkv = D.nq + 2 * D.kvd; D.vocab = c.vocab_size; D.max_seq = max_seq;
