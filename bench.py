@@ -79,7 +79,12 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons, sampled during the timed region."""
+    """nvidia-smi clocks and throttle reasons, sampled during the timed region.
+
+    nvidia-smi takes a few hundred milliseconds to print its first sample, so
+    entering the context waits (up to 3 s) until the first sample has arrived:
+    the samples then cover the timed region even when it is short (a multi-GPU
+    step of ~10 ms), at 50 ms intervals."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -88,27 +93,38 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.lines = []
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.strip():
+                self.lines.append(line)
+                self.first.set()
 
     def __enter__(self):
+        import threading
+        self.first = threading.Event()
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            self.first.wait(timeout=3.0)
+            self.lines = []              # the first sample precedes the timed region
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *a):
-        self.lines = []
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            self.reader.join(timeout=5)
 
     def summary(self):
         sm, mx, reasons = [], 0.0, set()

@@ -294,7 +294,9 @@ int moe_b200_device_info(int device, int *num_sms, int *cta_pairs);
  * llm.c beyond inference_step itself. */
 typedef struct moe_b200_decoder moe_b200_decoder;
 /* flags: 0 or MOE_B200_DECODER_STAGE_KERNELS = one kernel per stage (31
- * for six layers, the faster variant measured, the default);
+ * for six layers, the faster variant measured, the default; the stages hand
+ * off through completion counters, see INTEGRATION.md for the
+ * MOE_B200_DECODER_PDL / MOE_B200_DECODER_EARLY environment variables);
  * MOE_B200_DECODER_PERSISTENT = the whole step as ONE persistent cooperative
  * kernel (one CTA per SM, stages separated by a bounded grid-wide barrier).
  * Both run the same arithmetic and give the same bits; asking for both is
