@@ -295,8 +295,10 @@ int moe_b200_device_info(int device, int *num_sms, int *cta_pairs);
 typedef struct moe_b200_decoder moe_b200_decoder;
 /* flags: 0 or MOE_B200_DECODER_STAGE_KERNELS = one kernel per stage (31
  * for six layers, the faster variant measured, the default; the stages hand
- * off through completion counters, see INTEGRATION.md for the
- * MOE_B200_DECODER_PDL / MOE_B200_DECODER_EARLY environment variables);
+ * off through per-stage completion counters; the environment variable
+ * MOE_B200_DECODER_PDL=2 selects griddepcontrol.wait hand-offs instead, and
+ * MOE_B200_DECODER_EARLY is a bit mask of stage kinds whose CTAs let the
+ * next kernel be placed on entry, default 16 = the down stage);
  * MOE_B200_DECODER_PERSISTENT = the whole step as ONE persistent cooperative
  * kernel (one CTA per SM, stages separated by a bounded grid-wide barrier).
  * Both run the same arithmetic and give the same bits; asking for both is
