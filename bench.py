@@ -293,6 +293,45 @@ def reference_decode_ms(dec, steps, threads, prefill=()):
     return step_ms, moe_ms
 
 
+def stage_timeline(M, dec, cfg, prefill, toks):
+    """The device decoder's stage timeline (a decoder made with
+    MOE_B200_DECODER_STAMPS=1, outside the timed loops): per stage kind, the
+    median over layers and steps of its hand-off (its first CTA's return from
+    the wait, after the previous stage's last CTA exit), its work (last exit
+    after the last wait) and its span (last exit after the previous stage's
+    last exit), in microseconds; plus the step's device time."""
+    os.environ["MOE_B200_DECODER_STAMPS"] = "1"
+    try:
+        tdec = M.Decoder(C.addressof(dec.model), cfg.max_seq)
+    finally:
+        del os.environ["MOE_B200_DECODER_STAMPS"]
+    for t in prefill:
+        tdec.step(int(t))
+    kinds = ["qkv", "attn", "oproj", "upgate", "down"]
+    per = {k: {"handoff": [], "work": [], "span": []} for k in kinds + ["lmhead"]}
+    total = []
+    for t in toks:
+        tdec.step(int(t))
+        st = tdec.stage_times(cfg.n_layers)
+        prev_exit = 0.0
+        for i in range(st.shape[0]):
+            k = "lmhead" if i == st.shape[0] - 1 else kinds[i % 5]
+            entry, w0, w1, ex = st[i]
+            if i > 0:
+                per[k]["handoff"].append(w0 - prev_exit)
+                per[k]["span"].append(ex - prev_exit)
+            per[k]["work"].append(ex - w1)
+            prev_exit = ex
+        total.append(st[-1, 3])
+    tdec.free()
+    med = lambda v: float(np.median(v)) if v else None
+    return {"device_us_per_step": med(total), "steps": len(toks),
+            "stages_us": {k: {m: med(v) for m, v in d.items()} for k, d in per.items()},
+            "what": "median over layers and steps: handoff = first return from the wait after "
+                    "the previous stage's last CTA exit; work = last exit after the last wait; "
+                    "span = last exit after the previous stage's last exit (globaltimer stamps)"}
+
+
 def run_decode(args):
     import torch  # noqa: F401  (CUDA context before the library, as in the other arms)
     import moe_b200 as M
@@ -355,6 +394,7 @@ def run_decode(args):
     e2e_ms = 1000.0 * (time.perf_counter() - t0) / args.steps
     launches = ddec.launches
     ddec.free()
+    timeline = stage_timeline(M, dec, cfg, prefill, toks[args.warmup:]) if args.stage_times else None
     # the same step as one persistent cooperative kernel (one launch per step)
     sdec = M.Decoder(C.addressof(dec.model), cfg.max_seq, M.Decoder.PERSISTENT)
     for t in prefill:
@@ -433,6 +473,8 @@ def run_decode(args):
         "gpu_launches": launches * args.steps,
         "clocks": clk.summary(),
     }
+    if timeline is not None:
+        line["stage_timeline"] = timeline
     if not args.no_cpu_baseline and (REPO / "oracle" / "_ref" / "libllmref.so").exists():
         threads = len(os.sched_getaffinity(0))
         step_ms, moe_ms = reference_decode_ms(dec, 5, threads)
@@ -773,6 +815,9 @@ def main():
                     help="time the MoE backward (moe_b200_backward_device) instead of the forward")
     ap.add_argument("--cta-pair", action="store_true",
                     help="TF32 path on the CTA-pair (cta_group::2) GEMM kernels")
+    ap.add_argument("--stage-times", action="store_true",
+                    help="c2: add the device decoder's stage timeline (a separate decoder with "
+                         "globaltimer stamps, outside the timed loops)")
     ap.add_argument("--tokens", type=int, default=None,
                     help="override T (small profiling cases; the JSON config records it)")
     ap.add_argument("--d-ff", type=int, default=None,

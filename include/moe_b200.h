@@ -320,6 +320,15 @@ int moe_b200_decoder_launches(const moe_b200_decoder *dec);
  * per-layer parity against the reference's moe_forward with T=1 on the same
  * x_norm (src/transformer.c:287-366). */
 int moe_b200_decoder_trace(moe_b200_decoder *dec, int layer, float *x_norm, float *ffn_out);
+/* Stage timeline of the last step (stage kernels created with the
+ * environment variable MOE_B200_DECODER_STAMPS=1): for each of the 5 L + 1
+ * stages (5 l + {0 Q/K/V, 1 attention, 2 W_O, 3 up/gate, 4 down}, then the
+ * LM head) four times in microseconds from the step's first CTA entry: the
+ * earliest CTA entry, the earliest and the latest return from the stage's
+ * wait for its predecessor, the latest CTA exit (-1 when not recorded).
+ * out holds at least 4 * (5 L + 1) doubles; returns the stage count or a
+ * negative status.  Profiling aid, no counterpart in llm.c. */
+int moe_b200_decoder_stage_times(moe_b200_decoder *dec, double *out, int n);
 int moe_b200_decoder_destroy(moe_b200_decoder *dec);
 
 /* ---- llm.c checkpoints straight to the device ----------------------------

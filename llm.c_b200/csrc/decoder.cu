@@ -71,6 +71,7 @@ struct StepArgs {
     int *err;                          // barrier timeout flag
     int *err_host;                     // mapped pinned copy, written at the end of every step
     float *trace;                      // [L][2][d]: pre-FFN x_norm and FFN output per layer
+    unsigned long long *stamps;        // stage timeline [5 L + 1][4] (%globaltimer ns), or null
     int pdl_early;                     // stage kernels: let the next kernel launch on entry
     int flags;                         // stage kernels hand off through done[] (see stage_wait):
                                        // 1 the next kernel may launch after a CTA's wait, 2 after its work
@@ -153,6 +154,25 @@ __device__ __forceinline__ void prefetch_l2(const float *p, size_t n, int t, int
         asm volatile("prefetch.global.L2 [%0];" ::"l"(p + l * 32));
 }
 
+// Stage timeline (MOE_B200_DECODER_STAMPS=1): per stage, the earliest CTA
+// entry, the earliest and latest return from the stage's wait, and the
+// latest CTA exit, in %globaltimer nanoseconds (thread 0 of each CTA).
+__device__ __forceinline__ void stamp_min(const StepArgs &A, int st, int which) {
+    if (A.stamps && st >= 0 && threadIdx.x == 0)
+        atomicMin(A.stamps + 4 * st + which, (unsigned long long)globaltimer_ns());
+}
+__device__ __forceinline__ void stamp_max(const StepArgs &A, int st, int which) {
+    if (A.stamps && st >= 0 && threadIdx.x == 0)
+        atomicMax(A.stamps + 4 * st + which, (unsigned long long)globaltimer_ns());
+}
+// the CTA's exit: after every thread's work
+__device__ __forceinline__ void stamp_exit(const StepArgs &A, int st) {
+    if (A.stamps) {
+        __syncthreads();
+        stamp_max(A, st, 3);
+    }
+}
+
 // Flag mode: wait (thread 0, then the CTA) until done[idx] reaches target.
 __device__ __forceinline__ void flag_wait(const StepArgs &A, int idx, unsigned target) {
     if (threadIdx.x == 0) {
@@ -174,9 +194,13 @@ __device__ __forceinline__ void stage_wait(const StepArgs &A, int st) {
     if (st < 0) return;
     if (!A.flags) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        stamp_min(A, st, 1);
+        stamp_max(A, st, 2);
         return;
     }
     if (st > 0) flag_wait(A, st - 1, stage_ctas(A, st - 1));
+    stamp_min(A, st, 1);
+    stamp_max(A, st, 2);
     if (A.flags == 1) pdl_trigger();
 }
 
@@ -766,32 +790,39 @@ __device__ void lmhead_item(const StepArgs &A, int item, bool normed, Smem &S, i
 
 __global__ void __launch_bounds__(kThreads) qkv_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    stamp_min(A, 5 * layer, 0);
     if (A.pdl_early) pdl_trigger();
     if (A.flags == 1 && (A.early_mask >> 0 & 1)) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
     const int st = 5 * layer;
     qkv_item(A, Lp, layer, A.state[0], A.state[1], blockIdx.x, S, st);
+    stamp_exit(A, st);
     stage_signal(A, st);
 }
 __global__ void __launch_bounds__(kThreads) attn_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    stamp_min(A, 5 * layer + 1, 0);
     if (A.pdl_early) pdl_trigger();
     if (A.flags == 1 && (A.early_mask >> 1 & 1)) pdl_trigger();
     const int pos = A.state[1], st = 5 * layer + 1;
     // chunks past the step's position have no work (they still count as done)
     if ((int)blockIdx.y * CH <= pos) attn_item(A, layer, pos, blockIdx.x, blockIdx.y, S, st);
+    stamp_exit(A, st);
     stage_signal(A, st);
 }
 __global__ void __launch_bounds__(kThreads, 1) oproj_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    stamp_min(A, 5 * layer + 2, 0);
     if (A.pdl_early) pdl_trigger();
     if (A.flags == 1 && (A.early_mask >> 2 & 1)) pdl_trigger();
     const int st = 5 * layer + 2;
     oproj_item(A, A.layers[layer], A.state[1], blockIdx.x, S, st);
+    stamp_exit(A, st);
     stage_signal(A, st);
 }
 __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    stamp_min(A, 5 * layer + 3, 0);
     if (A.pdl_early) pdl_trigger();
     if (A.flags == 1 && (A.early_mask >> 3 & 1)) pdl_trigger();
     const LayerPtrs Lp = A.layers[layer];
@@ -801,26 +832,37 @@ __global__ void __launch_bounds__(kThreads) upgate_kernel(StepArgs A, int layer)
     if (A.flags != 1 || !down_flag_fits(Lp))
         prefetch_down(A, Lp, blockIdx.x * kThreads + threadIdx.x, gridDim.x * kThreads, S);
     upgate_item(A, Lp, blockIdx.x, S);
+    stamp_exit(A, st);
     stage_signal(A, st);
 }
 __global__ void __launch_bounds__(kThreads, 1) down_kernel(StepArgs A, int layer) {
     __shared__ Smem S;
+    stamp_min(A, 5 * layer + 4, 0);
     if (A.pdl_early) pdl_trigger();
     if (A.flags == 1 && (A.early_mask >> 4 & 1)) pdl_trigger();
     const int st = 5 * layer + 4;
     const LayerPtrs Lp = A.layers[layer];
     if (A.flags == 1 && down_flag_fits(Lp)) down_item_flag(A, Lp, layer, blockIdx.x, S, st);
     else down_item(A, Lp, layer, blockIdx.x, S, st);
+    stamp_exit(A, st);
     stage_signal(A, st);
 }
 __global__ void __launch_bounds__(kThreads) lmhead_kernel(StepArgs A) {
     __shared__ Smem S;
+    stamp_min(A, 5 * A.L, 0);
     if (A.pdl_early) pdl_trigger();
     lmhead_item(A, blockIdx.x, false, S, 5 * A.L);
+    stamp_exit(A, 5 * A.L);
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         A.state[1] += 1;
         *(volatile int *)A.err_host = *(volatile int *)A.err;   // read by the host after the step
     }
+}
+
+// the stage timeline back to "no stamp": minima to ~0, maxima to 0
+__global__ void stamps_reset_kernel(unsigned long long *stamps, int n) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        stamps[i] = (i % 4 < 2) ? ~0ull : 0ull;
 }
 
 // ---- the whole step as one persistent cooperative kernel ----
@@ -917,6 +959,7 @@ struct moe_b200_decoder {
     int *h_err = nullptr;                        // mapped pinned copy of err (StepArgs::err_host)
     int *d_err_host = nullptr;                   // its device address
     float *trace = nullptr;                      // [L][2][d], see StepArgs::trace
+    unsigned long long *stamps = nullptr;        // StepArgs::stamps (MOE_B200_DECODER_STAMPS=1)
     int *h_token = nullptr;                      // pinned
     int maxF_pad = 0;
     cudaStream_t stream = nullptr;
@@ -960,7 +1003,7 @@ void free_all(moe_b200_decoder *m) {
     cudaFree(m->rope_cos); cudaFree(m->rope_sin); cudaFree(m->kc); cudaFree(m->vc);
     cudaFree(m->x); cudaFree(m->q); cudaFree(m->part); cudaFree(m->h);
     cudaFree(m->logits); cudaFree(m->wts); cudaFree(m->state); cudaFree(m->ids);
-    cudaFree(m->bar); cudaFree(m->done); cudaFree(m->err); cudaFree(m->trace);
+    cudaFree(m->bar); cudaFree(m->done); cudaFree(m->stamps); cudaFree(m->err); cudaFree(m->trace);
     if (m->h_token) cudaFreeHost(m->h_token);
     if (m->h_err) cudaFreeHost(m->h_err);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -978,6 +1021,7 @@ StepArgs step_args(const moe_b200_decoder *m) {
     A.x = m->x; A.q = m->q; A.part = m->part; A.h = m->h; A.logits = m->logits; A.wts = m->wts;
     A.state = m->state; A.ids = m->ids; A.bar = m->bar; A.err = m->err;
     A.trace = m->trace;
+    A.stamps = (m->flags & MOE_B200_DECODER_PERSISTENT) ? nullptr : m->stamps;
     A.err_host = m->d_err_host;
     A.pdl_early = m->pdl == 1;
     A.flags = (m->flags & MOE_B200_DECODER_PERSISTENT) ? 0 : m->pdl == 3 ? 1 : m->pdl == 4 ? 2 : 0;
@@ -1015,6 +1059,10 @@ int enqueue_step(moe_b200_decoder *m) {
     // writes with griddepcontrol or, in flag mode, the done[] counters,
     // zeroed here: see stage_wait)
     if (m->pdl >= 3) DCK(cudaMemsetAsync(m->done, 0, (size_t)(6 * m->L + 1) * sizeof(unsigned), s));
+    if (m->stamps) {
+        stamps_reset_kernel<<<1, 256, 0, s>>>(m->stamps, 4 * (5 * m->L + 1));
+        DCK(cudaGetLastError());
+    }
     int n = 0;
     auto launch = [&](auto kernel, dim3 grid, auto... args) -> cudaError_t {
         cudaLaunchConfig_t cfg = {};
@@ -1076,6 +1124,8 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
     m->flags = flags;
     if (const char *p = std::getenv("MOE_B200_DECODER_PDL")) m->pdl = std::atoi(p);
     if (const char *p = std::getenv("MOE_B200_DECODER_EARLY")) m->early_mask = std::atoi(p);
+    const char *stp = std::getenv("MOE_B200_DECODER_STAMPS");
+    const bool want_stamps = stp && std::atoi(stp) != 0 && !persistent(flags);
     Dims &D = m->D;
     D.d = d; D.d_pad = round_up(d, 128); D.nh = nh; D.nkv = nkv; D.hd = hd; D.nq = nh * hd;
     D.kvd = nkv * hd; D.qkv = D.nq + 2 * D.kvd; D.vocab = c.vocab_size; D.max_seq = max_seq;
@@ -1130,6 +1180,8 @@ int moe::decoder_build(const DecSrc &src, int max_seq, int flags, moe_b200_decod
         cudaMalloc(&m->bar, 4) != cudaSuccess || cudaMalloc(&m->err, 4) != cudaSuccess ||
         cudaMalloc(&m->done, (size_t)(6 * L + 1) * sizeof(unsigned)) != cudaSuccess ||
         cudaMalloc(&m->trace, (size_t)m->L * 2 * d * 4) != cudaSuccess ||
+        (want_stamps &&
+         cudaMalloc(&m->stamps, (size_t)4 * (5 * L + 1) * sizeof(unsigned long long)) != cudaSuccess) ||
         cudaMallocHost(&m->h_token, 4) != cudaSuccess ||
         cudaHostAlloc(&m->h_err, 4, cudaHostAllocMapped) != cudaSuccess ||
         cudaHostGetDevicePointer((void **)&m->d_err_host, m->h_err, 0) != cudaSuccess) {
@@ -1253,6 +1305,25 @@ extern "C" int moe_b200_decoder_set_pos(moe_b200_decoder *m, int pos) {
 extern "C" int moe_b200_decoder_pos(const moe_b200_decoder *m) { return m ? m->pos : -1; }
 
 extern "C" int moe_b200_decoder_launches(const moe_b200_decoder *m) { return m ? m->launches : 0; }
+
+extern "C" int moe_b200_decoder_stage_times(moe_b200_decoder *m, double *out, int n) {
+    if (!m || !out) return dfail(MOE_B200_E_INVALID, "null argument");
+    if (!m->stamps) return dfail(MOE_B200_E_STATE, "stage timeline off (MOE_B200_DECODER_STAMPS=1)");
+    const int ns = 5 * m->L + 1;
+    if (n < 4 * ns) return dfail(MOE_B200_E_INVALID, "out holds fewer than 4 * (5 L + 1) values");
+    if (m->pos == 0) return dfail(MOE_B200_E_STATE, "no step taken yet");
+    DCK(cudaSetDevice(m->device));
+    DCK(cudaStreamSynchronize(m->stream));
+    std::vector<unsigned long long> h((size_t)4 * ns);
+    DCK(cudaMemcpy(h.data(), m->stamps, h.size() * sizeof(unsigned long long),
+                   cudaMemcpyDeviceToHost));
+    const unsigned long long t0 = h[0];
+    for (size_t i = 0; i < h.size(); i++) {
+        const bool unset = (i % 4 < 2) ? h[i] == ~0ull : h[i] == 0ull;
+        out[i] = unset ? -1.0 : (double)(long long)(h[i] - t0) * 1e-3;
+    }
+    return ns;
+}
 
 extern "C" int moe_b200_decoder_trace(moe_b200_decoder *m, int layer, float *x_norm,
                                       float *ffn_out) {

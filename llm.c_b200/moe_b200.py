@@ -105,6 +105,7 @@ def lib() -> C.CDLL:
     L.moe_b200_decoder_launches.argtypes = [_vp]
     L.moe_b200_decoder_destroy.argtypes = [_vp]
     L.moe_b200_decoder_trace.argtypes = [_vp, C.c_int, _fp, _fp]
+    L.moe_b200_decoder_stage_times.argtypes = [_vp, C.POINTER(C.c_double), C.c_int]
     L.moe_b200_llmc_trace_enable.argtypes = [C.c_int]
     L.moe_b200_llmc_trace_read.argtypes = [C.c_int, _fp, _fp]
     _lib = L
@@ -805,6 +806,18 @@ class Decoder:
         _check(lib().moe_b200_decoder_trace(self.handle, int(layer), _f(xn), _f(fo)),
                "moe_b200_decoder_trace")
         return xn, fo
+
+    def stage_times(self, n_layers: int) -> np.ndarray:
+        """[5 L + 1, 4] stage timeline of the last step in microseconds
+        (decoder created with MOE_B200_DECODER_STAMPS=1): earliest entry,
+        earliest and latest return from the wait, latest exit."""
+        ns = 5 * n_layers + 1
+        out = np.empty(4 * ns, np.float64)
+        rc = lib().moe_b200_decoder_stage_times(
+            self.handle, out.ctypes.data_as(C.POINTER(C.c_double)), int(out.size))
+        if rc < 0:
+            _check(rc, "moe_b200_decoder_stage_times")
+        return out.reshape(ns, 4)
 
     def free(self):
         if self.handle:

@@ -169,3 +169,29 @@ def test_device_decode_rejects_conflicting_flags(moe):
             M.Decoder(m, 4, flags)
         assert e.value.status == M.E_INVALID
     O.release_ref_model(m)
+
+
+def test_stage_timeline(moe, monkeypatch):
+    """MOE_B200_DECODER_STAMPS=1 records every stage's entry, wait and exit
+    times; the logits are the same bits as without it, the times are
+    ordered within a stage, and a decoder without it refuses the read."""
+    m = _model(8, 2, max_seq=16)
+    plain = M.Decoder(m, 16)
+    monkeypatch.setenv("MOE_B200_DECODER_STAMPS", "1")
+    timed = M.Decoder(m, 16)
+    a = np.empty(V, np.float32)
+    b = np.empty(V, np.float32)
+    for t in (3, 17, 4000, 5):
+        plain.step(t, a)
+        timed.step(t, b)
+        assert np.array_equal(a, b)
+        st = timed.stage_times(6)
+        assert st.shape == (31, 4)
+        assert st[0, 0] == 0.0 and np.all(st >= 0.0)
+        assert np.all(st[:, 1] <= st[:, 2]) and np.all(st[:, 2] <= st[:, 3])
+        assert np.all(st[:, 0] <= st[:, 3])
+        assert st[-1, 3] == st[:, 3].max()
+    with pytest.raises(M.MoEError):
+        plain.stage_times(6)
+    plain.free()
+    timed.free()
