@@ -84,7 +84,8 @@ class ClockSampler:
     nvidia-smi takes a few hundred milliseconds to print its first sample, so
     entering the context waits (up to 3 s) until the first sample has arrived:
     the samples then cover the timed region even when it is short (a multi-GPU
-    step of ~10 ms), at 50 ms intervals."""
+    step of ~10 ms), at 50 ms intervals; a region shorter than one interval
+    keeps the sample taken right after it."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -119,6 +120,11 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc is not None:
+            # a region shorter than the sampling interval still gets the
+            # sample that follows it (up to 0.2 s later)
+            t_end = time.time() + 0.2
+            while not self.lines and time.time() < t_end:
+                time.sleep(0.005)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
